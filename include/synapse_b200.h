@@ -1,0 +1,243 @@
+/*
+ * synapse_b200.h -- C ABI of the B200 (sm_100a) decode path.
+ *
+ * This is the drop-in boundary for branes-ai/synapse's Llama decode hot path:
+ * the quantized matrix-vector products behind op_matmul, RoPE + KV append +
+ * GQA decode attention behind op_rope / op_attention, the element-wise ops
+ * around them, the device arena the GGUF loader and static planner fill, and
+ * tensor parallelism over the GPUs of one NVLink box. Every comment cites the
+ * reference interface (path:line inside branes-ai/synapse v0.15.12,
+ * sdk/include/branes/synapse/) that the entry point replaces.
+ *
+ * Conventions (as the reference's kernels: no allocation, no throw):
+ *   - every kernel entry point is asynchronous on the caller's stream
+ *     (a cudaStream_t passed as void*; NULL = legacy default stream);
+ *   - pointers are device pointers unless the name says host_;
+ *   - scratch memory, where needed, is the caller's (a planned arena region);
+ *   - the return value is a syn_status: 0 on success, never an abort.
+ *
+ * Tensor types are GGUF ggml_type tags (gguf/tensor_type.hpp:25-46).
+ */
+#ifndef SYNAPSE_B200_H
+#define SYNAPSE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    SYN_OK = 0,
+    SYN_ERR_INVALID = 1,      /* bad argument (a precondition the reference asserts) */
+    SYN_ERR_UNSUPPORTED = 2,  /* a type / shape this build does not implement */
+    SYN_ERR_CUDA = 3,         /* a CUDA runtime error (launch, copy, memory) */
+    SYN_ERR_NO_MEMORY = 4,    /* device memory exhausted */
+    SYN_ERR_TIMEOUT = 5,      /* a bounded wait gave up (multi-GPU flags) */
+    SYN_ERR_NCCL = 6,         /* a collective failed */
+    SYN_ERR_FORMAT = 7,       /* malformed GGUF / model metadata */
+    SYN_ERR_RANGE = 8         /* token or position out of range: session::run returns false */
+} syn_status;
+
+enum { SYN_F32 = 0, SYN_F16 = 1, SYN_Q4_0 = 2, SYN_Q8_0 = 8 };
+
+/* Weight layouts in device memory.
+ *   SYN_LAYOUT_GGUF   : the GGUF bytes unchanged (rows of 18 B / 34 B blocks).
+ *   SYN_LAYOUT_PLANAR : repacked for 16-byte coalesced loads: the quant plane
+ *                       (rows x blocks x 16 B for Q4_0, x 32 B for Q8_0), then,
+ *                       at the next 256-byte boundary, the binary16 scale plane
+ *                       (rows x blocks). Same total bytes plus padding.
+ * Plain F32/F16 weights have one layout (row-major). */
+enum { SYN_LAYOUT_GGUF = 0, SYN_LAYOUT_PLANAR = 1 };
+
+/* Build-time identity: "sm_100a" and the library version. */
+const char* syn_build_info(void);
+/* Human-readable name of a status. */
+const char* syn_status_string(int status);
+/* The last CUDA error string seen by this thread (for SYN_ERR_CUDA). */
+const char* syn_last_error(void);
+
+/* ------------------------------------------------------------------------
+ * Q8_0 activations (quant/q8.hpp:54-69 quantize_row_q8_0; kernels/gemv.hpp:
+ * 72-116 prepare_activations). The device form of n_tok rows of `cols` is
+ * planar: int8 quants [n_tok][cols], then binary16 scales [n_tok][cols/32],
+ * then the decoded float scales [n_tok][cols/32], then the int32 block sums
+ * [n_tok][cols/32] (each plane 256-byte aligned). Quants and binary16 scales
+ * are bit-identical to the reference's block_q8_0 (quant/blocks.hpp:49-53).
+ * ---------------------------------------------------------------------- */
+size_t syn_q8_act_bytes(int n_tok, int cols);
+/* x: f32 [n_tok][cols] -> act. Replaces gemm_prepare_rows (gemm.hpp:111). */
+int syn_quantize_q8_0(const float* x, int n_tok, int cols, void* act, void* stream);
+/* act -> ggml block_q8_0 bytes [n_tok][cols/32][34] (checking / interchange). */
+int syn_q8_act_to_blocks(const void* act, int n_tok, int cols, void* blocks, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Weights: device bytes of a rows x cols matrix in a layout, and the
+ * GGUF -> planar repack the loader runs once per tensor (gguf/tensor_view.hpp:
+ * 33-40 view_as; SURVEY loader item (1)).
+ * ---------------------------------------------------------------------- */
+size_t syn_weight_bytes(int type, int rows, int cols, int layout);
+/* src (device, GGUF layout) -> dst (device, planar). src and dst must not overlap. */
+int syn_repack_planar(int type, const void* src, int rows, int cols, void* dst, void* stream);
+/* host GGUF bytes -> dst (device, `layout`), staged through the caller's device
+ * buffer `staging` of `staging_bytes` (>= 1 MiB; unused for GGUF layout and
+ * plain types). Synchronous with respect to the host buffer. */
+int syn_upload_weight(int type, const void* host_src, int rows, int cols, void* dst, int layout, void* staging,
+                      size_t staging_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * mul_mat: Y[t][r] = W[r,:] . X[t,:] for t < n_tok (kernels/gemm.hpp:143-230
+ * gemm_rows, the n_tok = 1 case being kernels/gemv.hpp:149-161 gemv).
+ *   Q4_0 / Q8_0 weights take Q8_0 activations (syn_quantize_q8_0); each block
+ *   is an exact integer dot scaled by d_w * d_a (kernels/dot.hpp:103-164,
+ *   :268-322); rows may be in either layout.
+ *   F32 / F16 weights take float activations (kernels/dot.hpp:404-433).
+ * residual (may be NULL): Y[t][r] += residual[t][r] after the dot, the
+ *   reference's following op_add (elementwise.hpp:29); it may alias y.
+ * ---------------------------------------------------------------------- */
+int syn_gemv_q(int type, const void* w, int layout, int rows, int cols, const void* act, int n_tok, float* y,
+               const float* residual, void* stream);
+int syn_gemv_f(int type, const void* w, int rows, int cols, const float* x, int n_tok, float* y,
+               const float* residual, void* stream);
+
+/* ------------------------------------------------------------------------
+ * RoPE + KV append + GQA decode attention (kernels/attention.hpp:89-129 rope,
+ * :165-175 kv_append, :185-244 attend_group, :254-269 attention), fused:
+ * for each query b < n_q, with its position p = pos[b] (device int32):
+ *   q_b and (if append) k_b are rotated at p; k_b, v_b are stored as F16 in
+ *   row p of the cache; out_b = softmax(scale * q_b K^T) V over rows 0..p,
+ *   query head h reading KV head h / (n_head / n_kv).
+ * Caches: K and V of query b start at (k|v)_cache + b * cache_stride halves,
+ *   rows of n_kv * head_dim halves (attention.hpp:133-143). cache_stride =
+ *   max_ctx * n_kv * head_dim for independent sequences (batched decode), or 0
+ *   for tokens of one sequence (then append must be 0: use syn_rope_kv_append
+ *   first, as session.hpp:349-356 appends every token before attending).
+ * max_len bounds pos[b] + 1 for every b (it sizes the split grid and scratch).
+ * rope_mode: 0 normal (Llama), 1 neox. freq_factors: NULL or head_dim/2 floats
+ * (device). yarn: NULL or 5 floats {freq_scale, ext_factor, attn_factor,
+ * corr_low, corr_high} (host), attention.hpp:60-66.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+    const float* q;        /* [n_q][n_head * head_dim], before RoPE */
+    const float* k;        /* [n_q][n_kv * head_dim], before RoPE (append only) */
+    const float* v;        /* [n_q][n_kv * head_dim] (append only) */
+    uint16_t* k_cache;     /* binary16 bits */
+    uint16_t* v_cache;
+    const int32_t* pos;    /* [n_q] device */
+    float* out;            /* [n_q][n_head * head_dim] */
+    void* scratch;         /* syn_attention_scratch_bytes */
+    size_t cache_stride;   /* halves between the caches of consecutive queries */
+    int n_q, n_head, n_kv, head_dim, max_len;
+    int append;            /* 1: rotate k and append (k, v) inside the kernel */
+    int rope;              /* 1: rotate q (and k) at pos; 0: q, k already rotated */
+    int rope_mode;
+    float theta_scale;     /* rope_theta_scale(base, head_dim), attention.hpp:47 */
+    float scale;           /* 1 / sqrt(head_dim), models/llama.hpp:407 */
+    const float* freq_factors;
+    const float* yarn;
+} syn_attention_args;
+
+size_t syn_attention_scratch_bytes(int n_q, int n_head, int n_kv, int head_dim, int max_len);
+int syn_attention(const syn_attention_args* a, void* stream);
+/* RoPE + F16 append only, for n_q tokens sharing one cache (prefill). */
+int syn_rope_kv_append(const syn_attention_args* a, void* stream);
+/* RoPE alone (attention.hpp:89): out[i] = rope(x[i], pos[i]) for n rows of
+ * n_heads * head_dim floats. */
+int syn_rope(const float* x, float* out, int n, int n_heads, int head_dim, const int32_t* pos, float theta_scale,
+             const float* freq_factors, int rope_mode, const float* yarn, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Element-wise ops (kernels/elementwise.hpp), each on n_tok rows.
+ * ---------------------------------------------------------------------- */
+/* out = x / rms(x) * gamma (elementwise.hpp:208-232), then optionally quantized
+ * to Q8_0 activations; out_f32 and act may each be NULL. */
+int syn_rms_norm(const float* x, const float* gamma, int n_tok, int cols, float eps, float* out_f32, void* act,
+                 void* stream);
+/* out = silu(g) * u (elementwise.hpp:76, :50), optionally quantized. */
+int syn_silu_mul(const float* g, const float* u, int n_tok, int cols, float* out_f32, void* act, void* stream);
+/* out = a + b (elementwise.hpp:29); out may alias a or b. */
+int syn_add(const float* a, const float* b, float* out, size_t n, void* stream);
+/* out[t] = row tokens[t] of the table (session.hpp:331-336 op_embed). */
+int syn_embed(int type, const void* table, int layout, int rows, int cols, const int32_t* tokens, int n_tok,
+              float* out, void* stream);
+/* out[t] = first index of the largest of x[t][0..n) (llama_decode.cpp:274,
+ * std::max_element: ties go to the lowest index). */
+int syn_argmax(const float* x, int n_tok, int n, int32_t* out, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Llama decode session (models/llama.hpp:324-489 load_llama + graph/
+ * session.hpp:82-171): weights, activations and the F16 KV cache in one device
+ * arena placed by the static planner (graph/planner.hpp:90-128); run() is a
+ * captured CUDA graph per token.
+ * ---------------------------------------------------------------------- */
+typedef struct syn_session syn_session;
+
+typedef struct {
+    int n_layer, n_embd, n_ff, n_head, n_head_kv, head_dim, n_vocab;
+    float rms_eps, rope_base;
+    int rope_mode;         /* 0 normal (llama) */
+    int type_embd;         /* token_embd type */
+    int type_layers;       /* attention + FFN matrices */
+    int type_output;       /* output head; -1 = tied to token_embd */
+} syn_llama_config;
+
+/* Open a GGUF Llama file (models/llama.hpp:206-319 read_llama_config rules). */
+int syn_session_open_gguf(const char* path, int max_ctx, int device, syn_session** out);
+/* A model of random N(0, 0.02) weights quantized on the device (seeded),
+ * norm weights 1; for benchmarks at shapes no file exists for. */
+int syn_session_open_synthetic(const syn_llama_config* c, int max_ctx, uint64_t seed, int device,
+                               syn_session** out);
+void syn_session_close(syn_session* s);
+int syn_session_config(const syn_session* s, syn_llama_config* out);
+/* Bytes of the device arena, of the weights and of the KV cache. */
+int syn_session_memory(const syn_session* s, size_t* arena, size_t* weights, size_t* kv);
+/* Zero the KV cache (session.hpp:127 reset). */
+int syn_session_reset(syn_session* s);
+/* One token at pos (session.hpp:133 run(step)): host_logits (n_vocab floats)
+ * and host_argmax may be NULL. Returns SYN_ERR_RANGE (running nothing) when
+ * token >= n_vocab or pos >= max_ctx. Blocks until the outputs are on the host. */
+int syn_session_step(syn_session* s, uint32_t token, uint32_t pos, float* host_logits, int32_t* host_argmax);
+/* n_steps steps on the device from position pos, with no host round trip
+ * between them: step i feeds prompt[i] while i < n_prompt, else the argmax of
+ * step i - 1 (greedy decode, llama_decode.cpp:267-291); host_tokens (n_steps)
+ * receives each step's argmax and the call returns when they are on the host;
+ * with host_tokens NULL the call only enqueues the steps on the session's
+ * stream (synchronise on syn_session_stream). 1 <= n_prompt <= n_steps. */
+int syn_session_generate(syn_session* s, const uint32_t* prompt, int n_prompt, uint32_t pos, int n_steps,
+                         int32_t* host_tokens);
+/* Kernel launches one step makes (each graph replay launches exactly these). */
+int syn_session_launches_per_step(const syn_session* s);
+
+/* One step at (token, pos) run op by op with CUDA events around every op on the
+ * session's stream (no graph), for per-kernel timing. For each op: its kind
+ * (SYN_OP_*), layer (-1 outside layers), weight type, rows, cols, device time
+ * (ms) and algorithmic bytes (what the op must move at least once: weights
+ * with their scales, activations in and out, KV rows 0..pos). Returns the op
+ * count in *n_ops (at most max_ops records written). */
+enum { SYN_OP_EMBED = 0, SYN_OP_RMS_NORM = 1, SYN_OP_QUANTIZE = 2, SYN_OP_MATMUL = 3, SYN_OP_ATTENTION = 4,
+       SYN_OP_SILU_MUL = 5, SYN_OP_ARGMAX = 6 };
+typedef struct {
+    int kind, layer, type, rows, cols;
+    float ms;
+    double bytes;
+} syn_op_profile;
+int syn_session_profile(syn_session* s, uint32_t token, uint32_t pos, syn_op_profile* out, int max_ops, int* n_ops);
+
+/* Copy device memory to the host (synchronous), e.g. a KV cache for checking. */
+int syn_copy_to_host(void* host_dst, const void* device_src, size_t bytes);
+
+/* Device pointers of the session's logits (n_vocab floats) and stream. */
+float* syn_session_logits(syn_session* s);
+void* syn_session_stream(syn_session* s);
+/* Device pointer and geometry of a layer's KV cache (K then V, max_ctx rows of
+ * n_head_kv * head_dim halves each). */
+uint16_t* syn_session_kv(syn_session* s, int layer, int which /*0 K, 1 V*/);
+/* Copy a tensor of the model to the host in GGUF layout (for checking). */
+int syn_session_weight(syn_session* s, const char* name, void* host_out, size_t bytes, int* type, int* rows,
+                       int* cols);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

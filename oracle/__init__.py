@@ -67,6 +67,9 @@ def lib():
         L.orc_llama_kcache.argtypes = [vp, sz]
         L.orc_llama_vcache.restype = vp
         L.orc_llama_vcache.argtypes = [vp, sz]
+        L.orc_llama_run.argtypes = [vp, ctypes.c_uint32, ctypes.c_uint32, sz, sz, ctypes.c_int, vp]
+        L.orc_llama_run.restype = ctypes.c_int
+        L.orc_fill_random.argtypes = [ctypes.c_int, sz, sz, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float, vp]
         L.orc_set_threads.argtypes = [ctypes.c_int]
         L.orc_get_threads.restype = ctypes.c_int
         _lib = L
@@ -144,6 +147,16 @@ def quantize_weights(x, type_):
         h = np.array([float_to_fp16(v) for v in x.reshape(-1)], dtype=np.uint16)
         return h.view(np.uint8).reshape(x.shape[0], -1)
     raise ValueError(type_)
+
+
+def random_weights(type_, rows, cols, seed, tensor, sigma=0.02):
+    """Seeded N(0, sigma) weights in GGUF bytes (float32 array for F32), made on the oracle's threads."""
+    if type_ == F32:
+        out = np.empty((rows, cols), dtype=np.float32)
+    else:
+        out = np.empty((rows, row_bytes(type_, cols)), dtype=np.uint8)
+    lib().orc_fill_random(type_, rows, cols, seed, tensor, sigma, _p(out))
+    return out
 
 
 def dequantize(type_, data, rows, cols):
@@ -289,6 +302,13 @@ class Llama:
         if rc != 0:
             raise ValueError("oracle step rejected token/pos")
         return logits
+
+    def run(self, token, pos, l0, l1, embed=True, logits=False):
+        """Part of a step (embedding, layers [l0, l1), optionally the head)."""
+        out = np.empty(self.cfg["n_vocab"], dtype=np.float32) if logits else None
+        if lib().orc_llama_run(self.h, int(token), int(pos), l0, l1, int(embed), _p(out)) != 0:
+            raise ValueError("oracle run rejected its arguments")
+        return out
 
     def reset(self):
         lib().orc_llama_reset(self.h)

@@ -495,12 +495,18 @@ static void matmul(const orc_tensor* w, size_t rows, size_t cols, const float* x
 }
 
 int orc_llama_step(orc_llama* m, uint32_t token, uint32_t pos, float* logits) {
+    return orc_llama_run(m, token, pos, 0, m->c.n_layer, 1, logits);
+}
+
+int orc_llama_run(orc_llama* m, uint32_t token, uint32_t pos, size_t l0, size_t l1, int embed, float* logits) {
     const orc_llama_config* c = &m->c;
-    if (token >= c->n_vocab || pos >= c->max_ctx) return 1; /* session::run returns false */
+    if (token >= c->n_vocab || pos >= c->max_ctx || l1 > c->n_layer) return 1; /* session::run returns false */
     const size_t d = c->n_embd, qrow = c->n_head * c->head_dim, kvrow = c->n_head_kv * c->head_dim;
     /* op_embed (session.hpp:331-336): decode_row of token_embd */
-    orc_dequantize_row(m->embd.type, (const uint8_t*)m->embd.data + token * orc_row_bytes(m->embd.type, d), d, m->x);
-    for (size_t l = 0; l < c->n_layer; ++l) {
+    if (embed)
+        orc_dequantize_row(m->embd.type, (const uint8_t*)m->embd.data + token * orc_row_bytes(m->embd.type, d), d,
+                           m->x);
+    for (size_t l = l0; l < l1; ++l) {
         const orc_layer* L = &m->layers[l];
         orc_rms_norm(m->x, (const float*)L->attn_norm.data, c->rms_eps, m->h, d);
         matmul(&L->wq, qrow, d, m->h, m->q);
@@ -520,7 +526,55 @@ int orc_llama_step(orc_llama* m, uint32_t token, uint32_t pos, float* logits) {
         matmul(&L->down, d, c->n_ff, m->act, m->dn);
         orc_add(m->dn, m->x, m->x, d);
     }
-    orc_rms_norm(m->x, (const float*)m->out_norm.data, c->rms_eps, m->last, d);
-    matmul(&m->out, c->n_vocab, d, m->last, logits);
+    if (logits) {
+        orc_rms_norm(m->x, (const float*)m->out_norm.data, c->rms_eps, m->last, d);
+        matmul(&m->out, c->n_vocab, d, m->last, logits);
+    }
     return 0;
+}
+
+/* ---- synthetic weights (not part of the reference: it only reads files) ---- */
+static uint64_t mix64(uint64_t z) {
+    z += 0x9e3779b97f4a7c15ull;
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    return z ^ (z >> 31);
+}
+
+typedef struct {
+    int type;
+    size_t cols;
+    uint64_t seed, tensor;
+    float sigma;
+    uint8_t* out;
+} orc_fill_ctx;
+
+static void fill_row(size_t r, void* p) {
+    orc_fill_ctx* c = (orc_fill_ctx*)p;
+    float buf[ORC_PLAIN_CHUNK];
+    const size_t rb = orc_row_bytes(c->type, c->cols);
+    for (size_t i = 0; i < c->cols; i += ORC_PLAIN_CHUNK) {
+        const size_t len = c->cols - i < ORC_PLAIN_CHUNK ? c->cols - i : ORC_PLAIN_CHUNK;
+        for (size_t j = 0; j < len; ++j) {
+            const uint64_t idx = r * c->cols + i + j;
+            const uint64_t h = mix64(c->seed ^ mix64(c->tensor * 0x100000001b3ull ^ mix64(idx)));
+            const float u1 = ((float)(uint32_t)(h >> 40) + 1.0f) * (1.0f / 16777217.0f);
+            const float u2 = (float)(uint32_t)(h & 0xffffffu) * (1.0f / 16777216.0f);
+            buf[j] = sqrtf(-2.0f * logf(u1)) * cosf(6.2831853f * u2) * c->sigma;
+        }
+        uint8_t* row = c->out + r * rb;
+        switch (c->type) {
+        case ORC_F32: memcpy(row + i * 4, buf, len * 4); break;
+        case ORC_F16:
+            for (size_t j = 0; j < len; ++j) ((uint16_t*)row)[i + j] = orc_float_to_fp16(buf[j]);
+            break;
+        case ORC_Q4_0: orc_quantize_row_q4_0(buf, len, (orc_block_q4_0*)(row + i / ORC_QK * 18)); break;
+        case ORC_Q8_0: orc_quantize_row_q8_0(buf, len, (orc_block_q8_0*)(row + i / ORC_QK * 34)); break;
+        }
+    }
+}
+
+void orc_fill_random(int type, size_t rows, size_t cols, uint64_t seed, uint64_t tensor, float sigma, void* out) {
+    orc_fill_ctx c = {type, cols, seed, tensor, sigma, (uint8_t*)out};
+    orc_parallel_for(rows, 1, fill_row, &c);
 }

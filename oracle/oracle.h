@@ -109,9 +109,18 @@ void orc_llama_destroy(orc_llama* m);
 void orc_llama_reset(orc_llama* m);
 /* Decode one token at pos (positions 0..pos-1 already run); logits: n_vocab. */
 int orc_llama_step(orc_llama* m, uint32_t token, uint32_t pos, float* logits);
+/* Part of a step, for bounded CPU timing samples: optionally the embedding of
+ * `token`, then layers [l0, l1) on the running hidden state, then (logits
+ * non-NULL) the final norm and head. */
+int orc_llama_run(orc_llama* m, uint32_t token, uint32_t pos, size_t l0, size_t l1, int embed, float* logits);
 /* Direct access to the KV cache of a layer (for tests): K then V, each max_ctx*n_kv*hd halves. */
 uint16_t* orc_llama_kcache(orc_llama* m, size_t layer);
 uint16_t* orc_llama_vcache(orc_llama* m, size_t layer);
+
+/* Seeded N(0, sigma) weights (splitmix64 counters, Box-Muller) in `type`
+ * (GGUF bytes; F32 as floats), rows x cols, on the oracle's threads. For
+ * synthetic CPU-baseline models only. */
+void orc_fill_random(int type, size_t rows, size_t cols, uint64_t seed, uint64_t tensor, float sigma, void* out);
 
 /* Threads the oracle may use (pthreads); results do not depend on it. */
 void orc_set_threads(int n);

@@ -1,0 +1,231 @@
+// The element-wise ops of a decode step (kernels/elementwise.hpp), with the
+// Q8_0 quantization of the next matmul's activations fused in where one
+// follows (rms_norm -> Q/K/V and gate/up, silu*mul -> down).
+#include "common.cuh"
+#include "internal.h"
+
+using namespace syn;
+
+namespace {
+
+constexpr int kNormThreads = 1024;
+
+// rms_norm (elementwise.hpp:208-232): sum of float squares in double,
+// mean = float(sum / n), scale = 1 / sqrtf(mean + eps) (IEEE), out = (x*scale)*g.
+__global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const float* __restrict__ x,
+                                                                const float* __restrict__ gamma, int cols,
+                                                                float eps, float* out, ActPlanes act) {
+    const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float* xr = x + size_t(t) * cols;
+    __shared__ double red[kNormThreads / 32];
+    __shared__ float s_scale;
+    double s = 0.0;
+    for (int i = tid; i < cols; i += kNormThreads) {
+        const float v = xr[i];
+        s += double(__fmul_rn(v, v));
+    }
+    s = warp_sum_d(s);
+    if (lane == 0) red[warp] = s;
+    __syncthreads();
+    if (tid == 0) {
+        double tot = 0.0;
+        for (int w = 0; w < kNormThreads / 32; ++w) tot += red[w];
+        const float mean = float(tot / double(cols));
+        s_scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    }
+    __syncthreads();
+    const float scale = s_scale;
+    if (out) {
+        for (int i = tid; i < cols; i += kNormThreads)
+            out[size_t(t) * cols + i] = __fmul_rn(__fmul_rn(xr[i], scale), gamma[i]);
+    }
+    if (act.qs) {
+        const int nb = cols / QK;
+        for (int b = warp; b < nb; b += kNormThreads / 32) {
+            const int i = b * QK + lane;
+            const Q8Lane r = quantize_q8_lane(__fmul_rn(__fmul_rn(xr[i], scale), gamma[i]));
+            act.qs[size_t(t) * cols + i] = r.q;
+            if (lane == 0) {
+                const size_t k = size_t(t) * nb + b;
+                act.dh[k] = r.dh;
+                act.d[k] = r.d;
+                act.sum[k] = r.sum;
+            }
+        }
+    }
+}
+
+// silu (elementwise.hpp:76-81) then mul (:50-55): out = (g / (1 + expf(-g))) * u.
+__device__ __forceinline__ float silu_mul(float g, float u) {
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+
+__global__ void __launch_bounds__(256) silu_mul_kernel(const float* __restrict__ g, const float* __restrict__ u,
+                                                       int n_tok, int cols, float* out, ActPlanes act) {
+    const int lane = threadIdx.x & 31;
+    if (act.qs) {
+        // one warp per 32-value block: compute, then quantize it
+        const int nb = cols / QK;
+        const long blk = (long(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+        if (blk >= long(n_tok) * nb) return;
+        const long t = blk / nb, b = blk % nb;
+        const size_t i = size_t(t) * cols + size_t(b) * QK + lane;
+        const float v = silu_mul(g[i], u[i]);
+        if (out) out[i] = v;
+        const Q8Lane r = quantize_q8_lane(v);
+        act.qs[i] = r.q;
+        if (lane == 0) {
+            act.dh[blk] = r.dh;
+            act.d[blk] = r.d;
+            act.sum[blk] = r.sum;
+        }
+    } else {
+        const size_t n = size_t(n_tok) * cols;
+        for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x)
+            out[i] = silu_mul(g[i], u[i]);
+    }
+}
+
+__global__ void add_kernel(const float* a, const float* b, float* out, size_t n) {
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x)
+        out[i] = __fadd_rn(a[i], b[i]);
+}
+
+// op_embed (session.hpp:331-336): decode_row of the table (blocks.hpp:72-106).
+__global__ void embed_kernel(int type, const uint8_t* __restrict__ table, int layout, int rows, int cols,
+                             const int32_t* __restrict__ tokens, float* out) {
+    const int t = blockIdx.x;
+    const int tok = tokens[t];
+    float* o = out + size_t(t) * cols;
+    if (tok < 0 || tok >= rows) {
+        for (int c = threadIdx.x; c < cols; c += blockDim.x) o[c] = 0.0f;  // rejected on the host before launch
+        return;
+    }
+    const int nb = cols / QK;
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+        float v;
+        if (type == SYN_F32) {
+            v = reinterpret_cast<const float*>(table)[size_t(tok) * cols + c];
+        } else if (type == SYN_F16) {
+            v = f16_from_bits(reinterpret_cast<const uint16_t*>(table)[size_t(tok) * cols + c]);
+        } else {
+            const int b = c / QK, j = c % QK;
+            const size_t blk = size_t(tok) * nb + b;
+            float d;
+            int q;
+            if (layout == SYN_LAYOUT_GGUF) {
+                const uint8_t* p = table + blk * gguf_block_bytes(type);
+                d = f16_from_bits(uint16_t(p[0] | (p[1] << 8)));
+                if (type == SYN_Q4_0) q = j < 16 ? (p[2 + j] & 0x0f) - 8 : (p[2 + j - 16] >> 4) - 8;
+                else q = int8_t(p[2 + j]);
+            } else {
+                const uint16_t* dh =
+                    reinterpret_cast<const uint16_t*>(table + planar_qs_bytes(type, rows, cols));
+                d = f16_from_bits(dh[blk]);
+                const uint8_t* p = table + blk * quant_bytes_per_block(type);
+                if (type == SYN_Q4_0) q = j < 16 ? (p[j] & 0x0f) - 8 : (p[j - 16] >> 4) - 8;
+                else q = int8_t(p[j]);
+            }
+            v = __fmul_rn(float(q), d);
+        }
+        o[c] = v;
+    }
+}
+
+// First index of the maximum (std::max_element, llama_decode.cpp:274).
+__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ x, int n, int32_t* out) {
+    const int t = blockIdx.x, tid = threadIdx.x;
+    const float* xr = x + size_t(t) * n;
+    float best = -INFINITY;
+    int bi = n;  // sentinel beyond every index
+    for (int i = tid; i < n; i += blockDim.x) {
+        const float v = xr[i];
+        if (v > best || (bi == n && !(v < best))) { best = v; bi = i; }
+    }
+    __shared__ float sv[1024];
+    __shared__ int si[1024];
+    sv[tid] = best;
+    si[tid] = bi;
+    __syncthreads();
+    for (int w = blockDim.x / 2; w > 0; w >>= 1) {
+        if (tid < w) {
+            const float ov = sv[tid + w];
+            const int oi = si[tid + w];
+            if (oi < n && (si[tid] == n || ov > sv[tid] || (ov == sv[tid] && oi < si[tid]))) {
+                sv[tid] = ov;
+                si[tid] = oi;
+            }
+        }
+        __syncthreads();
+    }
+    if (tid == 0) out[t] = si[0] == n ? 0 : si[0];
+}
+
+// io: [0] input token, [1] position, [2] argmax of this step, [3] steps done,
+// [4] forced (prompt) tokens. After a step: history[step] = argmax, the
+// position advances, and the next input is the next prompt token or the argmax.
+__global__ void advance_kernel(int32_t* io, const int32_t* forced, int32_t* history) {
+    const int step = io[3];
+    history[step] = io[2];
+    io[3] = step + 1;
+    io[1] = io[1] + 1;
+    io[0] = step + 1 < io[4] ? forced[step + 1] : io[2];
+}
+
+}  // namespace
+
+int syn_advance(int32_t* io, const int32_t* forced, int32_t* history, cudaStream_t s) {
+    advance_kernel<<<1, 1, 0, s>>>(io, forced, history);
+    return syn_check_launch();
+}
+
+extern "C" int syn_rms_norm(const float* x, const float* gamma, int n_tok, int cols, float eps, float* out_f32,
+                            void* act, void* stream) {
+    if (!x || !gamma || n_tok <= 0 || cols <= 0 || (!out_f32 && !act)) return SYN_ERR_INVALID;
+    if (act && cols % QK) return SYN_ERR_INVALID;
+    ActPlanes a{};
+    if (act) a = act_planes(act, n_tok, cols);
+    rms_norm_kernel<<<n_tok, kNormThreads, 0, static_cast<cudaStream_t>(stream)>>>(x, gamma, cols, eps, out_f32, a);
+    return syn_check_launch();
+}
+
+extern "C" int syn_silu_mul(const float* g, const float* u, int n_tok, int cols, float* out_f32, void* act,
+                            void* stream) {
+    if (!g || !u || n_tok <= 0 || cols <= 0 || (!out_f32 && !act)) return SYN_ERR_INVALID;
+    if (act && cols % QK) return SYN_ERR_INVALID;
+    ActPlanes a{};
+    long grid;
+    if (act) {
+        a = act_planes(act, n_tok, cols);
+        grid = (long(n_tok) * (cols / QK) * 32 + 255) / 256;
+    } else {
+        grid = (long(n_tok) * cols + 255) / 256;
+        if (grid > 4096) grid = 4096;
+    }
+    silu_mul_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(g, u, n_tok, cols, out_f32, a);
+    return syn_check_launch();
+}
+
+extern "C" int syn_add(const float* a, const float* b, float* out, size_t n, void* stream) {
+    if (!a || !b || !out || n == 0) return SYN_ERR_INVALID;
+    long grid = long((n + 255) / 256);
+    if (grid > 4096) grid = 4096;
+    add_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(a, b, out, n);
+    return syn_check_launch();
+}
+
+extern "C" int syn_embed(int type, const void* table, int layout, int rows, int cols, const int32_t* tokens,
+                         int n_tok, float* out, void* stream) {
+    if (type != SYN_F32 && type != SYN_F16 && type != SYN_Q4_0 && type != SYN_Q8_0) return SYN_ERR_UNSUPPORTED;
+    if (!table || !tokens || !out || rows <= 0 || cols <= 0 || n_tok <= 0) return SYN_ERR_INVALID;
+    if ((type == SYN_Q4_0 || type == SYN_Q8_0) && cols % QK) return SYN_ERR_INVALID;
+    embed_kernel<<<n_tok, 256, 0, static_cast<cudaStream_t>(stream)>>>(type, static_cast<const uint8_t*>(table),
+                                                                        layout, rows, cols, tokens, out);
+    return syn_check_launch();
+}
+
+extern "C" int syn_argmax(const float* x, int n_tok, int n, int32_t* out, void* stream) {
+    if (!x || !out || n_tok <= 0 || n <= 0) return SYN_ERR_INVALID;
+    argmax_kernel<<<n_tok, 1024, 0, static_cast<cudaStream_t>(stream)>>>(x, n, out);
+    return syn_check_launch();
+}

@@ -1,0 +1,928 @@
+// The Llama decode session on one B200 (models/llama.hpp:324-489 load_llama,
+// graph/session.hpp:82-469 session).
+//
+// load: GGUF metadata is read with the reference's rules (llama.hpp:206-319),
+//   every weight is bound with its shape checked (models/common.hpp:146-160),
+//   and uploaded into ONE device arena: Q4_0/Q8_0 matrices repacked to the
+//   planar layout, Q/K/V (and gate/up) of equal type concatenated by rows so
+//   one GEMV launch streams them together. The f16 KV cache and the step's
+//   activations live in the same arena; activations are placed by the
+//   reference's static planner (planner.hpp) over the step's node order.
+// build: the step is the reference's graph (embed; per layer rms_norm, Q/K/V,
+//   rope+attention, O + residual, rms_norm, gate/up, silu*mul, down +
+//   residual; rms_norm, logits) with these fusions, none of which changes a
+//   float operation: rms_norm / silu*mul quantize their output to Q8_0 in the
+//   same kernel, matmul adds the residual in its epilogue, rope + kv_append
+//   run inside the attention kernel.
+// run: the step is captured once as a CUDA graph; position and token live in
+//   device memory, so the same graph serves every position.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../internal.h"
+#include "gguf.hpp"
+#include "planner.hpp"
+#include "synapse_b200.h"
+
+namespace {
+
+constexpr size_t kAlign = 256;
+
+struct weight {
+    int type = -1, layout = SYN_LAYOUT_PLANAR, rows = 0, cols = 0;
+    size_t off = 0, bytes = 0;
+    bool quant() const { return type == SYN_Q4_0 || type == SYN_Q8_0; }
+};
+
+// A source tensor of a (possibly fused) weight: rows [row0, row0 + rows).
+struct part {
+    std::string name;
+    int row0 = 0, rows = 0;
+    uint64_t tensor_id = 0;  // synthetic generator stream
+};
+
+struct layer_w {
+    weight attn_norm, ffn_norm;
+    weight q, k, v;   // q holds k and v too when fused_qkv
+    weight o;
+    weight gate, up;  // gate holds up too when fused_gu
+    weight down;
+    bool fused_qkv = false, fused_gu = false;
+};
+
+enum class opk { embed, rms_norm, quantize, matmul, attention, silu_mul, argmax };
+
+struct op {
+    opk kind;
+    const weight* w = nullptr;
+    int in = -1, in2 = -1, out = -1, out2 = -1, res = -1, scratch = -1;  // tensor ids
+    size_t in_off = 0, out_off = 0, in2_off = 0, res_off = 0;           // float offsets inside tensors
+    int rows = 0, cols = 0;
+    int layer = 0;
+};
+
+struct tensor {
+    size_t bytes = 0;
+    size_t first = 0, last = 0;
+    bool used = false;
+    size_t off = 0;
+};
+
+}  // namespace
+
+struct syn_session {
+    syn_llama_config cfg{};
+    int max_ctx = 0, device = 0;
+    cudaStream_t stream = nullptr;
+    char* arena = nullptr;
+    size_t arena_bytes = 0, weight_bytes = 0, kv_bytes = 0, act_bytes = 0;
+    weight embd, out_norm, head;
+    std::vector<layer_w> layers;
+    std::vector<std::pair<std::string, std::pair<const weight*, int>>> sources;  // name -> (weight, row0)
+    size_t ff_off = 0;  // freq factors (floats), 0 = none
+    bool has_ff = false;
+    size_t kv_off = 0;
+    size_t act_off = 0;
+    size_t io_off = 0, forced_off = 0, hist_off = 0;
+    std::vector<tensor> tensors;
+    std::vector<op> ops;
+    int logits_t = -1;
+    float theta_scale = 0, scale = 0;
+    // host side
+    int32_t* h_io = nullptr;   // pinned: token, pos
+    float* h_logits = nullptr; // pinned
+    int32_t* h_next = nullptr; // pinned
+    cudaGraphExec_t step_exec = nullptr, gen_exec = nullptr;
+    bool use_graph = true;
+
+    template <typename T>
+    T* at(size_t off) { return reinterpret_cast<T*>(arena + off); }
+    float* tf(int t, size_t off = 0) { return at<float>(act_off + tensors[t].off) + off; }
+    void* tb(int t) { return arena + act_off + tensors[t].off; }
+    int32_t* io() { return at<int32_t>(io_off); }
+    uint16_t* kv(int layer, int which) {
+        const size_t per = size_t(max_ctx) * cfg.n_head_kv * cfg.head_dim;
+        return at<uint16_t>(kv_off) + (size_t(layer) * 2 + which) * per;
+    }
+};
+
+namespace {
+
+int set_err(int st, const std::string& msg) {
+    syn_set_error(msg.c_str());
+    return st;
+}
+
+int cuda(cudaError_t e) {
+    if (e == cudaSuccess) return SYN_OK;
+    syn_set_error((std::string(cudaGetErrorName(e)) + ": " + cudaGetErrorString(e)).c_str());
+    return e == cudaErrorMemoryAllocation ? SYN_ERR_NO_MEMORY : SYN_ERR_CUDA;
+}
+
+bool supported_type(int t) { return t == SYN_F32 || t == SYN_F16 || t == SYN_Q4_0 || t == SYN_Q8_0; }
+
+size_t weight_size(int type, int rows, int cols) {
+    return syn_weight_bytes(type, rows, cols, type == SYN_Q4_0 || type == SYN_Q8_0 ? SYN_LAYOUT_PLANAR : SYN_LAYOUT_GGUF);
+}
+
+// ---- arena layout -------------------------------------------------------------
+
+struct layout_builder {
+    size_t off = 0;
+    size_t take(size_t bytes) {
+        const size_t o = off;
+        off = (off + bytes + kAlign - 1) / kAlign * kAlign;
+        return o;
+    }
+};
+
+void define(weight& w, int type, int rows, int cols, layout_builder& lb) {
+    w.type = type;
+    w.rows = rows;
+    w.cols = cols;
+    w.layout = w.quant() ? SYN_LAYOUT_PLANAR : SYN_LAYOUT_GGUF;
+    w.bytes = weight_size(type, rows, cols);
+    w.off = lb.take(w.bytes);
+}
+
+// ---- the step graph --------------------------------------------------------
+
+struct graph_builder {
+    syn_session& s;
+    int new_tensor(size_t bytes) {
+        tensor t;
+        t.bytes = bytes;
+        s.tensors.push_back(t);
+        return int(s.tensors.size() - 1);
+    }
+    void use(int t) {
+        if (t < 0) return;
+        tensor& x = s.tensors[t];
+        const size_t i = s.ops.size();  // index of the op being added
+        if (!x.used) { x.first = i; x.used = true; }
+        x.last = i;
+    }
+    void add(op o) {
+        use(o.in); use(o.in2); use(o.out); use(o.out2); use(o.res); use(o.scratch);
+        s.ops.push_back(o);
+    }
+};
+
+size_t act_bytes_for(int cols) { return syn_q8_act_bytes(1, cols); }
+
+// Activation input of a matmul: the Q8_0 form for quantized weights, else f32.
+struct activation {
+    int f32 = -1;  // tensor with float values
+    int q8 = -1;   // tensor with Q8_0 activations
+};
+
+void build_step(syn_session& s) {
+    const syn_llama_config& c = s.cfg;
+    graph_builder g{s};
+    const int d = c.n_embd, qrows = c.n_head * c.head_dim, kvrows = c.n_head_kv * c.head_dim, ff = c.n_ff;
+
+    int x = g.new_tensor(size_t(d) * 4);
+    {
+        op o{opk::embed};
+        o.w = &s.embd;
+        o.out = x;
+        g.add(o);
+    }
+    auto norm = [&](int in, const weight& gamma, bool need_f32, bool need_q8) {
+        activation a;
+        op o{opk::rms_norm};
+        o.w = &gamma;
+        o.in = in;
+        o.cols = d;
+        if (need_f32) a.f32 = o.out = g.new_tensor(size_t(d) * 4);
+        if (need_q8) a.q8 = o.out2 = g.new_tensor(act_bytes_for(d));
+        g.add(o);
+        return a;
+    };
+    auto matmul = [&](const weight& w, const activation& a, int out, size_t out_off, int res) {
+        op o{opk::matmul};
+        o.w = &w;
+        o.in = w.quant() ? a.q8 : a.f32;
+        o.out = out;
+        o.out_off = out_off;
+        o.res = res;
+        o.rows = w.rows;
+        o.cols = w.cols;
+        g.add(o);
+    };
+    for (int l = 0; l < c.n_layer; ++l) {
+        const layer_w& L = s.layers[l];
+        const bool qk_any = L.q.quant() || (!L.fused_qkv && (L.k.quant() || L.v.quant()));
+        const bool qk_f = !L.q.quant() || (!L.fused_qkv && (!L.k.quant() || !L.v.quant()));
+        activation h = norm(x, L.attn_norm, qk_f, qk_any);
+        const int qkv = g.new_tensor(size_t(qrows + 2 * kvrows) * 4);
+        matmul(L.q, h, qkv, 0, -1);
+        if (!L.fused_qkv) {
+            matmul(L.k, h, qkv, qrows, -1);
+            matmul(L.v, h, qkv, qrows + kvrows, -1);
+        }
+        const int attn = g.new_tensor(size_t(qrows) * 4);
+        {
+            op o{opk::attention};
+            o.in = qkv;
+            o.out = attn;
+            o.layer = l;
+            o.scratch = g.new_tensor(syn_attention_scratch_bytes(1, c.n_head, c.n_head_kv, c.head_dim, s.max_ctx));
+            g.add(o);
+        }
+        activation a;
+        a.f32 = attn;
+        if (L.o.quant()) {
+            a.q8 = g.new_tensor(act_bytes_for(qrows));
+            op o{opk::quantize};
+            o.in = attn;
+            o.out = a.q8;
+            o.cols = qrows;
+            g.add(o);
+        }
+        const int x2 = g.new_tensor(size_t(d) * 4);
+        matmul(L.o, a, x2, 0, x);
+        x = x2;
+        const bool gu_any = L.gate.quant() || (!L.fused_gu && L.up.quant());
+        const bool gu_f = !L.gate.quant() || (!L.fused_gu && !L.up.quant());
+        activation h2 = norm(x, L.ffn_norm, gu_f, gu_any);
+        const int gu = g.new_tensor(size_t(2) * ff * 4);
+        matmul(L.gate, h2, gu, 0, -1);
+        if (!L.fused_gu) matmul(L.up, h2, gu, ff, -1);
+        activation f;
+        {
+            op o{opk::silu_mul};
+            o.in = gu;
+            o.cols = ff;
+            if (L.down.quant()) f.q8 = o.out2 = g.new_tensor(act_bytes_for(ff));
+            else f.f32 = o.out = g.new_tensor(size_t(ff) * 4);
+            g.add(o);
+        }
+        const int x3 = g.new_tensor(size_t(d) * 4);
+        matmul(L.down, f, x3, 0, x);
+        x = x3;
+    }
+    activation hl = norm(x, s.out_norm, !s.head.quant(), s.head.quant());
+    s.logits_t = g.new_tensor(size_t(c.n_vocab) * 4);
+    matmul(s.head, hl, s.logits_t, 0, -1);
+    {
+        op o{opk::argmax};
+        o.in = s.logits_t;
+        g.add(o);
+    }
+    // the logits are the step's output: live to the end (planner.hpp liveness)
+    s.tensors[s.logits_t].last = s.ops.size() - 1;
+}
+
+int plan_step(syn_session& s) {
+    std::vector<syn::plan::tensor> ts;
+    for (const tensor& t : s.tensors) ts.push_back({t.bytes, t.first, t.last});
+    const syn::plan::result r = syn::plan::place(ts, kAlign);
+    if (!syn::plan::valid(ts, r, kAlign)) return set_err(SYN_ERR_INVALID, "arena plan violates P1-P3");
+    for (size_t i = 0; i < s.tensors.size(); ++i) s.tensors[i].off = r.offset[i];
+    s.act_bytes = r.arena_bytes;
+    return SYN_OK;
+}
+
+// ---- execution ---------------------------------------------------------------
+
+int enqueue_body(syn_session& s, cudaStream_t st) {
+    const syn_llama_config& c = s.cfg;
+    const int qrows = c.n_head * c.head_dim, kvrows = c.n_head_kv * c.head_dim;
+    int rc = SYN_OK;
+    for (const op& o : s.ops) {
+        switch (o.kind) {
+        case opk::embed:
+            rc = syn_embed(s.embd.type, s.arena + s.embd.off, s.embd.layout, s.embd.rows, s.embd.cols, s.io(), 1,
+                           s.tf(o.out), st);
+            break;
+        case opk::rms_norm:
+            rc = syn_rms_norm(s.tf(o.in), s.at<float>(o.w->off), 1, o.cols, c.rms_eps,
+                              o.out >= 0 ? s.tf(o.out) : nullptr, o.out2 >= 0 ? s.tb(o.out2) : nullptr, st);
+            break;
+        case opk::quantize:
+            rc = syn_quantize_q8_0(s.tf(o.in), 1, o.cols, s.tb(o.out), st);
+            break;
+        case opk::matmul: {
+            float* y = s.tf(o.out, o.out_off);
+            const float* res = o.res >= 0 ? s.tf(o.res) : nullptr;
+            if (o.w->quant())
+                rc = syn_gemv_q(o.w->type, s.arena + o.w->off, o.w->layout, o.w->rows, o.w->cols, s.tb(o.in), 1, y,
+                                res, st);
+            else
+                rc = syn_gemv_f(o.w->type, s.arena + o.w->off, o.w->rows, o.w->cols, s.tf(o.in), 1, y, res, st);
+            break;
+        }
+        case opk::attention: {
+            syn_attention_args a{};
+            float* qkv = s.tf(o.in);
+            a.q = qkv;
+            a.k = qkv + qrows;
+            a.v = qkv + qrows + kvrows;
+            a.k_cache = s.kv(o.layer, 0);
+            a.v_cache = s.kv(o.layer, 1);
+            a.pos = s.io() + 1;
+            a.out = s.tf(o.out);
+            a.scratch = s.tb(o.scratch);
+            a.cache_stride = 0;
+            a.n_q = 1;
+            a.n_head = c.n_head;
+            a.n_kv = c.n_head_kv;
+            a.head_dim = c.head_dim;
+            a.max_len = s.max_ctx;
+            a.append = 1;
+            a.rope = 1;
+            a.rope_mode = c.rope_mode;
+            a.theta_scale = s.theta_scale;
+            a.scale = s.scale;
+            a.freq_factors = s.has_ff ? s.at<float>(s.ff_off) : nullptr;
+            rc = syn_attention(&a, st);
+            break;
+        }
+        case opk::silu_mul:
+            rc = syn_silu_mul(s.tf(o.in), s.tf(o.in, size_t(o.cols)), 1, o.cols, o.out >= 0 ? s.tf(o.out) : nullptr,
+                              o.out2 >= 0 ? s.tb(o.out2) : nullptr, st);
+            break;
+        case opk::argmax:
+            rc = syn_argmax(s.tf(o.in), 1, c.n_vocab, s.io() + 2, st);
+            break;
+        }
+        if (rc) return rc;
+    }
+    return SYN_OK;
+}
+
+int enqueue_step(syn_session& s, cudaStream_t st) {
+    int rc = cuda(cudaMemcpyAsync(s.io(), s.h_io, 2 * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    if (!rc) rc = enqueue_body(s, st);
+    if (!rc) rc = cuda(cudaMemcpyAsync(s.h_logits, s.tf(s.logits_t), size_t(s.cfg.n_vocab) * 4,
+                                       cudaMemcpyDeviceToHost, st));
+    if (!rc) rc = cuda(cudaMemcpyAsync(s.h_next, s.io() + 2, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+    return rc;
+}
+
+int enqueue_gen(syn_session& s, cudaStream_t st) {
+    int rc = enqueue_body(s, st);
+    if (!rc) rc = syn_advance(s.io(), s.at<int32_t>(s.forced_off), s.at<int32_t>(s.hist_off), st);
+    return rc;
+}
+
+int capture(syn_session& s, int (*fn)(syn_session&, cudaStream_t), cudaGraphExec_t* out) {
+    cudaGraph_t g = nullptr;
+    int rc = cuda(cudaStreamBeginCapture(s.stream, cudaStreamCaptureModeThreadLocal));
+    if (rc) return rc;
+    const int body = fn(s, s.stream);
+    rc = cuda(cudaStreamEndCapture(s.stream, &g));
+    if (body) {
+        if (g) cudaGraphDestroy(g);
+        return body;
+    }
+    if (rc) return rc;
+    rc = cuda(cudaGraphInstantiate(out, g, 0));
+    cudaGraphDestroy(g);
+    return rc;
+}
+
+// ---- config + weights ---------------------------------------------------------
+
+int finish(syn_session& s, layout_builder& lb) {
+    const syn_llama_config& c = s.cfg;
+    s.weight_bytes = lb.off;
+    s.kv_bytes = size_t(c.n_layer) * 2 * s.max_ctx * c.n_head_kv * c.head_dim * 2;
+    s.kv_off = lb.take(s.kv_bytes);
+    build_step(s);
+    int rc = plan_step(s);
+    if (rc) return rc;
+    s.act_off = lb.take(s.act_bytes);
+    s.io_off = lb.take(64);
+    s.forced_off = lb.take(size_t(s.max_ctx) * 4);
+    s.hist_off = lb.take(size_t(s.max_ctx) * 4);
+    s.arena_bytes = lb.off;
+    s.theta_scale = std::pow(c.rope_base, -2.0f / float(c.head_dim));  // attention.hpp:47
+    s.scale = 1.0f / std::sqrt(float(c.head_dim));                      // llama.hpp:407
+    if ((rc = cuda(cudaSetDevice(s.device)))) return rc;
+    if ((rc = cuda(cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking)))) return rc;
+    if ((rc = cuda(cudaMalloc(&s.arena, s.arena_bytes)))) return rc;
+    if ((rc = cuda(cudaMemset(s.arena + s.kv_off, 0, s.arena_bytes - s.kv_off)))) return rc;
+    if ((rc = cuda(cudaMallocHost(&s.h_io, 64)))) return rc;
+    if ((rc = cuda(cudaMallocHost(&s.h_logits, size_t(c.n_vocab) * 4)))) return rc;
+    if ((rc = cuda(cudaMallocHost(&s.h_next, 64)))) return rc;
+    return SYN_OK;
+}
+
+// One eager step at position 0 (sets per-device kernel attributes outside any
+// capture), then the KV cache and io are cleared and both graphs captured.
+int warm_and_capture(syn_session& s) {
+    s.h_io[0] = 0;
+    s.h_io[1] = 0;
+    int rc = enqueue_step(s, s.stream);
+    if (!rc) rc = cuda(cudaStreamSynchronize(s.stream));
+    if (!rc) rc = cuda(cudaMemsetAsync(s.arena + s.kv_off, 0, s.kv_bytes, s.stream));
+    if (!rc) rc = cuda(cudaMemsetAsync(s.io(), 0, 64, s.stream));
+    if (!rc) rc = cuda(cudaStreamSynchronize(s.stream));
+    if (rc) return rc;
+    const char* env = std::getenv("SYN_NO_GRAPH");
+    s.use_graph = !(env && env[0] == '1');
+    if (s.use_graph) {
+        if ((rc = capture(s, enqueue_step, &s.step_exec))) return rc;
+        if ((rc = capture(s, enqueue_gen, &s.gen_exec))) return rc;
+    }
+    return SYN_OK;
+}
+
+void layer_layout(syn_session& s, const std::vector<std::vector<int>>& types, layout_builder& lb) {
+    const syn_llama_config& c = s.cfg;
+    const int d = c.n_embd, qrows = c.n_head * c.head_dim, kvrows = c.n_head_kv * c.head_dim, ff = c.n_ff;
+    s.layers.resize(c.n_layer);
+    for (int l = 0; l < c.n_layer; ++l) {
+        layer_w& L = s.layers[l];
+        const std::vector<int>& t = types[l];  // attn_norm, q, k, v, o, ffn_norm, gate, up, down
+        const std::string p = "blk." + std::to_string(l) + ".";
+        define(L.attn_norm, SYN_F32, 1, d, lb);
+        L.fused_qkv = t[1] == t[2] && t[1] == t[3] && (t[1] == SYN_Q4_0 || t[1] == SYN_Q8_0);
+        if (L.fused_qkv) {
+            define(L.q, t[1], qrows + 2 * kvrows, d, lb);
+            s.sources.push_back({p + "attn_q.weight", {&L.q, 0}});
+            s.sources.push_back({p + "attn_k.weight", {&L.q, qrows}});
+            s.sources.push_back({p + "attn_v.weight", {&L.q, qrows + kvrows}});
+        } else {
+            define(L.q, t[1], qrows, d, lb);
+            define(L.k, t[2], kvrows, d, lb);
+            define(L.v, t[3], kvrows, d, lb);
+            s.sources.push_back({p + "attn_q.weight", {&L.q, 0}});
+            s.sources.push_back({p + "attn_k.weight", {&L.k, 0}});
+            s.sources.push_back({p + "attn_v.weight", {&L.v, 0}});
+        }
+        define(L.o, t[4], d, qrows, lb);
+        s.sources.push_back({p + "attn_output.weight", {&L.o, 0}});
+        define(L.ffn_norm, SYN_F32, 1, d, lb);
+        L.fused_gu = t[6] == t[7] && (t[6] == SYN_Q4_0 || t[6] == SYN_Q8_0);
+        if (L.fused_gu) {
+            define(L.gate, t[6], 2 * ff, d, lb);
+            s.sources.push_back({p + "ffn_gate.weight", {&L.gate, 0}});
+            s.sources.push_back({p + "ffn_up.weight", {&L.gate, ff}});
+        } else {
+            define(L.gate, t[6], ff, d, lb);
+            define(L.up, t[7], ff, d, lb);
+            s.sources.push_back({p + "ffn_gate.weight", {&L.gate, 0}});
+            s.sources.push_back({p + "ffn_up.weight", {&L.up, 0}});
+        }
+        define(L.down, t[8], d, ff, lb);
+        s.sources.push_back({p + "ffn_down.weight", {&L.down, 0}});
+        s.sources.push_back({p + "attn_norm.weight", {&L.attn_norm, 0}});
+        s.sources.push_back({p + "ffn_norm.weight", {&L.ffn_norm, 0}});
+    }
+}
+
+void destroy(syn_session* s) {
+    if (!s) return;
+    if (s->device >= 0) cudaSetDevice(s->device);
+    if (s->step_exec) cudaGraphExecDestroy(s->step_exec);
+    if (s->gen_exec) cudaGraphExecDestroy(s->gen_exec);
+    if (s->stream) cudaStreamSynchronize(s->stream);
+    if (s->arena) cudaFree(s->arena);
+    if (s->h_io) cudaFreeHost(s->h_io);
+    if (s->h_logits) cudaFreeHost(s->h_logits);
+    if (s->h_next) cudaFreeHost(s->h_next);
+    if (s->stream) cudaStreamDestroy(s->stream);
+    delete s;
+}
+
+// Rows (ne[1]) and columns (ne[0]) of a 2-D GGUF tensor (tensor_view.hpp:5-8).
+bool shape_is(const syn::gguf::tensor_info& t, uint64_t rows, uint64_t cols) {
+    return t.ne[0] == cols && t.rows() == rows;
+}
+
+}  // namespace
+
+extern "C" int syn_session_open_gguf(const char* path, int max_ctx, int device, syn_session** out) {
+    if (!path || !out || max_ctx <= 0) return SYN_ERR_INVALID;
+    *out = nullptr;
+    std::unique_ptr<syn::gguf::file> f;
+    std::string err;
+    int rc = syn::gguf::file::open(path, f, &err);
+    if (rc) return set_err(rc, err);
+    // read_llama_config (llama.hpp:206-319)
+    std::string_view arch;
+    if (!f->get_string("general.architecture", arch) || arch != "llama")
+        return set_err(SYN_ERR_UNSUPPORTED, "general.architecture: only llama");
+    auto count = [&](const char* k, uint64_t& v, bool required, uint64_t dflt) {
+        if (f->get_uint(std::string("llama.") + k, v)) return true;
+        if (f->find(std::string("llama.") + k)) return false;  // present, wrong type
+        v = dflt;
+        return !required;
+    };
+    uint64_t n_layer, n_embd, n_ff, n_head, ctx_train, n_kv, hd, vlen, rot, experts;
+    if (!count("block_count", n_layer, true, 0) || !count("embedding_length", n_embd, true, 0) ||
+        !count("feed_forward_length", n_ff, true, 0) || !count("attention.head_count", n_head, true, 0) ||
+        !count("context_length", ctx_train, true, 0) || !n_layer || !n_embd || !n_ff || !n_head || !ctx_train)
+        return set_err(SYN_ERR_FORMAT, "missing or zero llama.* count");
+    if (!count("attention.head_count_kv", n_kv, false, n_head) || !n_kv || n_head % n_kv)
+        return set_err(SYN_ERR_FORMAT, "llama.attention.head_count_kv");
+    if (!count("attention.key_length", hd, false, n_embd / n_head) || !hd)
+        return set_err(SYN_ERR_FORMAT, "llama.attention.key_length");
+    if (!count("attention.value_length", vlen, false, hd) || vlen != hd)
+        return set_err(SYN_ERR_UNSUPPORTED, "llama.attention.value_length");
+    if (!count("rope.dimension_count", rot, false, hd) || rot != hd)
+        return set_err(SYN_ERR_UNSUPPORTED, "llama.rope.dimension_count");
+    if (!count("expert_count", experts, false, 0) || experts)
+        return set_err(SYN_ERR_UNSUPPORTED, "llama.expert_count");
+    double eps, base = 10000.0;
+    if (!f->get_float("llama.attention.layer_norm_rms_epsilon", eps) || !(eps > 0))
+        return set_err(SYN_ERR_FORMAT, "llama.attention.layer_norm_rms_epsilon");
+    if (f->find("llama.rope.freq_base") && (!f->get_float("llama.rope.freq_base", base) || !(base > 0)))
+        return set_err(SYN_ERR_FORMAT, "llama.rope.freq_base");
+    std::string_view rs_type;
+    double rs_factor = 0;
+    if ((f->get_string("llama.rope.scaling.type", rs_type) && rs_type != "none" && rs_type != "linear") ||
+        (f->get_float("llama.rope.scaling.factor", rs_factor) && rs_factor != 0 && rs_factor != 1) ||
+        f->find("llama.rope.scale_linear") || f->find("llama.attention.scale"))
+        return set_err(SYN_ERR_UNSUPPORTED, "rope scaling / attention.scale");
+    const syn::gguf::tensor_info* te = f->tensor("token_embd.weight");
+    if (!te || te->ne[0] != n_embd || te->ne[2] != 1 || te->ne[3] != 1)
+        return set_err(SYN_ERR_FORMAT, "token_embd.weight");
+    if (hd % 8 || hd > 256 || n_embd % 32 || n_ff % 32 || (n_head * hd) % 32)
+        return set_err(SYN_ERR_UNSUPPORTED, "head_dim / widths not multiples of 8 / 32");
+
+    std::unique_ptr<syn_session, void (*)(syn_session*)> s(new syn_session(), destroy);
+    s->device = device;
+    s->max_ctx = max_ctx;
+    syn_llama_config& c = s->cfg;
+    c.n_layer = int(n_layer); c.n_embd = int(n_embd); c.n_ff = int(n_ff); c.n_head = int(n_head);
+    c.n_head_kv = int(n_kv); c.head_dim = int(hd); c.n_vocab = int(te->ne[1]);
+    c.rms_eps = float(eps); c.rope_base = float(base); c.rope_mode = 0;
+    c.type_embd = int(te->type);
+    const syn::gguf::tensor_info* tout = f->tensor("output.weight");
+    c.type_output = tout ? int(tout->type) : -1;
+    if (!supported_type(c.type_embd)) return set_err(SYN_ERR_UNSUPPORTED, "token_embd.weight type");
+
+    // bind every weight with its shape (models/common.hpp:146-160)
+    const uint64_t qrows = n_head * hd, kvrows = n_kv * hd;
+    struct want { const char* suffix; uint64_t rows, cols; };
+    const want layer_wants[9] = {{"attn_norm.weight", 1, n_embd}, {"attn_q.weight", qrows, n_embd},
+                                 {"attn_k.weight", kvrows, n_embd}, {"attn_v.weight", kvrows, n_embd},
+                                 {"attn_output.weight", n_embd, qrows}, {"ffn_norm.weight", 1, n_embd},
+                                 {"ffn_gate.weight", n_ff, n_embd}, {"ffn_up.weight", n_ff, n_embd},
+                                 {"ffn_down.weight", n_embd, n_ff}};
+    std::vector<std::vector<int>> types(n_layer, std::vector<int>(9));
+    for (uint64_t l = 0; l < n_layer; ++l) {
+        for (int i = 0; i < 9; ++i) {
+            const std::string name = "blk." + std::to_string(l) + "." + layer_wants[i].suffix;
+            const syn::gguf::tensor_info* t = f->tensor(name);
+            if (!t) return set_err(SYN_ERR_FORMAT, "missing " + name);
+            const bool norm = i == 0 || i == 5;
+            if (!(norm ? t->n_elements() == n_embd : shape_is(*t, layer_wants[i].rows, layer_wants[i].cols)))
+                return set_err(SYN_ERR_FORMAT, "bad shape " + name);
+            if (!supported_type(int(t->type)) || (norm && t->type != SYN_F32))
+                return set_err(SYN_ERR_UNSUPPORTED, "type of " + name);
+            types[l][i] = int(t->type);
+        }
+        for (const char* extra : {"attn_q.bias", "attn_k.bias", "attn_v.bias", "attn_output.bias", "ffn_gate.bias",
+                                  "ffn_up.bias", "ffn_down.bias", "ffn_gate_inp.weight"})
+            if (f->tensor("blk." + std::to_string(l) + "." + extra))
+                return set_err(SYN_ERR_UNSUPPORTED, std::string("blk.N.") + extra);
+    }
+    const syn::gguf::tensor_info* on = f->tensor("output_norm.weight");
+    if (!on || on->n_elements() != n_embd || on->type != SYN_F32) return set_err(SYN_ERR_FORMAT, "output_norm.weight");
+    if (tout && (!shape_is(*tout, uint64_t(c.n_vocab), n_embd) || !supported_type(int(tout->type))))
+        return set_err(SYN_ERR_UNSUPPORTED, "output.weight");
+    if (f->tensor("output.bias")) return set_err(SYN_ERR_UNSUPPORTED, "output.bias");
+    const syn::gguf::tensor_info* rf = f->tensor("rope_freqs.weight");
+    if (rf && (rf->type != SYN_F32 || rf->n_elements() != hd / 2)) return set_err(SYN_ERR_FORMAT, "rope_freqs.weight");
+
+    layout_builder lb;
+    define(s->embd, c.type_embd, c.n_vocab, c.n_embd, lb);
+    s->sources.push_back({"token_embd.weight", {&s->embd, 0}});
+    layer_layout(*s, types, lb);
+    define(s->out_norm, SYN_F32, 1, c.n_embd, lb);
+    s->sources.push_back({"output_norm.weight", {&s->out_norm, 0}});
+    if (tout) {
+        define(s->head, c.type_output, c.n_vocab, c.n_embd, lb);
+        s->sources.push_back({"output.weight", {&s->head, 0}});
+    } else {
+        s->head = s->embd;  // tied (llama.hpp:471-472)
+    }
+    if (rf) {
+        s->has_ff = true;
+        s->ff_off = lb.take(size_t(hd / 2) * 4);
+    }
+    if ((rc = finish(*s, lb))) return rc;
+
+    // upload: host -> staging (GGUF bytes) -> repack into the arena
+    const size_t staging_bytes = size_t(64) << 20;
+    void* staging = nullptr;
+    if ((rc = cuda(cudaMalloc(&staging, staging_bytes)))) return rc;
+    for (const auto& src : s->sources) {
+        const syn::gguf::tensor_info* t = f->tensor(src.first);
+        const weight& w = *src.second.first;
+        const int row0 = src.second.second;
+        const uint8_t* data = f->data(*t);
+        if (!w.quant()) {
+            rc = cuda(cudaMemcpyAsync(s->arena + w.off + size_t(row0) * w.cols * (w.type == SYN_F32 ? 4 : 2), data,
+                                      t->nbytes, cudaMemcpyHostToDevice, s->stream));
+        } else {
+            const int rows = int(t->rows());
+            const size_t row_bytes = t->nbytes / size_t(rows);
+            const int per = int(staging_bytes / row_bytes);
+            for (int r0 = 0; r0 < rows && !rc; r0 += per) {
+                const int n = rows - r0 < per ? rows - r0 : per;
+                rc = cuda(cudaMemcpyAsync(staging, data + size_t(r0) * row_bytes, size_t(n) * row_bytes,
+                                          cudaMemcpyHostToDevice, s->stream));
+                if (!rc) rc = syn_repack_rows(w.type, staging, n, w.cols, s->arena + w.off, w.rows, row0 + r0,
+                                              s->stream);
+                if (!rc) rc = cuda(cudaStreamSynchronize(s->stream));
+            }
+        }
+        if (!rc) rc = cuda(cudaStreamSynchronize(s->stream));
+        if (rc) break;
+    }
+    if (!rc && rf)
+        rc = cuda(cudaMemcpy(s->arena + s->ff_off, f->data(*rf), size_t(hd / 2) * 4, cudaMemcpyHostToDevice));
+    cudaFree(staging);
+    if (rc) return rc;
+    if ((rc = warm_and_capture(*s))) return rc;
+    *out = s.release();
+    return SYN_OK;
+}
+
+extern "C" int syn_session_open_synthetic(const syn_llama_config* cp, int max_ctx, uint64_t seed, int device,
+                                          syn_session** out) {
+    if (!cp || !out || max_ctx <= 0) return SYN_ERR_INVALID;
+    *out = nullptr;
+    const syn_llama_config& c0 = *cp;
+    if (c0.n_layer <= 0 || c0.n_embd <= 0 || c0.n_ff <= 0 || c0.n_head <= 0 || c0.n_head_kv <= 0 ||
+        c0.head_dim <= 0 || c0.n_vocab <= 0 || c0.n_head % c0.n_head_kv || !(c0.rms_eps > 0) || !(c0.rope_base > 0))
+        return SYN_ERR_INVALID;
+    if (c0.head_dim % 8 || c0.head_dim > 256 || c0.n_embd % 32 || c0.n_ff % 32 || (c0.n_head * c0.head_dim) % 32)
+        return SYN_ERR_UNSUPPORTED;
+    if (!supported_type(c0.type_embd) || !supported_type(c0.type_layers) ||
+        (c0.type_output != -1 && !supported_type(c0.type_output)))
+        return SYN_ERR_UNSUPPORTED;
+    std::unique_ptr<syn_session, void (*)(syn_session*)> s(new syn_session(), destroy);
+    s->device = device;
+    s->max_ctx = max_ctx;
+    s->cfg = c0;
+    s->cfg.rope_mode = 0;
+    const syn_llama_config& c = s->cfg;
+    layout_builder lb;
+    define(s->embd, c.type_embd, c.n_vocab, c.n_embd, lb);
+    s->sources.push_back({"token_embd.weight", {&s->embd, 0}});
+    const int T = c.type_layers;
+    layer_layout(*s, std::vector<std::vector<int>>(c.n_layer, {SYN_F32, T, T, T, T, SYN_F32, T, T, T}), lb);
+    define(s->out_norm, SYN_F32, 1, c.n_embd, lb);
+    s->sources.push_back({"output_norm.weight", {&s->out_norm, 0}});
+    if (c.type_output >= 0) {
+        define(s->head, c.type_output, c.n_vocab, c.n_embd, lb);
+        s->sources.push_back({"output.weight", {&s->head, 0}});
+    } else {
+        s->head = s->embd;
+    }
+    int rc = finish(*s, lb);
+    if (rc) return rc;
+    // Every matrix N(0, 0.02) (seeded per tensor name), norms 1.0.
+    uint64_t tensor_id = 0;
+    for (const auto& src : s->sources) {
+        const weight& w = *src.second.first;
+        const int row0 = src.second.second;
+        ++tensor_id;
+        if (src.first.find("norm") != std::string::npos) {
+            rc = syn_fill_f32(s->at<float>(w.off), size_t(w.cols), 1.0f, s->stream);
+        } else {
+            int rows = w.rows;
+            // the rows this source tensor covers inside a fused matrix
+            const std::string& n = src.first;
+            const int qrows = c.n_head * c.head_dim, kvrows = c.n_head_kv * c.head_dim;
+            if (n.find("attn_q.") != std::string::npos) rows = qrows;
+            else if (n.find("attn_k.") != std::string::npos || n.find("attn_v.") != std::string::npos) rows = kvrows;
+            else if (n.find("ffn_gate.") != std::string::npos || n.find("ffn_up.") != std::string::npos) rows = c.n_ff;
+            rc = syn_fill_random(w.type, rows, w.cols, s->arena + w.off, w.rows, row0, seed, tensor_id, 0.02f,
+                                 s->stream);
+        }
+        if (rc) return rc;
+    }
+    if ((rc = cuda(cudaStreamSynchronize(s->stream)))) return rc;
+    if ((rc = warm_and_capture(*s))) return rc;
+    *out = s.release();
+    return SYN_OK;
+}
+
+extern "C" void syn_session_close(syn_session* s) { destroy(s); }
+
+extern "C" int syn_session_config(const syn_session* s, syn_llama_config* out) {
+    if (!s || !out) return SYN_ERR_INVALID;
+    *out = s->cfg;
+    return SYN_OK;
+}
+
+extern "C" int syn_session_memory(const syn_session* s, size_t* arena, size_t* weights, size_t* kv) {
+    if (!s) return SYN_ERR_INVALID;
+    if (arena) *arena = s->arena_bytes;
+    if (weights) *weights = s->weight_bytes;
+    if (kv) *kv = s->kv_bytes;
+    return SYN_OK;
+}
+
+extern "C" int syn_session_reset(syn_session* s) {
+    if (!s) return SYN_ERR_INVALID;
+    int rc = cuda(cudaSetDevice(s->device));
+    if (!rc) rc = cuda(cudaMemsetAsync(s->arena + s->kv_off, 0, s->kv_bytes, s->stream));
+    if (!rc) rc = cuda(cudaStreamSynchronize(s->stream));
+    return rc;
+}
+
+extern "C" int syn_session_step(syn_session* s, uint32_t token, uint32_t pos, float* host_logits,
+                                int32_t* host_argmax) {
+    if (!s) return SYN_ERR_INVALID;
+    if (token >= uint32_t(s->cfg.n_vocab) || pos >= uint32_t(s->max_ctx)) return SYN_ERR_RANGE;
+    int rc = cuda(cudaSetDevice(s->device));
+    if (rc) return rc;
+    s->h_io[0] = int32_t(token);
+    s->h_io[1] = int32_t(pos);
+    rc = s->use_graph ? cuda(cudaGraphLaunch(s->step_exec, s->stream)) : enqueue_step(*s, s->stream);
+    if (!rc) rc = cuda(cudaStreamSynchronize(s->stream));
+    if (rc) return rc;
+    if (host_logits) std::memcpy(host_logits, s->h_logits, size_t(s->cfg.n_vocab) * 4);
+    if (host_argmax) *host_argmax = s->h_next[0];
+    return SYN_OK;
+}
+
+extern "C" int syn_session_generate(syn_session* s, const uint32_t* prompt, int n_prompt, uint32_t pos, int n_steps,
+                                    int32_t* host_tokens) {
+    if (!s || !prompt || n_prompt <= 0 || n_steps <= 0 || n_prompt > n_steps) return SYN_ERR_INVALID;
+    if (uint64_t(pos) + uint64_t(n_steps) > uint64_t(s->max_ctx)) return SYN_ERR_RANGE;
+    for (int i = 0; i < n_prompt; ++i)
+        if (prompt[i] >= uint32_t(s->cfg.n_vocab)) return SYN_ERR_RANGE;
+    int rc = cuda(cudaSetDevice(s->device));
+    if (rc) return rc;
+    std::vector<int32_t> forced(prompt, prompt + n_prompt);
+    int32_t io[5] = {int32_t(prompt[0]), int32_t(pos), 0, 0, n_prompt};
+    rc = cuda(cudaMemcpyAsync(s->at<int32_t>(s->forced_off), forced.data(), forced.size() * 4, cudaMemcpyHostToDevice,
+                              s->stream));
+    if (!rc) rc = cuda(cudaMemcpyAsync(s->io(), io, sizeof io, cudaMemcpyHostToDevice, s->stream));
+    for (int i = 0; i < n_steps && !rc; ++i)
+        rc = s->use_graph ? cuda(cudaGraphLaunch(s->gen_exec, s->stream)) : enqueue_gen(*s, s->stream);
+    if (!rc && host_tokens) {
+        rc = cuda(cudaMemcpyAsync(host_tokens, s->at<int32_t>(s->hist_off), size_t(n_steps) * 4,
+                                  cudaMemcpyDeviceToHost, s->stream));
+        if (!rc) rc = cuda(cudaStreamSynchronize(s->stream));
+    } else if (!rc) {
+        rc = cuda(cudaGetLastError());
+    }
+    return rc;
+}
+
+extern "C" int syn_session_launches_per_step(const syn_session* s) {
+    if (!s) return 0;
+    int n = 1;  // advance
+    for (const op& o : s->ops) n += o.kind == opk::attention ? 2 : 1;
+    return n;
+}
+
+namespace {
+
+// Algorithmic bytes of one op at position pos: every weight byte (with its
+// scales), activation byte in and out, and KV row it must touch once.
+double op_bytes(const syn_session& s, const op& o, uint32_t pos) {
+    const syn_llama_config& c = s.cfg;
+    switch (o.kind) {
+    case opk::embed: return double(c.n_embd) * 4 * 2;
+    case opk::rms_norm: return double(o.cols) * 4 * 3 + (o.out2 >= 0 ? double(o.cols) * 1.125 : 0);
+    case opk::quantize: return double(o.cols) * (4 + 1.125);
+    case opk::matmul: {
+        const weight& w = *o.w;
+        const double nb = double(w.cols) / 32;
+        double wb = w.quant() ? double(w.rows) * nb * (w.type == SYN_Q4_0 ? 18 : 34)
+                              : double(w.rows) * w.cols * (w.type == SYN_F32 ? 4 : 2);
+        const double in = w.quant() ? double(w.cols) + nb * 8 : double(w.cols) * 4;
+        return wb + in + double(w.rows) * 4 * (o.res >= 0 ? 2 : 1);
+    }
+    case opk::attention: {
+        const double L = double(pos) + 1, row = double(c.n_head_kv) * c.head_dim;
+        return 2 * L * row * 2 + double(c.n_head) * c.head_dim * 4 * 2 + 2 * row * 4;
+    }
+    case opk::silu_mul: return double(o.cols) * (8 + 1.125);
+    case opk::argmax: return double(c.n_vocab) * 4;
+    }
+    return 0;
+}
+
+int op_kind_code(opk k) {
+    switch (k) {
+    case opk::embed: return SYN_OP_EMBED;
+    case opk::rms_norm: return SYN_OP_RMS_NORM;
+    case opk::quantize: return SYN_OP_QUANTIZE;
+    case opk::matmul: return SYN_OP_MATMUL;
+    case opk::attention: return SYN_OP_ATTENTION;
+    case opk::silu_mul: return SYN_OP_SILU_MUL;
+    case opk::argmax: return SYN_OP_ARGMAX;
+    }
+    return -1;
+}
+
+}  // namespace
+
+extern "C" int syn_session_profile(syn_session* s, uint32_t token, uint32_t pos, syn_op_profile* out, int max_ops,
+                                   int* n_ops) {
+    if (!s || !n_ops) return SYN_ERR_INVALID;
+    if (token >= uint32_t(s->cfg.n_vocab) || pos >= uint32_t(s->max_ctx)) return SYN_ERR_RANGE;
+    int rc = cuda(cudaSetDevice(s->device));
+    if (rc) return rc;
+    const size_t n = s->ops.size();
+    *n_ops = int(n);
+    std::vector<cudaEvent_t> ev(n + 1);
+    for (auto& e : ev)
+        if ((rc = cuda(cudaEventCreate(&e)))) return rc;
+    int32_t io[2] = {int32_t(token), int32_t(pos)};
+    rc = cuda(cudaMemcpyAsync(s->io(), io, sizeof io, cudaMemcpyHostToDevice, s->stream));
+    // the same ops as enqueue_body, one at a time, with an event between each
+    std::vector<op> all;
+    all.swap(s->ops);
+    for (size_t i = 0; i < n && !rc; ++i) {
+        rc = cuda(cudaEventRecord(ev[i], s->stream));
+        s->ops.assign(1, all[i]);
+        if (!rc) rc = enqueue_body(*s, s->stream);
+    }
+    s->ops.swap(all);
+    if (!rc) rc = cuda(cudaEventRecord(ev[n], s->stream));
+    if (!rc) rc = cuda(cudaStreamSynchronize(s->stream));
+    for (size_t i = 0; i < n && !rc && out && int(i) < max_ops; ++i) {
+        const op& o = s->ops[i];
+        syn_op_profile& p = out[i];
+        p.kind = op_kind_code(o.kind);
+        p.layer = o.kind == opk::attention ? o.layer : -1;
+        p.type = o.w ? o.w->type : -1;
+        p.rows = o.w ? o.w->rows : 0;
+        p.cols = o.w ? o.w->cols : o.cols;
+        rc = cuda(cudaEventElapsedTime(&p.ms, ev[i], ev[i + 1]));
+        p.bytes = op_bytes(*s, o, pos);
+    }
+    for (auto& e : ev) cudaEventDestroy(e);
+    return rc;
+}
+
+extern "C" int syn_copy_to_host(void* host_dst, const void* device_src, size_t bytes) {
+    if (!host_dst || !device_src) return SYN_ERR_INVALID;
+    return cuda(cudaMemcpy(host_dst, device_src, bytes, cudaMemcpyDeviceToHost));
+}
+
+extern "C" float* syn_session_logits(syn_session* s) { return s ? s->tf(s->logits_t) : nullptr; }
+
+extern "C" void* syn_session_stream(syn_session* s) { return s ? s->stream : nullptr; }
+
+extern "C" uint16_t* syn_session_kv(syn_session* s, int layer, int which) {
+    if (!s || layer < 0 || layer >= s->cfg.n_layer || (which != 0 && which != 1)) return nullptr;
+    return s->kv(layer, which);
+}
+
+extern "C" int syn_session_weight(syn_session* s, const char* name, void* host_out, size_t bytes, int* type,
+                                  int* rows, int* cols) {
+    if (!s || !name) return SYN_ERR_INVALID;
+    for (const auto& src : s->sources) {
+        if (src.first != name) continue;
+        const weight& w = *src.second.first;
+        const int row0 = src.second.second;
+        int r = w.rows;
+        const syn_llama_config& c = s->cfg;
+        const std::string n(name);
+        const int qrows = c.n_head * c.head_dim, kvrows = c.n_head_kv * c.head_dim;
+        if (n.find("attn_q.") != std::string::npos) r = qrows;
+        else if (n.find("attn_k.") != std::string::npos || n.find("attn_v.") != std::string::npos) r = kvrows;
+        else if (n.find("ffn_gate.") != std::string::npos || n.find("ffn_up.") != std::string::npos) r = c.n_ff;
+        if (type) *type = w.type;
+        if (rows) *rows = r;
+        if (cols) *cols = w.cols;
+        const size_t need = syn_weight_bytes(w.type, r, w.cols, SYN_LAYOUT_GGUF);
+        if (!host_out) return SYN_OK;
+        if (bytes < need) return SYN_ERR_INVALID;
+        int rc = cuda(cudaSetDevice(s->device));
+        if (rc) return rc;
+        if (!w.quant()) {
+            const size_t es = w.type == SYN_F32 ? 4 : 2;
+            return cuda(cudaMemcpy(host_out, s->arena + w.off + size_t(row0) * w.cols * es, need,
+                                   cudaMemcpyDeviceToHost));
+        }
+        // planar -> GGUF blocks on the host
+        const int nb = w.cols / 32, qb = w.type == SYN_Q4_0 ? 16 : 32, bb = qb + 2;
+        std::vector<uint8_t> qs(size_t(r) * nb * qb);
+        std::vector<uint16_t> dh(size_t(r) * nb);
+        const size_t qplane = (size_t(w.rows) * nb * qb + 255) / 256 * 256;
+        rc = cuda(cudaMemcpy(qs.data(), s->arena + w.off + size_t(row0) * nb * qb, qs.size(), cudaMemcpyDeviceToHost));
+        if (!rc) rc = cuda(cudaMemcpy(dh.data(), s->arena + w.off + qplane + size_t(row0) * nb * 2, dh.size() * 2,
+                                      cudaMemcpyDeviceToHost));
+        if (rc) return rc;
+        uint8_t* o = static_cast<uint8_t*>(host_out);
+        for (size_t i = 0; i < size_t(r) * nb; ++i) {
+            std::memcpy(o + i * bb, &dh[i], 2);
+            std::memcpy(o + i * bb + 2, qs.data() + i * qb, qb);
+        }
+        return SYN_OK;
+    }
+    return set_err(SYN_ERR_INVALID, std::string("no tensor ") + name);
+}
