@@ -50,6 +50,8 @@ def parse():
     p.add_argument("--warmup", type=int, default=16)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--ncu-step", type=int, default=0,
+                   help="profiling mode: an 8-token prompt, then N graph steps inside the NVTX range decode_step")
     return p.parse_args()
 
 
@@ -219,6 +221,25 @@ def reference_arm(args, rank, world):
 
 # --------------------------------------------------------------------------- GPU arm
 
+def ncu_step(args, local):
+    """A short run for ncu launch lists: the 8B session, an 8-token prompt, then
+    args.ncu_step graph steps inside the NVTX range "decode_step"."""
+    import torch
+
+    import synapse_b200 as syn
+
+    cfg = dict(LLAMA8B, type_embd=syn.Q4_0, type_layers=syn.Q4_0, type_output=syn.Q8_0)
+    sess = syn.Session.synthetic(cfg, max_ctx=CTX, seed=1234, device=local)
+    toks = sess.generate(list(range(1, 9)), 0, 8)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("decode_step")
+    out = sess.generate([int(toks[-1])], 8, args.ncu_step)
+    torch.cuda.nvtx.range_pop()
+    print(json.dumps({"ncu_step": args.ncu_step, "launches_per_step": sess.launches_per_step(),
+                      "tokens": [int(t) for t in out]}))
+    sess.close()
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -237,6 +258,8 @@ def main():
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
+    if args.ncu_step:
+        return ncu_step(args, local)
     W = max(3, args.warmup)
     K = args.steps if args.steps is not None else CTX - PROMPT - W
     max_ctx = max(CTX, PROMPT + W + K)

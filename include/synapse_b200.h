@@ -86,6 +86,11 @@ int syn_repack_planar(int type, const void* src, int rows, int cols, void* dst, 
 int syn_upload_weight(int type, const void* host_src, int rows, int cols, void* dst, int layout, void* staging,
                       size_t staging_bytes, void* stream);
 
+/* Seeded N(0, 0.02) weights quantized on the device (ggml's reference
+ * quantizer) straight into a planar matrix: synthetic inputs for benchmarks
+ * (the reference only reads weights from files; no counterpart). */
+int syn_fill_random_planar(int type, int rows, int cols, void* dst, uint64_t seed, void* stream);
+
 /* ------------------------------------------------------------------------
  * mul_mat: Y[t][r] = W[r,:] . X[t,:] for t < n_tok (kernels/gemm.hpp:143-230
  * gemm_rows, the n_tok = 1 case being kernels/gemv.hpp:149-161 gemv).

@@ -25,6 +25,7 @@ namespace {
 
 constexpr int kThreads = 128;
 constexpr int kMaxChunk = 1024;  // positions per split (bounds shared memory)
+constexpr int kTile = 64;        // cached rows staged in shared memory at a time
 
 struct AttnParams {
     const float *q, *k, *v;
@@ -126,16 +127,10 @@ __device__ __forceinline__ void unpack8(uint4 v, float (&f)[8]) {
     }
 }
 
-// Lanes per cached row (each lane 8 halves) rounded up to a power of two.
-__device__ __forceinline__ int lanes_per_row(int hd) {
-    const int need = hd / 8;
-    int l = 1;
-    while (l < need) l <<= 1;
-    return l;
-}
-
 template <int GT>
 __global__ void __launch_bounds__(kThreads) attn_kpass(AttnParams a) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int j = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
     const int hd = a.hd, G = a.n_head / a.n_kv, H = a.n_head;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -147,8 +142,9 @@ __global__ void __launch_bounds__(kThreads) attn_kpass(AttnParams a) {
     extern __shared__ float sm[];
     float* cs = sm;              // [hd/2][2]
     float* qg = cs + hd;         // [G][hd], rotated and rounded to binary16
-    float* kr = qg + GT * hd;    // [hd], the appended key (binary16 values)
-    float* sc = kr + hd;         // [G][chunk]
+    float* sc = qg + GT * hd;    // [G][chunk]
+    uint16_t* krh = reinterpret_cast<uint16_t*>(sc + GT * kMaxChunk);  // [hd] the appended key, binary16
+    uint16_t* tile = krh + hd;   // [kTile][hd + 8] cached K rows (16-byte padded)
     __shared__ float red_f[kThreads / 32];
     __shared__ double red_d[kThreads / 32];
 
@@ -198,66 +194,62 @@ __global__ void __launch_bounds__(kThreads) attn_kpass(AttnParams a) {
                 const uint16_t h0 = f16_bits(o0), h1 = f16_bits(o1);
                 krow[i0] = h0;
                 krow[i1] = h1;
-                kr[i0] = f16_from_bits(h0);
-                kr[i1] = f16_from_bits(h1);
+                krh[i0] = h0;
+                krh[i1] = h1;
             }
         } else {
             for (int d = tid; d < hd; d += kThreads) {
                 const uint16_t h = f16_bits(kb[d]);
                 krow[d] = h;
-                kr[d] = f16_from_bits(h);
+                krh[d] = h;
             }
         }
         for (int d = tid; d < hd; d += kThreads) vrow[d] = f16_bits(vb[d]);
     }
     __syncthreads();
 
-    // Scores: LPP lanes per position, each dotting 8 dimensions.
-    const int LPP = lanes_per_row(hd), PPW = 32 / LPP;
-    const int seg = lane / LPP, sl = lane % LPP;
-    const bool dim_ok = sl * 8 < hd;
+    // Scores, a tile of kTile positions at a time: the tile's K rows are loaded
+    // coalesced into shared memory, then one thread per position runs the dot
+    // in dimension order as attend_group sums it (attention.hpp:214-219);
+    // binary16 products are exact in float, so each add is the reference's add.
     float* scores_b = a.scores + (size_t(b) * H + size_t(g) * G) * a.max_len;
-    for (int tb = t0 + warp * PPW; tb < t1; tb += (kThreads / 32) * PPW) {
-        const int t = tb + seg;
-        const bool ok = t < t1 && dim_ok;
-        float kf[8];
-        if (ok) {
-            if (owns_row && t == P) {
-#pragma unroll
-                for (int e = 0; e < 8; ++e) kf[e] = kr[sl * 8 + e];
-            } else {
-                const uint4 v = *reinterpret_cast<const uint4*>(kcb + size_t(t) * row + size_t(g) * hd + sl * 8);
-                unpack8(v, kf);
-            }
-        } else {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) kf[e] = 0.0f;
+    const int rowh = hd + 8, c8n = hd / 8;
+    for (int tb = t0; tb < t1; tb += kTile) {
+        const int n = min(kTile, t1 - tb);
+        for (int i = tid; i < n * c8n; i += kThreads) {
+            const int rr = i / c8n, c8 = i % c8n, t = tb + rr;
+            const uint4 v = (owns_row && t == P)
+                                ? *reinterpret_cast<const uint4*>(krh + c8 * 8)
+                                : __ldg(reinterpret_cast<const uint4*>(kcb + size_t(t) * row + size_t(g) * hd + c8 * 8));
+            *reinterpret_cast<uint4*>(tile + rr * rowh + c8 * 8) = v;
         }
-        float dot[GT];
+        __syncthreads();
+        if (tid < n) {
+            const uint16_t* kt = tile + tid * rowh;
+            float dot[GT];
 #pragma unroll
-        for (int jh = 0; jh < GT; ++jh) {
-            float s = 0.0f;
-            if (jh < G && ok) {
+            for (int jh = 0; jh < GT; ++jh) dot[jh] = 0.0f;
+            for (int d8 = 0; d8 < hd; d8 += 8) {
+                float kf[8];
+                unpack8(*reinterpret_cast<const uint4*>(kt + d8), kf);
 #pragma unroll
-                for (int e = 0; e < 8; ++e) s = fmaf(qg[jh * hd + sl * 8 + e], kf[e], s);  // exact products
+                for (int e = 0; e < 8; ++e)
+#pragma unroll
+                    for (int jh = 0; jh < GT; ++jh)
+                        if (jh < G) dot[jh] = __fadd_rn(dot[jh], __fmul_rn(qg[jh * hd + d8 + e], kf[e]));
             }
-            dot[jh] = s;
-        }
-#pragma unroll
-        for (int jh = 0; jh < GT; ++jh)
-            for (int o = LPP / 2; o > 0; o >>= 1) dot[jh] += __shfl_xor_sync(0xffffffffu, dot[jh], o);
-        if (sl == 0 && t < t1) {
+            const int t = tb + tid;
 #pragma unroll
             for (int jh = 0; jh < GT; ++jh) {
                 if (jh < G) {
-                    const float s = __fmul_rn(dot[jh], a.scale);
-                    sc[jh * chunk + (t - t0)] = s;
-                    scores_b[size_t(jh) * a.max_len + t] = s;
+                    const float sv = __fmul_rn(dot[jh], a.scale);
+                    sc[jh * chunk + (t - t0)] = sv;
+                    scores_b[size_t(jh) * a.max_len + t] = sv;
                 }
             }
         }
+        __syncthreads();
     }
-    __syncthreads();
 
     // Split statistics per query head: max, then the double sum of expf(s - max).
     for (int jh = 0; jh < G; ++jh) {
@@ -269,7 +261,7 @@ __global__ void __launch_bounds__(kThreads) attn_kpass(AttnParams a) {
         m = red_f[0];
         for (int w = 1; w < kThreads / 32; ++w) m = fmaxf(m, red_f[w]);
         double s = 0.0;
-        for (int t = tid; t < chunk; t += kThreads) s += double(expf(__fsub_rn(sc[jh * chunk + t], m)));
+        for (int t = tid; t < chunk; t += kThreads) s += double(exp_rn(__fsub_rn(sc[jh * chunk + t], m)));
         s = warp_sum_d(s);
         if (lane == 0) red_d[warp] = s;
         __syncthreads();
@@ -285,6 +277,8 @@ __global__ void __launch_bounds__(kThreads) attn_kpass(AttnParams a) {
 
 template <int GT>
 __global__ void __launch_bounds__(kThreads) attn_vpass(AttnParams a) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int j = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
     const int hd = a.hd, G = a.n_head / a.n_kv, H = a.n_head;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -296,8 +290,8 @@ __global__ void __launch_bounds__(kThreads) attn_vpass(AttnParams a) {
     const int chunk = t1 - t0;
 
     extern __shared__ float sm[];
-    float* pw = sm;                     // [G][chunk] probabilities
-    float* red = pw + GT * kMaxChunk;   // [PG][G][hd] partial sums
+    float* pw = sm;                                               // [G][chunk] probabilities
+    uint16_t* tile = reinterpret_cast<uint16_t*>(pw + GT * kMaxChunk);  // [kTile][hd + 8] cached V rows
     __shared__ float gm[GT], gscale[GT];
     __shared__ int is_last;
 
@@ -321,48 +315,47 @@ __global__ void __launch_bounds__(kThreads) attn_vpass(AttnParams a) {
     const float* scores_b = a.scores + (size_t(b) * H + size_t(g) * G) * a.max_len;
     for (int i = tid; i < G * chunk; i += kThreads) {
         const int jh = i / chunk, t = i % chunk;
-        const float e = expf(__fsub_rn(scores_b[size_t(jh) * a.max_len + t0 + t], gm[jh]));
+        const float e = exp_rn(__fsub_rn(scores_b[size_t(jh) * a.max_len + t0 + t], gm[jh]));
         pw[jh * chunk + t] = round_f16(__fmul_rn(e, gscale[jh]));
     }
     __syncthreads();
 
-    const int LPP = lanes_per_row(hd), PG = kThreads / LPP;
-    const int pg = tid / LPP, sl = tid % LPP;
-    const bool dim_ok = sl * 8 < hd;
+    // p.V a tile of kTile cached V rows at a time (loaded coalesced into shared
+    // memory); each thread owns outputs (head jh, dim d) and adds p_t * V_t,d
+    // in position order (attention.hpp:231-243) over the split's positions.
     const size_t row = size_t(a.n_kv) * hd;
-    const uint16_t* vcb = a.vc + size_t(b) * a.cache_stride + size_t(g) * hd + sl * 8;
-    float acc[GT][8];
+    const uint16_t* vcb = a.vc + size_t(b) * a.cache_stride + size_t(g) * hd;
+    const int rowh = hd + 8, c8n = hd / 8;
+    constexpr int kOut = (GT * 256 + kThreads - 1) / kThreads;  // outputs per thread, upper bound
+    float acc[kOut];
 #pragma unroll
-    for (int jh = 0; jh < GT; ++jh)
+    for (int k = 0; k < kOut; ++k) acc[k] = 0.0f;
+    const int n_out = G * hd;
+    for (int tb = t0; tb < t1; tb += kTile) {
+        const int n = min(kTile, t1 - tb);
+        for (int i = tid; i < n * c8n; i += kThreads) {
+            const int rr = i / c8n, c8 = i % c8n;
+            *reinterpret_cast<uint4*>(tile + rr * rowh + c8 * 8) =
+                __ldg(reinterpret_cast<const uint4*>(vcb + size_t(tb + rr) * row + c8 * 8));
+        }
+        __syncthreads();
+        for (int rr = 0; rr < n; ++rr) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[jh][e] = 0.0f;
-    if (dim_ok) {
-        for (int t = t0 + pg; t < t1; t += PG) {
-            const uint4 v = *reinterpret_cast<const uint4*>(vcb + size_t(t) * row);
-            float vf[8];
-            unpack8(v, vf);
-#pragma unroll
-            for (int jh = 0; jh < GT; ++jh) {
-                if (jh < G) {
-                    const float p = pw[jh * chunk + (t - t0)];
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) acc[jh][e] = fmaf(p, vf[e], acc[jh][e]);  // exact products
+            for (int k = 0; k < kOut; ++k) {
+                const int o = tid + k * kThreads;
+                if (o < n_out) {
+                    const int jh = o / hd, d = o % hd;  // fmaf: the products are exact
+                    acc[k] = fmaf(pw[jh * chunk + (tb - t0) + rr], f16_from_bits(tile[rr * rowh + d]), acc[k]);
                 }
             }
         }
-#pragma unroll
-        for (int jh = 0; jh < GT; ++jh)
-            if (jh < G)
-#pragma unroll
-                for (int e = 0; e < 8; ++e) red[(pg * G + jh) * hd + sl * 8 + e] = acc[jh][e];
+        __syncthreads();
     }
-    __syncthreads();
     float* part = a.partial + (stat0 + j) * hd;  // + jh * S * hd
-    for (int i = tid; i < G * hd; i += kThreads) {
-        const int jh = i / hd, d = i % hd;
-        float s = 0.0f;
-        for (int q = 0; q < PG; ++q) s += red[(q * G + jh) * hd + d];
-        part[size_t(jh) * a.S * hd + d] = s;
+#pragma unroll
+    for (int k = 0; k < kOut; ++k) {
+        const int o = tid + k * kThreads;
+        if (o < n_out) part[size_t(o / hd) * a.S * hd + o % hd] = acc[k];
     }
     __threadfence();
     __syncthreads();
@@ -382,6 +375,8 @@ __global__ void __launch_bounds__(kThreads) attn_vpass(AttnParams a) {
 
 // RoPE of k and F16 append of (k, v) at row pos[b], one CTA per token.
 __global__ void __launch_bounds__(kThreads) rope_append_kernel(AttnParams a) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int b = blockIdx.x, hd = a.hd, tid = threadIdx.x;
     const int P = a.pos[b];
     if (P < 0 || P >= a.max_len) return;  // outside the caller's bound
@@ -408,6 +403,8 @@ __global__ void __launch_bounds__(kThreads) rope_append_kernel(AttnParams a) {
 
 // Plain RoPE of n rows (attention.hpp:89-129), one CTA per row.
 __global__ void __launch_bounds__(kThreads) rope_kernel(AttnParams a, const float* x, float* out) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int r = blockIdx.x, hd = a.hd, tid = threadIdx.x;
     const int P = a.pos[r];
     extern __shared__ float cs[];
@@ -467,9 +464,9 @@ int check_args(const syn_attention_args* x, bool need_scratch) {
 template <int GT>
 int launch_attention(AttnParams a, cudaStream_t s) {
     const dim3 grid(a.S, a.n_kv, a.n_q);
-    const size_t kshm = size_t(a.hd + GT * a.hd + a.hd + GT * kMaxChunk) * 4;
-    const int LPP = [](int hd) { int l = 1; while (l < hd / 8) l <<= 1; return l; }(a.hd);
-    const size_t vshm = size_t(GT * kMaxChunk + (kThreads / LPP) * GT * a.hd) * 4;
+    const size_t tile_bytes = size_t(kTile) * (a.hd + 8) * 2;
+    const size_t kshm = size_t(a.hd + GT * a.hd + GT * kMaxChunk) * 4 + size_t(a.hd) * 2 + tile_bytes;
+    const size_t vshm = size_t(GT * kMaxChunk) * 4 + tile_bytes;
     // The opt-in above 48 KB is a per-device function attribute.
     static bool configured[64] = {};
     int dev = 0;
@@ -483,11 +480,9 @@ int launch_attention(AttnParams a, cudaStream_t s) {
         if (st) return st;
         configured[dev] = true;
     }
-    attn_kpass<GT><<<grid, kThreads, kshm, s>>>(a);
-    int st = syn_check_launch();
+    int st = syn_launch(attn_kpass<GT>, grid, kThreads, kshm, s, a);
     if (st) return st;
-    attn_vpass<GT><<<grid, kThreads, vshm, s>>>(a);
-    return syn_check_launch();
+    return syn_launch(attn_vpass<GT>, grid, kThreads, vshm, s, a);
 }
 
 }  // namespace
@@ -527,8 +522,8 @@ extern "C" int syn_rope_kv_append(const syn_attention_args* x, void* stream) {
     if (st) return st;
     if (!x->k || !x->v) return SYN_ERR_INVALID;
     AttnParams a = make_params(x);
-    rope_append_kernel<<<x->n_q, kThreads, size_t(x->head_dim) * 4, static_cast<cudaStream_t>(stream)>>>(a);
-    return syn_check_launch();
+    return syn_launch(rope_append_kernel, x->n_q, kThreads, size_t(x->head_dim) * 4,
+                      static_cast<cudaStream_t>(stream), a);
 }
 
 extern "C" int syn_rope(const float* x, float* out, int n, int n_heads, int head_dim, const int32_t* pos,
@@ -545,6 +540,5 @@ extern "C" int syn_rope(const float* x, float* out, int n, int n_heads, int head
     args.yarn = yarn;
     args.pos = pos;
     AttnParams a = make_params(&args);
-    rope_kernel<<<n, kThreads, size_t(head_dim) * 4, static_cast<cudaStream_t>(stream)>>>(a, x, out);
-    return syn_check_launch();
+    return syn_launch(rope_kernel, n, kThreads, size_t(head_dim) * 4, static_cast<cudaStream_t>(stream), a, x, out);
 }

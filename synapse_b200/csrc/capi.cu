@@ -7,7 +7,11 @@
 
 namespace {
 thread_local char g_last_error[256] = "";
+thread_local int g_pdl = 0;
 }
+
+int syn_pdl_enabled() { return g_pdl; }
+void syn_set_pdl(int on) { g_pdl = on; }
 
 int syn_cuda_status(cudaError_t e) {
     if (e == cudaSuccess) return SYN_OK;

@@ -85,6 +85,11 @@ __device__ __forceinline__ Q8Lane quantize_q8_lane(float x) {
     return r;
 }
 
+// expf rounded once from double precision: the correctly rounded float in all
+// but vanishingly rare cases, the closest a float result can be to the C
+// runtime's expf that the reference calls (std::exp on float).
+__device__ __forceinline__ float exp_rn(float x) { return float(exp(double(x))); }
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -111,9 +116,41 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 // its prologue early.
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
+// L2 prefetch of [p, p + bytes) (16-byte aligned, bytes a multiple of 16) by
+// the bulk-copy unit: weights the kernel will stream, requested before it
+// waits on the previous kernel.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+    if (bytes >= 16)
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes & ~15u) : "memory");
+}
+
 }  // namespace syn
 
 // Host-side error plumbing shared by the .cu files (defined in capi.cu).
 int syn_cuda_status(cudaError_t e);
 int syn_check_launch();
 int syn_num_sms();
+// Programmatic dependent launch for this thread's launches (the session turns
+// it on while it enqueues a step; plain C-ABI calls launch without it).
+int syn_pdl_enabled();
+void syn_set_pdl(int on);
+
+// Launch with the PDL attribute when enabled. Every kernel of this library
+// calls griddepcontrol.wait before it reads a predecessor's output or writes
+// any output, so a kernel may only start early, never read early.
+template <typename... KArgs, typename... Args>
+int syn_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    if (syn_pdl_enabled()) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    return syn_cuda_status(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
+}

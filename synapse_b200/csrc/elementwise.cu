@@ -15,6 +15,8 @@ constexpr int kNormThreads = 1024;
 __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const float* __restrict__ x,
                                                                 const float* __restrict__ gamma, int cols,
                                                                 float eps, float* out, ActPlanes act) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const float* xr = x + size_t(t) * cols;
     __shared__ double red[kNormThreads / 32];
@@ -57,11 +59,13 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const float* __r
 
 // silu (elementwise.hpp:76-81) then mul (:50-55): out = (g / (1 + expf(-g))) * u.
 __device__ __forceinline__ float silu_mul(float g, float u) {
-    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, exp_rn(-g))), u);
 }
 
 __global__ void __launch_bounds__(256) silu_mul_kernel(const float* __restrict__ g, const float* __restrict__ u,
                                                        int n_tok, int cols, float* out, ActPlanes act) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     if (act.qs) {
         // one warp per 32-value block: compute, then quantize it
@@ -87,6 +91,8 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const float* __restrict__
 }
 
 __global__ void add_kernel(const float* a, const float* b, float* out, size_t n) {
+    pdl_launch_dependents();
+    pdl_wait();
     for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x)
         out[i] = __fadd_rn(a[i], b[i]);
 }
@@ -94,6 +100,8 @@ __global__ void add_kernel(const float* a, const float* b, float* out, size_t n)
 // op_embed (session.hpp:331-336): decode_row of the table (blocks.hpp:72-106).
 __global__ void embed_kernel(int type, const uint8_t* __restrict__ table, int layout, int rows, int cols,
                              const int32_t* __restrict__ tokens, float* out) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int t = blockIdx.x;
     const int tok = tokens[t];
     float* o = out + size_t(t) * cols;
@@ -134,6 +142,8 @@ __global__ void embed_kernel(int type, const uint8_t* __restrict__ table, int la
 
 // First index of the maximum (std::max_element, llama_decode.cpp:274).
 __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ x, int n, int32_t* out) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int t = blockIdx.x, tid = threadIdx.x;
     const float* xr = x + size_t(t) * n;
     float best = -INFINITY;
@@ -165,6 +175,8 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
 // [4] forced (prompt) tokens. After a step: history[step] = argmax, the
 // position advances, and the next input is the next prompt token or the argmax.
 __global__ void advance_kernel(int32_t* io, const int32_t* forced, int32_t* history) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int step = io[3];
     history[step] = io[2];
     io[3] = step + 1;
@@ -175,8 +187,7 @@ __global__ void advance_kernel(int32_t* io, const int32_t* forced, int32_t* hist
 }  // namespace
 
 int syn_advance(int32_t* io, const int32_t* forced, int32_t* history, cudaStream_t s) {
-    advance_kernel<<<1, 1, 0, s>>>(io, forced, history);
-    return syn_check_launch();
+    return syn_launch(advance_kernel, 1, 1, 0, s, io, forced, history);
 }
 
 extern "C" int syn_rms_norm(const float* x, const float* gamma, int n_tok, int cols, float eps, float* out_f32,
@@ -185,8 +196,8 @@ extern "C" int syn_rms_norm(const float* x, const float* gamma, int n_tok, int c
     if (act && cols % QK) return SYN_ERR_INVALID;
     ActPlanes a{};
     if (act) a = act_planes(act, n_tok, cols);
-    rms_norm_kernel<<<n_tok, kNormThreads, 0, static_cast<cudaStream_t>(stream)>>>(x, gamma, cols, eps, out_f32, a);
-    return syn_check_launch();
+    return syn_launch(rms_norm_kernel, n_tok, kNormThreads, 0, static_cast<cudaStream_t>(stream), x, gamma, cols, eps,
+                      out_f32, a);
 }
 
 extern "C" int syn_silu_mul(const float* g, const float* u, int n_tok, int cols, float* out_f32, void* act,
@@ -202,16 +213,15 @@ extern "C" int syn_silu_mul(const float* g, const float* u, int n_tok, int cols,
         grid = (long(n_tok) * cols + 255) / 256;
         if (grid > 4096) grid = 4096;
     }
-    silu_mul_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(g, u, n_tok, cols, out_f32, a);
-    return syn_check_launch();
+    return syn_launch(silu_mul_kernel, unsigned(grid), 256, 0, static_cast<cudaStream_t>(stream), g, u, n_tok, cols,
+                      out_f32, a);
 }
 
 extern "C" int syn_add(const float* a, const float* b, float* out, size_t n, void* stream) {
     if (!a || !b || !out || n == 0) return SYN_ERR_INVALID;
     long grid = long((n + 255) / 256);
     if (grid > 4096) grid = 4096;
-    add_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(a, b, out, n);
-    return syn_check_launch();
+    return syn_launch(add_kernel, unsigned(grid), 256, 0, static_cast<cudaStream_t>(stream), a, b, out, n);
 }
 
 extern "C" int syn_embed(int type, const void* table, int layout, int rows, int cols, const int32_t* tokens,
@@ -219,13 +229,11 @@ extern "C" int syn_embed(int type, const void* table, int layout, int rows, int 
     if (type != SYN_F32 && type != SYN_F16 && type != SYN_Q4_0 && type != SYN_Q8_0) return SYN_ERR_UNSUPPORTED;
     if (!table || !tokens || !out || rows <= 0 || cols <= 0 || n_tok <= 0) return SYN_ERR_INVALID;
     if ((type == SYN_Q4_0 || type == SYN_Q8_0) && cols % QK) return SYN_ERR_INVALID;
-    embed_kernel<<<n_tok, 256, 0, static_cast<cudaStream_t>(stream)>>>(type, static_cast<const uint8_t*>(table),
-                                                                        layout, rows, cols, tokens, out);
-    return syn_check_launch();
+    return syn_launch(embed_kernel, n_tok, 256, 0, static_cast<cudaStream_t>(stream), type,
+                      static_cast<const uint8_t*>(table), layout, rows, cols, tokens, out);
 }
 
 extern "C" int syn_argmax(const float* x, int n_tok, int n, int32_t* out, void* stream) {
     if (!x || !out || n_tok <= 0 || n <= 0) return SYN_ERR_INVALID;
-    argmax_kernel<<<n_tok, 1024, 0, static_cast<cudaStream_t>(stream)>>>(x, n, out);
-    return syn_check_launch();
+    return syn_launch(argmax_kernel, n_tok, 1024, 0, static_cast<cudaStream_t>(stream), x, n, out);
 }

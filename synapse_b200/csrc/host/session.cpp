@@ -374,11 +374,26 @@ int enqueue_gen(syn_session& s, cudaStream_t st) {
     return rc;
 }
 
+// Programmatic dependent launch on for the launches of one scope.
+struct pdl_scope {
+    explicit pdl_scope(bool on) { syn_set_pdl(on ? 1 : 0); }
+    ~pdl_scope() { syn_set_pdl(0); }
+};
+
+bool pdl_wanted() {
+    const char* env = std::getenv("SYN_PDL");
+    return !(env && env[0] == '0');
+}
+
 int capture(syn_session& s, int (*fn)(syn_session&, cudaStream_t), cudaGraphExec_t* out) {
     cudaGraph_t g = nullptr;
     int rc = cuda(cudaStreamBeginCapture(s.stream, cudaStreamCaptureModeThreadLocal));
     if (rc) return rc;
-    const int body = fn(s, s.stream);
+    int body;
+    {
+        pdl_scope pdl(pdl_wanted());
+        body = fn(s, s.stream);
+    }
     rc = cuda(cudaStreamEndCapture(s.stream, &g));
     if (body) {
         if (g) cudaGraphDestroy(g);

@@ -22,5 +22,8 @@ int syn_fill_f32(float* dst, size_t n, float v, cudaStream_t s);
 // argmax, advances the position and picks the next input token.
 int syn_advance(int32_t* io, const int32_t* forced, int32_t* history, cudaStream_t s);
 
+// Programmatic dependent launch for this thread's launches.
+void syn_set_pdl(int on);
+
 // Sets the thread's last error message.
 void syn_set_error(const char* msg);

@@ -13,6 +13,8 @@ namespace {
 
 __global__ void __launch_bounds__(256) quantize_q8_kernel(const float* __restrict__ x, int n_tok, int cols,
                                                           ActPlanes a) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int nb = cols / QK;
     const long blk = (long(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -164,6 +166,12 @@ int syn_fill_random(int type, int rows, int cols, void* dst, int total_rows, int
     return syn_check_launch();
 }
 
+// Benchmark helper: a whole planar matrix of seeded N(0, 0.02) weights.
+extern "C" int syn_fill_random_planar(int type, int rows, int cols, void* dst, uint64_t seed, void* stream) {
+    if (!quant_type(type) || !dst || rows <= 0 || cols <= 0 || cols % QK) return SYN_ERR_INVALID;
+    return syn_fill_random(type, rows, cols, dst, rows, 0, seed, 1, 0.02f, static_cast<cudaStream_t>(stream));
+}
+
 int syn_fill_f32(float* dst, size_t n, float v, cudaStream_t s) {
     fill_f32_kernel<<<(n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096, 256, 0, s>>>(dst, n, v);
     return syn_check_launch();
@@ -179,9 +187,8 @@ extern "C" int syn_quantize_q8_0(const float* x, int n_tok, int cols, void* act,
     const long warps = long(n_tok) * (cols / QK);
     const int threads = 256;
     const long grid = (warps * 32 + threads - 1) / threads;
-    quantize_q8_kernel<<<grid, threads, 0, static_cast<cudaStream_t>(stream)>>>(x, n_tok, cols,
-                                                                                 act_planes(act, n_tok, cols));
-    return syn_check_launch();
+    return syn_launch(quantize_q8_kernel, unsigned(grid), threads, 0, static_cast<cudaStream_t>(stream), x, n_tok,
+                      cols, act_planes(act, n_tok, cols));
 }
 
 extern "C" int syn_q8_act_to_blocks(const void* act, int n_tok, int cols, void* blocks, void* stream) {

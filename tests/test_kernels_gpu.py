@@ -64,9 +64,9 @@ def check_gemv(ty, layout, rows, cols, n_tok, seed, row_subset=None):
     wsub = w.reshape(rows, -1)[rs]
     for t in range(n_tok):
         ref = orc.gemv_q8act(ty, wsub, len(rs), cols, blocks[t])
-        err = rel_l2(y[t, rs], ref)
-        assert err < 1e-3, (t, err)
-        assert err < 1e-5  # only float re-association separates them
+        assert rel_l2(y[t, rs], ref) < 1e-3
+        # the kernel keeps the reference's float order: bit-identical to the oracle
+        assert np.array_equal(y[t, rs].view(np.uint32), ref.view(np.uint32)), (t, rel_l2(y[t, rs], ref))
     return y
 
 
@@ -123,7 +123,8 @@ def test_gemv_plain(ty, rows, cols, n_tok):
     wd = syn.upload_weight(ty, w, rows, cols)
     y = syn.gemv_f(ty, wd, rows, cols, dev(x)).cpu().numpy()
     ref = orc.gemm(ty, w, rows, cols, x)
-    assert rel_l2(y, ref) < 1e-5
+    assert rel_l2(y, ref) < 1e-3
+    assert np.array_equal(y.view(np.uint32), ref.view(np.uint32)), rel_l2(y, ref)
 
 
 def test_repack_matches_upload():
@@ -187,7 +188,7 @@ def attention_case(n_head, n_kv, hd, L, n_q, seed, base=10000.0, freq_factors=No
         assert np.array_equal(vc_after[b], vref), "V row appended bit-exactly"
         err = rel_l2(out[b], ref)
         assert err < 1e-3, (b, err)
-        assert err < 2e-5, (b, err)
+        assert err < 1e-4, (b, err)  # scores exact; p.V re-associated across splits
     return out
 
 
@@ -232,7 +233,7 @@ def test_attention_growing_cache_matches_oracle_sequence():
         ref = orc.attention(orc.rope(q, hd, pos, ts), orc.rope(k, hd, pos, ts), v, kc, vc, max_ctx, n_kv, hd, pos,
                             n_head, scale)
         assert_f16_rows_close(kcd.cpu().numpy().view(np.uint16), kc)
-        assert rel_l2(out, ref) < 2e-5
+        assert rel_l2(out, ref) < 1e-4
 
 
 def test_rope_kv_append_then_attend_prefill():
@@ -261,7 +262,7 @@ def test_rope_kv_append_then_attend_prefill():
     assert np.array_equal(vcd.cpu().numpy(), vc)
     for i in range(n):
         ref = orc.attend(orc.rope(q[i], hd, p0 + i, ts), kc, vc, max_ctx, n_kv, hd, p0 + i, n_head, np.float32(scale))
-        assert rel_l2(out[i], ref) < 2e-5
+        assert rel_l2(out[i], ref) < 1e-4
 
 
 def test_rope_matches_oracle():
@@ -302,8 +303,9 @@ def test_silu_mul_and_quant(n_tok, cols):
     out, act = syn.silu_mul(dev(g), dev(u), want_f32=True, want_act=True)
     out = out.cpu().numpy()
     ref = np.stack([orc.silu(g[t]) * u[t] for t in range(n_tok)]).astype(np.float32)
-    # expf may differ from glibc's by an ulp
+    # exp rounded once from double; the C runtime's expf agrees but for rare last-ulp cases
     assert np.max(np.abs(out - ref) / np.maximum(np.abs(ref), 1e-30)) < 1e-6
+    assert np.count_nonzero(out != ref) <= out.size // 1000
     qs, dh, _, _ = act_planes_host(act.cpu().numpy(), n_tok, cols)
     ref_qs, ref_dh = blocks_to_planes(orc.quantize_q8_0(out), n_tok, cols)
     assert np.array_equal(qs, ref_qs) and np.array_equal(dh, ref_dh)
