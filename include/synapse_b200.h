@@ -145,6 +145,20 @@ typedef struct {
 
 size_t syn_attention_scratch_bytes(int n_q, int n_head, int n_kv, int head_dim, int max_len);
 int syn_attention(const syn_attention_args* a, void* stream);
+/* syn_attention for callers that cannot allocate device memory. It has no
+ * counterpart in the reference; it exists for callers such as a host that
+ * owns the whole device memory budget and passes a plugin only its tensors,
+ * or a decode loop that must not allocate once running. a->scratch is
+ * ignored: the scratch is a 16 MiB array in the library's own static device
+ * memory, present on every GPU that loads the library until the process
+ * exits. Shapes whose syn_attention_scratch_bytes exceed 16 MiB are rejected
+ * with SYN_ERR_INVALID. The first call on a device looks up the array's device
+ * address with that device current; make that first call before any stream
+ * capture. No call allocates. Every call on a device uses the same array, so
+ * calls whose GPU work overlaps (different streams, or different host
+ * threads) race and must be serialised by the caller; the array keeps the
+ * last call's contents, none of which a later call depends on. */
+int syn_attention_noalloc(const syn_attention_args* a, void* stream);
 /* RoPE + F16 append only, for n_q tokens sharing one cache (prefill). */
 int syn_rope_kv_append(const syn_attention_args* a, void* stream);
 /* RoPE alone (attention.hpp:89): out[i] = rope(x[i], pos[i]) for n rows of

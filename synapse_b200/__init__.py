@@ -77,6 +77,7 @@ def _declare(L):
         "syn_gemv_f": (i32, [i32, vp, i32, i32, vp, i32, vp, vp, vp]),
         "syn_attention_scratch_bytes": (sz, [i32, i32, i32, i32, i32]),
         "syn_attention": (i32, [vp, vp]),
+        "syn_attention_noalloc": (i32, [vp, vp]),
         "syn_rope_kv_append": (i32, [vp, vp]),
         "syn_rope": (i32, [vp, vp, i32, i32, i32, vp, f32, vp, i32, vp, vp]),
         "syn_rms_norm": (i32, [vp, vp, i32, i32, f32, vp, vp, vp]),

@@ -16,8 +16,10 @@
 // Each KV head's rows are read by one CTA per split for all G = n_head / n_kv
 // query heads of its group (GQA sharing: K/V cross HBM once).
 #include "common.cuh"
+#include "internal.h"
 
 #include <algorithm>
+#include <mutex>
 
 using namespace syn;
 
@@ -515,6 +517,63 @@ extern "C" int syn_attention(const syn_attention_args* x, void* stream) {
     case 16: return launch_attention<16>(a, s);
     }
     return SYN_ERR_UNSUPPORTED;
+}
+
+// ---- attention without caller scratch ---------------------------------------
+// Some callers cannot allocate device memory: a host program that hands a
+// plugin only the tensors it owns and keeps every other byte of the device
+// budget to itself, or a real-time decode loop that has promised not to
+// allocate once it is running (the reference's session::run makes the same
+// promise). For them, syn_attention_noalloc keeps its scratch in this fixed
+// array, which exists once per GPU that loads the library, until the process
+// exits. Host code never touches the array by name: the device address comes
+// from cudaGetSymbolAddress, looked up once per device.
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;  // 16 MiB
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+
+// Device address of g_noalloc_scratch on the current device, looked up on the
+// first call made with that device current (not inside a stream capture).
+int noalloc_scratch(void** out) {
+    static std::mutex mu;
+    static void* addr[64] = {};
+    int dev = 0;
+    int st = syn_cuda_status(cudaGetDevice(&dev));
+    if (st) return st;
+    if (dev < 0 || dev >= 64) return SYN_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        st = syn_cuda_status(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+        if (st) return st;
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return SYN_OK;
+}
+
+}  // namespace
+
+extern "C" int syn_attention_noalloc(const syn_attention_args* x, void* stream) {
+    if (!x) return SYN_ERR_INVALID;
+    const size_t need = syn_attention_scratch_bytes(x->n_q, x->n_head, x->n_kv, x->head_dim, x->max_len);
+    if (need == 0) return SYN_ERR_INVALID;
+    if (need > kNoAllocScratchBytes) {
+        syn_set_error("syn_attention_noalloc: this shape needs more scratch than the 16 MiB static array; "
+                      "call syn_attention with caller scratch instead");
+        return SYN_ERR_INVALID;
+    }
+    void* scratch = nullptr;
+    const int st = noalloc_scratch(&scratch);
+    if (st) return st;
+    // The kernels fully write every scratch value they read later in the same
+    // call (scores, split statistics and partial outputs), and the first pass
+    // zeroes the completion counters the second pass counts with, so nothing
+    // left from an earlier call needs clearing here.
+    syn_attention_args a = *x;
+    a.scratch = scratch;
+    return syn_attention(&a, stream);
 }
 
 extern "C" int syn_rope_kv_append(const syn_attention_args* x, void* stream) {
