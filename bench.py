@@ -50,6 +50,7 @@ def parse():
     p.add_argument("--warmup", type=int, default=16)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--profile-out", default=None, help="write the per-op device times of one step (JSON) here")
     p.add_argument("--ncu-step", type=int, default=0,
                    help="profiling mode: an 8-token prompt, then N graph steps inside the NVTX range decode_step")
     return p.parse_args()
@@ -334,6 +335,10 @@ def main():
     except Exception:
         pass
     step_bytes = sum(o["bytes"] for o in ops)
+    if args.profile_out and rank == 0:
+        with open(args.profile_out, "w") as f:
+            json.dump([dict(o, ms=t, gbps=o["bytes"] / (t / 1e3) / 1e9 if t > 0 else None)
+                       for o, t in zip(ops, per_op)], f, indent=0)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

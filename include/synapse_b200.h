@@ -57,6 +57,9 @@ const char* syn_build_info(void);
 const char* syn_status_string(int status);
 /* The last CUDA error string seen by this thread (for SYN_ERR_CUDA). */
 const char* syn_last_error(void);
+/* How many bounded device-side waits on the current device gave up (a copy
+ * that never arrived); 0 in a healthy run, -1 if it cannot be read. */
+int syn_device_errors(void);
 
 /* ------------------------------------------------------------------------
  * Q8_0 activations (quant/q8.hpp:54-69 quantize_row_q8_0; kernels/gemv.hpp:
@@ -75,7 +78,7 @@ int syn_q8_act_to_blocks(const void* act, int n_tok, int cols, void* blocks, voi
 /* ------------------------------------------------------------------------
  * Weights: device bytes of a rows x cols matrix in a layout, and the
  * GGUF -> planar repack the loader runs once per tensor (gguf/tensor_view.hpp:
- * 33-40 view_as; SURVEY loader item (1)).
+ * 33-40 view_as, where the reference views the mapped file in place).
  * ---------------------------------------------------------------------- */
 size_t syn_weight_bytes(int type, int rows, int cols, int layout);
 /* src (device, GGUF layout) -> dst (device, planar). src and dst must not overlap. */
@@ -106,6 +109,32 @@ int syn_gemv_q(int type, const void* w, int layout, int rows, int cols, const vo
 int syn_gemv_f(int type, const void* w, int rows, int cols, const float* x, int n_tok, float* y,
                const float* residual, void* stream);
 
+/* mul_mat with its neighbours fused in (what the session runs): the input
+ * quantized inside the kernel from floats (SYN_IN_F32: gemm_prepare_rows), or
+ * from the rms_norm of the floats (SYN_IN_RMSNORM: op_rms_norm then
+ * op_matmul, elementwise.hpp:208-232), and optionally rows taken in (gate, up)
+ * pairs to give silu(gate) * up (SYN_OUT_SILU_PAIRS: op_silu then op_mul, the
+ * output holding rows/2 values per token). Every value equals the separate
+ * ops' bit for bit. The fused modes need planar weights, 1-2 tokens and a
+ * shape the pipelined kernel takes (syn_gemv_fusable); SYN_IN_Q8 with
+ * SYN_OUT_ROWS is syn_gemv_q. */
+enum { SYN_IN_Q8 = 0, SYN_IN_F32 = 1, SYN_IN_RMSNORM = 2 };
+enum { SYN_OUT_ROWS = 0, SYN_OUT_SILU_PAIRS = 1 };
+typedef struct {
+    int type, layout, rows, cols, n_tok;
+    const void* w;
+    int in_mode;
+    const void* act;       /* SYN_IN_Q8 */
+    const float* x;        /* SYN_IN_F32 / SYN_IN_RMSNORM, [n_tok][cols], 16-byte aligned */
+    const float* gamma;    /* SYN_IN_RMSNORM: cols floats, 16-byte aligned */
+    float eps;
+    int out_mode;
+    float* y;              /* [n_tok][rows] (SYN_OUT_ROWS) or [n_tok][rows/2] */
+    const float* residual; /* SYN_OUT_ROWS only; may alias y */
+} syn_gemv_args;
+int syn_gemv(const syn_gemv_args* a, void* stream);
+int syn_gemv_fusable(int type, int layout, int rows, int cols, int n_tok, int out_mode);
+
 /* ------------------------------------------------------------------------
  * RoPE + KV append + GQA decode attention (kernels/attention.hpp:89-129 rope,
  * :165-175 kv_append, :185-244 attend_group, :254-269 attention), fused:
@@ -118,7 +147,8 @@ int syn_gemv_f(int type, const void* w, int rows, int cols, const float* x, int 
  *   max_ctx * n_kv * head_dim for independent sequences (batched decode), or 0
  *   for tokens of one sequence (then append must be 0: use syn_rope_kv_append
  *   first, as session.hpp:349-356 appends every token before attending).
- * max_len bounds pos[b] + 1 for every b (it sizes the split grid and scratch).
+ * max_len bounds pos[b] + 1 for every b (it sizes the CTA cluster per KV head
+ * and the score scratch).
  * rope_mode: 0 normal (Llama), 1 neox. freq_factors: NULL or head_dim/2 floats
  * (device). yarn: NULL or 5 floats {freq_scale, ext_factor, attn_factor,
  * corr_low, corr_high} (host), attention.hpp:60-66.
@@ -141,6 +171,7 @@ typedef struct {
     float scale;           /* 1 / sqrt(head_dim), models/llama.hpp:407 */
     const float* freq_factors;
     const float* yarn;
+    const float* rope_table; /* NULL, or syn_rope_table for these rope settings and max_len rows */
 } syn_attention_args;
 
 size_t syn_attention_scratch_bytes(int n_q, int n_head, int n_kv, int head_dim, int max_len);
@@ -159,6 +190,13 @@ int syn_attention(const syn_attention_args* a, void* stream);
  * threads) race and must be serialised by the caller; the array keeps the
  * last call's contents, none of which a later call depends on. */
 int syn_attention_noalloc(const syn_attention_args* a, void* stream);
+/* The (cos, sin) of every RoPE pair at every position p < max_len, as
+ * table[p][i] = {cos, sin} of pair i (max_len * head_dim floats), with the
+ * arithmetic of attention.hpp:102-119. An attention call given the table reads
+ * it instead of evaluating the trigonometry for its position (a session builds
+ * it once). Device table; freq_factors device, yarn host (as syn_attention). */
+int syn_rope_table(float* table, int max_len, int head_dim, float theta_scale, const float* freq_factors,
+                   const float* yarn, void* stream);
 /* RoPE + F16 append only, for n_q tokens sharing one cache (prefill). */
 int syn_rope_kv_append(const syn_attention_args* a, void* stream);
 /* RoPE alone (attention.hpp:89): out[i] = rope(x[i], pos[i]) for n rows of
@@ -181,7 +219,10 @@ int syn_add(const float* a, const float* b, float* out, size_t n, void* stream);
 int syn_embed(int type, const void* table, int layout, int rows, int cols, const int32_t* tokens, int n_tok,
               float* out, void* stream);
 /* out[t] = first index of the largest of x[t][0..n) (llama_decode.cpp:274,
- * std::max_element: ties go to the lowest index). */
+ * std::max_element: ties go to the lowest index). n_tok <= 64. Its partial
+ * results live in a small static device array shared by every call on a
+ * device, so calls that overlap on the GPU must be serialised by the caller
+ * (a session uses its own workspace instead). */
 int syn_argmax(const float* x, int n_tok, int n, int32_t* out, void* stream);
 
 /* ------------------------------------------------------------------------
@@ -228,8 +269,9 @@ int syn_session_generate(syn_session* s, const uint32_t* prompt, int n_prompt, u
 /* Kernel launches one step makes (each graph replay launches exactly these). */
 int syn_session_launches_per_step(const syn_session* s);
 
-/* One step at (token, pos) run op by op with CUDA events around every op on the
- * session's stream (no graph), for per-kernel timing. For each op: its kind
+/* One step at (token, pos) with CUDA events around every op on the session's
+ * stream (captured once as its own graph, without programmatic overlap between
+ * ops), for per-kernel timing. For each op: its kind
  * (SYN_OP_*), layer (-1 outside layers), weight type, rows, cols, device time
  * (ms) and algorithmic bytes (what the op must move at least once: weights
  * with their scales, activations in and out, KV rows 0..pos). Returns the op

@@ -67,6 +67,7 @@ def _declare(L):
         "syn_build_info": (ctypes.c_char_p, []),
         "syn_status_string": (ctypes.c_char_p, [i32]),
         "syn_last_error": (ctypes.c_char_p, []),
+        "syn_device_errors": (i32, []),
         "syn_q8_act_bytes": (sz, [i32, i32]),
         "syn_quantize_q8_0": (i32, [vp, i32, i32, vp, vp]),
         "syn_q8_act_to_blocks": (i32, [vp, i32, i32, vp, vp]),
@@ -75,11 +76,14 @@ def _declare(L):
         "syn_upload_weight": (i32, [i32, vp, i32, i32, vp, i32, vp, sz, vp]),
         "syn_gemv_q": (i32, [i32, vp, i32, i32, i32, vp, i32, vp, vp, vp]),
         "syn_gemv_f": (i32, [i32, vp, i32, i32, vp, i32, vp, vp, vp]),
+        "syn_gemv": (i32, [vp, vp]),
+        "syn_gemv_fusable": (i32, [i32, i32, i32, i32, i32, i32]),
         "syn_attention_scratch_bytes": (sz, [i32, i32, i32, i32, i32]),
         "syn_attention": (i32, [vp, vp]),
         "syn_attention_noalloc": (i32, [vp, vp]),
         "syn_rope_kv_append": (i32, [vp, vp]),
         "syn_rope": (i32, [vp, vp, i32, i32, i32, vp, f32, vp, i32, vp, vp]),
+        "syn_rope_table": (i32, [vp, i32, i32, f32, vp, vp, vp]),
         "syn_rms_norm": (i32, [vp, vp, i32, i32, f32, vp, vp, vp]),
         "syn_silu_mul": (i32, [vp, vp, i32, i32, vp, vp, vp]),
         "syn_add": (i32, [vp, vp, vp, sz, vp]),
@@ -209,6 +213,32 @@ def gemv_f(type_, w, rows, cols, x, y=None, residual=None, stream=None):
     return y
 
 
+IN_Q8, IN_F32, IN_RMSNORM = 0, 1, 2
+OUT_ROWS, OUT_SILU_PAIRS = 0, 1
+
+
+class GemvArgs(ctypes.Structure):
+    _fields_ = [("type", ctypes.c_int), ("layout", ctypes.c_int), ("rows", ctypes.c_int), ("cols", ctypes.c_int),
+                ("n_tok", ctypes.c_int), ("w", ctypes.c_void_p), ("in_mode", ctypes.c_int), ("act", ctypes.c_void_p),
+                ("x", ctypes.c_void_p), ("gamma", ctypes.c_void_p), ("eps", ctypes.c_float),
+                ("out_mode", ctypes.c_int), ("y", ctypes.c_void_p), ("residual", ctypes.c_void_p)]
+
+
+def gemv_fused(type_, w, rows, cols, x, in_mode=IN_F32, gamma=None, eps=1e-5, out_mode=OUT_ROWS, residual=None,
+               act=None, stream=None):
+    """syn_gemv: the matmul with its input quantization (and rms_norm) and its silu*mul fused in."""
+    torch = _torch()
+    n_tok = (1 if x.dim() == 1 else x.shape[0]) if x is not None else 1
+    out_rows = rows // 2 if out_mode == OUT_SILU_PAIRS else rows
+    y = torch.empty((n_tok, out_rows), dtype=torch.float32, device=w.device)
+    a = GemvArgs(type_, LAYOUT_PLANAR, rows, cols, n_tok, w.data_ptr(), in_mode,
+                 act.data_ptr() if act is not None else None, x.data_ptr() if x is not None else None,
+                 gamma.data_ptr() if gamma is not None else None, eps, out_mode, y.data_ptr(),
+                 residual.data_ptr() if residual is not None else None)
+    check(lib().syn_gemv(ctypes.byref(a), _stream(stream)), "syn_gemv")
+    return y
+
+
 def mul_mat(type_, w, layout, rows, cols, x, stream=None):
     """Y = X W^T for float activations x (n_tok, cols): quantizes x for Q4_0/Q8_0."""
     if type_ in (F32, F16):
@@ -229,7 +259,7 @@ class AttentionArgs(ctypes.Structure):
                 ("n_q", ctypes.c_int), ("n_head", ctypes.c_int), ("n_kv", ctypes.c_int), ("head_dim", ctypes.c_int),
                 ("max_len", ctypes.c_int), ("append", ctypes.c_int), ("rope", ctypes.c_int),
                 ("rope_mode", ctypes.c_int), ("theta_scale", ctypes.c_float), ("scale", ctypes.c_float),
-                ("freq_factors", ctypes.c_void_p), ("yarn", ctypes.c_void_p)]
+                ("freq_factors", ctypes.c_void_p), ("yarn", ctypes.c_void_p), ("rope_table", ctypes.c_void_p)]
 
 
 def attention_scratch_bytes(n_q, n_head, n_kv, head_dim, max_len):
@@ -238,7 +268,7 @@ def attention_scratch_bytes(n_q, n_head, n_kv, head_dim, max_len):
 
 def attention(q, k, v, k_cache, v_cache, pos, n_head, n_kv, head_dim, max_len, theta_scale, scale,
               cache_stride=None, append=True, rope=True, rope_mode=0, freq_factors=None, out=None, scratch=None,
-              stream=None):
+              rope_table=None, stream=None):
     """Fused RoPE + F16 append + decode attention for n_q queries (see syn_attention)."""
     torch = _torch()
     n_q = pos.numel()
@@ -252,9 +282,20 @@ def attention(q, k, v, k_cache, v_cache, pos, n_head, n_kv, head_dim, max_len, t
                       v.data_ptr() if v is not None else None, k_cache.data_ptr(), v_cache.data_ptr(),
                       pos.data_ptr(), out.data_ptr(), scratch.data_ptr(), cache_stride, n_q, n_head, n_kv, head_dim,
                       max_len, int(append), int(rope), rope_mode, theta_scale, scale,
-                      freq_factors.data_ptr() if freq_factors is not None else None, None)
+                      freq_factors.data_ptr() if freq_factors is not None else None, None,
+                      rope_table.data_ptr() if rope_table is not None else None)
     check(lib().syn_attention(ctypes.byref(a), _stream(stream)), "syn_attention")
     return out
+
+
+def rope_table(max_len, head_dim, theta_scale, freq_factors=None, device="cuda", stream=None):
+    """(cos, sin) of every RoPE pair at every position: a [max_len, head_dim / 2, 2] float tensor."""
+    torch = _torch()
+    t = torch.empty((max_len, head_dim // 2, 2), dtype=torch.float32, device=device)
+    check(lib().syn_rope_table(t.data_ptr(), max_len, head_dim, theta_scale,
+                               freq_factors.data_ptr() if freq_factors is not None else None, None,
+                               _stream(stream)), "syn_rope_table")
+    return t
 
 
 def rope_kv_append(k, v, k_cache, v_cache, pos, n_kv, head_dim, max_len, theta_scale, cache_stride=0,
@@ -397,7 +438,7 @@ class Session:
         """Per-op CUDA-event times of one eager step: list of dicts."""
         n = ctypes.c_int()
         check(lib().syn_session_profile(self.h, int(token), int(pos), None, 0, ctypes.byref(n)), "profile")
-        recs = (OpProfile * n.value)()
+        recs = (OpProfile * max(n.value, 1))()
         check(lib().syn_session_profile(self.h, int(token), int(pos), recs, n.value, ctypes.byref(n)), "profile")
         return [dict(kind=OP_KINDS[r.kind], layer=r.layer, type=r.type, rows=r.rows, cols=r.cols, ms=r.ms,
                      bytes=r.bytes) for r in recs]

@@ -1,46 +1,60 @@
 // RoPE + F16 KV append + GQA decode attention (kernels/attention.hpp:89-269).
 //
-// Numerics follow attend_group (attention.hpp:185-244) step for step:
-//   q rounded to binary16; s_t = (q . K_t) * scale; softmax with the float
-//   max, e_t = expf(s_t - max), a double sum and scale = float(1 / sum)
-//   (elementwise.hpp:174-201); p_t = binary16(e_t * scale); out = sum p_t V_t.
-// Because p_t is rounded AFTER normalisation, the kernel runs in two passes
-// over the cache, which still reads every K and V byte exactly once:
-//   K-pass (grid: splits x KV heads x queries): rotates q (and k), appends
-//     (k, v) as F16 at row pos, writes the scores of its positions and the
-//     split's (max, double sum of expf(s - max)).
-//   V-pass (same grid): merges the splits' statistics into the global max and
-//     sum, forms p_t exactly as above, accumulates p_t V_t over its positions,
-//     and the last split CTA of each (query, KV head) sums the partial outputs
-//     in split order (deterministic).
-// Each KV head's rows are read by one CTA per split for all G = n_head / n_kv
-// query heads of its group (GQA sharing: K/V cross HBM once).
+// Numerics follow attend_group (attention.hpp:185-244): q rounded to
+// binary16; s_t = (q . K_t) * scale with the dot in dimension order (the
+// binary16 products are exact in float, so each step is one fma); softmax
+// with the float max M, e_t = expf(s_t - M), the normaliser summed in double
+// and scale = float(1 / sum) (elementwise.hpp:174-201); p_t = binary16(e_t *
+// scale), rounded after normalisation as the reference rounds it;
+// out = sum_t p_t V_t.
+//
+// One kernel per call. A thread-block cluster of C CTAs serves one (query,
+// KV head) group; CTA j owns positions [j * chunk, (j + 1) * chunk) and reads
+// each of their K and V rows from HBM once, for all G = n_head / n_kv query
+// heads of the group. K and V tiles stream through one four-slot ring of
+// asynchronous copies (the V tiles load while the K tiles are scored).
+//   phase 1: scores of the CTA's positions, and per query head the chunk's
+//            max m_j and double sum of expf(s - m_j);
+//   cluster barrier: every CTA merges all C chunks' statistics from their
+//            shared memory (distributed shared memory): M = max m_j and
+//            sum = sum_j s_j * exp(m_j - M), in chunk order, in double;
+//   phase 2: p_t for the CTA's positions with the global M and scale, and the
+//            partial sum of p_t V_t in position order;
+//   cluster barrier: CTA j adds slice j of the outputs over the C partials in
+//            chunk order (deterministic) and stores it.
+// No statistics or partial outputs go through global memory, and no
+// completion counters are needed: the cluster barrier is the grid-wide step.
 #include "common.cuh"
 #include "internal.h"
 
+#include <cooperative_groups.h>
+
 #include <algorithm>
+#include <array>
 #include <mutex>
+#include <vector>
 
 using namespace syn;
 
 namespace {
 
-constexpr int kThreads = 128;
-constexpr int kMaxChunk = 1024;  // positions per split (bounds shared memory)
-constexpr int kTile = 64;        // cached rows staged in shared memory at a time
+constexpr int kThreads = 128;      // RoPE / append kernels
+constexpr int kAttnThreads = 256;  // the decode kernel
+constexpr int kTile = 64;          // K or V rows per ring slot
+constexpr int kSlots = 4;          // ring depth: up to four tiles in flight
+constexpr int kMaxCluster = 16;
+constexpr int kExactChunk = 256;   // positions per CTA below which the cluster does not split
 
 struct AttnParams {
     const float *q, *k, *v;
     uint16_t *kc, *vc;
     const int32_t* pos;
     float* out;
-    float* scores;    // [n_q][n_head][max_len]
-    float* stat_m;    // [n_q][n_head][S]
-    double* stat_s;   // [n_q][n_head][S]
-    float* partial;   // [n_q][n_head][S][hd]
-    unsigned* count;  // [n_q][n_kv]
+    float* scores;           // [n_q][n_head][max_len] when the chunk's scores do not fit in shared memory
+    const float* rope_tab;   // [max_len][head_dim / 2] (cos, sin), or NULL: computed in the kernel
+    int sc_smem, chunk_cap;  // scores in shared memory, chunk_cap per query head
     size_t cache_stride;
-    int n_q, n_head, n_kv, hd, max_len, S;
+    int n_q, n_head, n_kv, hd, max_len;
     int append, rope, rope_mode;
     float theta_scale, scale;
     const float* ff;
@@ -48,33 +62,19 @@ struct AttnParams {
     int has_yarn;
 };
 
-struct ScratchLayout {
-    int S;
-    size_t scores, stat_m, stat_s, partial, count, total;
-};
+size_t scratch_bytes(int n_q, int n_head, int max_len) { return align256(size_t(n_q) * n_head * max_len * 4); }
 
-ScratchLayout scratch_layout(int n_q, int n_head, int n_kv, int hd, int max_len) {
-    ScratchLayout l;
-    const long units = long(n_q) * n_kv;
-    long S = (512 + units - 1) / units;  // about 3-4 CTAs per SM of work per pass
-    S = std::min<long>(S, (max_len + 31) / 32);
-    S = std::max<long>(S, (max_len + kMaxChunk - 1) / kMaxChunk);
-    S = std::max<long>(S, 1);
-    l.S = int(S);
-    size_t off = 0;
-    l.scores = off;
-    off += align256(size_t(n_q) * n_head * max_len * 4);
-    l.stat_m = off;
-    off += align256(size_t(n_q) * n_head * S * 4);
-    l.stat_s = off;
-    off += align256(size_t(n_q) * n_head * S * 8);
-    l.partial = off;
-    off += align256(size_t(n_q) * n_head * S * hd * 4);
-    l.count = off;
-    off += align256(size_t(n_q) * n_kv * 4);
-    l.total = off;
-    return l;
+// 16-byte asynchronous copy global -> shared (the copy engine; no register
+// round trip), and its group fences.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
 }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+// Wait until at most kSlots - 1 of this thread's newest copy groups are pending.
+__device__ __forceinline__ void cp_async_wait_ring() { asm volatile("cp.async.wait_group 3;" ::: "memory"); }
+static_assert(kSlots == 4, "cp_async_wait_ring leaves kSlots - 1 groups pending");
 
 // cos and sin of pair i at position p (attention.hpp:102-119): theta built by
 // repeated float multiplication, divided by the frequency factor, then the
@@ -113,13 +113,6 @@ __device__ __forceinline__ void rotate(float x0, float x1, float c, float s, flo
     o1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
 }
 
-__device__ __forceinline__ void split_range(int L, int S, int j, int& t0, int& t1, int& n_active) {
-    const int chunk = (L + S - 1) / S;
-    t0 = j * chunk;
-    t1 = min(L, t0 + chunk);
-    n_active = (L + chunk - 1) / chunk;
-}
-
 __device__ __forceinline__ void unpack8(uint4 v, float (&f)[8]) {
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -129,44 +122,124 @@ __device__ __forceinline__ void unpack8(uint4 v, float (&f)[8]) {
     }
 }
 
+// Shared memory of the decode kernel (dynamic part). sc_cap: floats of the
+// score buffer (0 when the scores live in global scratch).
+struct DecodeSmem {
+    size_t cs, qg, pw, part, red_s, red_m, stat_s, stat_m, krh, vrh, sc, ring, total;
+};
+
+__host__ __device__ inline DecodeSmem decode_smem(int GT, int hd, size_t sc_cap) {
+    DecodeSmem l;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t o = off;
+        off = (off + bytes + 15) & ~size_t(15);
+        return o;
+    };
+    l.cs = take(size_t(hd) * 4);                     // cos, sin of the hd / 2 pairs
+    l.qg = take(size_t(GT) * hd * 4);                // rotated q of the group, binary16 values
+    l.pw = take(size_t(GT) * kTile * 4);             // p of one V tile
+    l.part = take(size_t(GT) * hd * 4);              // this CTA's p.V partial (read by the cluster)
+    l.red_s = take(size_t(GT) * kMaxCluster * 8);    // the cluster's chunk sums, gathered
+    l.red_m = take(size_t(GT) * kMaxCluster * 4);    // the cluster's chunk maxima, gathered
+    l.stat_s = take(size_t(GT) * 8);                 // this chunk's sums (double), read by the cluster
+    l.stat_m = take(size_t(GT) * 4);                 // this chunk's maxima, read by the cluster
+    l.krh = take(size_t(hd) * 2);                    // appended K row (binary16)
+    l.vrh = take(size_t(hd) * 2);                    // appended V row
+    l.sc = take(sc_cap * 4);                         // scores, then expf(s - M), of the chunk
+    l.ring = take(size_t(kSlots) * kTile * (hd + 8) * 2);
+    l.total = off;
+    return l;
+}
+
 template <int GT>
-__global__ void __launch_bounds__(kThreads) attn_kpass(AttnParams a) {
-    pdl_launch_dependents();
-    pdl_wait();
-    const int j = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnParams a) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int C = int(cluster.num_blocks());
+    const int j = int(cluster.block_rank()), g = blockIdx.y, b = blockIdx.z;
     const int hd = a.hd, G = a.n_head / a.n_kv, H = a.n_head;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // pos (and the RoPE table) are written before the step's first kernel, or
+    // by the caller, never by the kernel this one may overlap: read before the wait.
     const int P = a.pos[b], L = P + 1;
-    if (P < 0 || L > a.max_len) return;  // outside the caller's bound: nothing is read or written
-    int t0, t1, n_active;
-    split_range(L, a.S, j, t0, t1, n_active);
+    if (P < 0 || L > a.max_len) return;  // the whole cluster (same query) leaves together
+    const int chunk = (L + C - 1) / C;
+    const int t0 = min(L, j * chunk), t1 = min(L, t0 + chunk), n = t1 - t0;
+    const bool owns = a.append && t0 <= P && P < t1;
 
-    extern __shared__ float sm[];
-    float* cs = sm;              // [hd/2][2]
-    float* qg = cs + hd;         // [G][hd], rotated and rounded to binary16
-    float* sc = qg + GT * hd;    // [G][chunk]
-    uint16_t* krh = reinterpret_cast<uint16_t*>(sc + GT * kMaxChunk);  // [hd] the appended key, binary16
-    uint16_t* tile = krh + hd;   // [kTile][hd + 8] cached K rows (16-byte padded)
-    __shared__ float red_f[kThreads / 32];
-    __shared__ double red_d[kThreads / 32];
-
-    if (j == 0 && tid == 0) a.count[size_t(b) * a.n_kv + g] = 0u;
-    const size_t stat0 = (size_t(b) * H + size_t(g) * G) * a.S + j;
-    if (t0 >= L) {
-        if (tid < G) {
-            a.stat_m[stat0 + size_t(tid) * a.S] = -INFINITY;
-            a.stat_s[stat0 + size_t(tid) * a.S] = 0.0;
-        }
-        return;
+    extern __shared__ __align__(16) unsigned char smem[];
+    const DecodeSmem sl = decode_smem(GT, hd, a.sc_smem ? size_t(GT) * a.chunk_cap : 0);
+    float* cs = reinterpret_cast<float*>(smem + sl.cs);
+    float* qg = reinterpret_cast<float*>(smem + sl.qg);
+    float* pw = reinterpret_cast<float*>(smem + sl.pw);
+    float* part = reinterpret_cast<float*>(smem + sl.part);
+    double* red_s = reinterpret_cast<double*>(smem + sl.red_s);
+    float* red_m = reinterpret_cast<float*>(smem + sl.red_m);
+    double* stat_s = reinterpret_cast<double*>(smem + sl.stat_s);
+    float* stat_m = reinterpret_cast<float*>(smem + sl.stat_m);
+    uint16_t* krh = reinterpret_cast<uint16_t*>(smem + sl.krh);
+    uint16_t* vrh = reinterpret_cast<uint16_t*>(smem + sl.vrh);
+    uint16_t* ring = reinterpret_cast<uint16_t*>(smem + sl.ring);
+    __shared__ float gm[GT], gscale[GT];
+    // score (then e) of query head jh at position t: sc[jh * sstride + t - soff]
+    float* sc;
+    size_t sstride;
+    int soff;
+    if (a.sc_smem) {
+        sc = reinterpret_cast<float*>(smem + sl.sc);
+        sstride = size_t(a.chunk_cap);
+        soff = t0;
+    } else {
+        sc = a.scores + (size_t(b) * H + size_t(g) * G) * a.max_len;
+        sstride = size_t(a.max_len);
+        soff = 0;
     }
-    const int chunk = t1 - t0;
 
-    if (a.rope)
-        for (int i = tid; i < hd / 2; i += kThreads) rope_cs(a, P, i, cs[2 * i], cs[2 * i + 1]);
-    __syncthreads();
-    const float* qb = a.q + size_t(b) * H * hd + size_t(g) * G * hd;
+    const int rowh = hd + 8;  // halves per staged row: 16-byte padding keeps 16-byte reads conflict-free
+    const size_t row = size_t(a.n_kv) * hd;
+    uint16_t* kcb = a.kc + size_t(b) * a.cache_stride;
+    uint16_t* vcb = a.vc + size_t(b) * a.cache_stride;
+    const int c8n = hd / 8;
+    const int nt = (n + kTile - 1) / kTile;  // tiles per phase; tile u < nt is K tile u, else V tile u - nt
+    auto issue = [&](int u) {
+        if (u < 2 * nt) {
+            const bool is_k = u < nt;
+            const int tb = t0 + (is_k ? u : u - nt) * kTile, m = min(kTile, t1 - tb);
+            const uint16_t* src = (is_k ? kcb : vcb) + size_t(g) * hd;
+            uint16_t* dst = ring + size_t(u % kSlots) * kTile * rowh;
+            for (int i = tid; i < m * c8n; i += kAttnThreads) {
+                const int rr = i / c8n, c8 = i % c8n, t = tb + rr;
+                if (!(owns && t == P)) cp_async16(dst + rr * rowh + c8 * 8, src + size_t(t) * row + c8 * 8);
+            }
+        }
+        cp_async_commit();  // an empty group past the end keeps the pending count uniform
+    };
+
+    // With append, rows other than P were written by earlier calls: their
+    // copies start before the wait. Without it the caller's previous kernel
+    // may have written them (syn_rope_kv_append), so everything waits.
+    if (!a.append) pdl_wait();
+    for (int u = 0; u < kSlots; ++u) issue(u);
     if (a.rope) {
-        for (int i = tid; i < G * hd / 2; i += kThreads) {
+        if (a.rope_tab) {
+            const float2* tab = reinterpret_cast<const float2*>(a.rope_tab) + size_t(P) * (hd / 2);
+            for (int i = tid; i < hd / 2; i += kAttnThreads) {
+                const float2 v = tab[i];
+                cs[2 * i] = v.x;
+                cs[2 * i + 1] = v.y;
+            }
+        } else {
+            for (int i = tid; i < hd / 2; i += kAttnThreads) rope_cs(a, P, i, cs[2 * i], cs[2 * i + 1]);
+        }
+    }
+    pdl_launch_dependents();
+    if (a.append) pdl_wait();  // q, k, v come from the previous kernel
+    __syncthreads();
+
+    const float* qb = a.q + (size_t(b) * H + size_t(g) * G) * hd;
+    if (a.rope) {
+        for (int i = tid; i < G * hd / 2; i += kAttnThreads) {
             const int jh = i / (hd / 2), pi = i % (hd / 2);
             int i0, i1;
             pair_index(a.rope_mode, hd, pi, i0, i1);
@@ -176,19 +249,15 @@ __global__ void __launch_bounds__(kThreads) attn_kpass(AttnParams a) {
             qg[jh * hd + i1] = round_f16(o1);
         }
     } else {
-        for (int i = tid; i < G * hd; i += kThreads) qg[i] = round_f16(qb[i]);
+        for (int i = tid; i < G * hd; i += kAttnThreads) qg[i] = round_f16(qb[i]);
     }
-    const bool owns_row = a.append && t0 <= P && P < t1;
-    const size_t row = size_t(a.n_kv) * hd;
-    uint16_t* kcb = a.kc + size_t(b) * a.cache_stride;
-    uint16_t* vcb = a.vc + size_t(b) * a.cache_stride;
-    if (owns_row) {
+    if (owns) {
         const float* kb = a.k + size_t(b) * row + size_t(g) * hd;
         const float* vb = a.v + size_t(b) * row + size_t(g) * hd;
         uint16_t* krow = kcb + size_t(P) * row + size_t(g) * hd;
         uint16_t* vrow = vcb + size_t(P) * row + size_t(g) * hd;
         if (a.rope) {
-            for (int pi = tid; pi < hd / 2; pi += kThreads) {
+            for (int pi = tid; pi < hd / 2; pi += kAttnThreads) {
                 int i0, i1;
                 pair_index(a.rope_mode, hd, pi, i0, i1);
                 float o0, o1;
@@ -200,179 +269,151 @@ __global__ void __launch_bounds__(kThreads) attn_kpass(AttnParams a) {
                 krh[i1] = h1;
             }
         } else {
-            for (int d = tid; d < hd; d += kThreads) {
-                const uint16_t h = f16_bits(kb[d]);
-                krow[d] = h;
-                krh[d] = h;
-            }
+            for (int d = tid; d < hd; d += kAttnThreads) krow[d] = krh[d] = f16_bits(kb[d]);
         }
-        for (int d = tid; d < hd; d += kThreads) vrow[d] = f16_bits(vb[d]);
+        for (int d = tid; d < hd; d += kAttnThreads) vrow[d] = vrh[d] = f16_bits(vb[d]);
     }
     __syncthreads();
 
-    // Scores, a tile of kTile positions at a time: the tile's K rows are loaded
-    // coalesced into shared memory, then one thread per position runs the dot
-    // in dimension order as attend_group sums it (attention.hpp:214-219);
-    // binary16 products are exact in float, so each add is the reference's add.
-    float* scores_b = a.scores + (size_t(b) * H + size_t(g) * G) * a.max_len;
-    const int rowh = hd + 8, c8n = hd / 8;
-    for (int tb = t0; tb < t1; tb += kTile) {
-        const int n = min(kTile, t1 - tb);
-        for (int i = tid; i < n * c8n; i += kThreads) {
-            const int rr = i / c8n, c8 = i % c8n, t = tb + rr;
-            const uint4 v = (owns_row && t == P)
-                                ? *reinterpret_cast<const uint4*>(krh + c8 * 8)
-                                : __ldg(reinterpret_cast<const uint4*>(kcb + size_t(t) * row + size_t(g) * hd + c8 * 8));
-            *reinterpret_cast<uint4*>(tile + rr * rowh + c8 * 8) = v;
-        }
+    // Phase 1: scores, one (position, query head) per thread and step; the
+    // dot runs in dimension order (attention.hpp:214-219).
+    for (int u = 0; u < nt; ++u) {
+        cp_async_wait_ring();
+        const int tb = t0 + u * kTile, m = min(kTile, t1 - tb);
+        uint16_t* tile = ring + size_t(u % kSlots) * kTile * rowh;
+        if (owns && P >= tb && P < tb + m && tid < c8n)
+            *reinterpret_cast<uint4*>(tile + (P - tb) * rowh + tid * 8) = *reinterpret_cast<const uint4*>(krh + tid * 8);
         __syncthreads();
-        if (tid < n) {
-            const uint16_t* kt = tile + tid * rowh;
-            float dot[GT];
-#pragma unroll
-            for (int jh = 0; jh < GT; ++jh) dot[jh] = 0.0f;
-            for (int d8 = 0; d8 < hd; d8 += 8) {
+        for (int i = tid; i < m * G; i += kAttnThreads) {
+            const int jh = i / m, r = i % m;
+            const uint16_t* kt = tile + r * rowh;
+            const float4* qh = reinterpret_cast<const float4*>(qg + jh * hd);
+            float dot = 0.0f;
+#pragma unroll 4
+            for (int d8 = 0; d8 < hd / 8; ++d8) {
                 float kf[8];
-                unpack8(*reinterpret_cast<const uint4*>(kt + d8), kf);
-#pragma unroll
-                for (int e = 0; e < 8; ++e)
-#pragma unroll
-                    for (int jh = 0; jh < GT; ++jh)
-                        if (jh < G) dot[jh] = __fadd_rn(dot[jh], __fmul_rn(qg[jh * hd + d8 + e], kf[e]));
+                unpack8(*reinterpret_cast<const uint4*>(kt + 8 * d8), kf);
+                const float4 q0 = qh[2 * d8], q1 = qh[2 * d8 + 1];
+                dot = fmaf(q0.x, kf[0], dot);  // exact products: each fma is mul then add
+                dot = fmaf(q0.y, kf[1], dot);
+                dot = fmaf(q0.z, kf[2], dot);
+                dot = fmaf(q0.w, kf[3], dot);
+                dot = fmaf(q1.x, kf[4], dot);
+                dot = fmaf(q1.y, kf[5], dot);
+                dot = fmaf(q1.z, kf[6], dot);
+                dot = fmaf(q1.w, kf[7], dot);
             }
-            const int t = tb + tid;
-#pragma unroll
-            for (int jh = 0; jh < GT; ++jh) {
-                if (jh < G) {
-                    const float sv = __fmul_rn(dot[jh], a.scale);
-                    sc[jh * chunk + (t - t0)] = sv;
-                    scores_b[size_t(jh) * a.max_len + t] = sv;
-                }
-            }
+            sc[size_t(jh) * sstride + tb + r - soff] = __fmul_rn(dot, a.scale);
         }
         __syncthreads();
+        issue(u + kSlots);
     }
 
-    // Split statistics per query head: max, then the double sum of expf(s - max).
-    for (int jh = 0; jh < G; ++jh) {
-        float m = -INFINITY;
-        for (int t = tid; t < chunk; t += kThreads) m = fmaxf(m, sc[jh * chunk + t]);
-        m = warp_max(m);
-        if (lane == 0) red_f[warp] = m;
-        __syncthreads();
-        m = red_f[0];
-        for (int w = 1; w < kThreads / 32; ++w) m = fmaxf(m, red_f[w]);
-        double s = 0.0;
-        for (int t = tid; t < chunk; t += kThreads) s += double(exp_rn(__fsub_rn(sc[jh * chunk + t], m)));
-        s = warp_sum_d(s);
-        if (lane == 0) red_d[warp] = s;
-        __syncthreads();
-        if (tid == 0) {
-            double tot = 0.0;
-            for (int w = 0; w < kThreads / 32; ++w) tot += red_d[w];
-            a.stat_m[stat0 + size_t(jh) * a.S] = m;
-            a.stat_s[stat0 + size_t(jh) * a.S] = tot;
-        }
-        __syncthreads();
+    // The softmax over the whole context (elementwise.hpp:174-201): the
+    // cluster's max, then e_t = expf(s_t - M) once per score, then the
+    // cluster's double sum of every e_t, so p_t = binary16(e_t * (1 / sum))
+    // with the reference's M, e_t and scale.
+    for (int jh = warp; jh < G; jh += kAttnThreads / 32) {
+        const float* s = sc + size_t(jh) * sstride - soff;
+        float mx = -INFINITY;
+        for (int t = t0 + lane; t < t1; t += 32) mx = fmaxf(mx, s[t]);
+        mx = warp_max(mx);
+        if (lane == 0) stat_m[jh] = mx;
     }
-}
-
-template <int GT>
-__global__ void __launch_bounds__(kThreads) attn_vpass(AttnParams a) {
-    pdl_launch_dependents();
-    pdl_wait();
-    const int j = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
-    const int hd = a.hd, G = a.n_head / a.n_kv, H = a.n_head;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int P = a.pos[b], L = P + 1;
-    if (P < 0 || L > a.max_len) return;
-    int t0, t1, n_active;
-    split_range(L, a.S, j, t0, t1, n_active);
-    if (t0 >= L) return;
-    const int chunk = t1 - t0;
-
-    extern __shared__ float sm[];
-    float* pw = sm;                                               // [G][chunk] probabilities
-    uint16_t* tile = reinterpret_cast<uint16_t*>(pw + GT * kMaxChunk);  // [kTile][hd + 8] cached V rows
-    __shared__ float gm[GT], gscale[GT];
-    __shared__ int is_last;
-
-    // Global max and sum of each query head from the splits' statistics.
-    const size_t stat0 = (size_t(b) * H + size_t(g) * G) * a.S;
-    for (int jh = warp; jh < G; jh += kThreads / 32) {
-        const float* m = a.stat_m + stat0 + size_t(jh) * a.S;
-        const double* s = a.stat_s + stat0 + size_t(jh) * a.S;
+    cluster.sync();
+    for (int i = tid; i < G * C; i += kAttnThreads) red_m[i] = *cluster.map_shared_rank(stat_m + i / C, i % C);
+    __syncthreads();
+    for (int jh = tid; jh < G; jh += kAttnThreads) {
         float M = -INFINITY;
-        for (int k = lane; k < n_active; k += 32) M = fmaxf(M, m[k]);
-        M = warp_max(M);
-        double tot = 0.0;
-        for (int k = lane; k < n_active; k += 32) tot += s[k] * exp(double(m[k]) - double(M));
-        tot = warp_sum_d(tot);
-        if (lane == 0) {
-            gm[jh] = M;
-            gscale[jh] = float(1.0 / tot);
-        }
+        for (int r = 0; r < C; ++r) M = fmaxf(M, red_m[jh * C + r]);
+        gm[jh] = M;
     }
     __syncthreads();
-    const float* scores_b = a.scores + (size_t(b) * H + size_t(g) * G) * a.max_len;
-    for (int i = tid; i < G * chunk; i += kThreads) {
-        const int jh = i / chunk, t = i % chunk;
-        const float e = exp_rn(__fsub_rn(scores_b[size_t(jh) * a.max_len + t0 + t], gm[jh]));
-        pw[jh * chunk + t] = round_f16(__fmul_rn(e, gscale[jh]));
+    for (int jh = warp; jh < G; jh += kAttnThreads / 32) {
+        float* s = sc + size_t(jh) * sstride - soff;
+        const float M = gm[jh];
+        double acc = 0.0;
+        for (int t = t0 + lane; t < t1; t += 32) {
+            const float e = exp_rn(__fsub_rn(s[t], M));
+            s[t] = e;
+            acc += double(e);
+        }
+        acc = warp_sum_d(acc);
+        if (lane == 0) stat_s[jh] = acc;
+    }
+    cluster.sync();
+    for (int i = tid; i < G * C; i += kAttnThreads) red_s[i] = *cluster.map_shared_rank(stat_s + i / C, i % C);
+    __syncthreads();
+    for (int jh = tid; jh < G; jh += kAttnThreads) {
+        double tot = 0.0;
+        for (int r = 0; r < C; ++r) tot += red_s[jh * C + r];
+        gscale[jh] = float(1.0 / tot);
     }
     __syncthreads();
 
-    // p.V a tile of kTile cached V rows at a time (loaded coalesced into shared
-    // memory); each thread owns outputs (head jh, dim d) and adds p_t * V_t,d
-    // in position order (attention.hpp:231-243) over the split's positions.
-    const size_t row = size_t(a.n_kv) * hd;
-    const uint16_t* vcb = a.vc + size_t(b) * a.cache_stride + size_t(g) * hd;
-    const int rowh = hd + 8, c8n = hd / 8;
-    constexpr int kOut = (GT * 256 + kThreads - 1) / kThreads;  // outputs per thread, upper bound
-    float acc[kOut];
+    // Phase 2: the position-ordered sum of p_t V_t. Thread slot k owns the
+    // column pair (2 * (o % (hd / 2)), +1) of query head o / (hd / 2).
+    constexpr int KO = GT >= 2 ? GT / 2 : 1;  // pairs per thread: G * hd / 2 <= GT * 128 pairs over 256 threads
+    float acc0[KO], acc1[KO];
+    int pcol[KO], prow[KO];
+    const int n_pairs = G * hd / 2;
 #pragma unroll
-    for (int k = 0; k < kOut; ++k) acc[k] = 0.0f;
-    const int n_out = G * hd;
-    for (int tb = t0; tb < t1; tb += kTile) {
-        const int n = min(kTile, t1 - tb);
-        for (int i = tid; i < n * c8n; i += kThreads) {
-            const int rr = i / c8n, c8 = i % c8n;
-            *reinterpret_cast<uint4*>(tile + rr * rowh + c8 * 8) =
-                __ldg(reinterpret_cast<const uint4*>(vcb + size_t(tb + rr) * row + c8 * 8));
+    for (int k = 0; k < KO; ++k) {
+        const int o = tid + k * kAttnThreads;
+        acc0[k] = acc1[k] = 0.0f;
+        pcol[k] = o < n_pairs ? 2 * (o % (hd / 2)) : -1;
+        prow[k] = o < n_pairs ? (o / (hd / 2)) * kTile : 0;
+    }
+    for (int u = nt; u < 2 * nt; ++u) {
+        cp_async_wait_ring();
+        const int tb = t0 + (u - nt) * kTile, m = min(kTile, t1 - tb);
+        uint16_t* tile = ring + size_t(u % kSlots) * kTile * rowh;
+        if (owns && P >= tb && P < tb + m && tid < c8n)
+            *reinterpret_cast<uint4*>(tile + (P - tb) * rowh + tid * 8) = *reinterpret_cast<const uint4*>(vrh + tid * 8);
+        for (int i = tid; i < m * G; i += kAttnThreads) {
+            const int jh = i / m, r = i % m;
+            pw[jh * kTile + r] = round_f16(__fmul_rn(sc[size_t(jh) * sstride + tb + r - soff], gscale[jh]));
         }
         __syncthreads();
-        for (int rr = 0; rr < n; ++rr) {
+#pragma unroll 4
+        for (int r = 0; r < m; ++r) {
+            const uint16_t* vr = tile + r * rowh;
 #pragma unroll
-            for (int k = 0; k < kOut; ++k) {
-                const int o = tid + k * kThreads;
-                if (o < n_out) {
-                    const int jh = o / hd, d = o % hd;  // fmaf: the products are exact
-                    acc[k] = fmaf(pw[jh * chunk + (tb - t0) + rr], f16_from_bits(tile[rr * rowh + d]), acc[k]);
+            for (int k = 0; k < KO; ++k) {
+                if (pcol[k] >= 0) {
+                    const float p = pw[prow[k] + r];
+                    const uint32_t v2 = *reinterpret_cast<const uint32_t*>(vr + pcol[k]);
+                    acc0[k] = fmaf(p, f16_from_bits(uint16_t(v2 & 0xffff)), acc0[k]);  // exact products
+                    acc1[k] = fmaf(p, f16_from_bits(uint16_t(v2 >> 16)), acc1[k]);
                 }
             }
         }
         __syncthreads();
+        issue(u + kSlots);
     }
-    float* part = a.partial + (stat0 + j) * hd;  // + jh * S * hd
+    cp_async_wait_all();  // nothing is left in flight (the trailing groups are empty)
 #pragma unroll
-    for (int k = 0; k < kOut; ++k) {
-        const int o = tid + k * kThreads;
-        if (o < n_out) part[size_t(o / hd) * a.S * hd + o % hd] = acc[k];
+    for (int k = 0; k < KO; ++k) {
+        if (pcol[k] >= 0) {
+            const int o = (prow[k] / kTile) * hd + pcol[k];
+            part[o] = acc0[k];
+            part[o + 1] = acc1[k];
+        }
     }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) is_last = atomicAdd(&a.count[size_t(b) * a.n_kv + g], 1u) == unsigned(n_active - 1);
-    __syncthreads();
-    if (!is_last) return;
-    __threadfence();
-    const float* part0 = a.partial + stat0 * hd;
-    float* ob = a.out + size_t(b) * H * hd + size_t(g) * G * hd;
-    for (int i = tid; i < G * hd; i += kThreads) {
-        const int jh = i / hd, d = i % hd;
-        float s = 0.0f;
-        for (int k = 0; k < n_active; ++k) s += __ldcg(part0 + (size_t(jh) * a.S + k) * hd + d);
-        ob[i] = s;
+    cluster.sync();  // every partial is visible to the cluster
+    const int n_out = G * hd, per = (n_out + C - 1) / C;
+    float* ob = a.out + (size_t(b) * H + size_t(g) * G) * hd;
+    for (int i = j * per + tid; i < min(n_out, (j + 1) * per); i += kAttnThreads) {
+        float v[kMaxCluster];
+#pragma unroll
+        for (int r = 0; r < kMaxCluster; ++r) v[r] = r < C ? *cluster.map_shared_rank(part + i, r) : 0.0f;
+        float sum = 0.0f;
+#pragma unroll
+        for (int r = 0; r < kMaxCluster; ++r)
+            if (r < C) sum = __fadd_rn(sum, v[r]);
+        ob[i] = sum;
     }
+    cluster.sync();  // no CTA leaves while a peer may still read its shared memory
 }
 
 // RoPE of k and F16 append of (k, v) at row pos[b], one CTA per token.
@@ -401,6 +442,17 @@ __global__ void __launch_bounds__(kThreads) rope_append_kernel(AttnParams a) {
         krow[h * hd + i1] = f16_bits(o1);
     }
     for (size_t i = tid; i < row; i += kThreads) vrow[i] = f16_bits(vb[i]);
+}
+
+// The (cos, sin) table of syn_rope_table: one CTA per position.
+__global__ void __launch_bounds__(kThreads) rope_table_kernel(AttnParams a, float* table) {
+    const int p = blockIdx.x, half = a.hd / 2;
+    float2* row = reinterpret_cast<float2*>(table) + size_t(p) * half;
+    for (int i = threadIdx.x; i < half; i += kThreads) {
+        float c, s;
+        rope_cs(a, p, i, c, s);
+        row[i] = make_float2(c, s);
+    }
 }
 
 // Plain RoPE of n rows (attention.hpp:89-129), one CTA per row.
@@ -445,6 +497,7 @@ AttnParams make_params(const syn_attention_args* x) {
     a.append = x->append; a.rope = x->rope; a.rope_mode = x->rope_mode;
     a.theta_scale = x->theta_scale; a.scale = x->scale;
     a.ff = x->freq_factors;
+    a.rope_tab = x->rope_table;
     a.has_yarn = x->yarn != nullptr;
     for (int i = 0; i < 5; ++i) a.yarn[i] = x->yarn ? x->yarn[i] : 0.0f;
     return a;
@@ -460,38 +513,85 @@ int check_args(const syn_attention_args* x, bool need_scratch) {
     if ((reinterpret_cast<uintptr_t>(x->k_cache) | reinterpret_cast<uintptr_t>(x->v_cache)) & 15)
         return SYN_ERR_INVALID;
     if (x->cache_stride % 8) return SYN_ERR_INVALID;  // rows stay 16-byte aligned
+    if (reinterpret_cast<uintptr_t>(x->rope_table) & 7) return SYN_ERR_INVALID;
+    return SYN_OK;
+}
+
+// Scores of a chunk stay in shared memory up to this size per CTA.
+constexpr size_t kScoreSmemBytes = 32 * 1024;
+
+// Cluster size for a call: up to 16 CTAs per (query, KV head) group, at
+// least kExactChunk positions each at max_len, no more than about four CTAs
+// per SM over the grid, and a size the device can co-schedule with this
+// kernel's largest shared memory (checked once per device, group tier and
+// head size).
+template <int GT>
+int pick_cluster(const AttnParams& a, int* out) {
+    static std::mutex mu;
+    static std::vector<std::array<int, 3>> known;  // device, hd, largest schedulable cluster
+    int dev = 0;
+    int st = syn_cuda_status(cudaGetDevice(&dev));
+    if (st) return st;
+    int cmax = 0;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        for (const auto& k : known)
+            if (k[0] == dev && k[1] == a.hd) cmax = k[2];
+        if (!cmax) {
+            auto kern = attn_decode_kernel<GT>;
+            const size_t smem = decode_smem(GT, a.hd, kScoreSmemBytes / 4).total;
+            // The opt-in covers the largest head size, so configuring a smaller
+            // one later never lowers it below what an earlier one needs.
+            const size_t most = decode_smem(GT, 256, kScoreSmemBytes / 4).total;
+            st = syn_cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(most)));
+            if (!st) st = syn_cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+            if (st) return st;
+            for (int c = kMaxCluster; c >= 1 && !cmax; c /= 2) {
+                cudaLaunchConfig_t cfg = {};
+                cfg.gridDim = dim3(c, 1, 1);
+                cfg.blockDim = dim3(kAttnThreads);
+                cfg.dynamicSmemBytes = smem;
+                cudaLaunchAttribute attr[1];
+                attr[0].id = cudaLaunchAttributeClusterDimension;
+                attr[0].val.clusterDim.x = c;
+                attr[0].val.clusterDim.y = 1;
+                attr[0].val.clusterDim.z = 1;
+                cfg.attrs = attr;
+                cfg.numAttrs = 1;
+                int nc = 0;
+                if (cudaOccupancyMaxActiveClusters(&nc, kern, &cfg) == cudaSuccess && nc > 0) cmax = c;
+                else cudaGetLastError();
+            }
+            if (!cmax) return SYN_ERR_UNSUPPORTED;
+            known.push_back({dev, a.hd, cmax});
+        }
+    }
+    int c = cmax;
+    // At least kExactChunk positions per CTA at max_len: a context that fits
+    // one chunk sums p.V in the reference's position order exactly.
+    while (c > 1 && c * kExactChunk > a.max_len) c /= 2;
+    const long groups = long(a.n_q) * a.n_kv;
+    while (c > 1 && groups * c > 4L * syn_num_sms()) c /= 2;
+    *out = c;
     return SYN_OK;
 }
 
 template <int GT>
 int launch_attention(AttnParams a, cudaStream_t s) {
-    const dim3 grid(a.S, a.n_kv, a.n_q);
-    const size_t tile_bytes = size_t(kTile) * (a.hd + 8) * 2;
-    const size_t kshm = size_t(a.hd + GT * a.hd + GT * kMaxChunk) * 4 + size_t(a.hd) * 2 + tile_bytes;
-    const size_t vshm = size_t(GT * kMaxChunk) * 4 + tile_bytes;
-    // The opt-in above 48 KB is a per-device function attribute.
-    static bool configured[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !configured[dev]) {
-        int st = syn_cuda_status(
-            cudaFuncSetAttribute(attn_kpass<GT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        if (!st)
-            st = syn_cuda_status(
-                cudaFuncSetAttribute(attn_vpass<GT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        if (st) return st;
-        configured[dev] = true;
-    }
-    int st = syn_launch(attn_kpass<GT>, grid, kThreads, kshm, s, a);
+    int c = 1;
+    int st = pick_cluster<GT>(a, &c);
     if (st) return st;
-    return syn_launch(attn_vpass<GT>, grid, kThreads, vshm, s, a);
+    a.chunk_cap = (a.max_len + c - 1) / c;
+    a.sc_smem = size_t(GT) * a.chunk_cap * 4 <= kScoreSmemBytes;
+    const size_t smem = decode_smem(GT, a.hd, a.sc_smem ? size_t(GT) * a.chunk_cap : 0).total;
+    return syn_launch_cluster(attn_decode_kernel<GT>, dim3(c, a.n_kv, a.n_q), kAttnThreads, smem, c, s, a);
 }
 
 }  // namespace
 
 extern "C" size_t syn_attention_scratch_bytes(int n_q, int n_head, int n_kv, int head_dim, int max_len) {
     if (n_q <= 0 || n_head <= 0 || n_kv <= 0 || head_dim <= 0 || max_len <= 0) return 0;
-    return scratch_layout(n_q, n_head, n_kv, head_dim, max_len).total;
+    return scratch_bytes(n_q, n_head, max_len);
 }
 
 extern "C" int syn_attention(const syn_attention_args* x, void* stream) {
@@ -500,14 +600,7 @@ extern "C" int syn_attention(const syn_attention_args* x, void* stream) {
     if (x->append && x->cache_stride == 0 && x->n_q > 1) return SYN_ERR_INVALID;  // rows would race
     if (x->append && (!x->k || !x->v)) return SYN_ERR_INVALID;
     AttnParams a = make_params(x);
-    const ScratchLayout l = scratch_layout(x->n_q, x->n_head, x->n_kv, x->head_dim, x->max_len);
-    char* base = static_cast<char*>(x->scratch);
-    a.scores = reinterpret_cast<float*>(base + l.scores);
-    a.stat_m = reinterpret_cast<float*>(base + l.stat_m);
-    a.stat_s = reinterpret_cast<double*>(base + l.stat_s);
-    a.partial = reinterpret_cast<float*>(base + l.partial);
-    a.count = reinterpret_cast<unsigned*>(base + l.count);
-    a.S = l.S;
+    a.scores = static_cast<float*>(x->scratch);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     switch (group_tier(x->n_head / x->n_kv)) {
     case 1: return launch_attention<1>(a, s);
@@ -567,10 +660,8 @@ extern "C" int syn_attention_noalloc(const syn_attention_args* x, void* stream) 
     void* scratch = nullptr;
     const int st = noalloc_scratch(&scratch);
     if (st) return st;
-    // The kernels fully write every scratch value they read later in the same
-    // call (scores, split statistics and partial outputs), and the first pass
-    // zeroes the completion counters the second pass counts with, so nothing
-    // left from an earlier call needs clearing here.
+    // The kernel writes every score it reads later in the same call, so
+    // nothing left from an earlier call needs clearing here.
     syn_attention_args a = *x;
     a.scratch = scratch;
     return syn_attention(&a, stream);
@@ -583,6 +674,19 @@ extern "C" int syn_rope_kv_append(const syn_attention_args* x, void* stream) {
     AttnParams a = make_params(x);
     return syn_launch(rope_append_kernel, x->n_q, kThreads, size_t(x->head_dim) * 4,
                       static_cast<cudaStream_t>(stream), a);
+}
+
+extern "C" int syn_rope_table(float* table, int max_len, int head_dim, float theta_scale, const float* freq_factors,
+                              const float* yarn, void* stream) {
+    if (!table || max_len <= 0 || head_dim <= 0 || head_dim % 2) return SYN_ERR_INVALID;
+    if (reinterpret_cast<uintptr_t>(table) & 7) return SYN_ERR_INVALID;
+    syn_attention_args args{};
+    args.head_dim = head_dim;
+    args.theta_scale = theta_scale;
+    args.freq_factors = freq_factors;
+    args.yarn = yarn;
+    AttnParams a = make_params(&args);
+    return syn_launch(rope_table_kernel, max_len, kThreads, 0, static_cast<cudaStream_t>(stream), a, table);
 }
 
 extern "C" int syn_rope(const float* x, float* out, int n, int n_heads, int head_dim, const int32_t* pos,

@@ -12,6 +12,8 @@ thread_local int g_pdl = 0;
 
 int syn_pdl_enabled() { return g_pdl; }
 void syn_set_pdl(int on) { g_pdl = on; }
+// For microbenchmarks that capture kernels as the session does.
+extern "C" void syn_set_programmatic_launch(int on) { g_pdl = on; }
 
 int syn_cuda_status(cudaError_t e) {
     if (e == cudaSuccess) return SYN_OK;

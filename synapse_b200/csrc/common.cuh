@@ -46,11 +46,27 @@ __host__ __device__ inline size_t act_bytes(int n_tok, int cols) {
     return act_qs_bytes(n_tok, cols) + act_dh_bytes(n_tok, cols) + 2 * act_d_bytes(n_tok, cols);
 }
 
-// ---- planar weight planes ----------------------------------------------------
+// ---- planar (row-blocked) weights ---------------------------------------------
+// Row r holds its quants (blocks x 16 bytes for Q4_0, x 32 for Q8_0) followed by
+// its binary16 scales, padded to 16 bytes: one contiguous, 16-byte aligned run
+// per row, so a lane reads eight blocks' quants and their scales with 16-byte
+// loads.
 __host__ __device__ inline int quant_bytes_per_block(int type) { return type == SYN_Q4_0 ? 16 : 32; }
 __host__ __device__ inline int gguf_block_bytes(int type) { return type == SYN_Q4_0 ? 18 : 34; }
-__host__ __device__ inline size_t planar_qs_bytes(int type, int rows, int cols) {
-    return align256(size_t(rows) * (cols / QK) * quant_bytes_per_block(type));
+__host__ __device__ inline size_t planar_quant_bytes(int type, int cols) {
+    return size_t(cols / QK) * quant_bytes_per_block(type);
+}
+__host__ __device__ inline size_t planar_row_bytes(int type, int cols) {
+    return planar_quant_bytes(type, cols) + ((size_t(cols / QK) * 2 + 15) & ~size_t(15));
+}
+// Blocks sit in a row in order (every kernel and the host go through this map).
+__host__ __device__ inline int planar_block_pos(int, size_t, int b) { return b; }
+// Byte offsets of (logical) block b of row r: its quants, its binary16 scale.
+__host__ __device__ inline size_t planar_quant_at(int type, int cols, size_t r, size_t b) {
+    return r * planar_row_bytes(type, cols) + size_t(planar_block_pos(cols / QK, r, int(b))) * quant_bytes_per_block(type);
+}
+__host__ __device__ inline size_t planar_scale_at(int type, int cols, size_t r, size_t b) {
+    return r * planar_row_bytes(type, cols) + planar_quant_bytes(type, cols) + b * 2;
 }
 
 // ---- binary16 ---------------------------------------------------------------
@@ -85,10 +101,91 @@ __device__ __forceinline__ Q8Lane quantize_q8_lane(float x) {
     return r;
 }
 
-// expf rounded once from double precision: the correctly rounded float in all
-// but vanishingly rare cases, the closest a float result can be to the C
-// runtime's expf that the reference calls (std::exp on float).
-__device__ __forceinline__ float exp_rn(float x) { return float(exp(double(x))); }
+// expf rounded once (elementwise.hpp:180 calls std::exp on float): a
+// table-driven evaluation in float-float arithmetic (Tang's method: x = (64 e
+// + j) ln2/64 + r, exp(x) = 2^e 2^(j/64) exp(r), |r| <= ln2/128) accurate to
+// about 2^-44 relative, then one rounding to float. It agrees with the
+// correctly rounded result except within 2^-20 ulp of a rounding midpoint,
+// i.e. as a correctly rounded C runtime expf does. Subnormal results, where
+// the final scaling would round a second time, come from double precision.
+// Table: 2^(j/64) split into a float and the float nearest the remainder,
+// from the double 2^(j/64).
+__device__ const float2 kExp2J64[64] = {
+    {0x1.p+0f, 0.0f}, {0x1.02c9a4p+0f, -0x1.887fa0p-28f},
+    {0x1.059b0ep+0f, -0x1.9d4f52p-25f}, {0x1.087452p+0f, -0x1.e2990ep-26f},
+    {0x1.0b5586p+0f, 0x1.9f3122p-25f}, {0x1.0e3ec4p+0f, -0x1.a585ccp-25f},
+    {0x1.11301ep+0f, -0x1.fdb496p-25f}, {0x1.1429aap+0f, 0x1.d525bcp-25f},
+    {0x1.172b84p+0f, -0x1.c15742p-27f}, {0x1.1a35bep+0f, 0x1.6df96ep-25f},
+    {0x1.1d4874p+0f, -0x1.d2e8cap-25f}, {0x1.2063b8p+0f, 0x1.0c519ap-25f},
+    {0x1.2387a6p+0f, 0x1.ceac48p-25f}, {0x1.26b456p+0f, 0x1.789f38p-26f},
+    {0x1.29e9e0p+0f, -0x1.5c0424p-25f}, {0x1.2d285ap+0f, 0x1.b900c2p-26f},
+    {0x1.306fe0p+0f, 0x1.4636e2p-25f}, {0x1.33c08cp+0f, -0x1.b37d20p-25f},
+    {0x1.371a74p+0f, -0x1.18aac6p-25f}, {0x1.3a7db4p+0f, -0x1.634c02p-25f},
+    {0x1.3dea64p+0f, 0x1.824684p-25f}, {0x1.4160a2p+0f, 0x1.f72e2ap-28f},
+    {0x1.44e086p+0f, 0x1.8624b4p-30f}, {0x1.486a2cp+0f, -0x1.47d866p-25f},
+    {0x1.4bfdaep+0f, -0x1.593abcp-25f}, {0x1.4f9b28p+0f, -0x1.2c5a6cp-25f},
+    {0x1.5342b6p+0f, -0x1.2c5610p-25f}, {0x1.56f474p+0f, -0x1.295b04p-25f},
+    {0x1.5ab07ep+0f, -0x1.5bd5ecp-27f}, {0x1.5e76f2p+0f, -0x1.4a5bd8p-25f},
+    {0x1.6247ecp+0f, -0x1.f8b550p-25f}, {0x1.662388p+0f, 0x1.2a9112p-27f},
+    {0x1.6a09e6p+0f, 0x1.9fcef4p-26f}, {0x1.6dfb24p+0f, -0x1.cd72e8p-27f},
+    {0x1.71f75ep+0f, 0x1.1d8beep-25f}, {0x1.75feb6p+0f, -0x1.37b306p-25f},
+    {0x1.7a1148p+0f, -0x1.829fd0p-25f}, {0x1.7e2f34p+0f, -0x1.261634p-25f},
+    {0x1.82589ap+0f, -0x1.accc7cp-26f}, {0x1.868d9ap+0f, -0x1.2edb44p-26f},
+    {0x1.8ace54p+0f, 0x1.15506ep-27f}, {0x1.8f1aeap+0f, -0x1.baa232p-26f},
+    {0x1.93737cp+0f, -0x1.e64744p-25f}, {0x1.97d82ap+0f, -0x1.0d8d80p-31f},
+    {0x1.9c4918p+0f, 0x1.51f848p-27f}, {0x1.a0c668p+0f, -0x1.2886a6p-26f},
+    {0x1.a5503cp+0f, -0x1.b83b54p-25f}, {0x1.a9e6b6p+0f, -0x1.50c048p-25f},
+    {0x1.ae89fap+0f, -0x1.a94b14p-26f}, {0x1.b33a2cp+0f, -0x1.ec3a82p-26f},
+    {0x1.b7f770p+0f, -0x1.a09438p-25f}, {0x1.bcc1eap+0f, -0x1.f687c6p-25f},
+    {0x1.c199bep+0f, -0x1.3d56b2p-27f}, {0x1.c67f12p+0f, 0x1.cafa2ap-25f},
+    {0x1.cb720ep+0f, -0x1.8837ccp-27f}, {0x1.d072d4p+0f, 0x1.40f130p-25f},
+    {0x1.d5818ep+0f, -0x1.822dbcp-27f}, {0x1.da9e60p+0f, 0x1.ed9942p-27f},
+    {0x1.dfc974p+0f, -0x1.908c94p-25f}, {0x1.e502eep+0f, 0x1.e2cffep-26f},
+    {0x1.ea4afap+0f, 0x1.52486cp-27f}, {0x1.efa1bep+0f, 0x1.cc2b44p-25f},
+    {0x1.f50766p+0f, -0x1.246eb0p-26f}, {0x1.fa7c18p+0f, 0x1.9e90d8p-28f}};
+
+__device__ __forceinline__ void two_sum(float a, float b, float& s, float& e) {
+    s = __fadd_rn(a, b);
+    const float bb = __fsub_rn(s, a);
+    e = __fadd_rn(__fsub_rn(a, __fsub_rn(s, bb)), __fsub_rn(b, bb));
+}
+
+__device__ __forceinline__ float exp_rn(float x) {
+    if (!(x > -87.0f)) return x != x ? x : float(exp(double(x)));  // NaN, subnormal or zero results
+    if (x > 88.72284f) return __int_as_float(0x7f800000);
+    const float kf = rintf(__fmul_rn(x, 0x1.715476p+6f));  // 64 / ln2
+    const int k = int(kf);
+    // r = x - k ln2/64 as r_hi + r_lo: k * C_hi exactly (product and its
+    // error), x - p_hi exact by Sterbenz, then the low parts.
+    const float c_hi = 0x1.62e430p-7f, c_lo = -0x1.05c610p-35f;
+    const float p_hi = __fmul_rn(kf, c_hi);
+    const float p_lo = __fmaf_rn(kf, c_hi, -p_hi);
+    const float d = __fsub_rn(x, p_hi);
+    const float q = __fmaf_rn(-kf, c_lo, -p_lo);
+    float r_hi, r_lo;
+    two_sum(d, q, r_hi, r_lo);
+    // exp(r) - 1 = r + r^2/2 + r^3/6 + r^4/24 + r^5/120 (the next term < 2^-54)
+    const float sq = __fmul_rn(r_hi, r_hi);
+    const float sq_lo = __fmaf_rn(r_hi, r_hi, -sq);
+    const float tail = __fmul_rn(__fmul_rn(sq, r_hi),
+                                 __fmaf_rn(r_hi, __fmaf_rn(r_hi, 1.0f / 120.0f, 1.0f / 24.0f), 1.0f / 6.0f));
+    float s_hi, s_lo;
+    two_sum(r_hi, __fmul_rn(sq, 0.5f), s_hi, s_lo);
+    const float low = __fadd_rn(__fadd_rn(__fadd_rn(s_lo, r_lo), __fmul_rn(sq_lo, 0.5f)),
+                                __fadd_rn(tail, __fmul_rn(r_hi, r_lo)));
+    // 2^(j/64) (1 + s): T_hi + T_hi s_hi + (T_hi low + T_lo (1 + s_hi))
+    const float2 t = __ldg(&kExp2J64[k & 63]);  // lanes index freely (a constant-bank read would serialize)
+    const float m_hi = __fmul_rn(t.x, s_hi);
+    const float m_lo = __fmaf_rn(t.x, s_hi, -m_hi);
+    float a_hi, a_lo;
+    two_sum(t.x, m_hi, a_hi, a_lo);
+    const float rest = __fadd_rn(__fadd_rn(a_lo, m_lo), __fmaf_rn(t.x, low, __fmaf_rn(t.y, s_hi, t.y)));
+    const float y = __fadd_rn(a_hi, rest);
+    // times 2^e, exact for a normal result (e in [-126, 128] here; 2^128 in two steps)
+    const int e = k >> 6;
+    if (e > 127) return __fmul_rn(__fmul_rn(y, 0x1.p127f), 2.0f);
+    return __fmul_rn(y, __int_as_float((e + 127) << 23));
+}
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -124,6 +221,57 @@ __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
         asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes & ~15u) : "memory");
 }
 
+// ---- mbarrier + bulk async copy (global -> this CTA's shared memory) -------------
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+// Make barrier initialisation visible to the bulk-copy (async) proxy.
+__device__ __forceinline__ void mbar_init_fence() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// Order this thread's earlier generic accesses of shared memory before later
+// bulk copies into it.
+__device__ __forceinline__ void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+// A non-multicast bulk copy of `bytes` (multiple of 16, both ends 16-byte
+// aligned) completing on `bar`.
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_addr(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_addr(bar))
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Wait for phase `parity` of `bar`, giving up after `limit_ns` of wall time
+// (returns false then: the caller records the error and stops).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    while (!mbar_try_wait(bar, parity))
+        if (global_ns() - t0 > limit_ns) return false;
+    return true;
+}
+
 }  // namespace syn
 
 // Host-side error plumbing shared by the .cu files (defined in capi.cu).
@@ -151,6 +299,30 @@ int syn_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cud
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
+    }
+    return syn_cuda_status(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
+}
+
+// syn_launch with thread-block clusters of cluster_x CTAs along x.
+template <typename... KArgs, typename... Args>
+int syn_launch_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, int cluster_x, cudaStream_t s,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = unsigned(cluster_x);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (syn_pdl_enabled()) {
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
+        cfg.numAttrs = 2;
     }
     return syn_cuda_status(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
 }

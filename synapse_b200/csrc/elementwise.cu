@@ -4,6 +4,9 @@
 #include "common.cuh"
 #include "internal.h"
 
+#include <algorithm>
+#include <mutex>
+
 using namespace syn;
 
 namespace {
@@ -102,15 +105,16 @@ __global__ void embed_kernel(int type, const uint8_t* __restrict__ table, int la
                              const int32_t* __restrict__ tokens, float* out) {
     pdl_launch_dependents();
     pdl_wait();
-    const int t = blockIdx.x;
+    const int t = blockIdx.y;
     const int tok = tokens[t];
     float* o = out + size_t(t) * cols;
+    const int c_begin = blockIdx.x * blockDim.x, c_step = gridDim.x * blockDim.x;
     if (tok < 0 || tok >= rows) {
-        for (int c = threadIdx.x; c < cols; c += blockDim.x) o[c] = 0.0f;  // rejected on the host before launch
+        for (int c = c_begin + threadIdx.x; c < cols; c += c_step) o[c] = 0.0f;  // rejected on the host before launch
         return;
     }
     const int nb = cols / QK;
-    for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+    for (int c = c_begin + threadIdx.x; c < cols; c += c_step) {
         float v;
         if (type == SYN_F32) {
             v = reinterpret_cast<const float*>(table)[size_t(tok) * cols + c];
@@ -127,10 +131,8 @@ __global__ void embed_kernel(int type, const uint8_t* __restrict__ table, int la
                 if (type == SYN_Q4_0) q = j < 16 ? (p[2 + j] & 0x0f) - 8 : (p[2 + j - 16] >> 4) - 8;
                 else q = int8_t(p[2 + j]);
             } else {
-                const uint16_t* dh =
-                    reinterpret_cast<const uint16_t*>(table + planar_qs_bytes(type, rows, cols));
-                d = f16_from_bits(dh[blk]);
-                const uint8_t* p = table + blk * quant_bytes_per_block(type);
+                d = f16_from_bits(*reinterpret_cast<const uint16_t*>(table + planar_scale_at(type, cols, tok, b)));
+                const uint8_t* p = table + planar_quant_at(type, cols, tok, b);
                 if (type == SYN_Q4_0) q = j < 16 ? (p[j] & 0x0f) - 8 : (p[j - 16] >> 4) - 8;
                 else q = int8_t(p[j]);
             }
@@ -140,36 +142,70 @@ __global__ void embed_kernel(int type, const uint8_t* __restrict__ table, int la
     }
 }
 
-// First index of the maximum (std::max_element, llama_decode.cpp:274).
-__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ x, int n, int32_t* out) {
+// First index of the maximum (std::max_element, llama_decode.cpp:274): the
+// larger value wins, equal values go to the lower index, so any split of the
+// row gives the same answer.
+__device__ __forceinline__ void argmax_merge(float& v, int& i, float ov, int oi, int n) {
+    if (oi < n && (i >= n || ov > v || (ov == v && oi < i))) {
+        v = ov;
+        i = oi;
+    }
+}
+
+// Grid (slices, n_tok): each CTA reduces a slice of its row into a partial;
+// the last CTA of the row (atomic count) merges the partials and re-arms the
+// counter for the next launch.
+constexpr int kArgmaxThreads = 512;
+constexpr int kArgmaxSlices = 64;
+
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __restrict__ x, int n, int32_t* out,
+                                                                float* part_v, int* part_i, unsigned* count) {
     pdl_launch_dependents();
     pdl_wait();
-    const int t = blockIdx.x, tid = threadIdx.x;
+    const int t = blockIdx.y, tid = threadIdx.x, slices = gridDim.x;
     const float* xr = x + size_t(t) * n;
+    const int per = (n + slices - 1) / slices;
+    const int c0 = blockIdx.x * per, c1 = min(n, c0 + per);
     float best = -INFINITY;
-    int bi = n;  // sentinel beyond every index
-    for (int i = tid; i < n; i += blockDim.x) {
-        const float v = xr[i];
-        if (v > best || (bi == n && !(v < best))) { best = v; bi = i; }
+    int bi = n;
+    for (int c = c0 + tid; c < c1; c += kArgmaxThreads) {
+        const float v = xr[c];
+        if (bi >= n || v > best) { best = v; bi = c; }  // ascending c: ties keep the lower index
     }
-    __shared__ float sv[1024];
-    __shared__ int si[1024];
+    __shared__ float sv[kArgmaxThreads];
+    __shared__ int si[kArgmaxThreads];
+    __shared__ bool last;
     sv[tid] = best;
     si[tid] = bi;
     __syncthreads();
-    for (int w = blockDim.x / 2; w > 0; w >>= 1) {
-        if (tid < w) {
-            const float ov = sv[tid + w];
-            const int oi = si[tid + w];
-            if (oi < n && (si[tid] == n || ov > sv[tid] || (ov == sv[tid] && oi < si[tid]))) {
-                sv[tid] = ov;
-                si[tid] = oi;
-            }
-        }
+    for (int w = kArgmaxThreads / 2; w > 0; w >>= 1) {
+        if (tid < w) argmax_merge(sv[tid], si[tid], sv[tid + w], si[tid + w], n);
         __syncthreads();
     }
-    if (tid == 0) out[t] = si[0] == n ? 0 : si[0];
+    if (tid == 0) {
+        part_v[size_t(t) * slices + blockIdx.x] = sv[0];
+        part_i[size_t(t) * slices + blockIdx.x] = si[0];
+        __threadfence();
+        last = atomicAdd(&count[t], 1u) == unsigned(slices - 1);
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    if (tid == 0) {
+        float v = -INFINITY;
+        int i = n;
+        for (int k = 0; k < slices; ++k)
+            argmax_merge(v, i, __ldcg(part_v + size_t(t) * slices + k), __ldcg(part_i + size_t(t) * slices + k), n);
+        out[t] = i >= n ? 0 : i;
+        count[t] = 0u;
+    }
 }
+
+// Scratch of syn_argmax for n_tok rows, in static device memory (partials
+// plus the per-row completion counters, which start at zero and are re-armed
+// by every launch).
+constexpr int kArgmaxMaxTok = 64;
+__device__ __align__(256) unsigned char g_argmax_ws[kArgmaxMaxTok * kArgmaxSlices * 8 + kArgmaxMaxTok * 4 + 256];
 
 // io: [0] input token, [1] position, [2] argmax of this step, [3] steps done,
 // [4] forced (prompt) tokens. After a step: history[step] = argmax, the
@@ -229,11 +265,52 @@ extern "C" int syn_embed(int type, const void* table, int layout, int rows, int 
     if (type != SYN_F32 && type != SYN_F16 && type != SYN_Q4_0 && type != SYN_Q8_0) return SYN_ERR_UNSUPPORTED;
     if (!table || !tokens || !out || rows <= 0 || cols <= 0 || n_tok <= 0) return SYN_ERR_INVALID;
     if ((type == SYN_Q4_0 || type == SYN_Q8_0) && cols % QK) return SYN_ERR_INVALID;
-    return syn_launch(embed_kernel, n_tok, 256, 0, static_cast<cudaStream_t>(stream), type,
+    return syn_launch(embed_kernel, dim3((cols + 255) / 256, n_tok), 256, 0, static_cast<cudaStream_t>(stream), type,
                       static_cast<const uint8_t*>(table), layout, rows, cols, tokens, out);
+}
+
+size_t syn_argmax_ws_bytes(int n_tok) {
+    return size_t(n_tok) * kArgmaxSlices * 8 + ((size_t(n_tok) * 4 + 255) & ~size_t(255));
+}
+
+// ws: partials then per-row counters (zero before the first launch; every
+// launch leaves them zero again).
+int syn_argmax_ws(const float* x, int n_tok, int n, int32_t* out, void* ws, cudaStream_t s) {
+    if (!x || !out || !ws || n_tok <= 0 || n <= 0) return SYN_ERR_INVALID;
+    const int slices = std::min(kArgmaxSlices, std::max(1, (n + 4095) / 4096));
+    float* pv = static_cast<float*>(ws);
+    int* pi = reinterpret_cast<int*>(pv + size_t(n_tok) * kArgmaxSlices);
+    unsigned* pc = reinterpret_cast<unsigned*>(pi + size_t(n_tok) * kArgmaxSlices);
+    return syn_launch(argmax_kernel, dim3(slices, n_tok), kArgmaxThreads, 0, s, x, n, out, pv, pi, pc);
 }
 
 extern "C" int syn_argmax(const float* x, int n_tok, int n, int32_t* out, void* stream) {
     if (!x || !out || n_tok <= 0 || n <= 0) return SYN_ERR_INVALID;
-    return syn_launch(argmax_kernel, n_tok, 1024, 0, static_cast<cudaStream_t>(stream), x, n, out);
+    if (n_tok > kArgmaxMaxTok) return SYN_ERR_UNSUPPORTED;
+    static std::mutex mu;
+    static void* ws[64] = {};
+    int dev = 0;
+    int st = syn_cuda_status(cudaGetDevice(&dev));
+    if (st) return st;
+    if (dev < 0 || dev >= 64) return SYN_ERR_UNSUPPORTED;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!ws[dev] && (st = syn_cuda_status(cudaGetSymbolAddress(&ws[dev], g_argmax_ws)))) return st;
+    }
+    return syn_argmax_ws(x, n_tok, n, out, ws[dev], static_cast<cudaStream_t>(stream));
+}
+
+namespace {
+__global__ void check_exp_kernel(const float* x, float* y, float* y_ref, int n) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        y[i] = exp_rn(x[i]);
+        y_ref[i] = float(exp(double(x[i])));
+    }
+}
+}  // namespace
+
+extern "C" int syn_check_exp(const float* x, float* y, float* y_ref, int n, void* stream) {
+    if (!x || !y || !y_ref || n <= 0) return SYN_ERR_INVALID;
+    return syn_launch(check_exp_kernel, dim3(4 * syn_num_sms()), dim3(256), 0, static_cast<cudaStream_t>(stream), x,
+                      y, y_ref, n);
 }

@@ -21,6 +21,9 @@
 #include "common.cuh"
 
 #include <algorithm>
+#include <mutex>
+#include <utility>
+#include <vector>
 
 using namespace syn;
 
@@ -33,12 +36,17 @@ constexpr int kThreads = kWarps * 32;
 constexpr size_t kRowStageBytes = 16 * 1024;
 
 struct GemvArgs {
-    const uint8_t* w;    // GGUF rows, or the quant plane (planar)
-    const uint16_t* dh;  // planar scale plane (planar only)
+    const uint8_t* w;    // GGUF rows, or planar rows
+    const uint16_t* dh;  // unused (kept for layout symmetry)
     int rows, cols, nb, n_tok;
-    ActPlanes act;
+    ActPlanes act;       // SYN_IN_Q8: the Q8_0 activations
     float* y;
     const float* residual;
+    int in_mode;         // SYN_IN_Q8 / SYN_IN_F32 / SYN_IN_RMSNORM
+    const float* x;      // SYN_IN_F32, SYN_IN_RMSNORM: [n_tok][cols] floats
+    const float* gamma;  // SYN_IN_RMSNORM
+    float eps;
+    int out_mode;        // SYN_OUT_ROWS / SYN_OUT_SILU_PAIRS
 };
 
 // Block b of row r: its quants as 32-bit words and its decoded scale.
@@ -46,16 +54,16 @@ template <int TYPE, int LAYOUT>
 __device__ __forceinline__ void load_block(const GemvArgs& p, int r, int b, uint32_t (&w)[8], float& dw) {
     const size_t i = size_t(r) * p.nb + b;
     if (LAYOUT == SYN_LAYOUT_PLANAR) {
+        const uint4* q = reinterpret_cast<const uint4*>(p.w + planar_quant_at(TYPE, p.cols, r, b));
         if (TYPE == SYN_Q4_0) {
-            const uint4 v = __ldg(reinterpret_cast<const uint4*>(p.w) + i);
+            const uint4 v = __ldg(q);
             w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
         } else {
-            const uint4* q = reinterpret_cast<const uint4*>(p.w) + 2 * i;
             const uint4 v0 = __ldg(q), v1 = __ldg(q + 1);
             w[0] = v0.x; w[1] = v0.y; w[2] = v0.z; w[3] = v0.w;
             w[4] = v1.x; w[5] = v1.y; w[6] = v1.z; w[7] = v1.w;
         }
-        dw = f16_from_bits(__ldg(p.dh + i));
+        dw = f16_from_bits(__ldg(reinterpret_cast<const uint16_t*>(p.w + planar_scale_at(TYPE, p.cols, r, b))));
     } else {
         // GGUF AoS: 18 / 34-byte blocks, 2-byte aligned.
         const uint16_t* s = reinterpret_cast<const uint16_t*>(p.w + i * gguf_block_bytes(TYPE));
@@ -102,6 +110,23 @@ __host__ __device__ inline size_t warp_stage_bytes(int nb, int nt, bool whole_ro
     const int nch = (nb + 31) / 32;
     const size_t b = size_t(nt) * staged_blocks(nb, whole_row) * 8 + size_t(nt) * nch * 4;
     return (b + 15) & ~size_t(15);
+}
+
+// One chunk's accumulation in block order: acc = fma(isum_b, scale_b, acc)
+// (dot.hpp:277-287 with one lane). A full chunk is unrolled so its shared
+// memory loads issue ahead of the dependent fma chain.
+__device__ __forceinline__ float chunk_chain(const float2* s, int n) {
+    float acc = 0.0f;
+    if (n == 32) {
+        float2 v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = s[i];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc = fmaf(v[i].x, v[i].y, acc);
+    } else {
+        for (int i = 0; i < n; ++i) acc = fmaf(s[i].x, s[i].y, acc);
+    }
+    return acc;
 }
 
 // Warp w of W takes rows [rows*w/W, rows*(w+1)/W).
@@ -155,9 +180,7 @@ __global__ void __launch_bounds__(kThreads) gemv_q_kernel(GemvArgs p) {
                     const int t = k / nch, ch = k % nch;
                     const float2* s = stage + t * SB + ch * 33;
                     const int n = min(32, nb - ch * 32);
-                    float acc = 0.0f;
-                    for (int i = 0; i < n; ++i) acc = fmaf(s[i].x, s[i].y, acc);
-                    chunk_sum[t * nch + ch] = acc;
+                    chunk_sum[t * nch + ch] = chunk_chain(s, n);
                 }
                 __syncwarp();
                 if (lane < NT) {
@@ -169,10 +192,7 @@ __global__ void __launch_bounds__(kThreads) gemv_q_kernel(GemvArgs p) {
                 }
             } else {
                 if (lane < NT) {
-                    const float2* s = stage + lane * SB;
-                    const int n = b_end - b_begin;
-                    float acc = 0.0f;
-                    for (int i = 0; i < n; ++i) acc = fmaf(s[i].x, s[i].y, acc);
+                    const float acc = chunk_chain(stage + lane * SB, b_end - b_begin);
 #pragma unroll
                     for (int t = 0; t < NT; ++t)
                         if (t == lane) y[t] = __fadd_rn(y[t], acc);
@@ -187,6 +207,421 @@ __global__ void __launch_bounds__(kThreads) gemv_q_kernel(GemvArgs p) {
                 p.y[o] = p.residual ? __fadd_rn(y[t], p.residual[o]) : y[t];
             }
         }
+    }
+}
+
+// ---- lane-streamed variant (planar rows, 1-2 tokens) ----------------------------
+// Each lane streams its own run of blocks straight from HBM into registers
+// (16-byte loads, eight blocks in flight), so many warps per SM keep the
+// memory system busy without any shared-memory staging of weights. Lane
+// layout: a row's nch 32-block chunks are split over S lanes each (S = 1, 2
+// or 4: 32 / S consecutive blocks per lane), nch * S lanes per row, 32 /
+// (nch * S) rows per warp. Every lane forms (float(isum_b), d_w * d_a) for its
+// blocks; a chunk's fma chain then runs in block order, sub-lane after
+// sub-lane (the running sum moves one lane up by shuffle), and the row sum
+// adds the chunks in order: the reference's float order exactly.
+// The activations sit in shared memory with 16 bytes of padding after every
+// 8 blocks, so the sub-lanes' 16-byte reads spread over the banks.
+__device__ unsigned g_gemv_timeouts = 0;  // bounded waits that gave up (syn_device_errors; none here)
+
+__host__ __device__ inline size_t a16(size_t n) { return (n + 15) & ~size_t(15); }
+__host__ __device__ inline size_t act_pad_off(int b) { return size_t(b) * QK + size_t(b >> 3) * 16; }
+__host__ __device__ inline size_t act_pad_stride(int nb) { return a16(act_pad_off(nb)); }
+// The staged kernel's activation layout: 16 bytes of padding after every 4 blocks.
+__host__ __device__ inline size_t sact_off(int b) { return size_t(b) * QK + size_t(b >> 2) * 16; }
+// Shared memory of the lane kernel: NT padded quant rows, then (d, sum) per token and block.
+__host__ __device__ inline size_t lane_act_bytes(int nt, int nb) {
+    return size_t(nt) * act_pad_stride(nb) + size_t(nt) * nb * 8;
+}
+
+// The activations made in the kernel: every CTA quantizes the float input
+// (SYN_IN_F32), or its rms_norm (SYN_IN_RMSNORM), into shared memory with the
+// exact arithmetic of syn_quantize_q8_0 / syn_rms_norm (quant/q8.hpp:54-69,
+// elementwise.hpp:208-232), one 32-value block per thread.
+// LAYOUT 1: the lane kernel's (16 bytes after every 8 blocks); 2: the staged
+// kernel's (16 bytes after every 4 blocks).
+template <int NT, int LAYOUT = 1>
+__device__ void prologue_quantize(const GemvArgs& p, uint8_t* aq, float2* dsum) {
+    __shared__ double red[NT * (kThreads / 32)];
+    __shared__ float scale_t[NT];
+    const int cols = p.cols, nb = p.nb, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const size_t stride = act_pad_stride(nb);
+    if (p.in_mode == SYN_IN_RMSNORM) {
+        // Sum of squares per token: each thread's blocks with all eight
+        // 16-byte loads of a block in flight at once, then one block reduction.
+        double part[NT];
+#pragma unroll
+        for (int t = 0; t < NT; ++t) part[t] = 0.0;
+        for (int blk = threadIdx.x; blk < NT * nb; blk += blockDim.x) {
+            const int t = blk / nb, b = blk % nb;
+            const float4* src = reinterpret_cast<const float4*>(p.x + size_t(t) * cols + size_t(b) * QK);
+            float4 f[QK / 4];
+#pragma unroll
+            for (int k = 0; k < QK / 4; ++k) f[k] = src[k];
+            double sum = 0.0;
+#pragma unroll
+            for (int k = 0; k < QK / 4; ++k) {
+                sum += double(__fmul_rn(f[k].x, f[k].x));
+                sum += double(__fmul_rn(f[k].y, f[k].y));
+                sum += double(__fmul_rn(f[k].z, f[k].z));
+                sum += double(__fmul_rn(f[k].w, f[k].w));
+            }
+#pragma unroll
+            for (int tt = 0; tt < NT; ++tt)
+                if (tt == t) part[tt] += sum;
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            const double w = warp_sum_d(part[t]);
+            if (lane == 0) red[t * (kThreads / 32) + warp] = w;
+        }
+        __syncthreads();
+        if (threadIdx.x < NT) {
+            double tot = 0.0;
+            for (int w = 0; w < int(blockDim.x >> 5); ++w) tot += red[threadIdx.x * (kThreads / 32) + w];
+            const float mean = float(tot / double(cols));
+            scale_t[threadIdx.x] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+        }
+        __syncthreads();
+    }
+    // Quantize one block per thread in two passes over its 32 values (the
+    // second reads them again from L1), so few registers stay live.
+    const bool norm = p.in_mode == SYN_IN_RMSNORM;
+    for (int blk = threadIdx.x; blk < NT * nb; blk += blockDim.x) {
+        const int t = blk / nb, b = blk % nb;
+        const float4* src = reinterpret_cast<const float4*>(p.x + size_t(t) * cols + size_t(b) * QK);
+        const float4* g4 = reinterpret_cast<const float4*>(p.gamma + size_t(b) * QK);
+        const float sc = norm ? scale_t[t] : 1.0f;
+        auto value = [&](float x, float g) { return norm ? __fmul_rn(__fmul_rn(x, sc), g) : x; };
+        float amax = 0.0f;
+#pragma unroll
+        for (int k = 0; k < QK / 4; ++k) {
+            const float4 f = src[k];
+            const float4 g = norm ? __ldg(g4 + k) : make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+            amax = fmaxf(amax, fabsf(value(f.x, g.x)));
+            amax = fmaxf(amax, fabsf(value(f.y, g.y)));
+            amax = fmaxf(amax, fabsf(value(f.z, g.z)));
+            amax = fmaxf(amax, fabsf(value(f.w, g.w)));
+        }
+        const float d = __fdiv_rn(amax, 127.0f);
+        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        int qsum = 0;
+        uint32_t* dst = reinterpret_cast<uint32_t*>(aq + size_t(t) * stride +
+                                                    (LAYOUT == 1 ? act_pad_off(b) : sact_off(b)));
+#pragma unroll
+        for (int k = 0; k < QK / 4; ++k) {
+            const float4 f = src[k];
+            const float4 g = norm ? __ldg(g4 + k) : make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+            const int q0 = int(roundf(__fmul_rn(value(f.x, g.x), id)));
+            const int q1 = int(roundf(__fmul_rn(value(f.y, g.y), id)));
+            const int q2 = int(roundf(__fmul_rn(value(f.z, g.z), id)));
+            const int q3 = int(roundf(__fmul_rn(value(f.w, g.w), id)));
+            qsum += q0 + q1 + q2 + q3;
+            dst[k] = (uint32_t(q0) & 0xffu) | ((uint32_t(q1) & 0xffu) << 8) | ((uint32_t(q2) & 0xffu) << 16) |
+                     ((uint32_t(q3) & 0xffu) << 24);
+        }
+        dsum[t * nb + b] = make_float2(f16_from_bits(f16_bits(d)), __int_as_float(qsum));
+    }
+}
+
+// S sub-lanes per chunk; BPL = 32 / S blocks per lane.
+template <int TYPE, int NT, int S>
+__global__ void __launch_bounds__(kThreads, 2) gemv_lane_kernel(GemvArgs p) {
+    constexpr int BPL = 32 / S;
+    constexpr int QB = TYPE == SYN_Q4_0 ? 16 : 32;  // quant bytes per block
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nb = p.nb, nch = (nb + 31) / 32, lpr = nch * S, rpw = 32 / lpr;
+    const size_t stride = act_pad_stride(nb);
+    uint8_t* aq = smem;
+    float2* dsum = reinterpret_cast<float2*>(smem + size_t(NT) * stride);
+    const int rl = lane / lpr, rem = lane % lpr, c = rem / S, s = rem % S;
+    const int m = rl < rpw ? min(32, nb - 32 * c) : 0;  // blocks of this lane's chunk
+    const int j0 = s * BPL, nblk = max(0, min(m, j0 + BPL) - j0);
+    const int b0 = 32 * c + j0;  // this lane's first block
+    const size_t row_b = planar_row_bytes(TYPE, p.cols), qbytes = planar_quant_bytes(TYPE, p.cols);
+    const long n_groups = (p.rows + rpw - 1) / rpw;
+    const long nw = long(gridDim.x) * (blockDim.x >> 5);
+    const long gw0 = long(blockIdx.x) * (blockDim.x >> 5) + warp;
+
+    pdl_launch_dependents();
+    pdl_wait();  // the activations (and the residual) come from the previous kernel
+    if (p.in_mode == SYN_IN_Q8) {
+        for (int i = threadIdx.x; i < NT * nb * 2; i += blockDim.x) {
+            const int t = i / (2 * nb), b = (i / 2) % nb, h = i & 1;
+            reinterpret_cast<int4*>(aq + size_t(t) * stride + act_pad_off(b))[h] =
+                __ldg(reinterpret_cast<const int4*>(p.act.qs + size_t(t) * p.cols + size_t(b) * QK) + h);
+        }
+        for (int i = threadIdx.x; i < NT * nb; i += blockDim.x)
+            dsum[i] = make_float2(__ldg(p.act.d + i), __int_as_float(__ldg(p.act.sum + i)));
+    } else {
+        prologue_quantize<NT>(p, aq, dsum);
+    }
+    __syncthreads();
+
+    for (long grp = gw0; grp < n_groups; grp += nw) {
+        const long row = grp * rpw + rl;
+        const bool live = nblk > 0 && row < p.rows;
+        float acc[NT];
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
+        float px[S > 1 ? NT : 1][S > 1 ? BPL : 1], ps[S > 1 ? NT : 1][S > 1 ? BPL : 1];
+        if (live) {
+            const uint8_t* wrow = p.w + size_t(row) * row_b;
+            // LD blocks per batch: 128 bytes of quants in flight per lane
+            constexpr int LD = TYPE == SYN_Q4_0 ? 8 : 4;
+#pragma unroll
+            for (int k0 = 0; k0 < BPL; k0 += LD) {
+                if (k0 < nblk) {
+                    uint4 wv[LD][QB / 16];
+#pragma unroll
+                    for (int k = 0; k < LD; ++k)
+                        if (k0 + k < nblk) {
+#pragma unroll
+                            for (int h = 0; h < QB / 16; ++h)
+                                wv[k][h] = __ldg(reinterpret_cast<const uint4*>(
+                                                     wrow + size_t(planar_block_pos(nb, size_t(row), b0 + k0 + k)) * QB) + h);
+                        }
+                    // the batch's binary16 scales (8-byte aligned: k0 is a multiple of 4)
+                    const uint2 sv = __ldg(reinterpret_cast<const uint2*>(wrow + qbytes + size_t(b0 + k0) * 2));
+                    uint2 sv2 = make_uint2(0u, 0u);
+                    if (LD == 8) sv2 = __ldg(reinterpret_cast<const uint2*>(wrow + qbytes + size_t(b0 + k0 + 4) * 2));
+                    const uint32_t sw[4] = {sv.x, sv.y, sv2.x, sv2.y};
+#pragma unroll
+                    for (int k = 0; k < LD; ++k) {
+                        if (k0 + k < nblk) {
+                            const int b = b0 + k0 + k;
+                            uint32_t w[8];
+                            w[0] = wv[k][0].x; w[1] = wv[k][0].y; w[2] = wv[k][0].z; w[3] = wv[k][0].w;
+                            if (QB == 32) {
+                                w[4] = wv[k][QB / 16 - 1].x; w[5] = wv[k][QB / 16 - 1].y;
+                                w[6] = wv[k][QB / 16 - 1].z; w[7] = wv[k][QB / 16 - 1].w;
+                            }
+                            const float dw = f16_from_bits(uint16_t(sw[k >> 1] >> (16 * (k & 1))));
+#pragma unroll
+                            for (int t = 0; t < NT; ++t) {
+                                const int4* ap = reinterpret_cast<const int4*>(aq + size_t(t) * stride + act_pad_off(b));
+                                const float2 ds = dsum[t * nb + b];
+                                const int isum = block_dot<TYPE>(w, ap[0], ap[1], TYPE == SYN_Q4_0 ? __float_as_int(ds.y) : 0);
+                                const float sc = __fmul_rn(dw, ds.x);
+                                if (S == 1) {
+                                    acc[t] = fmaf(float(isum), sc, acc[t]);  // dot.hpp:286, in block order
+                                } else {
+                                    px[S > 1 ? t : 0][S > 1 ? k0 + k : 0] = float(isum);
+                                    ps[S > 1 ? t : 0][S > 1 ? k0 + k : 0] = sc;
+                                }
+                            }
+                        }
+                    }
+                }
+            }
+        }
+        if (S > 1) {
+            // the chunk's chain, sub-lane 0 first: each continues from the previous one's sum
+#pragma unroll
+            for (int st = 0; st < S; ++st) {
+                if (live && s == st) {
+#pragma unroll
+                    for (int k = 0; k < BPL; ++k)
+                        if (k < nblk) {
+#pragma unroll
+                            for (int t = 0; t < NT; ++t)
+                                acc[t] = fmaf(px[S > 1 ? t : 0][S > 1 ? k : 0], ps[S > 1 ? t : 0][S > 1 ? k : 0], acc[t]);
+                        }
+                }
+                if (st + 1 < S) {
+#pragma unroll
+                    for (int t = 0; t < NT; ++t) {
+                        const float from = __shfl_up_sync(0xffffffffu, acc[t], 1);
+                        if (s == st + 1) acc[t] = from;
+                    }
+                }
+            }
+        }
+        // Row sums: ((0 + chunk 0) + chunk 1) + ... (dot.hpp:398); chunk c's sum is in its last sub-lane.
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            float y = 0.0f;
+            for (int cc = 0; cc < nch; ++cc)
+                y = __fadd_rn(y, __shfl_sync(0xffffffffu, acc[t], (rl * lpr + cc * S + S - 1) & 31));
+            if (p.out_mode == SYN_OUT_SILU_PAIRS) {
+                // rows 2i (gate) and 2i+1 (up) are rows rl, rl + 1 of the warp's group:
+                // out[i] = silu(gate) * up (elementwise.hpp:76, :50)
+                const float up = __shfl_sync(0xffffffffu, y, ((rl + 1) * lpr) & 31);
+                if (rem == 0 && (rl & 1) == 0 && rl < rpw && row < p.rows)
+                    p.y[size_t(t) * (p.rows / 2) + size_t(row / 2)] =
+                        __fmul_rn(__fdiv_rn(y, __fadd_rn(1.0f, exp_rn(-y))), up);
+            } else if (rem == 0 && rl < rpw && row < p.rows) {
+                const size_t o = size_t(t) * p.rows + size_t(row);
+                p.y[o] = p.residual ? __fadd_rn(y, p.residual[o]) : y;
+            }
+        }
+    }
+}
+
+// ---- staged kernel (planar rows, one token) -------------------------------------
+// A warp takes batches of R consecutive rows. Each batch lands in one of the
+// warp's two shared-memory buffers by one bulk copy (the first two are
+// requested before the kernel waits on its predecessor: weights never depend
+// on it). Then
+//   blocks: lane l forms (float(isum_b), d_w * d_a) for blocks l, l+32, ...
+//           of every row of the batch (consecutive lanes read consecutive
+//           16-byte quants: no bank conflicts) and stages the pairs;
+//   chains: one lane per (row, 32-block chunk) runs that chunk's fma chain in
+//           block order over the staged pairs (dot.hpp:277-287);
+//   rows:   one lane per row adds its chunks in order (dot.hpp:398) and
+//           writes the row, its residual sum, or silu(gate) * up.
+// The activations (Q8_0, padded 16 bytes per 4 blocks so consecutive lanes'
+// 32-byte reads spread over the banks) sit in shared memory once per CTA.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+constexpr int kStageWarps = 8;
+constexpr size_t kBatchBytes = 9728;  // target bytes of weights per batch
+
+struct StageShape {
+    int nb, nch, R;                          // blocks, chunks per row; rows per batch
+    size_t row_b, batch_bytes, act_bytes, stage_floats2, warp_bytes, smem;
+};
+
+__host__ __device__ inline StageShape stage_shape(int type, int cols) {
+    StageShape s;
+    s.nb = cols / QK;
+    s.nch = (s.nb + 31) / 32;
+    s.row_b = planar_row_bytes(type, cols);
+    int R = int(kBatchBytes / s.row_b);
+    if (R < 1) R = 1;
+    const int rmax = s.nch >= 32 ? 1 : 32 / s.nch;  // every (row, chunk) chain gets a lane
+    if (R > rmax) R = rmax;
+    if (R > 1 && (R & 1)) --R;                       // even: gate/up pairs stay in one batch
+    s.R = R;
+    s.batch_bytes = size_t(R) * s.row_b;
+    s.act_bytes = a16(a16(sact_off(s.nb)) + size_t(s.nb) * 8);
+    s.stage_floats2 = size_t(R) * (s.nb + s.nch);    // one float2 of padding per chunk
+    s.warp_bytes = 32 + 2 * s.batch_bytes + a16(s.stage_floats2 * 8) + a16(size_t(R) * s.nch * 4);
+    s.smem = s.act_bytes + kStageWarps * s.warp_bytes;
+    return s;
+}
+
+template <int TYPE>
+__global__ void __launch_bounds__(kStageWarps * 32) gemv_stage_kernel(GemvArgs p) {
+    constexpr int QB = TYPE == SYN_Q4_0 ? 16 : 32;
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const StageShape sh = stage_shape(TYPE, p.cols);
+    const int nb = sh.nb, nch = sh.nch, R = sh.R;
+    const size_t row_b = sh.row_b, qbytes = planar_quant_bytes(TYPE, p.cols);
+    uint8_t* aq = smem;
+    float2* dsum = reinterpret_cast<float2*>(smem + a16(sact_off(nb)));
+    unsigned char* wbase = smem + sh.act_bytes + size_t(warp) * sh.warp_bytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(wbase);
+    unsigned char* buf = wbase + 32;
+    float2* stage = reinterpret_cast<float2*>(buf + 2 * sh.batch_bytes);
+    float* chsum = reinterpret_cast<float*>(buf + 2 * sh.batch_bytes + a16(sh.stage_floats2 * 8));
+    const int spr = nb + nch;  // staged pairs per row
+
+    const long n_batch = (p.rows + R - 1) / R;
+    const long gw = long(blockIdx.x) * kStageWarps + warp, nw = long(gridDim.x) * kStageWarps;
+    const long k0 = n_batch * gw / nw, k1 = n_batch * (gw + 1) / nw;
+    const int nbatch = int(k1 - k0);
+    auto batch_rows = [&](int k) { return int(min(long(R), long(p.rows) - (k0 + k) * R)); };
+    auto issue = [&](int k) {
+        const uint32_t bytes = uint32_t(size_t(batch_rows(k)) * row_b);
+        mbar_expect_tx(&bars[k & 1], bytes);
+        bulk_copy_g2s(buf + size_t(k & 1) * sh.batch_bytes, p.w + size_t((k0 + k) * R) * row_b, bytes, &bars[k & 1]);
+    };
+    if (lane == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        mbar_init_fence();
+        for (int k = 0; k < min(2, nbatch); ++k) issue(k);
+    }
+    __syncwarp();
+    pdl_launch_dependents();
+    pdl_wait();  // the activations (and the residual) come from the previous kernel
+    if (p.in_mode == SYN_IN_Q8) {
+        for (int i = threadIdx.x; i < nb * 2; i += blockDim.x)
+            reinterpret_cast<int4*>(aq + sact_off(i >> 1))[i & 1] =
+                __ldg(reinterpret_cast<const int4*>(p.act.qs) + i);
+        for (int i = threadIdx.x; i < nb; i += blockDim.x)
+            dsum[i] = make_float2(__ldg(p.act.d + i), __int_as_float(__ldg(p.act.sum + i)));
+    } else {
+        prologue_quantize<1, 2>(p, aq, dsum);
+    }
+    __syncthreads();
+
+    int k = 0;
+    bool ok = true;
+    for (; k < nbatch; ++k) {
+        const bool got = mbar_wait_bounded(&bars[k & 1], uint32_t((k >> 1) & 1), kWaitLimitNs);
+        if (!__all_sync(0xffffffffu, got)) {
+            ok = false;
+            break;
+        }
+        const int rows_k = batch_rows(k);
+        const unsigned char* bb = buf + size_t(k & 1) * sh.batch_bytes;
+        // blocks: every (row, block) pair of the batch, lane-parallel
+        for (int r = 0; r < rows_k; ++r) {
+            const unsigned char* wr = bb + size_t(r) * row_b;
+#pragma unroll 4
+            for (int b = lane; b < nb; b += 32) {
+                uint32_t w[8];
+                const uint4 v0 = *reinterpret_cast<const uint4*>(wr + size_t(b) * QB);
+                w[0] = v0.x; w[1] = v0.y; w[2] = v0.z; w[3] = v0.w;
+                if (QB == 32) {
+                    const uint4 v1 = *reinterpret_cast<const uint4*>(wr + size_t(b) * QB + (QB - 16));
+                    w[4] = v1.x; w[5] = v1.y; w[6] = v1.z; w[7] = v1.w;
+                }
+                const float dw = f16_from_bits(*reinterpret_cast<const uint16_t*>(wr + qbytes + size_t(b) * 2));
+                const int4* ap = reinterpret_cast<const int4*>(aq + sact_off(b));
+                const float2 ds = dsum[b];
+                const int isum = block_dot<TYPE>(w, ap[0], ap[1], TYPE == SYN_Q4_0 ? __float_as_int(ds.y) : 0);
+                stage[r * spr + b + (b >> 5)] = make_float2(float(isum), __fmul_rn(dw, ds.x));
+            }
+        }
+        __syncwarp();
+        // chains: one lane per (row, chunk)
+        for (int ch = lane; ch < rows_k * nch; ch += 32) {
+            const int r = ch / nch, c = ch - r * nch;
+            const int m = min(32, nb - 32 * c);
+            const float2* sp = stage + r * spr + 33 * c;
+            float acc = 0.0f;
+            if (m == 32) {
+#pragma unroll 8
+                for (int j = 0; j < 32; ++j) {
+                    const float2 v = sp[j];
+                    acc = fmaf(v.x, v.y, acc);
+                }
+            } else {
+                for (int j = 0; j < m; ++j) {
+                    const float2 v = sp[j];
+                    acc = fmaf(v.x, v.y, acc);
+                }
+            }
+            chsum[ch] = acc;
+        }
+        __syncwarp();
+        // rows: chunks in order
+        float y = 0.0f;
+        const long row = (k0 + k) * R + lane;
+        if (lane < rows_k)
+            for (int c = 0; c < nch; ++c) y = __fadd_rn(y, chsum[lane * nch + c]);
+        if (p.out_mode == SYN_OUT_SILU_PAIRS) {
+            // rows 2i (gate) and 2i+1 (up) are lanes l, l+1 of the batch: out[i] = silu(gate) * up
+            const float up = __shfl_down_sync(0xffffffffu, y, 1);
+            if (lane < rows_k && (lane & 1) == 0)
+                p.y[size_t(row / 2)] = __fmul_rn(__fdiv_rn(y, __fadd_rn(1.0f, exp_rn(-y))), up);
+        } else if (lane < rows_k) {
+            p.y[row] = p.residual ? __fadd_rn(y, p.residual[row]) : y;
+        }
+        __syncwarp();
+        if (lane == 0 && k + 2 < nbatch) {
+            fence_async_shared();  // the warp's reads of this buffer come before the copy that refills it
+            issue(k + 2);
+        }
+    }
+    if (!ok && lane == 0) {
+        // record it, then let the copies still in flight into this warp's buffers land (bounded)
+        atomicAdd(&g_gemv_timeouts, 1u);
+        for (int q = k; q < min(nbatch, k + 2); ++q) mbar_wait_bounded(&bars[q & 1], uint32_t((q >> 1) & 1), kWaitLimitNs);
     }
 }
 
@@ -265,25 +700,105 @@ int persistent_grid(K kernel, size_t smem, long work_warps) {
     return int(std::max<long>(1, std::min(want, cap)));
 }
 
-template <typename K>
-int configure(K kernel, size_t smem) {
-    if (smem > 48 * 1024)
-        return syn_cuda_status(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-    return SYN_OK;
+// The shared memory opt-in of a kernel, set once per device (a per-device
+// function attribute) to the most any shape of this library asks for.
+int configure(const void* kernel, size_t smem) {
+    static std::mutex mu;
+    static std::vector<std::pair<const void*, int>> done;
+    if (smem <= 48 * 1024) return SYN_OK;
+    int dev = 0;
+    int st = syn_cuda_status(cudaGetDevice(&dev));
+    if (st) return st;
+    std::lock_guard<std::mutex> lock(mu);
+    for (const auto& d : done)
+        if (d.first == kernel && d.second == dev) return SYN_OK;
+    st = syn_cuda_status(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    if (!st) done.push_back({kernel, dev});
+    return st;
+}
+
+// Sub-lanes per chunk for the lane kernel: split chunks (S = 2, 4) only when
+// there are too few (row, chunk) pairs to give every resident warp work; with
+// two tokens S = 2 would hold too many pairs in registers. 0: not this kernel
+// (a row of more than 32 chunks, or gate/up pairs that would straddle warps).
+int lane_split(int nt, int rows, int cols, int out_mode) {
+    const int nb = cols / QK, nch = (nb + 31) / 32;
+    const long units = long(rows) * nch, target = long(syn_num_sms()) * 48 * 32;
+    int order[3] = {1, 2, 4};
+    if (units < target / 4) { order[0] = 4; order[1] = 2; order[2] = 1; }
+    else if (units < target / 2) { order[0] = 2; order[1] = 4; order[2] = 1; }
+    for (int S : order) {
+        if (nt == 2 && S == 2) continue;
+        const int lpr = nch * S;
+        if (lpr > 32) continue;
+        const int rpw = 32 / lpr;
+        if (out_mode == SYN_OUT_SILU_PAIRS && (rpw % 2 || rows % 2)) continue;
+        return S;
+    }
+    return 0;
+}
+
+template <int TYPE, int NT, int S>
+int launch_lane_s(const GemvArgs& p, cudaStream_t s) {
+    auto k = gemv_lane_kernel<TYPE, NT, S>;
+    const size_t smem = lane_act_bytes(NT, p.nb);
+    int st = configure(reinterpret_cast<const void*>(k), smem);
+    if (st) return st;
+    const int nch = (p.nb + 31) / 32, rpw = 32 / (nch * S);
+    const long groups = (p.rows + rpw - 1) / rpw;
+    return syn_launch(k, persistent_grid(k, smem, groups), kThreads, smem, s, p);
+}
+
+template <int TYPE, int NT>
+int launch_lane(const GemvArgs& p, int S, cudaStream_t s) {
+    switch (S) {
+    case 1: return launch_lane_s<TYPE, NT, 1>(p, s);
+    case 2: return launch_lane_s<TYPE, NT, 2>(p, s);
+    case 4: return launch_lane_s<TYPE, NT, 4>(p, s);
+    }
+    return SYN_ERR_UNSUPPORTED;
+}
+
+// Whether the staged kernel takes this one-token shape (gate/up pairs need
+// even batches).
+bool stage_ok(int type, int rows, int cols, int out_mode) {
+    const StageShape sh = stage_shape(type, cols);
+    if (sh.smem > 200 * 1024) return false;
+    if (out_mode == SYN_OUT_SILU_PAIRS && (sh.R % 2 || rows % 2)) return false;
+    return true;
+}
+
+template <int TYPE>
+int launch_stage(const GemvArgs& p, cudaStream_t s) {
+    auto k = gemv_stage_kernel<TYPE>;
+    const StageShape sh = stage_shape(TYPE, p.cols);
+    int st = configure(reinterpret_cast<const void*>(k), sh.smem);
+    if (st) return st;
+    // One CTA of 8 warps per SM (measured best: 16 KB of weights in flight
+    // per warp, chains and rows of 8 warps interleaved).
+    const long batches = (p.rows + sh.R - 1) / sh.R;
+    const long grid = std::max<long>(1, std::min<long>(long(syn_num_sms()), (batches + kStageWarps - 1) / kStageWarps));
+    return syn_launch(k, unsigned(grid), unsigned(kStageWarps * 32), sh.smem, s, p);
 }
 
 template <int TYPE, int LAYOUT, int NT>
 int launch_q(const GemvArgs& p, cudaStream_t s) {
+    if (LAYOUT == SYN_LAYOUT_PLANAR && NT == 1 && stage_ok(TYPE, p.rows, p.cols, SYN_OUT_ROWS))
+        return launch_stage<TYPE>(p, s);
+    if (LAYOUT == SYN_LAYOUT_PLANAR && NT <= 2) {
+        const int S = lane_split(NT, p.rows, p.cols, SYN_OUT_ROWS);
+        if (S) return launch_lane<TYPE, NT <= 2 ? NT : 1>(p, S, s);
+    }
     const bool whole = warp_stage_bytes(p.nb, NT, true) <= kRowStageBytes;
     const size_t smem = size_t(kWarps) * warp_stage_bytes(p.nb, NT, whole);
     if (whole) {
         auto k = gemv_q_kernel<TYPE, LAYOUT, NT, true>;
-        int st = configure(k, smem);
+        int st = configure(reinterpret_cast<const void*>(k), smem);
         if (st) return st;
         return syn_launch(k, persistent_grid(k, smem, p.rows), kThreads, smem, s, p);
     }
     auto k = gemv_q_kernel<TYPE, LAYOUT, NT, false>;
-    int st = configure(k, smem);
+    int st = configure(reinterpret_cast<const void*>(k), smem);
     if (st) return st;
     return syn_launch(k, persistent_grid(k, smem, p.rows), kThreads, smem, s, p);
 }
@@ -307,7 +822,7 @@ template <int TYPE, int NT>
 int launch_f(const void* w, int rows, int cols, const float* x, float* y, const float* res, cudaStream_t s) {
     const size_t smem = size_t(kWarps) * NT * ((cols + 255) / 256) * 4;
     auto k = gemv_f_kernel<TYPE, NT>;
-    int st = configure(k, smem);
+    int st = configure(reinterpret_cast<const void*>(k), smem);
     if (st) return st;
     return syn_launch(k, persistent_grid(k, smem, rows), kThreads, smem, s, w, rows, cols, x, y, res);
 }
@@ -342,11 +857,9 @@ extern "C" int syn_gemv_q(int type, const void* w, int layout, int rows, int col
     const int nb = cols / QK;
     for (int t0 = 0; t0 < n_tok; t0 += 8) {
         const int n = n_tok - t0 < 8 ? n_tok - t0 : 8;
-        GemvArgs p;
+        GemvArgs p{};
         p.w = static_cast<const uint8_t*>(w);
-        p.dh = layout == SYN_LAYOUT_PLANAR
-                   ? reinterpret_cast<const uint16_t*>(p.w + planar_qs_bytes(type, rows, cols))
-                   : nullptr;
+        p.dh = nullptr;
         p.rows = rows;
         p.cols = cols;
         p.nb = nb;
@@ -357,6 +870,8 @@ extern "C" int syn_gemv_q(int type, const void* w, int layout, int rows, int col
         p.act.sum = all.sum + size_t(t0) * nb;
         p.y = y + size_t(t0) * rows;
         p.residual = residual ? residual + size_t(t0) * rows : nullptr;
+        p.in_mode = SYN_IN_Q8;
+        p.out_mode = SYN_OUT_ROWS;
         int st;
         if (type == SYN_Q4_0)
             st = layout == SYN_LAYOUT_PLANAR ? dispatch_q<SYN_Q4_0, SYN_LAYOUT_PLANAR>(p, n, s)
@@ -367,6 +882,57 @@ extern "C" int syn_gemv_q(int type, const void* w, int layout, int rows, int col
         if (st) return st;
     }
     return SYN_OK;
+}
+
+extern "C" int syn_gemv_fusable(int type, int layout, int rows, int cols, int n_tok, int out_mode) {
+    if ((type != SYN_Q4_0 && type != SYN_Q8_0) || layout != SYN_LAYOUT_PLANAR) return 0;
+    if (rows <= 0 || cols <= 0 || cols % QK || n_tok < 1 || n_tok > 2) return 0;
+    if (n_tok == 1 && stage_ok(type, rows, cols, out_mode)) return 1;
+    if (lane_split(n_tok, rows, cols, out_mode) == 0) return 0;
+    return lane_act_bytes(n_tok, cols / QK) <= 200 * 1024;
+}
+
+extern "C" int syn_gemv(const syn_gemv_args* a, void* stream) {
+    if (!a) return SYN_ERR_INVALID;
+    if (a->in_mode == SYN_IN_Q8 && a->out_mode == SYN_OUT_ROWS)
+        return syn_gemv_q(a->type, a->w, a->layout, a->rows, a->cols, a->act, a->n_tok, a->y, a->residual, stream);
+    if (a->in_mode != SYN_IN_Q8 && a->in_mode != SYN_IN_F32 && a->in_mode != SYN_IN_RMSNORM) return SYN_ERR_INVALID;
+    if (a->out_mode != SYN_OUT_ROWS && a->out_mode != SYN_OUT_SILU_PAIRS) return SYN_ERR_INVALID;
+    if (!a->w || !a->y) return SYN_ERR_INVALID;
+    if (a->in_mode == SYN_IN_Q8 ? !a->act : !a->x) return SYN_ERR_INVALID;
+    if (a->in_mode == SYN_IN_RMSNORM && !a->gamma) return SYN_ERR_INVALID;
+    if (a->out_mode == SYN_OUT_SILU_PAIRS && a->residual) return SYN_ERR_INVALID;
+    if (!syn_gemv_fusable(a->type, a->layout, a->rows, a->cols, a->n_tok, a->out_mode)) return SYN_ERR_UNSUPPORTED;
+    if ((reinterpret_cast<uintptr_t>(a->w) | reinterpret_cast<uintptr_t>(a->x) |
+         reinterpret_cast<uintptr_t>(a->act) | reinterpret_cast<uintptr_t>(a->gamma)) & 15)
+        return SYN_ERR_INVALID;
+    GemvArgs p{};
+    p.w = static_cast<const uint8_t*>(a->w);
+    p.rows = a->rows;
+    p.cols = a->cols;
+    p.nb = a->cols / QK;
+    p.n_tok = a->n_tok;
+    if (a->in_mode == SYN_IN_Q8) p.act = act_planes(const_cast<void*>(a->act), a->n_tok, a->cols);
+    p.y = a->y;
+    p.residual = a->residual;
+    p.in_mode = a->in_mode;
+    p.x = a->x;
+    p.gamma = a->gamma;
+    p.eps = a->eps;
+    p.out_mode = a->out_mode;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (a->n_tok == 1 && stage_ok(a->type, a->rows, a->cols, a->out_mode))
+        return a->type == SYN_Q4_0 ? launch_stage<SYN_Q4_0>(p, s) : launch_stage<SYN_Q8_0>(p, s);
+    const int S = lane_split(a->n_tok, a->rows, a->cols, a->out_mode);
+    if (a->type == SYN_Q4_0)
+        return a->n_tok == 1 ? launch_lane<SYN_Q4_0, 1>(p, S, s) : launch_lane<SYN_Q4_0, 2>(p, S, s);
+    return a->n_tok == 1 ? launch_lane<SYN_Q8_0, 1>(p, S, s) : launch_lane<SYN_Q8_0, 2>(p, S, s);
+}
+
+extern "C" int syn_device_errors(void) {
+    unsigned n = 0;
+    if (cudaMemcpyFromSymbol(&n, g_gemv_timeouts, sizeof n) != cudaSuccess) return -1;
+    return int(n);
 }
 
 extern "C" int syn_gemv_f(int type, const void* w, int rows, int cols, const float* x, int n_tok, float* y,

@@ -41,11 +41,12 @@ struct weight {
     bool quant() const { return type == SYN_Q4_0 || type == SYN_Q8_0; }
 };
 
-// A source tensor of a (possibly fused) weight: rows [row0, row0 + rows).
-struct part {
+// A file tensor inside a (possibly fused) device matrix: its row i is the
+// matrix's row row0 + i * step.
+struct source {
     std::string name;
-    int row0 = 0, rows = 0;
-    uint64_t tensor_id = 0;  // synthetic generator stream
+    const weight* w = nullptr;
+    int row0 = 0, step = 1, rows = 0;
 };
 
 struct layer_w {
@@ -55,6 +56,7 @@ struct layer_w {
     weight gate, up;  // gate holds up too when fused_gu
     weight down;
     bool fused_qkv = false, fused_gu = false;
+    bool gu_pairs = false;  // gate/up rows interleaved (gate i at 2i, up i at 2i+1) for the silu-pair epilogue
 };
 
 enum class opk { embed, rms_norm, quantize, matmul, attention, silu_mul, argmax };
@@ -66,6 +68,8 @@ struct op {
     size_t in_off = 0, out_off = 0, in2_off = 0, res_off = 0;           // float offsets inside tensors
     int rows = 0, cols = 0;
     int layer = 0;
+    int in_mode = SYN_IN_Q8, out_mode = SYN_OUT_ROWS;  // matmul: fused input / output (syn_gemv)
+    const weight* gamma = nullptr;                     // matmul with SYN_IN_RMSNORM
 };
 
 struct tensor {
@@ -85,12 +89,13 @@ struct syn_session {
     size_t arena_bytes = 0, weight_bytes = 0, kv_bytes = 0, act_bytes = 0;
     weight embd, out_norm, head;
     std::vector<layer_w> layers;
-    std::vector<std::pair<std::string, std::pair<const weight*, int>>> sources;  // name -> (weight, row0)
+    std::vector<source> sources;
     size_t ff_off = 0;  // freq factors (floats), 0 = none
     bool has_ff = false;
     size_t kv_off = 0;
     size_t act_off = 0;
-    size_t io_off = 0, forced_off = 0, hist_off = 0;
+    size_t io_off = 0, forced_off = 0, hist_off = 0, argmax_ws_off = 0;
+    size_t rope_tab_off = 0;  // (cos, sin) of every RoPE pair at every position < max_ctx
     std::vector<tensor> tensors;
     std::vector<op> ops;
     int logits_t = -1;
@@ -99,7 +104,8 @@ struct syn_session {
     int32_t* h_io = nullptr;   // pinned: token, pos
     float* h_logits = nullptr; // pinned
     int32_t* h_next = nullptr; // pinned
-    cudaGraphExec_t step_exec = nullptr, gen_exec = nullptr;
+    cudaGraphExec_t step_exec = nullptr, gen_exec = nullptr, prof_exec = nullptr;
+    std::vector<cudaEvent_t> prof_events;
     bool use_graph = true;
 
     template <typename T>
@@ -183,6 +189,14 @@ struct activation {
     int q8 = -1;   // tensor with Q8_0 activations
 };
 
+bool fusable(const weight& w, int out_mode = SYN_OUT_ROWS) {
+    return w.quant() && syn_gemv_fusable(w.type, w.layout, w.rows, w.cols, 1, out_mode);
+}
+
+// The step as ops. Where the pipelined GEMV takes the shape, each matmul
+// absorbs its neighbours: the rms_norm (and Q8_0 quantization) before it, the
+// residual add after it, and for gate/up the silu * up epilogue, so a layer is
+// four GEMVs and one attention launch.
 void build_step(syn_session& s) {
     const syn_llama_config& c = s.cfg;
     graph_builder g{s};
@@ -217,16 +231,45 @@ void build_step(syn_session& s) {
         o.cols = w.cols;
         g.add(o);
     };
+    // y = W * prologue(in) (+ res), the input floats quantized inside the GEMV
+    auto fused = [&](const weight& w, int in, const weight* gamma, int out, int res, int out_mode) {
+        op o{opk::matmul};
+        o.w = &w;
+        o.in = in;
+        o.gamma = gamma;
+        o.in_mode = gamma ? SYN_IN_RMSNORM : SYN_IN_F32;
+        o.out_mode = out_mode;
+        o.out = out;
+        o.res = res;
+        o.rows = w.rows;
+        o.cols = w.cols;
+        g.add(o);
+    };
+    auto quantize = [&](int in, int cols) {
+        activation a;
+        a.f32 = in;
+        a.q8 = g.new_tensor(act_bytes_for(cols));
+        op o{opk::quantize};
+        o.in = in;
+        o.out = a.q8;
+        o.cols = cols;
+        g.add(o);
+        return a;
+    };
     for (int l = 0; l < c.n_layer; ++l) {
         const layer_w& L = s.layers[l];
-        const bool qk_any = L.q.quant() || (!L.fused_qkv && (L.k.quant() || L.v.quant()));
-        const bool qk_f = !L.q.quant() || (!L.fused_qkv && (!L.k.quant() || !L.v.quant()));
-        activation h = norm(x, L.attn_norm, qk_f, qk_any);
         const int qkv = g.new_tensor(size_t(qrows + 2 * kvrows) * 4);
-        matmul(L.q, h, qkv, 0, -1);
-        if (!L.fused_qkv) {
-            matmul(L.k, h, qkv, qrows, -1);
-            matmul(L.v, h, qkv, qrows + kvrows, -1);
+        if (L.fused_qkv && fusable(L.q)) {
+            fused(L.q, x, &L.attn_norm, qkv, -1, SYN_OUT_ROWS);
+        } else {
+            const bool qk_any = L.q.quant() || (!L.fused_qkv && (L.k.quant() || L.v.quant()));
+            const bool qk_f = !L.q.quant() || (!L.fused_qkv && (!L.k.quant() || !L.v.quant()));
+            activation h = norm(x, L.attn_norm, qk_f, qk_any);
+            matmul(L.q, h, qkv, 0, -1);
+            if (!L.fused_qkv) {
+                matmul(L.k, h, qkv, qrows, -1);
+                matmul(L.v, h, qkv, qrows + kvrows, -1);
+            }
         }
         const int attn = g.new_tensor(size_t(qrows) * 4);
         {
@@ -237,41 +280,55 @@ void build_step(syn_session& s) {
             o.scratch = g.new_tensor(syn_attention_scratch_bytes(1, c.n_head, c.n_head_kv, c.head_dim, s.max_ctx));
             g.add(o);
         }
-        activation a;
-        a.f32 = attn;
-        if (L.o.quant()) {
-            a.q8 = g.new_tensor(act_bytes_for(qrows));
-            op o{opk::quantize};
-            o.in = attn;
-            o.out = a.q8;
-            o.cols = qrows;
-            g.add(o);
-        }
         const int x2 = g.new_tensor(size_t(d) * 4);
-        matmul(L.o, a, x2, 0, x);
-        x = x2;
-        const bool gu_any = L.gate.quant() || (!L.fused_gu && L.up.quant());
-        const bool gu_f = !L.gate.quant() || (!L.fused_gu && !L.up.quant());
-        activation h2 = norm(x, L.ffn_norm, gu_f, gu_any);
-        const int gu = g.new_tensor(size_t(2) * ff * 4);
-        matmul(L.gate, h2, gu, 0, -1);
-        if (!L.fused_gu) matmul(L.up, h2, gu, ff, -1);
-        activation f;
-        {
-            op o{opk::silu_mul};
-            o.in = gu;
-            o.cols = ff;
-            if (L.down.quant()) f.q8 = o.out2 = g.new_tensor(act_bytes_for(ff));
-            else f.f32 = o.out = g.new_tensor(size_t(ff) * 4);
-            g.add(o);
+        if (fusable(L.o)) {
+            fused(L.o, attn, nullptr, x2, x, SYN_OUT_ROWS);
+        } else {
+            activation a;
+            a.f32 = attn;
+            if (L.o.quant()) a = quantize(attn, qrows);
+            matmul(L.o, a, x2, 0, x);
         }
+        x = x2;
         const int x3 = g.new_tensor(size_t(d) * 4);
-        matmul(L.down, f, x3, 0, x);
+        if (L.gu_pairs) {  // fusable(L.gate, SYN_OUT_SILU_PAIRS) held when the rows were interleaved
+            const int act = g.new_tensor(size_t(ff) * 4);
+            fused(L.gate, x, &L.ffn_norm, act, -1, SYN_OUT_SILU_PAIRS);
+            if (fusable(L.down)) {
+                fused(L.down, act, nullptr, x3, x, SYN_OUT_ROWS);
+            } else {
+                activation f;
+                f.f32 = act;
+                if (L.down.quant()) f = quantize(act, ff);
+                matmul(L.down, f, x3, 0, x);
+            }
+        } else {
+            const bool gu_any = L.gate.quant() || (!L.fused_gu && L.up.quant());
+            const bool gu_f = !L.gate.quant() || (!L.fused_gu && !L.up.quant());
+            activation h2 = norm(x, L.ffn_norm, gu_f, gu_any);
+            const int gu = g.new_tensor(size_t(2) * ff * 4);
+            matmul(L.gate, h2, gu, 0, -1);
+            if (!L.fused_gu) matmul(L.up, h2, gu, ff, -1);
+            activation f;
+            {
+                op o{opk::silu_mul};
+                o.in = gu;
+                o.cols = ff;
+                if (L.down.quant()) f.q8 = o.out2 = g.new_tensor(act_bytes_for(ff));
+                else f.f32 = o.out = g.new_tensor(size_t(ff) * 4);
+                g.add(o);
+            }
+            matmul(L.down, f, x3, 0, x);
+        }
         x = x3;
     }
-    activation hl = norm(x, s.out_norm, !s.head.quant(), s.head.quant());
     s.logits_t = g.new_tensor(size_t(c.n_vocab) * 4);
-    matmul(s.head, hl, s.logits_t, 0, -1);
+    if (fusable(s.head)) {
+        fused(s.head, x, &s.out_norm, s.logits_t, -1, SYN_OUT_ROWS);
+    } else {
+        activation hl = norm(x, s.out_norm, !s.head.quant(), s.head.quant());
+        matmul(s.head, hl, s.logits_t, 0, -1);
+    }
     {
         op o{opk::argmax};
         o.in = s.logits_t;
@@ -313,7 +370,23 @@ int enqueue_body(syn_session& s, cudaStream_t st) {
         case opk::matmul: {
             float* y = s.tf(o.out, o.out_off);
             const float* res = o.res >= 0 ? s.tf(o.res) : nullptr;
-            if (o.w->quant())
+            if (o.in_mode != SYN_IN_Q8 || o.out_mode != SYN_OUT_ROWS) {
+                syn_gemv_args a{};
+                a.type = o.w->type;
+                a.layout = o.w->layout;
+                a.rows = o.rows;
+                a.cols = o.cols;
+                a.n_tok = 1;
+                a.w = s.arena + o.w->off;
+                a.in_mode = o.in_mode;
+                a.x = s.tf(o.in);
+                a.gamma = o.gamma ? s.at<float>(o.gamma->off) : nullptr;
+                a.eps = c.rms_eps;
+                a.out_mode = o.out_mode;
+                a.y = y;
+                a.residual = res;
+                rc = syn_gemv(&a, st);
+            } else if (o.w->quant())
                 rc = syn_gemv_q(o.w->type, s.arena + o.w->off, o.w->layout, o.w->rows, o.w->cols, s.tb(o.in), 1, y,
                                 res, st);
             else
@@ -343,6 +416,7 @@ int enqueue_body(syn_session& s, cudaStream_t st) {
             a.theta_scale = s.theta_scale;
             a.scale = s.scale;
             a.freq_factors = s.has_ff ? s.at<float>(s.ff_off) : nullptr;
+            a.rope_table = s.at<float>(s.rope_tab_off);
             rc = syn_attention(&a, st);
             break;
         }
@@ -351,7 +425,7 @@ int enqueue_body(syn_session& s, cudaStream_t st) {
                               o.out2 >= 0 ? s.tb(o.out2) : nullptr, st);
             break;
         case opk::argmax:
-            rc = syn_argmax(s.tf(o.in), 1, c.n_vocab, s.io() + 2, st);
+            rc = syn_argmax_ws(s.tf(o.in), 1, c.n_vocab, s.io() + 2, s.arena + s.argmax_ws_off, st);
             break;
         }
         if (rc) return rc;
@@ -419,6 +493,8 @@ int finish(syn_session& s, layout_builder& lb) {
     s.io_off = lb.take(64);
     s.forced_off = lb.take(size_t(s.max_ctx) * 4);
     s.hist_off = lb.take(size_t(s.max_ctx) * 4);
+    s.argmax_ws_off = lb.take(syn_argmax_ws_bytes(1));  // persistent: its counters must stay zero between steps
+    s.rope_tab_off = lb.take(size_t(s.max_ctx) * c.head_dim * 4);
     s.arena_bytes = lb.off;
     s.theta_scale = std::pow(c.rope_base, -2.0f / float(c.head_dim));  // attention.hpp:47
     s.scale = 1.0f / std::sqrt(float(c.head_dim));                      // llama.hpp:407
@@ -432,12 +508,15 @@ int finish(syn_session& s, layout_builder& lb) {
     return SYN_OK;
 }
 
-// One eager step at position 0 (sets per-device kernel attributes outside any
-// capture), then the KV cache and io are cleared and both graphs captured.
+// The RoPE table, one eager step at position 0 (sets per-device kernel
+// attributes outside any capture), then the KV cache and io are cleared and
+// both graphs captured.
 int warm_and_capture(syn_session& s) {
     s.h_io[0] = 0;
     s.h_io[1] = 0;
-    int rc = enqueue_step(s, s.stream);
+    int rc = syn_rope_table(s.at<float>(s.rope_tab_off), s.max_ctx, s.cfg.head_dim, s.theta_scale,
+                            s.has_ff ? s.at<float>(s.ff_off) : nullptr, nullptr, s.stream);
+    if (!rc) rc = enqueue_step(s, s.stream);
     if (!rc) rc = cuda(cudaStreamSynchronize(s.stream));
     if (!rc) rc = cuda(cudaMemsetAsync(s.arena + s.kv_off, 0, s.kv_bytes, s.stream));
     if (!rc) rc = cuda(cudaMemsetAsync(s.io(), 0, 64, s.stream));
@@ -464,35 +543,41 @@ void layer_layout(syn_session& s, const std::vector<std::vector<int>>& types, la
         L.fused_qkv = t[1] == t[2] && t[1] == t[3] && (t[1] == SYN_Q4_0 || t[1] == SYN_Q8_0);
         if (L.fused_qkv) {
             define(L.q, t[1], qrows + 2 * kvrows, d, lb);
-            s.sources.push_back({p + "attn_q.weight", {&L.q, 0}});
-            s.sources.push_back({p + "attn_k.weight", {&L.q, qrows}});
-            s.sources.push_back({p + "attn_v.weight", {&L.q, qrows + kvrows}});
+            s.sources.push_back({p + "attn_q.weight", &L.q, 0, 1, qrows});
+            s.sources.push_back({p + "attn_k.weight", &L.q, qrows, 1, kvrows});
+            s.sources.push_back({p + "attn_v.weight", &L.q, qrows + kvrows, 1, kvrows});
         } else {
             define(L.q, t[1], qrows, d, lb);
             define(L.k, t[2], kvrows, d, lb);
             define(L.v, t[3], kvrows, d, lb);
-            s.sources.push_back({p + "attn_q.weight", {&L.q, 0}});
-            s.sources.push_back({p + "attn_k.weight", {&L.k, 0}});
-            s.sources.push_back({p + "attn_v.weight", {&L.v, 0}});
+            s.sources.push_back({p + "attn_q.weight", &L.q, 0, 1, qrows});
+            s.sources.push_back({p + "attn_k.weight", &L.k, 0, 1, kvrows});
+            s.sources.push_back({p + "attn_v.weight", &L.v, 0, 1, kvrows});
         }
         define(L.o, t[4], d, qrows, lb);
-        s.sources.push_back({p + "attn_output.weight", {&L.o, 0}});
+        s.sources.push_back({p + "attn_output.weight", &L.o, 0, 1, d});
         define(L.ffn_norm, SYN_F32, 1, d, lb);
         L.fused_gu = t[6] == t[7] && (t[6] == SYN_Q4_0 || t[6] == SYN_Q8_0);
         if (L.fused_gu) {
             define(L.gate, t[6], 2 * ff, d, lb);
-            s.sources.push_back({p + "ffn_gate.weight", {&L.gate, 0}});
-            s.sources.push_back({p + "ffn_up.weight", {&L.gate, ff}});
+            L.gu_pairs = syn_gemv_fusable(t[6], SYN_LAYOUT_PLANAR, 2 * ff, d, 1, SYN_OUT_SILU_PAIRS) != 0;
+            if (L.gu_pairs) {
+                s.sources.push_back({p + "ffn_gate.weight", &L.gate, 0, 2, ff});
+                s.sources.push_back({p + "ffn_up.weight", &L.gate, 1, 2, ff});
+            } else {
+                s.sources.push_back({p + "ffn_gate.weight", &L.gate, 0, 1, ff});
+                s.sources.push_back({p + "ffn_up.weight", &L.gate, ff, 1, ff});
+            }
         } else {
             define(L.gate, t[6], ff, d, lb);
             define(L.up, t[7], ff, d, lb);
-            s.sources.push_back({p + "ffn_gate.weight", {&L.gate, 0}});
-            s.sources.push_back({p + "ffn_up.weight", {&L.up, 0}});
+            s.sources.push_back({p + "ffn_gate.weight", &L.gate, 0, 1, ff});
+            s.sources.push_back({p + "ffn_up.weight", &L.up, 0, 1, ff});
         }
         define(L.down, t[8], d, ff, lb);
-        s.sources.push_back({p + "ffn_down.weight", {&L.down, 0}});
-        s.sources.push_back({p + "attn_norm.weight", {&L.attn_norm, 0}});
-        s.sources.push_back({p + "ffn_norm.weight", {&L.ffn_norm, 0}});
+        s.sources.push_back({p + "ffn_down.weight", &L.down, 0, 1, d});
+        s.sources.push_back({p + "attn_norm.weight", &L.attn_norm, 0, 1, 1});
+        s.sources.push_back({p + "ffn_norm.weight", &L.ffn_norm, 0, 1, 1});
     }
 }
 
@@ -501,6 +586,8 @@ void destroy(syn_session* s) {
     if (s->device >= 0) cudaSetDevice(s->device);
     if (s->step_exec) cudaGraphExecDestroy(s->step_exec);
     if (s->gen_exec) cudaGraphExecDestroy(s->gen_exec);
+    if (s->prof_exec) cudaGraphExecDestroy(s->prof_exec);
+    for (auto& e : s->prof_events) cudaEventDestroy(e);
     if (s->stream) cudaStreamSynchronize(s->stream);
     if (s->arena) cudaFree(s->arena);
     if (s->h_io) cudaFreeHost(s->h_io);
@@ -614,13 +701,13 @@ extern "C" int syn_session_open_gguf(const char* path, int max_ctx, int device, 
 
     layout_builder lb;
     define(s->embd, c.type_embd, c.n_vocab, c.n_embd, lb);
-    s->sources.push_back({"token_embd.weight", {&s->embd, 0}});
+    s->sources.push_back({"token_embd.weight", &s->embd, 0, 1, c.n_vocab});
     layer_layout(*s, types, lb);
     define(s->out_norm, SYN_F32, 1, c.n_embd, lb);
-    s->sources.push_back({"output_norm.weight", {&s->out_norm, 0}});
+    s->sources.push_back({"output_norm.weight", &s->out_norm, 0, 1, 1});
     if (tout) {
         define(s->head, c.type_output, c.n_vocab, c.n_embd, lb);
-        s->sources.push_back({"output.weight", {&s->head, 0}});
+        s->sources.push_back({"output.weight", &s->head, 0, 1, c.n_vocab});
     } else {
         s->head = s->embd;  // tied (llama.hpp:471-472)
     }
@@ -635,12 +722,11 @@ extern "C" int syn_session_open_gguf(const char* path, int max_ctx, int device, 
     void* staging = nullptr;
     if ((rc = cuda(cudaMalloc(&staging, staging_bytes)))) return rc;
     for (const auto& src : s->sources) {
-        const syn::gguf::tensor_info* t = f->tensor(src.first);
-        const weight& w = *src.second.first;
-        const int row0 = src.second.second;
+        const syn::gguf::tensor_info* t = f->tensor(src.name);
+        const weight& w = *src.w;
         const uint8_t* data = f->data(*t);
         if (!w.quant()) {
-            rc = cuda(cudaMemcpyAsync(s->arena + w.off + size_t(row0) * w.cols * (w.type == SYN_F32 ? 4 : 2), data,
+            rc = cuda(cudaMemcpyAsync(s->arena + w.off + size_t(src.row0) * w.cols * (w.type == SYN_F32 ? 4 : 2), data,
                                       t->nbytes, cudaMemcpyHostToDevice, s->stream));
         } else {
             const int rows = int(t->rows());
@@ -650,8 +736,9 @@ extern "C" int syn_session_open_gguf(const char* path, int max_ctx, int device, 
                 const int n = rows - r0 < per ? rows - r0 : per;
                 rc = cuda(cudaMemcpyAsync(staging, data + size_t(r0) * row_bytes, size_t(n) * row_bytes,
                                           cudaMemcpyHostToDevice, s->stream));
-                if (!rc) rc = syn_repack_rows(w.type, staging, n, w.cols, s->arena + w.off, w.rows, row0 + r0,
-                                              s->stream);
+                if (!rc)
+                    rc = syn_repack_rows(w.type, staging, n, w.cols, s->arena + w.off, w.rows,
+                                         src.row0 + r0 * src.step, s->stream, src.step);
                 if (!rc) rc = cuda(cudaStreamSynchronize(s->stream));
             }
         }
@@ -688,14 +775,14 @@ extern "C" int syn_session_open_synthetic(const syn_llama_config* cp, int max_ct
     const syn_llama_config& c = s->cfg;
     layout_builder lb;
     define(s->embd, c.type_embd, c.n_vocab, c.n_embd, lb);
-    s->sources.push_back({"token_embd.weight", {&s->embd, 0}});
+    s->sources.push_back({"token_embd.weight", &s->embd, 0, 1, c.n_vocab});
     const int T = c.type_layers;
     layer_layout(*s, std::vector<std::vector<int>>(c.n_layer, {SYN_F32, T, T, T, T, SYN_F32, T, T, T}), lb);
     define(s->out_norm, SYN_F32, 1, c.n_embd, lb);
-    s->sources.push_back({"output_norm.weight", {&s->out_norm, 0}});
+    s->sources.push_back({"output_norm.weight", &s->out_norm, 0, 1, 1});
     if (c.type_output >= 0) {
         define(s->head, c.type_output, c.n_vocab, c.n_embd, lb);
-        s->sources.push_back({"output.weight", {&s->head, 0}});
+        s->sources.push_back({"output.weight", &s->head, 0, 1, c.n_vocab});
     } else {
         s->head = s->embd;
     }
@@ -704,22 +791,13 @@ extern "C" int syn_session_open_synthetic(const syn_llama_config* cp, int max_ct
     // Every matrix N(0, 0.02) (seeded per tensor name), norms 1.0.
     uint64_t tensor_id = 0;
     for (const auto& src : s->sources) {
-        const weight& w = *src.second.first;
-        const int row0 = src.second.second;
+        const weight& w = *src.w;
         ++tensor_id;
-        if (src.first.find("norm") != std::string::npos) {
+        if (src.name.find("norm") != std::string::npos)
             rc = syn_fill_f32(s->at<float>(w.off), size_t(w.cols), 1.0f, s->stream);
-        } else {
-            int rows = w.rows;
-            // the rows this source tensor covers inside a fused matrix
-            const std::string& n = src.first;
-            const int qrows = c.n_head * c.head_dim, kvrows = c.n_head_kv * c.head_dim;
-            if (n.find("attn_q.") != std::string::npos) rows = qrows;
-            else if (n.find("attn_k.") != std::string::npos || n.find("attn_v.") != std::string::npos) rows = kvrows;
-            else if (n.find("ffn_gate.") != std::string::npos || n.find("ffn_up.") != std::string::npos) rows = c.n_ff;
-            rc = syn_fill_random(w.type, rows, w.cols, s->arena + w.off, w.rows, row0, seed, tensor_id, 0.02f,
-                                 s->stream);
-        }
+        else
+            rc = syn_fill_random(w.type, src.rows, w.cols, s->arena + w.off, w.rows, src.row0, seed, tensor_id, 0.02f,
+                                 s->stream, src.step);
         if (rc) return rc;
     }
     if ((rc = cuda(cudaStreamSynchronize(s->stream)))) return rc;
@@ -815,8 +893,10 @@ double op_bytes(const syn_session& s, const op& o, uint32_t pos) {
         const double nb = double(w.cols) / 32;
         double wb = w.quant() ? double(w.rows) * nb * (w.type == SYN_Q4_0 ? 18 : 34)
                               : double(w.rows) * w.cols * (w.type == SYN_F32 ? 4 : 2);
-        const double in = w.quant() ? double(w.cols) + nb * 8 : double(w.cols) * 4;
-        return wb + in + double(w.rows) * 4 * (o.res >= 0 ? 2 : 1);
+        double in = w.quant() ? double(w.cols) + nb * 8 : double(w.cols) * 4;
+        if (o.in_mode != SYN_IN_Q8) in = double(w.cols) * 4 * (o.in_mode == SYN_IN_RMSNORM ? 2 : 1);  // x (+ gamma)
+        const double out = o.out_mode == SYN_OUT_SILU_PAIRS ? double(w.rows) / 2 : double(w.rows);
+        return wb + in + out * 4 * (o.res >= 0 ? 2 : 1);
     }
     case opk::attention: {
         const double L = double(pos) + 1, row = double(c.n_head_kv) * c.head_dim;
@@ -843,6 +923,9 @@ int op_kind_code(opk k) {
 
 }  // namespace
 
+// The step with an event recorded between every two ops, captured once as a
+// graph and replayed, so each op's time is the device's alone (no host gaps,
+// no programmatic overlap between ops).
 extern "C" int syn_session_profile(syn_session* s, uint32_t token, uint32_t pos, syn_op_profile* out, int max_ops,
                                    int* n_ops) {
     if (!s || !n_ops) return SYN_ERR_INVALID;
@@ -851,23 +934,39 @@ extern "C" int syn_session_profile(syn_session* s, uint32_t token, uint32_t pos,
     if (rc) return rc;
     const size_t n = s->ops.size();
     *n_ops = int(n);
-    std::vector<cudaEvent_t> ev(n + 1);
-    for (auto& e : ev)
-        if ((rc = cuda(cudaEventCreate(&e)))) return rc;
+    if (!out) return SYN_OK;
+    if (s->prof_events.empty()) {
+        s->prof_events.resize(n + 1);
+        for (auto& e : s->prof_events)
+            if ((rc = cuda(cudaEventCreate(&e)))) return rc;
+        cudaGraph_t g = nullptr;
+        if ((rc = cuda(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal)))) return rc;
+        int body = SYN_OK;
+        std::vector<op> all;
+        all.swap(s->ops);
+        // External event records: timestamps readable after the replay (an
+        // event recorded inside a capture is otherwise internal to the graph).
+        for (size_t i = 0; i < n && !body; ++i) {
+            body = cuda(cudaEventRecordWithFlags(s->prof_events[i], s->stream, cudaEventRecordExternal));
+            s->ops.assign(1, all[i]);
+            if (!body) body = enqueue_body(*s, s->stream);
+        }
+        s->ops.swap(all);
+        if (!body) body = cuda(cudaEventRecordWithFlags(s->prof_events[n], s->stream, cudaEventRecordExternal));
+        rc = cuda(cudaStreamEndCapture(s->stream, &g));
+        if (body || rc) {
+            if (g) cudaGraphDestroy(g);
+            return body ? body : rc;
+        }
+        rc = cuda(cudaGraphInstantiate(&s->prof_exec, g, 0));
+        cudaGraphDestroy(g);
+        if (rc) return rc;
+    }
     int32_t io[2] = {int32_t(token), int32_t(pos)};
     rc = cuda(cudaMemcpyAsync(s->io(), io, sizeof io, cudaMemcpyHostToDevice, s->stream));
-    // the same ops as enqueue_body, one at a time, with an event between each
-    std::vector<op> all;
-    all.swap(s->ops);
-    for (size_t i = 0; i < n && !rc; ++i) {
-        rc = cuda(cudaEventRecord(ev[i], s->stream));
-        s->ops.assign(1, all[i]);
-        if (!rc) rc = enqueue_body(*s, s->stream);
-    }
-    s->ops.swap(all);
-    if (!rc) rc = cuda(cudaEventRecord(ev[n], s->stream));
+    if (!rc) rc = cuda(cudaGraphLaunch(s->prof_exec, s->stream));
     if (!rc) rc = cuda(cudaStreamSynchronize(s->stream));
-    for (size_t i = 0; i < n && !rc && out && int(i) < max_ops; ++i) {
+    for (size_t i = 0; i < n && !rc && int(i) < max_ops; ++i) {
         const op& o = s->ops[i];
         syn_op_profile& p = out[i];
         p.kind = op_kind_code(o.kind);
@@ -875,10 +974,9 @@ extern "C" int syn_session_profile(syn_session* s, uint32_t token, uint32_t pos,
         p.type = o.w ? o.w->type : -1;
         p.rows = o.w ? o.w->rows : 0;
         p.cols = o.w ? o.w->cols : o.cols;
-        rc = cuda(cudaEventElapsedTime(&p.ms, ev[i], ev[i + 1]));
+        rc = cuda(cudaEventElapsedTime(&p.ms, s->prof_events[i], s->prof_events[i + 1]));
         p.bytes = op_bytes(*s, o, pos);
     }
-    for (auto& e : ev) cudaEventDestroy(e);
     return rc;
 }
 
@@ -900,16 +998,9 @@ extern "C" int syn_session_weight(syn_session* s, const char* name, void* host_o
                                   int* rows, int* cols) {
     if (!s || !name) return SYN_ERR_INVALID;
     for (const auto& src : s->sources) {
-        if (src.first != name) continue;
-        const weight& w = *src.second.first;
-        const int row0 = src.second.second;
-        int r = w.rows;
-        const syn_llama_config& c = s->cfg;
-        const std::string n(name);
-        const int qrows = c.n_head * c.head_dim, kvrows = c.n_head_kv * c.head_dim;
-        if (n.find("attn_q.") != std::string::npos) r = qrows;
-        else if (n.find("attn_k.") != std::string::npos || n.find("attn_v.") != std::string::npos) r = kvrows;
-        else if (n.find("ffn_gate.") != std::string::npos || n.find("ffn_up.") != std::string::npos) r = c.n_ff;
+        if (src.name != name) continue;
+        const weight& w = *src.w;
+        const int r = src.rows;
         if (type) *type = w.type;
         if (rows) *rows = r;
         if (cols) *cols = w.cols;
@@ -920,22 +1011,24 @@ extern "C" int syn_session_weight(syn_session* s, const char* name, void* host_o
         if (rc) return rc;
         if (!w.quant()) {
             const size_t es = w.type == SYN_F32 ? 4 : 2;
-            return cuda(cudaMemcpy(host_out, s->arena + w.off + size_t(row0) * w.cols * es, need,
+            return cuda(cudaMemcpy(host_out, s->arena + w.off + size_t(src.row0) * w.cols * es, need,
                                    cudaMemcpyDeviceToHost));
         }
-        // planar -> GGUF blocks on the host
+        // planar rows (quants, then binary16 scales, padded) -> GGUF blocks on the host
         const int nb = w.cols / 32, qb = w.type == SYN_Q4_0 ? 16 : 32, bb = qb + 2;
-        std::vector<uint8_t> qs(size_t(r) * nb * qb);
-        std::vector<uint16_t> dh(size_t(r) * nb);
-        const size_t qplane = (size_t(w.rows) * nb * qb + 255) / 256 * 256;
-        rc = cuda(cudaMemcpy(qs.data(), s->arena + w.off + size_t(row0) * nb * qb, qs.size(), cudaMemcpyDeviceToHost));
-        if (!rc) rc = cuda(cudaMemcpy(dh.data(), s->arena + w.off + qplane + size_t(row0) * nb * 2, dh.size() * 2,
-                                      cudaMemcpyDeviceToHost));
-        if (rc) return rc;
+        const size_t row_b = size_t(nb) * qb + ((size_t(nb) * 2 + 15) & ~size_t(15));
+        std::vector<uint8_t> rowbuf(row_b);
         uint8_t* o = static_cast<uint8_t*>(host_out);
-        for (size_t i = 0; i < size_t(r) * nb; ++i) {
-            std::memcpy(o + i * bb, &dh[i], 2);
-            std::memcpy(o + i * bb + 2, qs.data() + i * qb, qb);
+        for (int rr = 0; rr < r; ++rr) {
+            const size_t dr = size_t(src.row0) + size_t(rr) * src.step;
+            rc = cuda(cudaMemcpy(rowbuf.data(), s->arena + w.off + dr * row_b, row_b, cudaMemcpyDeviceToHost));
+            if (rc) return rc;
+            for (int b = 0; b < nb; ++b) {
+                uint8_t* blk = o + (size_t(rr) * nb + b) * bb;
+                const size_t pos = size_t(syn_planar_block_pos(nb, dr, b));
+                std::memcpy(blk, rowbuf.data() + size_t(nb) * qb + size_t(b) * 2, 2);
+                std::memcpy(blk + 2, rowbuf.data() + pos * qb, qb);
+            }
         }
         return SYN_OK;
     }

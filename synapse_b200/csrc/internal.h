@@ -7,14 +7,15 @@
 
 // GGUF blocks of `rows` rows (device) -> rows [row0, row0 + rows) of a planar
 // matrix of `total_rows` rows at dst.
+// Source row i lands on destination row row0 + i * row_step.
 int syn_repack_rows(int type, const void* src, int rows, int cols, void* dst, int total_rows, int row0,
-                    cudaStream_t s);
+                    cudaStream_t s, int row_step = 1);
 
 // Random N(0, sigma) values, seeded by (seed, tensor, element), quantized with
 // ggml's reference quantizer (Q4_0 / Q8_0) into rows [row0, row0 + rows) of a
 // planar matrix of total_rows, or written as F32 / F16 (row0 must be 0).
 int syn_fill_random(int type, int rows, int cols, void* dst, int total_rows, int row0, uint64_t seed,
-                    uint64_t tensor, float sigma, cudaStream_t s);
+                    uint64_t tensor, float sigma, cudaStream_t s, int row_step = 1);
 // dst[i] = v for n floats.
 int syn_fill_f32(float* dst, size_t n, float v, cudaStream_t s);
 
@@ -22,8 +23,24 @@ int syn_fill_f32(float* dst, size_t n, float v, cudaStream_t s);
 // argmax, advances the position and picks the next input token.
 int syn_advance(int32_t* io, const int32_t* forced, int32_t* history, cudaStream_t s);
 
+// Argmax with a caller-owned persistent workspace of syn_argmax_ws_bytes
+// (zeroed once; each launch leaves its counters zero again).
+size_t syn_argmax_ws_bytes(int n_tok);
+int syn_argmax_ws(const float* x, int n_tok, int n, int32_t* out, void* ws, cudaStream_t s);
+
+// Physical position of logical block b in row r of a planar matrix of nb
+// blocks per row (the loader's chunk rotation).
+int syn_planar_block_pos(int nb, size_t r, int b);
+
 // Programmatic dependent launch for this thread's launches.
 void syn_set_pdl(int on);
+// The same, exported for microbenchmarks that time kernels captured the way
+// the session captures them.
+extern "C" void syn_set_programmatic_launch(int on);
 
 // Sets the thread's last error message.
 void syn_set_error(const char* msg);
+
+// Self-check of the library's expf (exp_rn): y = exp_rn(x) and, for
+// comparison, y_ref = exp(double(x)) rounded to float, for n device floats.
+extern "C" int syn_check_exp(const float* x, float* y, float* y_ref, int n, void* stream);

@@ -7,6 +7,8 @@
 #include "common.cuh"
 #include "internal.h"
 
+#include <algorithm>
+
 using namespace syn;
 
 namespace {
@@ -43,28 +45,21 @@ __global__ void act_to_blocks_kernel(ActPlanes a, int n_tok, int cols, uint8_t* 
 
 // GGUF blocks [rows*nb] (18 / 34 B) -> quant plane (16 / 32 B per block) and
 // binary16 scale plane. One thread per block; a one-time loader pass.
-__global__ void repack_kernel(int type, const uint8_t* __restrict__ src, long n_blocks, uint8_t* __restrict__ qs,
-                              uint16_t* __restrict__ dh) {
-    const long i = long(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i >= n_blocks) return;
-    const int bb = gguf_block_bytes(type), qb = quant_bytes_per_block(type);
-    const uint8_t* s = src + i * bb;
-    dh[i] = static_cast<uint16_t>(s[0] | (s[1] << 8));
-    uint8_t* q = qs + i * qb;
-    for (int j = 0; j < qb; ++j) q[j] = s[2 + j];
-}
-
-// Rows [row0, row0 + rows) of a planar matrix of total_rows rows.
-__global__ void repack_rows_kernel(int type, const uint8_t* __restrict__ src, int rows, int nb, uint8_t* qs,
-                                   uint16_t* dh, long first_block) {
+// GGUF blocks of rows [row0, row0 + rows) -> the planar matrix at dst (one
+// thread per block; a one-time loader pass).
+__global__ void repack_rows_kernel(int type, const uint8_t* __restrict__ src, int rows, int cols, uint8_t* dst,
+                                   int row0, int row_step) {
+    const int nb = cols / QK;
     const long i = long(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= long(rows) * nb) return;
     const int bb = gguf_block_bytes(type), qb = quant_bytes_per_block(type);
     const uint8_t* s = src + i * bb;
-    const long o = first_block + i;
-    dh[o] = static_cast<uint16_t>(s[0] | (s[1] << 8));
-    uint8_t* q = qs + o * qb;
+    const size_t r = size_t(row0) + size_t(i / nb) * row_step, b = size_t(i % nb);
+    uint8_t* q = dst + planar_quant_at(type, cols, r, b);
     for (int j = 0; j < qb; ++j) q[j] = s[2 + j];
+    uint8_t* d = dst + planar_scale_at(type, cols, r, b);
+    d[0] = s[0];
+    d[1] = s[1];
 }
 
 // ---- seeded synthetic weights ---------------------------------------------
@@ -86,8 +81,9 @@ __device__ __forceinline__ float normal_at(uint64_t seed, uint64_t tensor, uint6
 
 // One thread per 32-weight block: generate, then ggml's reference quantizer
 // (quantize_row_q4_0_ref / quantize_row_q8_0_ref; quant/q8.hpp:54-69).
-__global__ void fill_random_q_kernel(int type, int rows, int nb, uint8_t* qs, uint16_t* dh, long first_block,
+__global__ void fill_random_q_kernel(int type, int rows, int cols, uint8_t* dst, int row0, int row_step,
                                      uint64_t seed, uint64_t tensor, float sigma) {
+    const int nb = cols / QK;
     const long i = long(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= long(rows) * nb) return;
     float x[QK];
@@ -97,12 +93,13 @@ __global__ void fill_random_q_kernel(int type, int rows, int nb, uint8_t* qs, ui
         const float a = fabsf(x[j]);
         if (amax < a) { amax = a; mx = x[j]; }
     }
-    const long o = first_block + i;
+    const size_t r = size_t(row0) + size_t(i / nb) * row_step, b = size_t(i % nb);
+    uint16_t* dh = reinterpret_cast<uint16_t*>(dst + planar_scale_at(type, cols, r, b));
     if (type == SYN_Q4_0) {
         const float d = __fdiv_rn(mx, -8.0f);
         const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-        dh[o] = f16_bits(d);
-        uint8_t* q = qs + o * 16;
+        *dh = f16_bits(d);
+        uint8_t* q = dst + planar_quant_at(type, cols, r, b);
         for (int j = 0; j < 16; ++j) {
             int lo = int(int8_t(__fadd_rn(__fmul_rn(x[j], id), 8.5f)));
             int hi = int(int8_t(__fadd_rn(__fmul_rn(x[16 + j], id), 8.5f)));
@@ -113,8 +110,8 @@ __global__ void fill_random_q_kernel(int type, int rows, int nb, uint8_t* qs, ui
     } else {
         const float d = __fdiv_rn(amax, 127.0f);
         const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-        dh[o] = f16_bits(d);
-        int8_t* q = reinterpret_cast<int8_t*>(qs + o * 32);
+        *dh = f16_bits(d);
+        int8_t* q = reinterpret_cast<int8_t*>(dst + planar_quant_at(type, cols, r, b));
         for (int j = 0; j < QK; ++j) q[j] = int8_t(roundf(__fmul_rn(x[j], id)));
     }
 }
@@ -136,27 +133,25 @@ bool quant_type(int type) { return type == SYN_Q4_0 || type == SYN_Q8_0; }
 
 }  // namespace
 
+int syn_planar_block_pos(int nb, size_t r, int b) { return planar_block_pos(nb, r, b); }
+
 int syn_repack_rows(int type, const void* src, int rows, int cols, void* dst, int total_rows, int row0,
-                    cudaStream_t s) {
+                    cudaStream_t s, int row_step) {
     if (!quant_type(type)) return SYN_ERR_UNSUPPORTED;
-    const int nb = cols / QK;
-    uint8_t* qs = static_cast<uint8_t*>(dst);
-    uint16_t* dh = reinterpret_cast<uint16_t*>(qs + planar_qs_bytes(type, total_rows, cols));
-    const long n = long(rows) * nb;
-    repack_rows_kernel<<<(n + 255) / 256, 256, 0, s>>>(type, static_cast<const uint8_t*>(src), rows, nb, qs, dh,
-                                                        long(row0) * nb);
+    if (row0 < 0 || row_step < 1 || long(row0) + long(rows - 1) * row_step >= total_rows) return SYN_ERR_INVALID;
+    const long n = long(rows) * (cols / QK);
+    repack_rows_kernel<<<(n + 255) / 256, 256, 0, s>>>(type, static_cast<const uint8_t*>(src), rows, cols,
+                                                        static_cast<uint8_t*>(dst), row0, row_step);
     return syn_check_launch();
 }
 
 int syn_fill_random(int type, int rows, int cols, void* dst, int total_rows, int row0, uint64_t seed,
-                    uint64_t tensor, float sigma, cudaStream_t s) {
+                    uint64_t tensor, float sigma, cudaStream_t s, int row_step) {
     if (quant_type(type)) {
-        const int nb = cols / QK;
-        uint8_t* qs = static_cast<uint8_t*>(dst);
-        uint16_t* dh = reinterpret_cast<uint16_t*>(qs + planar_qs_bytes(type, total_rows, cols));
-        const long n = long(rows) * nb;
-        fill_random_q_kernel<<<(n + 127) / 128, 128, 0, s>>>(type, rows, nb, qs, dh, long(row0) * nb, seed, tensor,
-                                                              sigma);
+        if (row0 < 0 || row_step < 1 || long(row0) + long(rows - 1) * row_step >= total_rows) return SYN_ERR_INVALID;
+        const long n = long(rows) * (cols / QK);
+        fill_random_q_kernel<<<(n + 127) / 128, 128, 0, s>>>(type, rows, cols, static_cast<uint8_t*>(dst), row0,
+                                                              row_step, seed, tensor, sigma);
     } else if (type == SYN_F32 || type == SYN_F16) {
         if (row0 != 0) return SYN_ERR_INVALID;
         fill_random_f_kernel<<<4096, 256, 0, s>>>(type, size_t(rows) * cols, dst, seed, tensor, sigma);
@@ -208,7 +203,7 @@ extern "C" size_t syn_weight_bytes(int type, int rows, int cols, int layout) {
     case SYN_Q8_0:
         if (cols % QK) return 0;
         if (layout == SYN_LAYOUT_GGUF) return size_t(rows) * (cols / QK) * gguf_block_bytes(type);
-        return planar_qs_bytes(type, rows, cols) + align256(size_t(rows) * (cols / QK) * 2);
+        return size_t(rows) * planar_row_bytes(type, cols);
     default: return 0;
     }
 }
@@ -231,19 +226,16 @@ extern "C" int syn_upload_weight(int type, const void* host_src, int rows, int c
         return syn_cuda_status(cudaStreamSynchronize(s));
     }
     if (!staging || staging_bytes < (1u << 20)) return SYN_ERR_INVALID;
-    const int bb = gguf_block_bytes(type), qb = quant_bytes_per_block(type);
-    const long n_blocks = long(rows) * (cols / QK);
-    const long per_chunk = long(staging_bytes / bb);
-    uint8_t* qs = static_cast<uint8_t*>(dst);
-    uint16_t* dh = reinterpret_cast<uint16_t*>(qs + planar_qs_bytes(type, rows, cols));
+    const size_t row_b = size_t(cols / QK) * gguf_block_bytes(type);
+    const int per = int(std::max<size_t>(1, staging_bytes / row_b));
+    if (row_b > staging_bytes) return SYN_ERR_INVALID;
     const uint8_t* h = static_cast<const uint8_t*>(host_src);
-    for (long b0 = 0; b0 < n_blocks; b0 += per_chunk) {
-        const long n = n_blocks - b0 < per_chunk ? n_blocks - b0 : per_chunk;
-        int st = syn_cuda_status(cudaMemcpyAsync(staging, h + b0 * bb, size_t(n) * bb, cudaMemcpyHostToDevice, s));
+    for (int r0 = 0; r0 < rows; r0 += per) {
+        const int n = rows - r0 < per ? rows - r0 : per;
+        int st = syn_cuda_status(cudaMemcpyAsync(staging, h + size_t(r0) * row_b, size_t(n) * row_b,
+                                                 cudaMemcpyHostToDevice, s));
         if (st) return st;
-        repack_kernel<<<(n + 255) / 256, 256, 0, s>>>(type, static_cast<const uint8_t*>(staging), n, qs + b0 * qb,
-                                                        dh + b0);
-        if ((st = syn_check_launch())) return st;
+        if ((st = syn_repack_rows(type, staging, n, cols, dst, rows, r0, s))) return st;
         if ((st = syn_cuda_status(cudaStreamSynchronize(s)))) return st;
     }
     return SYN_OK;

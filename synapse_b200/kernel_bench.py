@@ -11,7 +11,8 @@ attention: the fused RoPE + F16 append + split-KV attention (syn_attention)
 with H 32 / KV 8 / hd 128, theta 500000, caches of N(0,1) F16 at context L,
 batch 1/8/32.
 Each line: JSON with the average CUDA-event time per launch, the algorithmic
-bytes per launch and GB/s.
+bytes per launch and GB/s. Launches are captured with programmatic dependent
+launch as in the session's graphs (--no-pdl: without).
 """
 import argparse
 import ctypes
@@ -20,11 +21,46 @@ import math
 
 import numpy as np
 
-from . import LAYOUT_PLANAR, Q4_0, Q8_0, _ptr, _stream, attention, attention_scratch_bytes, check, empty_bytes, \
-    gemv_q, lib, q8_act_bytes, quantize_q8_0, weight_bytes
+from . import IN_F32, IN_Q8, IN_RMSNORM, LAYOUT_PLANAR, OUT_ROWS, OUT_SILU_PAIRS, Q4_0, Q8_0, GemvArgs, _ptr, \
+    _stream, attention, attention_scratch_bytes, check, empty_bytes, gemv_q, lib, q8_act_bytes, quantize_q8_0, \
+    rope_table, weight_bytes
 
 L2_BYTES = 126 << 20
 TYPES = {"q4_0": Q4_0, "q8_0": Q8_0}
+
+
+PDL = True
+
+
+def _graph_time(launch, iters):
+    """Average device time per launch: `iters` launches captured in one CUDA graph, replayed
+    twice (the second timed with CUDA events), so host launch overhead is not measured. With
+    PDL the launches are captured with programmatic dependent launch, as the session's step
+    graph captures them (a kernel's weight prefetch overlaps its predecessor's tail)."""
+    import torch
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    L = lib()
+    L.syn_set_programmatic_launch.argtypes = [ctypes.c_int]
+    L.syn_set_programmatic_launch.restype = None
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s, capture_error_mode="thread_local"):
+            L.syn_set_programmatic_launch(1 if PDL else 0)
+            try:
+                for i in range(iters):
+                    launch(i)
+            finally:
+                L.syn_set_programmatic_launch(0)
+    torch.cuda.current_stream().wait_stream(s)
+    g.replay()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    torch.cuda.synchronize()
+    ev[0].record()
+    g.replay()
+    ev[1].record()
+    ev[1].synchronize()
+    return ev[0].elapsed_time(ev[1]) / iters
 
 
 def _fill_random(type_, rows, cols, dst, seed):
@@ -38,7 +74,9 @@ def _fill_random(type_, rows, cols, dst, seed):
     check(fn(type_, rows, cols, ctypes.c_void_p(dst.data_ptr()), seed, _stream()), "fill")
 
 
-def bench_gemv(type_name, rows, cols, batch, iters=50):
+def bench_gemv(type_name, rows, cols, batch, iters=50, mode="q8"):
+    """mode: q8 (syn_gemv_q on Q8_0 activations), f32 (floats quantized inside the kernel), rmsnorm
+    (rms_norm + quantization inside), silu (rmsnorm input, rows taken as (gate, up) pairs)."""
     import torch
     ty = TYPES[type_name]
     wb = weight_bytes(ty, rows, cols, LAYOUT_PLANAR)
@@ -47,23 +85,30 @@ def bench_gemv(type_name, rows, cols, batch, iters=50):
     for i, w in enumerate(ws):
         _fill_random(ty, rows, cols, w, 1000 + i)
     x = torch.randn(batch, cols, device="cuda")
+    gamma = torch.ones(cols, device="cuda")
     act = quantize_q8_0(x)
-    y = torch.empty(batch, rows, device="cuda")
+    out_rows = rows // 2 if mode == "silu" else rows
+    y = torch.empty(batch, out_rows, device="cuda")
+    if mode == "q8":
+        def launch(i):
+            gemv_q(ty, ws[i % copies], LAYOUT_PLANAR, rows, cols, act, batch, y=y)
+    else:
+        in_mode = IN_F32 if mode == "f32" else IN_RMSNORM
+        out_mode = OUT_SILU_PAIRS if mode == "silu" else OUT_ROWS
+        args = [GemvArgs(ty, LAYOUT_PLANAR, rows, cols, batch, w.data_ptr(), in_mode, None, x.data_ptr(),
+                         gamma.data_ptr(), 1e-5, out_mode, y.data_ptr(), None) for w in ws]
+
+        def launch(i):
+            check(lib().syn_gemv(ctypes.byref(args[i % copies]), _stream()), "syn_gemv")
     for i in range(3 * copies):  # warm-up
-        gemv_q(ty, ws[i % copies], LAYOUT_PLANAR, rows, cols, act, batch, y=y)
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-    torch.cuda.synchronize()
-    ev[0].record()
-    for i in range(iters):
-        gemv_q(ty, ws[i % copies], LAYOUT_PLANAR, rows, cols, act, batch, y=y)
-    ev[1].record()
-    ev[1].synchronize()
-    ms = ev[0].elapsed_time(ev[1]) / iters
+        launch(i)
+    ms = _graph_time(launch, iters)
     nb = cols // 32
-    alg = rows * nb * (18 if ty == Q4_0 else 34) + batch * (cols + nb * 8) + batch * rows * 4
-    return {"kernel": "gemv_q", "type": type_name, "rows": rows, "cols": cols, "batch": batch,
-            "us_per_launch": round(ms * 1e3, 3), "bytes_per_launch": alg, "GBps": round(alg / (ms * 1e-3) / 1e9, 1),
-            "rotating_copies": copies}
+    act_bytes = batch * (cols + nb * 8) if mode == "q8" else batch * cols * 4 * (2 if mode != "f32" else 1)
+    alg = rows * nb * (18 if ty == Q4_0 else 34) + act_bytes + batch * out_rows * 4
+    return {"kernel": "gemv_q" if mode == "q8" else "gemv_" + mode, "type": type_name, "rows": rows, "cols": cols,
+            "batch": batch, "us_per_launch": round(ms * 1e3, 3), "bytes_per_launch": alg,
+            "GBps": round(alg / (ms * 1e-3) / 1e9, 1), "rotating_copies": copies}
 
 
 def bench_attention(ctx, batch, iters=20, n_head=32, n_kv=8, hd=128):
@@ -83,18 +128,12 @@ def bench_attention(ctx, batch, iters=20, n_head=32, n_kv=8, hd=128):
     scale = 1.0 / math.sqrt(hd)
     out = torch.empty(batch, n_head * hd, device="cuda")
     scratch = empty_bytes(attention_scratch_bytes(batch, n_head, n_kv, hd, ctx))
+    tab = rope_table(ctx, hd, ts)
+    run = lambda i: attention(q, k, v, kcs[i % copies], vcs[i % copies], pos, n_head, n_kv, hd, ctx, ts, scale,
+                              cache_stride=per_seq, out=out, scratch=scratch, rope_table=tab)
     for i in range(2 * copies):
-        attention(q, k, v, kcs[i % copies], vcs[i % copies], pos, n_head, n_kv, hd, ctx, ts, scale,
-                  cache_stride=per_seq, out=out, scratch=scratch)
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-    torch.cuda.synchronize()
-    ev[0].record()
-    for i in range(iters):
-        attention(q, k, v, kcs[i % copies], vcs[i % copies], pos, n_head, n_kv, hd, ctx, ts, scale,
-                  cache_stride=per_seq, out=out, scratch=scratch)
-    ev[1].record()
-    ev[1].synchronize()
-    ms = ev[0].elapsed_time(ev[1]) / iters
+        run(i)
+    ms = _graph_time(run, iters)
     alg = batch * (2 * ctx * row * 2 + n_head * hd * 8 + 2 * row * 4)
     return {"kernel": "attention", "ctx": ctx, "batch": batch, "heads": f"{n_head}/{n_kv}x{hd}",
             "us_per_launch": round(ms * 1e3, 3), "bytes_per_launch": alg, "GBps": round(alg / (ms * 1e-3) / 1e9, 1),
@@ -110,13 +149,24 @@ def main():
     p.add_argument("--batch", type=int, default=None)
     p.add_argument("--ctx", type=int, default=None)
     p.add_argument("--iters", type=int, default=None)
+    p.add_argument("--no-pdl", action="store_true", help="capture without programmatic dependent launch")
+    p.add_argument("--mode", default="q8", choices=["q8", "f32", "rmsnorm", "silu", "step"],
+                   help="gemv input/output fusion; step: the four fused GEMVs of an 8B layer")
     a = p.parse_args()
-    if a.what in ("gemv", "all"):
+    global PDL
+    PDL = not a.no_pdl
+    if a.what in ("gemv", "all") and a.mode == "step":
+        # the fused GEMVs of one Llama-3-8B layer: qkv (rms_norm in), o (f32 in), gate/up pairs, down (f32 in)
+        for t in ([a.type] if a.type else ["q4_0"]):
+            for mode, r, c in (("rmsnorm", 6144, 4096), ("f32", 4096, 4096), ("silu", 28672, 4096),
+                               ("f32", 4096, 14336)):
+                print(json.dumps(bench_gemv(t, r, c, 1, a.iters or 50, mode)), flush=True)
+    elif a.what in ("gemv", "all"):
         shapes = [(a.rows, a.cols)] if a.rows else [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)]
         for t in ([a.type] if a.type else ["q4_0", "q8_0"]):
             for r, c in shapes:
                 for n in ([a.batch] if a.batch else [1, 4, 16]):
-                    print(json.dumps(bench_gemv(t, r, c, n, a.iters or 50)), flush=True)
+                    print(json.dumps(bench_gemv(t, r, c, n, a.iters or 50, a.mode)), flush=True)
     if a.what in ("attention", "all"):
         for L in ([a.ctx] if a.ctx else [1024, 4096, 16384, 32768]):
             for b in ([a.batch] if a.batch else [1, 8, 32]):

@@ -47,9 +47,11 @@ def test_size_queries_without_gpu():
     assert syn.q8_act_bytes(1, 4096) == 4096 + 256 + 512 + 512
     assert syn.q8_act_bytes(1, 33) == 0
     assert syn.weight_bytes(syn.Q4_0, 4096, 4096, syn.LAYOUT_GGUF) == 4096 * 128 * 18
-    assert syn.weight_bytes(syn.Q4_0, 4096, 4096, syn.LAYOUT_PLANAR) == 4096 * 128 * 16 + 4096 * 128 * 2
-    assert syn.weight_bytes(syn.Q8_0, 3, 64, syn.LAYOUT_PLANAR) == 256 + 256
-    assert syn.attention_scratch_bytes(1, 32, 8, 128, 4096) > 32 * 4096 * 4
+    # planar rows: quants, then binary16 scales padded to 16 bytes
+    assert syn.weight_bytes(syn.Q4_0, 4096, 4096, syn.LAYOUT_PLANAR) == 4096 * (128 * 16 + 128 * 2)
+    assert syn.weight_bytes(syn.Q8_0, 3, 64, syn.LAYOUT_PLANAR) == 3 * (2 * 32 + 16)
+    assert syn.weight_bytes(syn.Q4_0, 2, 288, syn.LAYOUT_PLANAR) == 2 * (9 * 16 + 32)
+    assert syn.attention_scratch_bytes(1, 32, 8, 128, 4096) >= 32 * 4096 * 4
 
 
 @pytest.mark.parametrize("ty", [model.Q4_0, model.Q8_0])

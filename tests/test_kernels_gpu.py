@@ -4,6 +4,7 @@ Tolerances are the north star's: GEMV and attention outputs within 1e-3
 relative L2 of the oracle on identical inputs (the same Q8_0 activations);
 the Q8_0 quantizer, the F16 cache rows and argmax are bit-exact.
 """
+import ctypes
 import math
 
 import numpy as np
@@ -113,6 +114,98 @@ def test_gemv_residual_epilogue():
     assert np.array_equal(y1, (y0 + r).astype(np.float32))  # in place, one float add as op_add
 
 
+# ---------------------------------------------------------------- fused GEMV (syn_gemv)
+
+FUSED_SHAPES = [(288, 288, 1), (768, 288, 2), (6144, 4096, 1), (4096, 4096, 2), (4096, 14336, 1), (1000, 2048, 2)]
+
+
+def same_bits(a, b):
+    return np.array_equal(np.asarray(a).view(np.uint32), np.asarray(b).view(np.uint32))
+
+
+@pytest.mark.parametrize("ty", [syn.Q4_0, syn.Q8_0])
+@pytest.mark.parametrize("rows,cols,n_tok", FUSED_SHAPES)
+def test_gemv_fused_f32_input_matches_separate_ops(ty, rows, cols, n_tok):
+    # gemm_prepare_rows inside the GEMV, then op_add: bit-identical to quantize -> gemv_q -> add
+    rng = np.random.default_rng(rows + cols + n_tok)
+    w = orc.quantize_weights(random_weights(rng, rows, cols), ty)
+    x = dev(rng.standard_normal((n_tok, cols), dtype=np.float32))
+    r = dev(rng.standard_normal((n_tok, rows), dtype=np.float32))
+    wd = syn.upload_weight(ty, w, rows, cols)
+    want = syn.gemv_q(ty, wd, syn.LAYOUT_PLANAR, rows, cols, syn.quantize_q8_0(x), n_tok, residual=r)
+    got = syn.gemv_fused(ty, wd, rows, cols, x, in_mode=syn.IN_F32, residual=r)
+    assert same_bits(got.cpu().numpy(), want.cpu().numpy())
+    # and the oracle's separate ops on the host
+    blocks = orc.quantize_q8_0(x.cpu().numpy())
+    for t in range(n_tok):
+        ref = orc.gemv_q8act(ty, w, rows, cols, blocks[t]) + r.cpu().numpy()[t]
+        assert same_bits(got.cpu().numpy()[t], ref.astype(np.float32))
+
+
+@pytest.mark.parametrize("ty", [syn.Q4_0, syn.Q8_0])
+@pytest.mark.parametrize("rows,cols,n_tok", FUSED_SHAPES)
+def test_gemv_fused_rms_norm_matches_separate_ops(ty, rows, cols, n_tok):
+    # op_rms_norm -> op_matmul in one kernel (every CTA normalizes the row it needs)
+    rng = np.random.default_rng(3 * rows + cols + n_tok)
+    w = orc.quantize_weights(random_weights(rng, rows, cols), ty)
+    xh = (2.0 * rng.standard_normal((n_tok, cols))).astype(np.float32)
+    gh = (1.0 + 0.1 * rng.standard_normal(cols)).astype(np.float32)
+    x, gamma = dev(xh), dev(gh)
+    wd = syn.upload_weight(ty, w, rows, cols)
+    _, act = syn.rms_norm(x, gamma, 1e-5, want_f32=False, want_act=True)
+    want = syn.gemv_q(ty, wd, syn.LAYOUT_PLANAR, rows, cols, act, n_tok)
+    got = syn.gemv_fused(ty, wd, rows, cols, x, in_mode=syn.IN_RMSNORM, gamma=gamma, eps=1e-5)
+    assert same_bits(got.cpu().numpy(), want.cpu().numpy())
+    for t in range(n_tok):
+        h = orc.rms_norm(xh[t], gh, np.float32(1e-5))
+        ref = orc.gemv_q8act(ty, w, rows, cols, orc.quantize_q8_0(h[None, :])[0])
+        assert same_bits(got.cpu().numpy()[t], ref)
+
+
+def interleave_rows(a, b, rows, cols, ty):
+    """Rows of a and b alternating (a0, b0, a1, b1, ...) as GGUF bytes."""
+    rb = (cols // 32) * (18 if ty == syn.Q4_0 else 34)
+    out = np.empty((2 * rows, rb), np.uint8)
+    out[0::2] = a.reshape(rows, rb)
+    out[1::2] = b.reshape(rows, rb)
+    return out.reshape(-1)
+
+
+@pytest.mark.parametrize("ty", [syn.Q4_0, syn.Q8_0])
+@pytest.mark.parametrize("ff,cols,n_tok", [(384, 288, 1), (768, 288, 2), (14336, 4096, 1), (2048, 4096, 2)])
+def test_gemv_fused_silu_pairs_matches_separate_ops(ty, ff, cols, n_tok):
+    # gate and up rows interleaved in one matrix: rms_norm -> matmul -> silu(gate) * up in one kernel
+    rng = np.random.default_rng(ff + cols + n_tok)
+    wg = orc.quantize_weights(random_weights(rng, ff, cols), ty)
+    wu = orc.quantize_weights(random_weights(rng, ff, cols), ty)
+    xh = rng.standard_normal((n_tok, cols), dtype=np.float32)
+    gh = (1.0 + 0.1 * rng.standard_normal(cols)).astype(np.float32)
+    x, gamma = dev(xh), dev(gh)
+    wgu = syn.upload_weight(ty, interleave_rows(wg, wu, ff, cols, ty), 2 * ff, cols)
+    assert syn.lib().syn_gemv_fusable(ty, syn.LAYOUT_PLANAR, 2 * ff, cols, n_tok, syn.OUT_SILU_PAIRS) == 1
+    got = syn.gemv_fused(ty, wgu, 2 * ff, cols, x, in_mode=syn.IN_RMSNORM, gamma=gamma, eps=1e-5,
+                         out_mode=syn.OUT_SILU_PAIRS).cpu().numpy()
+    _, act = syn.rms_norm(x, gamma, 1e-5, want_f32=False, want_act=True)
+    g = syn.gemv_q(ty, syn.upload_weight(ty, wg, ff, cols), syn.LAYOUT_PLANAR, ff, cols, act, n_tok)
+    u = syn.gemv_q(ty, syn.upload_weight(ty, wu, ff, cols), syn.LAYOUT_PLANAR, ff, cols, act, n_tok)
+    want, _ = syn.silu_mul(g, u, want_f32=True, want_act=False)
+    assert got.shape == (n_tok, ff)
+    assert same_bits(got, want.cpu().numpy())
+
+
+def test_gemv_fused_rejects_what_it_cannot_take():
+    rows, cols = 64, 512
+    wd = syn.empty_bytes(syn.weight_bytes(syn.Q4_0, rows, cols, syn.LAYOUT_GGUF))
+    x = torch.zeros(1, cols, device="cuda")
+    a = syn.GemvArgs(syn.Q4_0, syn.LAYOUT_GGUF, rows, cols, 1, wd.data_ptr(), syn.IN_F32, None, x.data_ptr(),
+                     None, 1e-5, syn.OUT_ROWS, x.data_ptr(), None)
+    assert syn.lib().syn_gemv(ctypes.byref(a), syn._stream()) == 2  # SYN_ERR_UNSUPPORTED: fused modes need planar rows
+    assert syn.lib().syn_gemv_fusable(syn.Q4_0, syn.LAYOUT_PLANAR, 63, cols, 1, syn.OUT_SILU_PAIRS) == 0
+    assert syn.lib().syn_gemv_fusable(syn.Q4_0, syn.LAYOUT_PLANAR, rows, cols, 3, syn.OUT_ROWS) == 0
+    a.layout, a.in_mode = syn.LAYOUT_PLANAR, syn.IN_RMSNORM  # rms_norm without gamma
+    assert syn.lib().syn_gemv(ctypes.byref(a), syn._stream()) == 1
+
+
 @pytest.mark.parametrize("ty", [syn.F32, syn.F16])
 @pytest.mark.parametrize("rows,cols,n_tok", [(32000, 288, 1), (128, 64, 1), (100, 130, 3), (512, 4096, 2)])
 def test_gemv_plain(ty, rows, cols, n_tok):
@@ -136,8 +229,7 @@ def test_repack_matches_upload():
     p2 = syn.empty_bytes(syn.weight_bytes(syn.Q4_0, rows, cols))
     p2.zero_()
     syn.check(syn.lib().syn_repack_planar(syn.Q4_0, syn._ptr(g), rows, cols, syn._ptr(p2), syn._stream()), "repack")
-    nq = rows * cols // 32 * 16
-    assert torch.equal(p[:nq].cpu(), p2[:nq].cpu())
+    assert torch.equal(p.cpu(), p2.cpu())
 
 
 def test_gemv_rejects_bad_args():
@@ -276,6 +368,44 @@ def test_rope_matches_oracle():
         ref = orc.rope(x[i], hd, int(pos[i]), ts)
         assert np.max(np.abs(got[i] - ref)) <= 1e-5 * (1 + pos[i])
         assert np.max(np.abs(got[i] - ref)) <= 4e-6 * np.max(np.abs(ref))
+
+
+# ---------------------------------------------------------------- expf
+
+def test_exp_rn_is_correctly_rounded():
+    # the float-float expf against exp in double rounded once: equal but within
+    # 2^-20 ulp of a rounding midpoint, and never more than one ulp apart
+    rng = np.random.default_rng(5)
+    x = np.concatenate([rng.uniform(-87.0, 88.7, 1 << 22), rng.uniform(-30.0, 0.0, 1 << 22),
+                        np.float32([0.0, -0.0, 1e-30, -1e-30, 88.72, -86.99, 0.5, -0.5])]).astype(np.float32)
+    xd = dev(x)
+    y, yr = torch.empty_like(xd), torch.empty_like(xd)
+    syn.lib().syn_check_exp.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int, ctypes.c_void_p]
+    assert syn.lib().syn_check_exp(xd.data_ptr(), y.data_ptr(), yr.data_ptr(), x.size, syn._stream()) == 0
+    a = y.cpu().numpy().view(np.int32).astype(np.int64)
+    b = yr.cpu().numpy().view(np.int32).astype(np.int64)
+    diff = np.abs(a - b)
+    assert diff.max() <= 1
+    assert np.count_nonzero(diff) <= x.size * 1e-5, np.count_nonzero(diff)
+    # and the C runtime's expf (the oracle's) on a sample
+    assert np.max(np.abs(y.cpu().numpy()[:4096] - np.exp(x[:4096].astype(np.float64)).astype(np.float32))
+                  / np.exp(x[:4096].astype(np.float64))) < 1.2e-7
+
+
+def test_attention_rope_table_matches_inline_rope():
+    n_head, n_kv, hd, L = 32, 8, 128, 700
+    ts = 500000.0 ** (-2.0 / hd)
+    g = torch.Generator(device="cpu").manual_seed(4)
+    row = n_kv * hd
+    kc = torch.randn(L * row, generator=g).half().view(torch.int16).cuda()
+    vc = torch.randn(L * row, generator=g).half().view(torch.int16).cuda()
+    q, k, v = (torch.randn(1, n, generator=g).cuda() for n in (n_head * hd, row, row))
+    pos = torch.full((1,), L - 1, dtype=torch.int32).cuda()
+    kc2, vc2 = kc.clone(), vc.clone()
+    tab = syn.rope_table(L, hd, ts)
+    a = syn.attention(q, k, v, kc, vc, pos, n_head, n_kv, hd, L, ts, 1 / math.sqrt(hd))
+    b = syn.attention(q, k, v, kc2, vc2, pos, n_head, n_kv, hd, L, ts, 1 / math.sqrt(hd), rope_table=tab)
+    assert torch.equal(a, b) and torch.equal(kc, kc2) and torch.equal(vc, vc2)
 
 
 # ---------------------------------------------------------------- element-wise
