@@ -164,7 +164,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnParams a)
     // by the caller, never by the kernel this one may overlap: read before the wait.
     const int P = a.pos[b], L = P + 1;
     if (P < 0 || L > a.max_len) return;  // the whole cluster (same query) leaves together
-    const int chunk = (L + C - 1) / C;
+    // A context of up to kExactChunk positions stays in CTA 0: p.V in the
+    // reference's position order (the other CTAs idle).
+    const int chunk = L <= kExactChunk ? L : (L + C - 1) / C;
     const int t0 = min(L, j * chunk), t1 = min(L, t0 + chunk), n = t1 - t0;
     const bool owns = a.append && t0 <= P && P < t1;
 

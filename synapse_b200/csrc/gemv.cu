@@ -18,7 +18,7 @@
 //
 // Rows are split in contiguous ranges over a persistent grid (SMs x resident
 // CTAs), so every SM streams the same number of bytes.
-#include "common.cuh"
+#include "gemv_core.cuh"
 
 #include <algorithm>
 #include <mutex>
@@ -72,33 +72,6 @@ __device__ __forceinline__ void load_block(const GemvArgs& p, int r, int b, uint
 #pragma unroll
         for (int k = 0; k < words; ++k) w[k] = uint32_t(__ldg(s + 1 + 2 * k)) | (uint32_t(__ldg(s + 2 + 2 * k)) << 16);
     }
-}
-
-template <int TYPE>
-__device__ __forceinline__ int block_dot(const uint32_t (&w)[8], const int4 a0, const int4 a1, int asum) {
-    int s = 0;
-    if (TYPE == SYN_Q4_0) {
-        // byte j: low nibble = weight j, high nibble = weight j + 16 (blocks.hpp:36-40)
-        s = __dp4a(int(w[0] & 0x0f0f0f0fu), a0.x, s);
-        s = __dp4a(int(w[1] & 0x0f0f0f0fu), a0.y, s);
-        s = __dp4a(int(w[2] & 0x0f0f0f0fu), a0.z, s);
-        s = __dp4a(int(w[3] & 0x0f0f0f0fu), a0.w, s);
-        s = __dp4a(int((w[0] >> 4) & 0x0f0f0f0fu), a1.x, s);
-        s = __dp4a(int((w[1] >> 4) & 0x0f0f0f0fu), a1.y, s);
-        s = __dp4a(int((w[2] >> 4) & 0x0f0f0f0fu), a1.z, s);
-        s = __dp4a(int((w[3] >> 4) & 0x0f0f0f0fu), a1.w, s);
-        s -= 8 * asum;
-    } else {
-        s = __dp4a(int(w[0]), a0.x, s);
-        s = __dp4a(int(w[1]), a0.y, s);
-        s = __dp4a(int(w[2]), a0.z, s);
-        s = __dp4a(int(w[3]), a0.w, s);
-        s = __dp4a(int(w[4]), a1.x, s);
-        s = __dp4a(int(w[5]), a1.y, s);
-        s = __dp4a(int(w[6]), a1.z, s);
-        s = __dp4a(int(w[7]), a1.w, s);
-    }
-    return s;
 }
 
 // Per warp shared memory: (isum, scale) per token per staged block (block b at
@@ -224,106 +197,6 @@ __global__ void __launch_bounds__(kThreads) gemv_q_kernel(GemvArgs p) {
 // 8 blocks, so the sub-lanes' 16-byte reads spread over the banks.
 __device__ unsigned g_gemv_timeouts = 0;  // bounded waits that gave up (syn_device_errors; none here)
 
-__host__ __device__ inline size_t a16(size_t n) { return (n + 15) & ~size_t(15); }
-__host__ __device__ inline size_t act_pad_off(int b) { return size_t(b) * QK + size_t(b >> 3) * 16; }
-__host__ __device__ inline size_t act_pad_stride(int nb) { return a16(act_pad_off(nb)); }
-// The staged kernel's activation layout: 16 bytes of padding after every 4 blocks.
-__host__ __device__ inline size_t sact_off(int b) { return size_t(b) * QK + size_t(b >> 2) * 16; }
-// Shared memory of the lane kernel: NT padded quant rows, then (d, sum) per token and block.
-__host__ __device__ inline size_t lane_act_bytes(int nt, int nb) {
-    return size_t(nt) * act_pad_stride(nb) + size_t(nt) * nb * 8;
-}
-
-// The activations made in the kernel: every CTA quantizes the float input
-// (SYN_IN_F32), or its rms_norm (SYN_IN_RMSNORM), into shared memory with the
-// exact arithmetic of syn_quantize_q8_0 / syn_rms_norm (quant/q8.hpp:54-69,
-// elementwise.hpp:208-232), one 32-value block per thread.
-// LAYOUT 1: the lane kernel's (16 bytes after every 8 blocks); 2: the staged
-// kernel's (16 bytes after every 4 blocks).
-template <int NT, int LAYOUT = 1>
-__device__ void prologue_quantize(const GemvArgs& p, uint8_t* aq, float2* dsum) {
-    __shared__ double red[NT * (kThreads / 32)];
-    __shared__ float scale_t[NT];
-    const int cols = p.cols, nb = p.nb, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const size_t stride = act_pad_stride(nb);
-    if (p.in_mode == SYN_IN_RMSNORM) {
-        // Sum of squares per token: each thread's blocks with all eight
-        // 16-byte loads of a block in flight at once, then one block reduction.
-        double part[NT];
-#pragma unroll
-        for (int t = 0; t < NT; ++t) part[t] = 0.0;
-        for (int blk = threadIdx.x; blk < NT * nb; blk += blockDim.x) {
-            const int t = blk / nb, b = blk % nb;
-            const float4* src = reinterpret_cast<const float4*>(p.x + size_t(t) * cols + size_t(b) * QK);
-            float4 f[QK / 4];
-#pragma unroll
-            for (int k = 0; k < QK / 4; ++k) f[k] = src[k];
-            double sum = 0.0;
-#pragma unroll
-            for (int k = 0; k < QK / 4; ++k) {
-                sum += double(__fmul_rn(f[k].x, f[k].x));
-                sum += double(__fmul_rn(f[k].y, f[k].y));
-                sum += double(__fmul_rn(f[k].z, f[k].z));
-                sum += double(__fmul_rn(f[k].w, f[k].w));
-            }
-#pragma unroll
-            for (int tt = 0; tt < NT; ++tt)
-                if (tt == t) part[tt] += sum;
-        }
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-            const double w = warp_sum_d(part[t]);
-            if (lane == 0) red[t * (kThreads / 32) + warp] = w;
-        }
-        __syncthreads();
-        if (threadIdx.x < NT) {
-            double tot = 0.0;
-            for (int w = 0; w < int(blockDim.x >> 5); ++w) tot += red[threadIdx.x * (kThreads / 32) + w];
-            const float mean = float(tot / double(cols));
-            scale_t[threadIdx.x] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
-        }
-        __syncthreads();
-    }
-    // Quantize one block per thread in two passes over its 32 values (the
-    // second reads them again from L1), so few registers stay live.
-    const bool norm = p.in_mode == SYN_IN_RMSNORM;
-    for (int blk = threadIdx.x; blk < NT * nb; blk += blockDim.x) {
-        const int t = blk / nb, b = blk % nb;
-        const float4* src = reinterpret_cast<const float4*>(p.x + size_t(t) * cols + size_t(b) * QK);
-        const float4* g4 = reinterpret_cast<const float4*>(p.gamma + size_t(b) * QK);
-        const float sc = norm ? scale_t[t] : 1.0f;
-        auto value = [&](float x, float g) { return norm ? __fmul_rn(__fmul_rn(x, sc), g) : x; };
-        float amax = 0.0f;
-#pragma unroll
-        for (int k = 0; k < QK / 4; ++k) {
-            const float4 f = src[k];
-            const float4 g = norm ? __ldg(g4 + k) : make_float4(1.0f, 1.0f, 1.0f, 1.0f);
-            amax = fmaxf(amax, fabsf(value(f.x, g.x)));
-            amax = fmaxf(amax, fabsf(value(f.y, g.y)));
-            amax = fmaxf(amax, fabsf(value(f.z, g.z)));
-            amax = fmaxf(amax, fabsf(value(f.w, g.w)));
-        }
-        const float d = __fdiv_rn(amax, 127.0f);
-        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-        int qsum = 0;
-        uint32_t* dst = reinterpret_cast<uint32_t*>(aq + size_t(t) * stride +
-                                                    (LAYOUT == 1 ? act_pad_off(b) : sact_off(b)));
-#pragma unroll
-        for (int k = 0; k < QK / 4; ++k) {
-            const float4 f = src[k];
-            const float4 g = norm ? __ldg(g4 + k) : make_float4(1.0f, 1.0f, 1.0f, 1.0f);
-            const int q0 = int(roundf(__fmul_rn(value(f.x, g.x), id)));
-            const int q1 = int(roundf(__fmul_rn(value(f.y, g.y), id)));
-            const int q2 = int(roundf(__fmul_rn(value(f.z, g.z), id)));
-            const int q3 = int(roundf(__fmul_rn(value(f.w, g.w), id)));
-            qsum += q0 + q1 + q2 + q3;
-            dst[k] = (uint32_t(q0) & 0xffu) | ((uint32_t(q1) & 0xffu) << 8) | ((uint32_t(q2) & 0xffu) << 16) |
-                     ((uint32_t(q3) & 0xffu) << 24);
-        }
-        dsum[t * nb + b] = make_float2(f16_from_bits(f16_bits(d)), __int_as_float(qsum));
-    }
-}
-
 // S sub-lanes per chunk; BPL = 32 / S blocks per lane.
 template <int TYPE, int NT, int S>
 __global__ void __launch_bounds__(kThreads, 2) gemv_lane_kernel(GemvArgs p) {
@@ -355,7 +228,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_lane_kernel(GemvArgs p) {
         for (int i = threadIdx.x; i < NT * nb; i += blockDim.x)
             dsum[i] = make_float2(__ldg(p.act.d + i), __int_as_float(__ldg(p.act.sum + i)));
     } else {
-        prologue_quantize<NT>(p, aq, dsum);
+        quantize_act<NT, 1>(p.x, p.gamma, p.eps, p.in_mode == SYN_IN_RMSNORM, p.cols, aq, dsum);
     }
     __syncthreads();
 
@@ -474,36 +347,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_lane_kernel(GemvArgs p) {
 // The activations (Q8_0, padded 16 bytes per 4 blocks so consecutive lanes'
 // 32-byte reads spread over the banks) sit in shared memory once per CTA.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
-constexpr int kStageWarps = 8;
-constexpr size_t kBatchBytes = 9728;  // target bytes of weights per batch
-
-struct StageShape {
-    int nb, nch, R;                          // blocks, chunks per row; rows per batch
-    size_t row_b, batch_bytes, act_bytes, stage_floats2, warp_bytes, smem;
-};
-
-__host__ __device__ inline StageShape stage_shape(int type, int cols) {
-    StageShape s;
-    s.nb = cols / QK;
-    s.nch = (s.nb + 31) / 32;
-    s.row_b = planar_row_bytes(type, cols);
-    int R = int(kBatchBytes / s.row_b);
-    if (R < 1) R = 1;
-    const int rmax = s.nch >= 32 ? 1 : 32 / s.nch;  // every (row, chunk) chain gets a lane
-    if (R > rmax) R = rmax;
-    if (R > 1 && (R & 1)) --R;                       // even: gate/up pairs stay in one batch
-    s.R = R;
-    s.batch_bytes = size_t(R) * s.row_b;
-    s.act_bytes = a16(a16(sact_off(s.nb)) + size_t(s.nb) * 8);
-    s.stage_floats2 = size_t(R) * (s.nb + s.nch);    // one float2 of padding per chunk
-    s.warp_bytes = 32 + 2 * s.batch_bytes + a16(s.stage_floats2 * 8) + a16(size_t(R) * s.nch * 4);
-    s.smem = s.act_bytes + kStageWarps * s.warp_bytes;
-    return s;
-}
 
 template <int TYPE>
 __global__ void __launch_bounds__(kStageWarps * 32) gemv_stage_kernel(GemvArgs p) {
-    constexpr int QB = TYPE == SYN_Q4_0 ? 16 : 32;
     extern __shared__ __align__(128) unsigned char smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const StageShape sh = stage_shape(TYPE, p.cols);
@@ -516,8 +362,6 @@ __global__ void __launch_bounds__(kStageWarps * 32) gemv_stage_kernel(GemvArgs p
     unsigned char* buf = wbase + 32;
     float2* stage = reinterpret_cast<float2*>(buf + 2 * sh.batch_bytes);
     float* chsum = reinterpret_cast<float*>(buf + 2 * sh.batch_bytes + a16(sh.stage_floats2 * 8));
-    const int spr = nb + nch;  // staged pairs per row
-
     const long n_batch = (p.rows + R - 1) / R;
     const long gw = long(blockIdx.x) * kStageWarps + warp, nw = long(gridDim.x) * kStageWarps;
     const long k0 = n_batch * gw / nw, k1 = n_batch * (gw + 1) / nw;
@@ -544,7 +388,7 @@ __global__ void __launch_bounds__(kStageWarps * 32) gemv_stage_kernel(GemvArgs p
         for (int i = threadIdx.x; i < nb; i += blockDim.x)
             dsum[i] = make_float2(__ldg(p.act.d + i), __int_as_float(__ldg(p.act.sum + i)));
     } else {
-        prologue_quantize<1, 2>(p, aq, dsum);
+        quantize_act1(p.x, p.gamma, p.eps, p.in_mode == SYN_IN_RMSNORM, p.cols, aq, dsum);
     }
     __syncthreads();
 
@@ -557,58 +401,14 @@ __global__ void __launch_bounds__(kStageWarps * 32) gemv_stage_kernel(GemvArgs p
             break;
         }
         const int rows_k = batch_rows(k);
-        const unsigned char* bb = buf + size_t(k & 1) * sh.batch_bytes;
-        // blocks: every (row, block) pair of the batch, lane-parallel
-        for (int r = 0; r < rows_k; ++r) {
-            const unsigned char* wr = bb + size_t(r) * row_b;
-#pragma unroll 4
-            for (int b = lane; b < nb; b += 32) {
-                uint32_t w[8];
-                const uint4 v0 = *reinterpret_cast<const uint4*>(wr + size_t(b) * QB);
-                w[0] = v0.x; w[1] = v0.y; w[2] = v0.z; w[3] = v0.w;
-                if (QB == 32) {
-                    const uint4 v1 = *reinterpret_cast<const uint4*>(wr + size_t(b) * QB + (QB - 16));
-                    w[4] = v1.x; w[5] = v1.y; w[6] = v1.z; w[7] = v1.w;
-                }
-                const float dw = f16_from_bits(*reinterpret_cast<const uint16_t*>(wr + qbytes + size_t(b) * 2));
-                const int4* ap = reinterpret_cast<const int4*>(aq + sact_off(b));
-                const float2 ds = dsum[b];
-                const int isum = block_dot<TYPE>(w, ap[0], ap[1], TYPE == SYN_Q4_0 ? __float_as_int(ds.y) : 0);
-                stage[r * spr + b + (b >> 5)] = make_float2(float(isum), __fmul_rn(dw, ds.x));
-            }
-        }
-        __syncwarp();
-        // chains: one lane per (row, chunk)
-        for (int ch = lane; ch < rows_k * nch; ch += 32) {
-            const int r = ch / nch, c = ch - r * nch;
-            const int m = min(32, nb - 32 * c);
-            const float2* sp = stage + r * spr + 33 * c;
-            float acc = 0.0f;
-            if (m == 32) {
-#pragma unroll 8
-                for (int j = 0; j < 32; ++j) {
-                    const float2 v = sp[j];
-                    acc = fmaf(v.x, v.y, acc);
-                }
-            } else {
-                for (int j = 0; j < m; ++j) {
-                    const float2 v = sp[j];
-                    acc = fmaf(v.x, v.y, acc);
-                }
-            }
-            chsum[ch] = acc;
-        }
-        __syncwarp();
-        // rows: chunks in order
-        float y = 0.0f;
+        stage_batch<TYPE>(buf + size_t(k & 1) * sh.batch_bytes, rows_k, sh, qbytes, aq, dsum, stage, chsum, lane);
+        const float y = stage_row(chsum, nch, rows_k, lane);
         const long row = (k0 + k) * R + lane;
-        if (lane < rows_k)
-            for (int c = 0; c < nch; ++c) y = __fadd_rn(y, chsum[lane * nch + c]);
         if (p.out_mode == SYN_OUT_SILU_PAIRS) {
             // rows 2i (gate) and 2i+1 (up) are lanes l, l+1 of the batch: out[i] = silu(gate) * up
             const float up = __shfl_down_sync(0xffffffffu, y, 1);
             if (lane < rows_k && (lane & 1) == 0)
-                p.y[size_t(row / 2)] = __fmul_rn(__fdiv_rn(y, __fadd_rn(1.0f, exp_rn(-y))), up);
+                p.y[size_t(row / 2)] = silu_mul1(y, up);
         } else if (lane < rows_k) {
             p.y[row] = p.residual ? __fadd_rn(y, p.residual[row]) : y;
         }
