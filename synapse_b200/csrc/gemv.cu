@@ -348,11 +348,12 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_lane_kernel(GemvArgs p) {
 // 32-byte reads spread over the banks) sit in shared memory once per CTA.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
-template <int TYPE>
-__global__ void __launch_bounds__(kStageWarps * 32) gemv_stage_kernel(GemvArgs p) {
+// W warps per CTA, batches of about BB bytes of rows.
+template <int TYPE, int W, int BB>
+__global__ void __launch_bounds__(W * 32) gemv_stage_kernel(GemvArgs p) {
     extern __shared__ __align__(128) unsigned char smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const StageShape sh = stage_shape(TYPE, p.cols);
+    const StageShape sh = stage_shape(TYPE, p.cols, W, BB);
     const int nb = sh.nb, nch = sh.nch, R = sh.R;
     const size_t row_b = sh.row_b, qbytes = planar_quant_bytes(TYPE, p.cols);
     uint8_t* aq = smem;
@@ -363,7 +364,7 @@ __global__ void __launch_bounds__(kStageWarps * 32) gemv_stage_kernel(GemvArgs p
     float2* stage = reinterpret_cast<float2*>(buf + 2 * sh.batch_bytes);
     float* chsum = reinterpret_cast<float*>(buf + 2 * sh.batch_bytes + a16(sh.stage_floats2 * 8));
     const long n_batch = (p.rows + R - 1) / R;
-    const long gw = long(blockIdx.x) * kStageWarps + warp, nw = long(gridDim.x) * kStageWarps;
+    const long gw = long(blockIdx.x) * W + warp, nw = long(gridDim.x) * W;
     const long k0 = n_batch * gw / nw, k1 = n_batch * (gw + 1) / nw;
     const int nbatch = int(k1 - k0);
     auto batch_rows = [&](int k) { return int(min(long(R), long(p.rows) - (k0 + k) * R)); };
@@ -559,26 +560,47 @@ int launch_lane(const GemvArgs& p, int S, cudaStream_t s) {
     return SYN_ERR_UNSUPPORTED;
 }
 
+// Configuration of the staged kernel per shape: warps per CTA and batch bytes.
+struct StageCfg {
+    int warps;
+    int batch;
+};
+StageCfg stage_cfg(int type, int rows, int cols) {
+    (void)type;
+    (void)rows;
+    (void)cols;
+    return {8, 9728};
+}
+
 // Whether the staged kernel takes this one-token shape (gate/up pairs need
 // even batches).
 bool stage_ok(int type, int rows, int cols, int out_mode) {
-    const StageShape sh = stage_shape(type, cols);
+    const StageCfg cfg = stage_cfg(type, rows, cols);
+    const StageShape sh = stage_shape(type, cols, cfg.warps, size_t(cfg.batch));
     if (sh.smem > 200 * 1024) return false;
     if (out_mode == SYN_OUT_SILU_PAIRS && (sh.R % 2 || rows % 2)) return false;
     return true;
 }
 
-template <int TYPE>
-int launch_stage(const GemvArgs& p, cudaStream_t s) {
-    auto k = gemv_stage_kernel<TYPE>;
-    const StageShape sh = stage_shape(TYPE, p.cols);
+template <int TYPE, int W, int BB>
+int launch_stage_cfg(const GemvArgs& p, cudaStream_t s) {
+    auto k = gemv_stage_kernel<TYPE, W, BB>;
+    const StageShape sh = stage_shape(TYPE, p.cols, W, BB);
     int st = configure(reinterpret_cast<const void*>(k), sh.smem);
     if (st) return st;
-    // One CTA of 8 warps per SM (measured best: 16 KB of weights in flight
-    // per warp, chains and rows of 8 warps interleaved).
+    // One CTA per SM (W warps streaming ~BB-byte batches of rows each).
     const long batches = (p.rows + sh.R - 1) / sh.R;
-    const long grid = std::max<long>(1, std::min<long>(long(syn_num_sms()), (batches + kStageWarps - 1) / kStageWarps));
-    return syn_launch(k, unsigned(grid), unsigned(kStageWarps * 32), sh.smem, s, p);
+    const long grid = std::max<long>(1, std::min<long>(long(syn_num_sms()), (batches + W - 1) / W));
+    return syn_launch(k, unsigned(grid), unsigned(W * 32), sh.smem, s, p);
+}
+
+template <int TYPE>
+int launch_stage(const GemvArgs& p, cudaStream_t s) {
+    const StageCfg c = stage_cfg(TYPE, p.rows, p.cols);
+    if (c.warps == 16 && c.batch == 4864) return launch_stage_cfg<TYPE, 16, 4864>(p, s);
+    if (c.warps == 12 && c.batch == 4864) return launch_stage_cfg<TYPE, 12, 4864>(p, s);
+    if (c.warps == 8 && c.batch == 16384) return launch_stage_cfg<TYPE, 8, 16384>(p, s);
+    return launch_stage_cfg<TYPE, 8, 9728>(p, s);
 }
 
 template <int TYPE, int LAYOUT, int NT>

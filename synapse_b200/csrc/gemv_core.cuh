@@ -12,21 +12,29 @@ namespace syn {
 constexpr int kStageWarps = 8;
 constexpr size_t kBatchBytes = 9728;  // target bytes of weights per batch
 
+// dp4a of unsigned bytes (a) with signed bytes (b), plus c.
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
 template <int TYPE>
 __device__ __forceinline__ int block_dot(const uint32_t (&w)[8], const int4 a0, const int4 a1, int asum) {
     // two independent dp4a chains (an exact integer sum in any order)
     int s0 = 0, s1 = 0;
     if (TYPE == SYN_Q4_0) {
-        // byte j: low nibble = weight j, high nibble = weight j + 16 (blocks.hpp:36-40)
+        // byte j: low nibble = weight j, high nibble = weight j + 16 (blocks.hpp:36-40).
+        // The high nibbles stay in place (16 x their value), so s1 = 16 * their dot.
         s0 = __dp4a(int(w[0] & 0x0f0f0f0fu), a0.x, s0);
-        s1 = __dp4a(int((w[0] >> 4) & 0x0f0f0f0fu), a1.x, s1);
+        s1 = dp4a_us(w[0] & 0xf0f0f0f0u, a1.x, s1);
         s0 = __dp4a(int(w[1] & 0x0f0f0f0fu), a0.y, s0);
-        s1 = __dp4a(int((w[1] >> 4) & 0x0f0f0f0fu), a1.y, s1);
+        s1 = dp4a_us(w[1] & 0xf0f0f0f0u, a1.y, s1);
         s0 = __dp4a(int(w[2] & 0x0f0f0f0fu), a0.z, s0);
-        s1 = __dp4a(int((w[2] >> 4) & 0x0f0f0f0fu), a1.z, s1);
+        s1 = dp4a_us(w[2] & 0xf0f0f0f0u, a1.z, s1);
         s0 = __dp4a(int(w[3] & 0x0f0f0f0fu), a0.w, s0);
-        s1 = __dp4a(int((w[3] >> 4) & 0x0f0f0f0fu), a1.w, s1);
-        return s0 + s1 - 8 * asum;
+        s1 = dp4a_us(w[3] & 0xf0f0f0f0u, a1.w, s1);
+        return s0 + (s1 >> 4) - 8 * asum;  // s1 is a multiple of 16: the shift is exact
     }
     s0 = __dp4a(int(w[0]), a0.x, s0);
     s1 = __dp4a(int(w[4]), a1.x, s1);
@@ -228,12 +236,13 @@ struct StageShape {
     size_t row_b, batch_bytes, act_bytes, stage_floats2, warp_bytes, smem;
 };
 
-__host__ __device__ inline StageShape stage_shape(int type, int cols, int warps = kStageWarps) {
+__host__ __device__ inline StageShape stage_shape(int type, int cols, int warps = kStageWarps,
+                                                  size_t batch_target = kBatchBytes) {
     StageShape s;
     s.nb = cols / QK;
     s.nch = (s.nb + 31) / 32;
     s.row_b = planar_row_bytes(type, cols);
-    int R = int(kBatchBytes / s.row_b);
+    int R = int(batch_target / s.row_b);
     if (R < 1) R = 1;
     const int rmax = s.nch >= 32 ? 1 : 32 / s.nch;  // every (row, chunk) chain gets a lane
     if (R > rmax) R = rmax;
@@ -249,6 +258,40 @@ __host__ __device__ inline StageShape stage_shape(int type, int cols, int warps 
 
 // The blocks and chains of one batch of rows_k rows (bb: the rows, planar):
 // chsum[r * nch + c] = chunk c of row r, by the reference's fma chain.
+// The block dots of rows [0, R) of a batch (R fixed, 32-bit shared offsets).
+template <int TYPE, int R>
+__device__ __forceinline__ void stage_blocks(const unsigned char* bb, uint32_t row_b, uint32_t qbytes, int nb,
+                                             const uint8_t* aq, const float2* dsum, float2* stage, int spr, int lane) {
+    constexpr int QB = TYPE == SYN_Q4_0 ? 16 : 32;
+    for (int b = lane; b < nb; b += 32) {
+        const int4* ap = reinterpret_cast<const int4*>(aq + sact_off(b));
+        const int4 a0 = ap[0], a1 = ap[1];
+        const float2 ds = dsum[b];
+        const int asum = TYPE == SYN_Q4_0 ? __float_as_int(ds.y) : 0;
+        const uint32_t wo = uint32_t(b) * QB, so = qbytes + uint32_t(b) * 2;
+        const int si = b + (b >> 5);
+        uint4 v0[R], v1[R];
+        uint16_t dwh[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const unsigned char* wr = bb + uint32_t(r) * row_b;
+            v0[r] = *reinterpret_cast<const uint4*>(wr + wo);
+            if (QB == 32) v1[r] = *reinterpret_cast<const uint4*>(wr + wo + 16);
+            dwh[r] = *reinterpret_cast<const uint16_t*>(wr + so);
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            uint32_t w[8];
+            w[0] = v0[r].x; w[1] = v0[r].y; w[2] = v0[r].z; w[3] = v0[r].w;
+            if (QB == 32) {
+                w[4] = v1[r].x; w[5] = v1[r].y; w[6] = v1[r].z; w[7] = v1[r].w;
+            }
+            const int isum = block_dot<TYPE>(w, a0, a1, asum);
+            stage[r * spr + si] = make_float2(float(isum), __fmul_rn(f16_from_bits(dwh[r]), ds.x));
+        }
+    }
+}
+
 template <int TYPE>
 __device__ __forceinline__ void stage_batch(const unsigned char* bb, int rows_k, const StageShape& sh, size_t qbytes,
                                             const uint8_t* aq, const float2* dsum, float2* stage, float* chsum,
@@ -257,26 +300,18 @@ __device__ __forceinline__ void stage_batch(const unsigned char* bb, int rows_k,
     const int nb = sh.nb, nch = sh.nch, spr = nb + nch;
     // Block b's activations are read once and meet the batch's rows_k rows;
     // the rows' dots are independent, so their loads and dp4a chains overlap.
-    for (int b = lane; b < nb; b += 32) {
-        const int4* ap = reinterpret_cast<const int4*>(aq + sact_off(b));
-        const int4 a0 = ap[0], a1 = ap[1];
-        const float2 ds = dsum[b];
-        const int asum = TYPE == SYN_Q4_0 ? __float_as_int(ds.y) : 0;
-#pragma unroll 4
-        for (int r = 0; r < rows_k; ++r) {
-            const unsigned char* wr = bb + size_t(r) * sh.row_b;
-            uint32_t w[8];
-            const uint4 v0 = *reinterpret_cast<const uint4*>(wr + size_t(b) * QB);
-            w[0] = v0.x; w[1] = v0.y; w[2] = v0.z; w[3] = v0.w;
-            if (QB == 32) {
-                const uint4 v1 = *reinterpret_cast<const uint4*>(wr + size_t(b) * QB + (QB - 16));
-                w[4] = v1.x; w[5] = v1.y; w[6] = v1.z; w[7] = v1.w;
-            }
-            const float dw = f16_from_bits(*reinterpret_cast<const uint16_t*>(wr + qbytes + size_t(b) * 2));
-            const int isum = block_dot<TYPE>(w, a0, a1, asum);
-            stage[r * spr + b + (b >> 5)] = make_float2(float(isum), __fmul_rn(dw, ds.x));
-        }
+    const uint32_t rb = uint32_t(sh.row_b), qb = uint32_t(qbytes);
+    if (rows_k == 4) {
+        stage_blocks<TYPE, 4>(bb, rb, qb, nb, aq, dsum, stage, spr, lane);
+    } else if (rows_k == 2) {
+        stage_blocks<TYPE, 2>(bb, rb, qb, nb, aq, dsum, stage, spr, lane);
+    } else if (rows_k == 1) {
+        stage_blocks<TYPE, 1>(bb, rb, qb, nb, aq, dsum, stage, spr, lane);
+    } else {
+        for (int r = 0; r < rows_k; ++r)
+            stage_blocks<TYPE, 1>(bb + uint32_t(r) * rb, rb, qb, nb, aq, dsum, stage + r * spr, spr, lane);
     }
+    (void)QB;
     __syncwarp();
     for (int ch = lane; ch < rows_k * nch; ch += 32) {
         const int r = ch / nch, c = ch - r * nch;
