@@ -14,12 +14,13 @@
 // heads of the group. K and V tiles stream through one four-slot ring of
 // asynchronous copies (the V tiles load while the K tiles are scored).
 //   phase 1: scores of the CTA's positions, and per query head the chunk's
-//            max m_j and double sum of expf(s - m_j);
+//            max m_j and double sum s_j of expf(s - m_j);
 //   cluster barrier: every CTA merges all C chunks' statistics from their
 //            shared memory (distributed shared memory): M = max m_j and
-//            sum = sum_j s_j * exp(m_j - M), in chunk order, in double;
-//   phase 2: p_t for the CTA's positions with the global M and scale, and the
-//            partial sum of p_t V_t in position order;
+//            sum = sum_j s_j * exp(m_j - M), in chunk order, in double (with
+//            one chunk, the reference's sum of expf(s - M) exactly);
+//   phase 2: p_t = binary16(expf(s_t - M) * (1 / sum)) for the CTA's
+//            positions, and the partial sum of p_t V_t in position order;
 //   cluster barrier: CTA j adds slice j of the outputs over the C partials in
 //            chunk order (deterministic) and stores it.
 // No statistics or partial outputs go through global memory, and no
@@ -40,8 +41,9 @@ namespace {
 
 constexpr int kThreads = 128;      // RoPE / append kernels
 constexpr int kAttnThreads = 256;  // the decode kernel
-constexpr int kTile = 64;          // K or V rows per ring slot
-constexpr int kSlots = 4;          // ring depth: up to four tiles in flight
+constexpr int kTile = 64;          // K or V rows per ring slot (head_dim <= 128; 32 rows above)
+__host__ __device__ inline int tile_rows(int hd) { return hd <= 128 ? kTile : kTile / 2; }
+constexpr int kSlots = 5;          // ring depth: a slot is refilled one step after it is read
 constexpr int kMaxCluster = 16;
 constexpr int kExactChunk = 256;   // positions per CTA below which the cluster does not split
 
@@ -72,9 +74,11 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
-// Wait until at most kSlots - 1 of this thread's newest copy groups are pending.
+// Wait until at most kSlots - 2 of this thread's newest copy groups are
+// pending: at step u, tiles up to u + kSlots - 2 have been requested (the
+// slot read at step u - 1 is refilled after this wait), so tile u is in.
 __device__ __forceinline__ void cp_async_wait_ring() { asm volatile("cp.async.wait_group 3;" ::: "memory"); }
-static_assert(kSlots == 4, "cp_async_wait_ring leaves kSlots - 1 groups pending");
+static_assert(kSlots == 5, "cp_async_wait_ring leaves kSlots - 2 groups pending");
 
 // cos and sin of pair i at position p (attention.hpp:102-119): theta built by
 // repeated float multiplication, divided by the frequency factor, then the
@@ -125,7 +129,7 @@ __device__ __forceinline__ void unpack8(uint4 v, float (&f)[8]) {
 // Shared memory of the decode kernel (dynamic part). sc_cap: floats of the
 // score buffer (0 when the scores live in global scratch).
 struct DecodeSmem {
-    size_t cs, qg, pw, part, red_s, red_m, stat_s, stat_m, krh, vrh, sc, ring, total;
+    size_t cs, qg, part, stat_s, stat_m, krh, vrh, sc, ring, total;
 };
 
 __host__ __device__ inline DecodeSmem decode_smem(int GT, int hd, size_t sc_cap) {
@@ -138,22 +142,42 @@ __host__ __device__ inline DecodeSmem decode_smem(int GT, int hd, size_t sc_cap)
     };
     l.cs = take(size_t(hd) * 4);                     // cos, sin of the hd / 2 pairs
     l.qg = take(size_t(GT) * hd * 4);                // rotated q of the group, binary16 values
-    l.pw = take(size_t(GT) * kTile * 4);             // p of one V tile
     l.part = take(size_t(GT) * hd * 4);              // this CTA's p.V partial (read by the cluster)
-    l.red_s = take(size_t(GT) * kMaxCluster * 8);    // the cluster's chunk sums, gathered
-    l.red_m = take(size_t(GT) * kMaxCluster * 4);    // the cluster's chunk maxima, gathered
     l.stat_s = take(size_t(GT) * 8);                 // this chunk's sums (double), read by the cluster
     l.stat_m = take(size_t(GT) * 4);                 // this chunk's maxima, read by the cluster
     l.krh = take(size_t(hd) * 2);                    // appended K row (binary16)
     l.vrh = take(size_t(hd) * 2);                    // appended V row
-    l.sc = take(sc_cap * 4);                         // scores, then expf(s - M), of the chunk
-    l.ring = take(size_t(kSlots) * kTile * (hd + 8) * 2);
+    l.sc = take(sc_cap * 4);                         // scores, then p, of the chunk
+    l.ring = take(size_t(kSlots) * tile_rows(hd) * (hd + 8) * 2);
     l.total = off;
     return l;
 }
 
+// Tensor-core tiles for contexts beyond kExactChunk (where the reference's
+// summation order is re-associated over chunks anyway): m16n8k16, binary16
+// inputs (q, K, p and V are binary16 values already), fp32 accumulation.
+// Fragment layouts (PTX ISA, mma.m16n8k16 .f16): lane = 4 g + t;
+//   A: a0 = A[g][2t..2t+1], a1 = A[g+8][2t..], a2 = A[g][2t+8..], a3 = A[g+8][2t+8..]
+//   B: b0 = B[2t..2t+1][g], b1 = B[2t+8..2t+9][g]
+//   C: c0, c1 = C[g][2t], C[g][2t+1]; c2, c3 = C[g+8][...]
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {  // exact: both are binary16 values
+    return uint32_t(f16_bits(lo)) | (uint32_t(f16_bits(hi)) << 16);
+}
+__device__ __forceinline__ void ldsm_x2_trans(uint32_t& r0, uint32_t& r1, const void* row_addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
+                 : "=r"(r0), "=r"(r1)
+                 : "r"(static_cast<unsigned>(__cvta_generic_to_shared(row_addr))));
+}
+
 template <int GT>
-__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnParams a) {
+__global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(AttnParams a) {
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
     const int C = int(cluster.num_blocks());
@@ -174,16 +198,15 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnParams a)
     const DecodeSmem sl = decode_smem(GT, hd, a.sc_smem ? size_t(GT) * a.chunk_cap : 0);
     float* cs = reinterpret_cast<float*>(smem + sl.cs);
     float* qg = reinterpret_cast<float*>(smem + sl.qg);
-    float* pw = reinterpret_cast<float*>(smem + sl.pw);
     float* part = reinterpret_cast<float*>(smem + sl.part);
-    double* red_s = reinterpret_cast<double*>(smem + sl.red_s);
-    float* red_m = reinterpret_cast<float*>(smem + sl.red_m);
     double* stat_s = reinterpret_cast<double*>(smem + sl.stat_s);
     float* stat_m = reinterpret_cast<float*>(smem + sl.stat_m);
     uint16_t* krh = reinterpret_cast<uint16_t*>(smem + sl.krh);
     uint16_t* vrh = reinterpret_cast<uint16_t*>(smem + sl.vrh);
     uint16_t* ring = reinterpret_cast<uint16_t*>(smem + sl.ring);
     __shared__ float gm[GT], gscale[GT];
+    __shared__ float2 etab[64];  // 2^(j/64) for exp_rn_neg
+    if (tid < 64) etab[tid] = kExp2J64[tid];
     // score (then e) of query head jh at position t: sc[jh * sstride + t - soff]
     float* sc;
     size_t sstride;
@@ -203,16 +226,28 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnParams a)
     uint16_t* kcb = a.kc + size_t(b) * a.cache_stride;
     uint16_t* vcb = a.vc + size_t(b) * a.cache_stride;
     const int c8n = hd / 8;
-    const int nt = (n + kTile - 1) / kTile;  // tiles per phase; tile u < nt is K tile u, else V tile u - nt
+    const int TR = tile_rows(hd);            // rows per ring slot
+    const int nt = (n + TR - 1) / TR;        // tiles per phase; tile u < nt is K tile u, else V tile u - nt
+    // This thread's 16-byte column of the tile rows it copies (fixed when the
+    // block's threads cover whole rows; else the general index split).
+    const bool even_cols = kAttnThreads % c8n == 0;
+    const int my_c8 = tid % c8n, my_r0 = tid / c8n, r_step = kAttnThreads / c8n;
     auto issue = [&](int u) {
         if (u < 2 * nt) {
             const bool is_k = u < nt;
-            const int tb = t0 + (is_k ? u : u - nt) * kTile, m = min(kTile, t1 - tb);
+            const int tb = t0 + (is_k ? u : u - nt) * TR, m = min(TR, t1 - tb);
             const uint16_t* src = (is_k ? kcb : vcb) + size_t(g) * hd;
-            uint16_t* dst = ring + size_t(u % kSlots) * kTile * rowh;
-            for (int i = tid; i < m * c8n; i += kAttnThreads) {
-                const int rr = i / c8n, c8 = i % c8n, t = tb + rr;
-                if (!(owns && t == P)) cp_async16(dst + rr * rowh + c8 * 8, src + size_t(t) * row + c8 * 8);
+            uint16_t* dst = ring + size_t(u % kSlots) * TR * rowh;
+            if (even_cols) {
+                const uint16_t* sp = src + size_t(tb + my_r0) * row + my_c8 * 8;
+                uint16_t* dp = dst + my_r0 * rowh + my_c8 * 8;
+                for (int rr = my_r0; rr < m; rr += r_step, sp += size_t(r_step) * row, dp += r_step * rowh)
+                    if (!(owns && tb + rr == P)) cp_async16(dp, sp);
+            } else {
+                for (int i = tid; i < m * c8n; i += kAttnThreads) {
+                    const int rr = i / c8n, c8 = i % c8n, t = tb + rr;
+                    if (!(owns && t == P)) cp_async16(dst + rr * rowh + c8 * 8, src + size_t(t) * row + c8 * 8);
+                }
             }
         }
         cp_async_commit();  // an empty group past the end keeps the pending count uniform
@@ -222,12 +257,14 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnParams a)
     // copies start before the wait. Without it the caller's previous kernel
     // may have written them (syn_rope_kv_append), so everything waits.
     if (!a.append) pdl_wait();
+    float2 cs_v = make_float2(0.0f, 0.0f);  // this thread's (cos, sin), requested before the copies
+    if (a.rope && a.rope_tab && tid < hd / 2)
+        cs_v = reinterpret_cast<const float2*>(a.rope_tab)[size_t(P) * (hd / 2) + tid];
     for (int u = 0; u < kSlots; ++u) issue(u);
     if (a.rope) {
         if (a.rope_tab) {
-            const float2* tab = reinterpret_cast<const float2*>(a.rope_tab) + size_t(P) * (hd / 2);
             for (int i = tid; i < hd / 2; i += kAttnThreads) {
-                const float2 v = tab[i];
+                const float2 v = i == tid ? cs_v : reinterpret_cast<const float2*>(a.rope_tab)[size_t(P) * (hd / 2) + i];
                 cs[2 * i] = v.x;
                 cs[2 * i + 1] = v.y;
             }
@@ -277,15 +314,61 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnParams a)
     }
     __syncthreads();
 
+    // The tensor-core path (above kExactChunk positions; uniform over the
+    // cluster): q of head g as A fragments, all head_dim / 16 k-steps.
+    const bool tc = L > kExactChunk && hd % 16 == 0 && hd <= 128 && G <= 8;
+    const int gq = lane >> 2, tq = lane & 3;
+    uint32_t qa[16];  // per k-step (head_dim <= 128): a0 (row gq, k 2tq..), a2 (row gq, k 2tq+8..)
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+        qa[2 * ks] = qa[2 * ks + 1] = 0u;
+        if (tc && ks < hd / 16 && gq < G) {
+            const float* qr = qg + gq * hd + 16 * ks + 2 * tq;
+            qa[2 * ks] = pack_h2(qr[0], qr[1]);
+            qa[2 * ks + 1] = pack_h2(qr[8], qr[9]);
+        }
+    }
+
     // Phase 1: scores, one (position, query head) per thread and step; the
-    // dot runs in dimension order (attention.hpp:214-219).
+    // dot runs in dimension order (attention.hpp:214-219). The tensor-core
+    // lanes keep the max of the scores they produce (lmx).
+    float lmx = -INFINITY;
     for (int u = 0; u < nt; ++u) {
         cp_async_wait_ring();
-        const int tb = t0 + u * kTile, m = min(kTile, t1 - tb);
-        uint16_t* tile = ring + size_t(u % kSlots) * kTile * rowh;
+        const int tb = t0 + u * TR, m = min(TR, t1 - tb);
+        uint16_t* tile = ring + size_t(u % kSlots) * TR * rowh;
         if (owns && P >= tb && P < tb + m && tid < c8n)
             *reinterpret_cast<uint4*>(tile + (P - tb) * rowh + tid * 8) = *reinterpret_cast<const uint4*>(krh + tid * 8);
-        __syncthreads();
+        __syncthreads();  // tile u is visible, and every thread is done with tile u - 1
+        if (u > 0) issue(u - 1 + kSlots);
+        if (tc) {
+            // warp w scores positions tb + 8w .. + 7 of all G heads: C[h][n] = sum_k q[h][k] K[n][k]
+            const int n0 = 8 * warp;
+            if (n0 < m) {
+                float cacc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                const uint16_t* krow = tile + (n0 + gq) * rowh + 2 * tq;  // B: rows past m read stale data, never stored
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks) {
+                    if (ks >= hd / 16) break;
+                    const uint32_t b0 = *reinterpret_cast<const uint32_t*>(krow + 16 * ks);
+                    const uint32_t b1 = *reinterpret_cast<const uint32_t*>(krow + 16 * ks + 8);
+                    const uint32_t af[4] = {qa[2 * ks], 0u, qa[2 * ks + 1], 0u};
+                    mma16816(cacc, af, b0, b1);
+                }
+                if (gq < G) {
+                    const int r0 = n0 + 2 * tq;
+                    const float v0 = __fmul_rn(cacc[0], a.scale), v1 = __fmul_rn(cacc[1], a.scale);
+                    if (r0 < m) {
+                        sc[size_t(gq) * sstride + tb + r0 - soff] = v0;
+                        lmx = fmaxf(lmx, v0);
+                    }
+                    if (r0 + 1 < m) {
+                        sc[size_t(gq) * sstride + tb + r0 + 1 - soff] = v1;
+                        lmx = fmaxf(lmx, v1);
+                    }
+                }
+            }
+        } else
         for (int i = tid; i < m * G; i += kAttnThreads) {
             const int jh = i / m, r = i % m;
             const uint16_t* kt = tile + r * rowh;
@@ -307,49 +390,108 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnParams a)
             }
             sc[size_t(jh) * sstride + tb + r - soff] = __fmul_rn(dot, a.scale);
         }
-        __syncthreads();
-        issue(u + kSlots);
     }
+    __syncthreads();  // the last tile's scores are visible
 
-    // The softmax over the whole context (elementwise.hpp:174-201): the
-    // cluster's max, then e_t = expf(s_t - M) once per score, then the
-    // cluster's double sum of every e_t, so p_t = binary16(e_t * (1 / sum))
-    // with the reference's M, e_t and scale.
-    for (int jh = warp; jh < G; jh += kAttnThreads / 32) {
-        const float* s = sc + size_t(jh) * sstride - soff;
-        float mx = -INFINITY;
-        for (int t = t0 + lane; t < t1; t += 32) mx = fmaxf(mx, s[t]);
-        mx = warp_max(mx);
-        if (lane == 0) stat_m[jh] = mx;
-    }
-    cluster.sync();
-    for (int i = tid; i < G * C; i += kAttnThreads) red_m[i] = *cluster.map_shared_rank(stat_m + i / C, i % C);
-    __syncthreads();
-    for (int jh = tid; jh < G; jh += kAttnThreads) {
-        float M = -INFINITY;
-        for (int r = 0; r < C; ++r) M = fmaxf(M, red_m[jh * C + r]);
-        gm[jh] = M;
-    }
-    __syncthreads();
-    for (int jh = warp; jh < G; jh += kAttnThreads / 32) {
-        float* s = sc + size_t(jh) * sstride - soff;
-        const float M = gm[jh];
-        double acc = 0.0;
-        for (int t = t0 + lane; t < t1; t += 32) {
-            const float e = exp_rn(__fsub_rn(s[t], M));
-            s[t] = e;
-            acc += double(e);
+    // The softmax over the whole context (elementwise.hpp:174-201).
+    // The chunk's statistics per query head: the max m_j (from the
+    // tensor-core lanes, else by every thread over positions t0 + tid,
+    // + 256, ...), then the double sum s_j of expf(s - m_j) over the same
+    // positions, partials meeting in lane and warp order.
+    __shared__ float red_mx[GT][kAttnThreads / 32];
+    __shared__ double red_sm[GT][kAttnThreads / 32];
+    __shared__ float m_loc[GT];
+    {
+        if (tc) {
+            float w = fmaxf(lmx, __shfl_xor_sync(0xffffffffu, lmx, 1));
+            w = fmaxf(w, __shfl_xor_sync(0xffffffffu, w, 2));
+            if (tq == 0 && gq < G) red_mx[gq][warp] = w;
+        } else {
+#pragma unroll 1
+            for (int h = 0; h < G; ++h) {
+                const float* sh = sc + size_t(h) * sstride + t0 - soff;
+                float mx = -INFINITY;
+                for (int t = tid; t < n; t += kAttnThreads) mx = fmaxf(mx, sh[t]);
+                mx = warp_max(mx);
+                if (lane == 0) red_mx[h][warp] = mx;
+            }
         }
-        acc = warp_sum_d(acc);
-        if (lane == 0) stat_s[jh] = acc;
+        __syncthreads();
+        if (tid < G) {
+            float m = -INFINITY;
+            for (int w = 0; w < kAttnThreads / 32; ++w) m = fmaxf(m, red_mx[tid][w]);
+            m_loc[tid] = m;
+        }
+        __syncthreads();
+        double acc[GT];
+        float mh[GT];
+#pragma unroll
+        for (int h = 0; h < GT; ++h) {
+            acc[h] = 0.0;
+            mh[h] = h < G ? m_loc[h] : 0.0f;
+        }
+        const float* sh = sc + t0 - soff;
+        for (int t = tid; t < n; t += kAttnThreads) {
+#pragma unroll
+            for (int h = 0; h < GT; ++h)
+                if (h < G) acc[h] += double(exp_rn_neg(__fsub_rn(sh[size_t(h) * sstride + t], mh[h]), etab));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+            for (int h = 0; h < GT; ++h) acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], o);
+        }
+        if (lane < G) {
+            double v = 0.0;
+#pragma unroll
+            for (int h = 0; h < GT; ++h)
+                if (h == lane) v = acc[h];
+            red_sm[lane][warp] = v;
+        }
+        __syncthreads();
+        if (tid < G) {
+            double sum = 0.0;
+            for (int w = 0; w < kAttnThreads / 32; ++w) sum += red_sm[tid][w];
+            stat_m[tid] = m_loc[tid];
+            stat_s[tid] = sum;
+        }
     }
-    cluster.sync();
-    for (int i = tid; i < G * C; i += kAttnThreads) red_s[i] = *cluster.map_shared_rank(stat_s + i / C, i % C);
+    cluster.sync();  // every chunk's statistics are visible to the cluster
+    // The context's max M and normaliser sum_j s_j * exp(m_j - M), one warp
+    // per query head with lane r holding chunk r. With one chunk (or one
+    // chunk holding every position) the weight is exactly 1 and the sum is
+    // the reference's sum of expf(s - M); with several, the chunks' weights
+    // and their sum order are the approximation of the re-associated sum.
+    for (int h = warp; h < G; h += kAttnThreads / 32) {
+        const float mr = lane < C ? *cluster.map_shared_rank(stat_m + h, lane) : -INFINITY;
+        const double sr = lane < C ? *cluster.map_shared_rank(stat_s + h, lane) : 0.0;
+        const float M = warp_max(mr);
+        const double w = sr > 0.0 ? sr * double(mr == M ? 1.0f : expf(__fsub_rn(mr, M))) : 0.0;
+        const double tot = warp_sum_d(w);
+        if (lane == 0) {
+            gm[h] = M;
+            gscale[h] = float(1.0 / tot);
+        }
+    }
     __syncthreads();
-    for (int jh = tid; jh < G; jh += kAttnThreads) {
-        double tot = 0.0;
-        for (int r = 0; r < C; ++r) tot += red_s[jh * C + r];
-        gscale[jh] = float(1.0 / tot);
+    // p_t = binary16(expf(s_t - M) * (1 / sum)) of the chunk, in place of the
+    // scores (the first V tiles are already in flight).
+    {
+        float mh[GT], gs[GT];
+#pragma unroll
+        for (int h = 0; h < GT; ++h) {
+            mh[h] = h < G ? gm[h] : 0.0f;
+            gs[h] = h < G ? gscale[h] : 0.0f;
+        }
+        float* sh = sc + t0 - soff;
+        for (int t = tid; t < n; t += kAttnThreads) {
+#pragma unroll
+            for (int h = 0; h < GT; ++h)
+                if (h < G) {
+                    float& x = sh[size_t(h) * sstride + t];
+                    x = round_f16(__fmul_rn(exp_rn_neg(__fsub_rn(x, mh[h]), etab), gs[h]));
+                }
+        }
     }
     __syncthreads();
 
@@ -364,42 +506,81 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnParams a)
         const int o = tid + k * kAttnThreads;
         acc0[k] = acc1[k] = 0.0f;
         pcol[k] = o < n_pairs ? 2 * (o % (hd / 2)) : -1;
-        prow[k] = o < n_pairs ? (o / (hd / 2)) * kTile : 0;
+        prow[k] = o < n_pairs ? (o / (hd / 2)) * int(sstride) : 0;
     }
+    float vacc[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
     for (int u = nt; u < 2 * nt; ++u) {
         cp_async_wait_ring();
-        const int tb = t0 + (u - nt) * kTile, m = min(kTile, t1 - tb);
-        uint16_t* tile = ring + size_t(u % kSlots) * kTile * rowh;
+        const int tb = t0 + (u - nt) * TR, m = min(TR, t1 - tb);
+        uint16_t* tile = ring + size_t(u % kSlots) * TR * rowh;
         if (owns && P >= tb && P < tb + m && tid < c8n)
             *reinterpret_cast<uint4*>(tile + (P - tb) * rowh + tid * 8) = *reinterpret_cast<const uint4*>(vrh + tid * 8);
-        for (int i = tid; i < m * G; i += kAttnThreads) {
-            const int jh = i / m, r = i % m;
-            pw[jh * kTile + r] = round_f16(__fmul_rn(sc[size_t(jh) * sstride + tb + r - soff], gscale[jh]));
+        const float* pt = sc + (tb - soff);  // p of head h at tile row r: pt[h * sstride + r]
+        if (tc && m < TR) {
+            // V rows past m of the last tile are 0 (stale bits could be a NaN; their p is 0)
+            for (int i = tid; i < (kTile - m) * c8n; i += kAttnThreads)
+                *reinterpret_cast<uint4*>(tile + (m + i / c8n) * rowh + (i % c8n) * 8) = make_uint4(0u, 0u, 0u, 0u);
         }
-        __syncthreads();
+        __syncthreads();  // tile u is visible, and every thread is done with tile u - 1
+        issue(u - 1 + kSlots);
+        if (tc) {
+            // warp w accumulates dims 16w .. 16w + 15 of all G heads: C[h][d] += sum_k p[h][k] V[k][d]
+            const int d0 = 16 * warp;
+            if (d0 < hd) {
+#pragma unroll
+                for (int ks = 0; ks < kTile / 16; ++ks) {
+                    if (16 * ks < m) {
+                        uint32_t af[4] = {0u, 0u, 0u, 0u};
+                        if (gq < G) {
+                            const int r = 16 * ks + 2 * tq;  // p past row m is 0
+                            const float* pr = pt + size_t(gq) * sstride + r;
+                            af[0] = pack_h2(r < m ? pr[0] : 0.0f, r + 1 < m ? pr[1] : 0.0f);
+                            af[2] = pack_h2(r + 8 < m ? pr[8] : 0.0f, r + 9 < m ? pr[9] : 0.0f);
+                        }
+#pragma unroll
+                        for (int nt2 = 0; nt2 < 2; ++nt2) {
+                            uint32_t b0, b1;
+                            // lanes 0-7: rows 16ks..+7 at column d0 + 8nt2; lanes 8-15: rows +8..+15
+                            const int rr = 16 * ks + (lane & 15);
+                            ldsm_x2_trans(b0, b1, tile + rr * rowh + d0 + 8 * nt2);
+                            mma16816(vacc[nt2], af, b0, b1);
+                        }
+                    }
+                }
+            }
+        } else
 #pragma unroll 4
         for (int r = 0; r < m; ++r) {
             const uint16_t* vr = tile + r * rowh;
 #pragma unroll
             for (int k = 0; k < KO; ++k) {
                 if (pcol[k] >= 0) {
-                    const float p = pw[prow[k] + r];
+                    const float p = pt[prow[k] + r];
                     const uint32_t v2 = *reinterpret_cast<const uint32_t*>(vr + pcol[k]);
                     acc0[k] = fmaf(p, f16_from_bits(uint16_t(v2 & 0xffff)), acc0[k]);  // exact products
                     acc1[k] = fmaf(p, f16_from_bits(uint16_t(v2 >> 16)), acc1[k]);
                 }
             }
         }
-        __syncthreads();
-        issue(u + kSlots);
     }
     cp_async_wait_all();  // nothing is left in flight (the trailing groups are empty)
+    if (tc) {
+        if (16 * warp < hd && gq < G) {
 #pragma unroll
-    for (int k = 0; k < KO; ++k) {
-        if (pcol[k] >= 0) {
-            const int o = (prow[k] / kTile) * hd + pcol[k];
-            part[o] = acc0[k];
-            part[o + 1] = acc1[k];
+            for (int nt2 = 0; nt2 < 2; ++nt2) {
+                const int o = gq * hd + 16 * warp + 8 * nt2 + 2 * tq;
+                part[o] = vacc[nt2][0];
+                part[o + 1] = vacc[nt2][1];
+            }
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < KO; ++k) {
+            if (pcol[k] >= 0) {
+                const int o = 2 * (tid + k * kAttnThreads);  // head * hd + pcol[k]
+                part[o] = acc0[k];
+                part[o + 1] = acc1[k];
+            }
         }
     }
     cluster.sync();  // every partial is visible to the cluster
@@ -520,26 +701,31 @@ int check_args(const syn_attention_args* x, bool need_scratch) {
 }
 
 // Scores of a chunk stay in shared memory up to this size per CTA.
-constexpr size_t kScoreSmemBytes = 32 * 1024;
+constexpr size_t kScoreSmemBytes = 96 * 1024;
 
-// Cluster size for a call: up to 16 CTAs per (query, KV head) group, at
-// least kExactChunk positions each at max_len, no more than about four CTAs
-// per SM over the grid, and a size the device can co-schedule with this
-// kernel's largest shared memory (checked once per device, group tier and
-// head size).
+// Cluster size for a call: 1 to 16 CTAs per (query, KV head) group, at least
+// kExactChunk positions each at max_len, chosen by the number of clusters of
+// each size the device keeps resident with this kernel's largest shared
+// memory (checked once per device, group tier and head size): a 16-CTA
+// cluster needs 16 free SMs of one GPC, so fewer of those fit at once than
+// 148 / 16.
 template <int GT>
 int pick_cluster(const AttnParams& a, int* out) {
+    // Per (device, head size): how many clusters of 1 .. kMaxCluster CTAs can
+    // be resident at once (0 = that size cannot be scheduled).
+    struct Fit { int dev, hd; int active[kMaxCluster + 1]; };
     static std::mutex mu;
-    static std::vector<std::array<int, 3>> known;  // device, hd, largest schedulable cluster
+    static std::vector<Fit> known;
     int dev = 0;
     int st = syn_cuda_status(cudaGetDevice(&dev));
     if (st) return st;
-    int cmax = 0;
+    Fit fit = {dev, a.hd, {}};
     {
         std::lock_guard<std::mutex> lock(mu);
+        bool found = false;
         for (const auto& k : known)
-            if (k[0] == dev && k[1] == a.hd) cmax = k[2];
-        if (!cmax) {
+            if (k.dev == dev && k.hd == a.hd) fit = k, found = true;
+        if (!found) {
             auto kern = attn_decode_kernel<GT>;
             const size_t smem = decode_smem(GT, a.hd, kScoreSmemBytes / 4).total;
             // The opt-in covers the largest head size, so configuring a smaller
@@ -548,7 +734,7 @@ int pick_cluster(const AttnParams& a, int* out) {
             st = syn_cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(most)));
             if (!st) st = syn_cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
             if (st) return st;
-            for (int c = kMaxCluster; c >= 1 && !cmax; c /= 2) {
+            for (int c = 1; c <= kMaxCluster; ++c) {
                 cudaLaunchConfig_t cfg = {};
                 cfg.gridDim = dim3(c, 1, 1);
                 cfg.blockDim = dim3(kAttnThreads);
@@ -561,20 +747,30 @@ int pick_cluster(const AttnParams& a, int* out) {
                 cfg.attrs = attr;
                 cfg.numAttrs = 1;
                 int nc = 0;
-                if (cudaOccupancyMaxActiveClusters(&nc, kern, &cfg) == cudaSuccess && nc > 0) cmax = c;
-                else cudaGetLastError();
+                if (cudaOccupancyMaxActiveClusters(&nc, kern, &cfg) != cudaSuccess) {
+                    cudaGetLastError();
+                    nc = 0;
+                }
+                fit.active[c] = nc;
             }
-            if (!cmax) return SYN_ERR_UNSUPPORTED;
-            known.push_back({dev, a.hd, cmax});
+            if (!fit.active[1]) return SYN_ERR_UNSUPPORTED;
+            known.push_back(fit);
         }
     }
-    int c = cmax;
-    // At least kExactChunk positions per CTA at max_len: a context that fits
-    // one chunk sums p.V in the reference's position order exactly.
-    while (c > 1 && c * kExactChunk > a.max_len) c /= 2;
+    // Cluster sizes with at least kExactChunk positions per CTA at max_len (a
+    // context that fits one chunk sums p.V in the reference's order); of
+    // those, the fewest waves x positions per CTA, a tie keeping the smaller
+    // cluster, which merges fewer partials.
     const long groups = long(a.n_q) * a.n_kv;
-    while (c > 1 && groups * c > 4L * syn_num_sms()) c /= 2;
-    *out = c;
+    int best = 1;
+    long best_cost = -1;
+    for (int c = 1; c <= kMaxCluster; ++c) {
+        if (!fit.active[c] || (c > 1 && long(c) * kExactChunk > a.max_len)) continue;
+        const long waves = (groups + fit.active[c] - 1) / fit.active[c];
+        const long cost = waves * ((a.max_len + c - 1) / c);
+        if (best_cost < 0 || cost < best_cost) best = c, best_cost = cost;
+    }
+    *out = best;
     return SYN_OK;
 }
 

@@ -150,9 +150,11 @@ __device__ __forceinline__ void two_sum(float a, float b, float& s, float& e) {
     e = __fadd_rn(__fsub_rn(a, __fsub_rn(s, bb)), __fsub_rn(b, bb));
 }
 
-__device__ __forceinline__ float exp_rn(float x) {
-    if (!(x > -87.0f)) return x != x ? x : float(exp(double(x)));  // NaN, subnormal or zero results
-    if (x > 88.72284f) return __int_as_float(0x7f800000);
+// exp_rn for x in (-87, 88.72]: the reduction, the polynomial and the
+// reconstruction from 2^(j/64). tab is kExp2J64 in global memory (read
+// through the read-only cache) or a shared-memory copy of it.
+template <bool kSharedTab>
+__device__ __forceinline__ float exp_rn_core(float x, const float2* tab) {
     const float kf = rintf(__fmul_rn(x, 0x1.715476p+6f));  // 64 / ln2
     const int k = int(kf);
     // r = x - k ln2/64 as r_hi + r_lo: k * C_hi exactly (product and its
@@ -174,7 +176,8 @@ __device__ __forceinline__ float exp_rn(float x) {
     const float low = __fadd_rn(__fadd_rn(__fadd_rn(s_lo, r_lo), __fmul_rn(sq_lo, 0.5f)),
                                 __fadd_rn(tail, __fmul_rn(r_hi, r_lo)));
     // 2^(j/64) (1 + s): T_hi + T_hi s_hi + (T_hi low + T_lo (1 + s_hi))
-    const float2 t = __ldg(&kExp2J64[k & 63]);  // lanes index freely (a constant-bank read would serialize)
+    // lanes index freely (a constant-bank read would serialize)
+    const float2 t = kSharedTab ? tab[k & 63] : __ldg(&tab[k & 63]);
     const float m_hi = __fmul_rn(t.x, s_hi);
     const float m_lo = __fmaf_rn(t.x, s_hi, -m_hi);
     float a_hi, a_lo;
@@ -185,6 +188,23 @@ __device__ __forceinline__ float exp_rn(float x) {
     const int e = k >> 6;
     if (e > 127) return __fmul_rn(__fmul_rn(y, 0x1.p127f), 2.0f);
     return __fmul_rn(y, __int_as_float((e + 127) << 23));
+}
+
+__device__ __forceinline__ float exp_rn(float x) {
+    if (!(x > -87.0f)) return x != x ? x : float(exp(double(x)));  // NaN, subnormal or zero results
+    if (x > 88.72284f) return __int_as_float(0x7f800000);
+    return exp_rn_core<false>(x, kExp2J64);
+}
+
+// exp_rn for x <= 0 whose result is only added to a double sum that reaches
+// at least 1 (a softmax denominator holds exp(0) = 1) or scaled by at most 1
+// and rounded to binary16: a result below 2^-125 changes neither (it is under
+// half an ulp of 1 in double, and under half the smallest binary16
+// subnormal), so x <= -87 returns 0 without the double-precision tail. NaN
+// propagates. tab: a shared-memory copy of kExp2J64.
+__device__ __forceinline__ float exp_rn_neg(float x, const float2* tab) {
+    if (!(x > -87.0f)) return x != x ? x : 0.0f;
+    return exp_rn_core<true>(x, tab);
 }
 
 __device__ __forceinline__ float warp_sum(float v) {
