@@ -44,10 +44,10 @@ enum { SYN_F32 = 0, SYN_F16 = 1, SYN_Q4_0 = 2, SYN_Q8_0 = 8 };
 
 /* Weight layouts in device memory.
  *   SYN_LAYOUT_GGUF   : the GGUF bytes unchanged (rows of 18 B / 34 B blocks).
- *   SYN_LAYOUT_PLANAR : repacked for 16-byte coalesced loads: the quant plane
- *                       (rows x blocks x 16 B for Q4_0, x 32 B for Q8_0), then,
- *                       at the next 256-byte boundary, the binary16 scale plane
- *                       (rows x blocks). Same total bytes plus padding.
+ *   SYN_LAYOUT_PLANAR : repacked for 16-byte coalesced loads, row after row:
+ *                       a row's quants (blocks x 16 B for Q4_0, x 32 B for
+ *                       Q8_0), then its binary16 scales, padded to 16 bytes.
+ *                       A range of rows is one contiguous byte range.
  * Plain F32/F16 weights have one layout (row-major). */
 enum { SYN_LAYOUT_GGUF = 0, SYN_LAYOUT_PLANAR = 1 };
 
@@ -172,6 +172,9 @@ typedef struct {
     const float* freq_factors;
     const float* yarn;
     const float* rope_table; /* NULL, or syn_rope_table for these rope settings and max_len rows */
+    int split_groups;        /* (query, KV head) groups the context split is sized for; 0 = n_q * n_kv.
+                              * A tensor-parallel rank passes the whole model's count so that it splits
+                              * every context as one GPU does (bit-identical results). */
 } syn_attention_args;
 
 size_t syn_attention_scratch_bytes(int n_q, int n_head, int n_kv, int head_dim, int max_len);
@@ -277,13 +280,56 @@ int syn_session_launches_per_step(const syn_session* s);
  * with their scales, activations in and out, KV rows 0..pos). Returns the op
  * count in *n_ops (at most max_ops records written). */
 enum { SYN_OP_EMBED = 0, SYN_OP_RMS_NORM = 1, SYN_OP_QUANTIZE = 2, SYN_OP_MATMUL = 3, SYN_OP_ATTENTION = 4,
-       SYN_OP_SILU_MUL = 5, SYN_OP_ARGMAX = 6 };
+       SYN_OP_SILU_MUL = 5, SYN_OP_ARGMAX = 6, SYN_OP_ALLGATHER = 7 };
 typedef struct {
     int kind, layer, type, rows, cols;
     float ms;
     double bytes;
 } syn_op_profile;
 int syn_session_profile(syn_session* s, uint32_t token, uint32_t pos, syn_op_profile* out, int max_ops, int* n_ops);
+
+/* ------------------------------------------------------------------------
+ * Tensor parallelism over the GPUs of one node, one process (or thread) per
+ * GPU. The reference computes every output element of a GEMV with one
+ * thread's arithmetic whatever the thread count (its D1 contract,
+ * tests/unit/llama_threads.cpp:32, over kernels/gemv.hpp:72-161 row ranges);
+ * the sharding here keeps that across GPUs: attention by KV-head groups, every
+ * matrix by output rows, and the four per-layer activations (attention output,
+ * residual after O, silu*up, residual after down) plus the logits all-gathered
+ * in place. Each rank's results are bit-identical to one GPU's.
+ * ---------------------------------------------------------------------- */
+typedef struct syn_tp syn_tp;
+#define SYN_TP_ID_BYTES 128
+/* A new communicator id (an ncclUniqueId) on the rank that creates it; every
+ * rank passes the same id to syn_tp_init. */
+int syn_tp_unique_id(void* id_out);
+/* Join the group as rank of world on device (collective over all ranks). */
+int syn_tp_init(int rank, int world, const void* id, int device, syn_tp** out);
+void syn_tp_close(syn_tp* tp);
+/* In-place all-gather on stream: rank r's bytes_per_rank bytes sit at
+ * buf + r * bytes_per_rank; afterwards every rank holds all of them. */
+int syn_allgather(syn_tp* tp, void* buf, size_t bytes_per_rank, void* stream);
+
+/* A rank's share of a model (what it loads, computes and owns). */
+typedef struct {
+    int rank, world;
+    int head0, n_head;    /* query heads (attn_q rows head0 * head_dim ..) */
+    int kv_head0, n_kv;   /* KV heads: attn_k / attn_v rows and this rank's KV cache */
+    int embd0, n_embd;    /* rows of attn_output and ffn_down: the residual slice */
+    int ff0, n_ff;        /* rows of ffn_gate and ffn_up */
+    int vocab0, n_vocab;  /* rows of output.weight: the logits slice */
+} syn_tp_layout;
+/* The layout of rank of world for config c (host only): contiguous equal
+ * shares; SYN_ERR_UNSUPPORTED unless world divides n_head_kv, n_embd, n_ff
+ * and n_vocab. */
+int syn_tp_layout_of(const syn_llama_config* c, int rank, int world, syn_tp_layout* out);
+/* Sessions sharded over tp (NULL = one GPU). All ranks open, step, generate,
+ * reset and close together (each call runs the same collectives); logits and
+ * tokens come back whole on every rank. */
+int syn_session_open_gguf_tp(const char* path, int max_ctx, int device, syn_tp* tp, syn_session** out);
+int syn_session_open_synthetic_tp(const syn_llama_config* c, int max_ctx, uint64_t seed, int device, syn_tp* tp,
+                                  syn_session** out);
+int syn_session_tp_layout(const syn_session* s, syn_tp_layout* out);
 
 /* Copy device memory to the host (synchronous), e.g. a KV cache for checking. */
 int syn_copy_to_host(void* host_dst, const void* device_src, size_t bytes);

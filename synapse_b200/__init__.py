@@ -108,6 +108,15 @@ def _declare(L):
         "syn_session_launches_per_step": (i32, [vp]),
         "syn_session_profile": (i32, [vp, ctypes.c_uint32, ctypes.c_uint32, vp, i32, ctypes.POINTER(i32)]),
         "syn_copy_to_host": (i32, [vp, vp, sz]),
+        "syn_tp_unique_id": (i32, [vp]),
+        "syn_tp_init": (i32, [i32, i32, vp, i32, ctypes.POINTER(vp)]),
+        "syn_tp_close": (None, [vp]),
+        "syn_allgather": (i32, [vp, vp, sz, vp]),
+        "syn_tp_layout_of": (i32, [ctypes.POINTER(LlamaConfig), i32, i32, ctypes.POINTER(TPLayout)]),
+        "syn_session_open_gguf_tp": (i32, [ctypes.c_char_p, i32, i32, vp, ctypes.POINTER(vp)]),
+        "syn_session_open_synthetic_tp": (i32, [ctypes.POINTER(LlamaConfig), i32, ctypes.c_uint64, i32, vp,
+                                                ctypes.POINTER(vp)]),
+        "syn_session_tp_layout": (i32, [vp, ctypes.POINTER(TPLayout)]),
     })
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -259,7 +268,8 @@ class AttentionArgs(ctypes.Structure):
                 ("n_q", ctypes.c_int), ("n_head", ctypes.c_int), ("n_kv", ctypes.c_int), ("head_dim", ctypes.c_int),
                 ("max_len", ctypes.c_int), ("append", ctypes.c_int), ("rope", ctypes.c_int),
                 ("rope_mode", ctypes.c_int), ("theta_scale", ctypes.c_float), ("scale", ctypes.c_float),
-                ("freq_factors", ctypes.c_void_p), ("yarn", ctypes.c_void_p), ("rope_table", ctypes.c_void_p)]
+                ("freq_factors", ctypes.c_void_p), ("yarn", ctypes.c_void_p), ("rope_table", ctypes.c_void_p),
+                ("split_groups", ctypes.c_int)]
 
 
 def attention_scratch_bytes(n_q, n_head, n_kv, head_dim, max_len):
@@ -376,7 +386,8 @@ class OpProfile(ctypes.Structure):
                 ("cols", ctypes.c_int), ("ms", ctypes.c_float), ("bytes", ctypes.c_double)]
 
 
-OP_KINDS = {0: "embed", 1: "rms_norm", 2: "quantize", 3: "matmul", 4: "attention", 5: "silu_mul", 6: "argmax"}
+OP_KINDS = {0: "embed", 1: "rms_norm", 2: "quantize", 3: "matmul", 4: "attention", 5: "silu_mul", 6: "argmax",
+            7: "allgather"}
 
 
 def copy_to_host(ptr, nbytes, dtype=np.uint8):
@@ -385,9 +396,67 @@ def copy_to_host(ptr, nbytes, dtype=np.uint8):
     return out.view(dtype)
 
 
+class TPLayout(ctypes.Structure):
+    """A rank's share of a model under tensor parallelism (syn_tp_layout)."""
+    _fields_ = [(k, ctypes.c_int) for k in ("rank", "world", "head0", "n_head", "kv_head0", "n_kv", "embd0",
+                                             "n_embd", "ff0", "n_ff", "vocab0", "n_vocab")]
+
+    def as_dict(self):
+        return {k: getattr(self, k) for k, _ in self._fields_}
+
+
+def tp_layout(cfg, rank, world):
+    """The rows and heads rank of world holds for a model config (host only; no GPU needed)."""
+    c = LlamaConfig(**{k: cfg[k] for k, _ in LlamaConfig._fields_ if k in cfg})
+    out = TPLayout()
+    check(lib().syn_tp_layout_of(ctypes.byref(c), int(rank), int(world), ctypes.byref(out)), "syn_tp_layout_of")
+    return out.as_dict()
+
+
+class TP:
+    """A tensor-parallel group: one rank per GPU, joined through an id that rank 0 creates.
+
+    share_id(id_bytes) -> id_bytes must give every rank rank 0's bytes (e.g. a
+    torch.distributed broadcast); it is called on every rank."""
+
+    def __init__(self, rank, world, device, share_id):
+        import ctypes as C
+        buf = (C.c_char * 128)()
+        if rank == 0:
+            check(lib().syn_tp_unique_id(buf), "syn_tp_unique_id")
+        got = share_id(bytes(buf))
+        if len(got) != 128:
+            raise ValueError("tp id must be 128 bytes")
+        buf = (C.c_char * 128).from_buffer_copy(got)
+        self.h = ctypes.c_void_p()
+        self.rank, self.world, self.device = int(rank), int(world), int(device)
+        check(lib().syn_tp_init(self.rank, self.world, buf, self.device, ctypes.byref(self.h)), "syn_tp_init")
+
+    @classmethod
+    def from_torch_distributed(cls, device):
+        """Join with the ranks of the default torch.distributed group (any backend)."""
+        import torch.distributed as dist
+        rank, world = dist.get_rank(), dist.get_world_size()
+
+        def share(b):
+            obj = [b]
+            dist.broadcast_object_list(obj, src=0)
+            return obj[0]
+        return cls(rank, world, device, share)
+
+    def allgather(self, buf_ptr, bytes_per_rank, stream=None):
+        check(lib().syn_allgather(self.h, buf_ptr, int(bytes_per_rank), stream), "syn_allgather")
+
+    def close(self):
+        if self.h:
+            lib().syn_tp_close(self.h)
+            self.h = None
+
+
 class Session:
-    """A Llama decode session on one GPU: weights, activations and the F16 KV
-    cache in one device arena; each step is a captured CUDA graph."""
+    """A Llama decode session on one GPU (or this rank's share of a
+    tensor-parallel group): weights, activations and the F16 KV cache in one
+    device arena; each step is a captured CUDA graph."""
 
     def __init__(self, handle):
         self.h = handle
@@ -398,21 +467,27 @@ class Session:
         self._logits = np.empty(self.n_vocab, dtype=np.float32)
 
     @classmethod
-    def open(cls, path, max_ctx, device=0):
+    def open(cls, path, max_ctx, device=0, tp=None):
         h = ctypes.c_void_p()
-        check(lib().syn_session_open_gguf(str(path).encode(), int(max_ctx), int(device), ctypes.byref(h)),
-              f"syn_session_open_gguf({path})")
+        check(lib().syn_session_open_gguf_tp(str(path).encode(), int(max_ctx), int(device), tp.h if tp else None,
+                                             ctypes.byref(h)), f"syn_session_open_gguf({path})")
         return cls(h)
 
     @classmethod
-    def synthetic(cls, cfg, max_ctx, seed=0, device=0):
+    def synthetic(cls, cfg, max_ctx, seed=0, device=0, tp=None):
         """cfg: dict with n_layer, n_embd, n_ff, n_head, n_head_kv, head_dim, n_vocab, rms_eps, rope_base,
-        type_embd, type_layers, type_output (-1 = tied)."""
+        type_embd, type_layers, type_output (-1 = tied). tp: a TP group (every rank opens together)."""
         c = LlamaConfig(**{k: cfg[k] for k, _ in LlamaConfig._fields_ if k in cfg})
         h = ctypes.c_void_p()
-        check(lib().syn_session_open_synthetic(ctypes.byref(c), int(max_ctx), int(seed), int(device),
-                                               ctypes.byref(h)), "syn_session_open_synthetic")
+        check(lib().syn_session_open_synthetic_tp(ctypes.byref(c), int(max_ctx), int(seed), int(device),
+                                                  tp.h if tp else None, ctypes.byref(h)),
+              "syn_session_open_synthetic")
         return cls(h)
+
+    def tp_layout(self):
+        out = TPLayout()
+        check(lib().syn_session_tp_layout(self.h, ctypes.byref(out)), "syn_session_tp_layout")
+        return out.as_dict()
 
     def step(self, token, pos, logits=True):
         """One token at pos: (logits copy or None, argmax)."""

@@ -62,6 +62,7 @@ struct AttnParams {
     const float* ff;
     float yarn[5];
     int has_yarn;
+    int split_groups;        // groups the cluster size is chosen for (the whole model's under tensor parallelism)
 };
 
 size_t scratch_bytes(int n_q, int n_head, int max_len) { return align256(size_t(n_q) * n_head * max_len * 4); }
@@ -681,6 +682,7 @@ AttnParams make_params(const syn_attention_args* x) {
     a.theta_scale = x->theta_scale; a.scale = x->scale;
     a.ff = x->freq_factors;
     a.rope_tab = x->rope_table;
+    a.split_groups = x->split_groups > 0 ? x->split_groups : x->n_q * x->n_kv;
     a.has_yarn = x->yarn != nullptr;
     for (int i = 0; i < 5; ++i) a.yarn[i] = x->yarn ? x->yarn[i] : 0.0f;
     return a;
@@ -761,7 +763,7 @@ int pick_cluster(const AttnParams& a, int* out) {
     // context that fits one chunk sums p.V in the reference's order); of
     // those, the fewest waves x positions per CTA, a tie keeping the smaller
     // cluster, which merges fewer partials.
-    const long groups = long(a.n_q) * a.n_kv;
+    const long groups = a.split_groups;
     int best = 1;
     long best_cost = -1;
     for (int c = 1; c <= kMaxCluster; ++c) {

@@ -41,12 +41,13 @@ struct weight {
     bool quant() const { return type == SYN_Q4_0 || type == SYN_Q8_0; }
 };
 
-// A file tensor inside a (possibly fused) device matrix: its row i is the
-// matrix's row row0 + i * step.
+// A file tensor (rows first .. first + rows - 1 of it) inside a (possibly
+// fused) device matrix: its row first + i is the matrix's row row0 + i * step.
 struct source {
     std::string name;
     const weight* w = nullptr;
     int row0 = 0, step = 1, rows = 0;
+    int first = 0;
 };
 
 struct layer_w {
@@ -59,14 +60,14 @@ struct layer_w {
     bool gu_pairs = false;  // gate/up rows interleaved (gate i at 2i, up i at 2i+1) for the silu-pair epilogue
 };
 
-enum class opk { embed, rms_norm, quantize, matmul, attention, silu_mul, argmax };
+enum class opk { embed, rms_norm, quantize, matmul, attention, silu_mul, argmax, allgather };
 
 struct op {
     opk kind;
     const weight* w = nullptr;
     int in = -1, in2 = -1, out = -1, out2 = -1, res = -1, scratch = -1;  // tensor ids
     size_t in_off = 0, out_off = 0, in2_off = 0, res_off = 0;           // float offsets inside tensors
-    int rows = 0, cols = 0;
+    int rows = 0, cols = 0;  // allgather: floats per rank at out_off = rank * cols
     int layer = 0;
     int in_mode = SYN_IN_Q8, out_mode = SYN_OUT_ROWS;  // matmul: fused input / output (syn_gemv)
     const weight* gamma = nullptr;                     // matmul with SYN_IN_RMSNORM
@@ -84,6 +85,8 @@ struct tensor {
 struct syn_session {
     syn_llama_config cfg{};
     int max_ctx = 0, device = 0;
+    syn_tp* tp = nullptr;   // tensor-parallel group (not owned); NULL = one GPU
+    syn_tp_layout part{};   // this rank's share (the whole model when world = 1)
     cudaStream_t stream = nullptr;
     char* arena = nullptr;
     size_t arena_bytes = 0, weight_bytes = 0, kv_bytes = 0, act_bytes = 0;
@@ -121,7 +124,7 @@ struct syn_session {
     void* tb(int t) { return arena + act_off + tensors[t].off; }
     int32_t* io() { return at<int32_t>(io_off); }
     uint16_t* kv(int layer, int which) {
-        const size_t per = size_t(max_ctx) * cfg.n_head_kv * cfg.head_dim;
+        const size_t per = size_t(max_ctx) * part.n_kv * cfg.head_dim;
         return at<uint16_t>(kv_off) + (size_t(layer) * 2 + which) * per;
     }
 };
@@ -204,11 +207,29 @@ bool fusable(const weight& w, int out_mode = SYN_OUT_ROWS) {
 // absorbs its neighbours: the rms_norm (and Q8_0 quantization) before it, the
 // residual add after it, and for gate/up the silu * up epilogue, so a layer is
 // four GEMVs and one attention launch.
+//
+// Sharded over world > 1 ranks, every matrix holds this rank's output rows,
+// attention runs this rank's heads, and each op writes its slice in place
+// into a whole-width tensor that an all-gather then completes on every rank:
+// the attention output, the residual after O, silu * up, the residual after
+// down, and the logits. Inputs (x, the gathered vectors) are whole on every
+// rank, so each output element is computed exactly as on one GPU.
 void build_step(syn_session& s) {
     const syn_llama_config& c = s.cfg;
+    const syn_tp_layout& P = s.part;
+    const bool tp = P.world > 1;
     graph_builder g{s};
-    const int d = c.n_embd, qrows = c.n_head * c.head_dim, kvrows = c.n_head_kv * c.head_dim, ff = c.n_ff;
+    const int d = c.n_embd, hd = c.head_dim, ff = c.n_ff;
+    const int qrows = P.n_head * hd, kvrows = P.n_kv * hd, qall = c.n_head * hd;  // rank's Q, K (V) rows; all heads
+    const size_t x_off = size_t(P.embd0), a_off = size_t(P.head0) * hd, f_off = size_t(P.ff0);
 
+    auto gather = [&](int t, int per_rank) {
+        if (!tp) return;
+        op o{opk::allgather};
+        o.out = t;
+        o.cols = per_rank;
+        g.add(o);
+    };
     int x = g.new_tensor(size_t(d) * 4);
     {
         op o{opk::embed};
@@ -227,19 +248,21 @@ void build_step(syn_session& s) {
         g.add(o);
         return a;
     };
-    auto matmul = [&](const weight& w, const activation& a, int out, size_t out_off, int res) {
+    auto matmul = [&](const weight& w, const activation& a, int out, size_t out_off, int res, size_t res_off) {
         op o{opk::matmul};
         o.w = &w;
         o.in = w.quant() ? a.q8 : a.f32;
         o.out = out;
         o.out_off = out_off;
         o.res = res;
+        o.res_off = res_off;
         o.rows = w.rows;
         o.cols = w.cols;
         g.add(o);
     };
     // y = W * prologue(in) (+ res), the input floats quantized inside the GEMV
-    auto fused = [&](const weight& w, int in, const weight* gamma, int out, int res, int out_mode) {
+    auto fused = [&](const weight& w, int in, const weight* gamma, int out, size_t out_off, int res, size_t res_off,
+                     int out_mode) {
         op o{opk::matmul};
         o.w = &w;
         o.in = in;
@@ -247,7 +270,9 @@ void build_step(syn_session& s) {
         o.in_mode = gamma ? SYN_IN_RMSNORM : SYN_IN_F32;
         o.out_mode = out_mode;
         o.out = out;
+        o.out_off = out_off;
         o.res = res;
+        o.res_off = res_off;
         o.rows = w.rows;
         o.cols = w.cols;
         g.add(o);
@@ -267,75 +292,91 @@ void build_step(syn_session& s) {
         const layer_w& L = s.layers[l];
         const int qkv = g.new_tensor(size_t(qrows + 2 * kvrows) * 4);
         if (L.fused_qkv && fusable(L.q)) {
-            fused(L.q, x, &L.attn_norm, qkv, -1, SYN_OUT_ROWS);
+            fused(L.q, x, &L.attn_norm, qkv, 0, -1, 0, SYN_OUT_ROWS);
         } else {
             const bool qk_any = L.q.quant() || (!L.fused_qkv && (L.k.quant() || L.v.quant()));
             const bool qk_f = !L.q.quant() || (!L.fused_qkv && (!L.k.quant() || !L.v.quant()));
             activation h = norm(x, L.attn_norm, qk_f, qk_any);
-            matmul(L.q, h, qkv, 0, -1);
+            matmul(L.q, h, qkv, 0, -1, 0);
             if (!L.fused_qkv) {
-                matmul(L.k, h, qkv, qrows, -1);
-                matmul(L.v, h, qkv, qrows + kvrows, -1);
+                matmul(L.k, h, qkv, qrows, -1, 0);
+                matmul(L.v, h, qkv, qrows + kvrows, -1, 0);
             }
         }
-        const int attn = g.new_tensor(size_t(qrows) * 4);
+        const int attn = g.new_tensor(size_t(qall) * 4);
         {
             op o{opk::attention};
             o.in = qkv;
             o.out = attn;
+            o.out_off = a_off;
             o.layer = l;
-            o.scratch = g.new_tensor(syn_attention_scratch_bytes(1, c.n_head, c.n_head_kv, c.head_dim, s.max_ctx));
+            o.scratch = g.new_tensor(syn_attention_scratch_bytes(1, P.n_head, P.n_kv, hd, s.max_ctx));
             g.add(o);
         }
+        gather(attn, qrows);
         const int x2 = g.new_tensor(size_t(d) * 4);
         if (fusable(L.o)) {
-            fused(L.o, attn, nullptr, x2, x, SYN_OUT_ROWS);
+            fused(L.o, attn, nullptr, x2, x_off, x, x_off, SYN_OUT_ROWS);
         } else {
             activation a;
             a.f32 = attn;
-            if (L.o.quant()) a = quantize(attn, qrows);
-            matmul(L.o, a, x2, 0, x);
+            if (L.o.quant()) a = quantize(attn, qall);
+            matmul(L.o, a, x2, x_off, x, x_off);
         }
+        gather(x2, P.n_embd);
         x = x2;
         const int x3 = g.new_tensor(size_t(d) * 4);
         if (L.gu_pairs) {  // fusable(L.gate, SYN_OUT_SILU_PAIRS) held when the rows were interleaved
             const int act = g.new_tensor(size_t(ff) * 4);
-            fused(L.gate, x, &L.ffn_norm, act, -1, SYN_OUT_SILU_PAIRS);
+            fused(L.gate, x, &L.ffn_norm, act, f_off, -1, 0, SYN_OUT_SILU_PAIRS);
+            gather(act, P.n_ff);
             if (fusable(L.down)) {
-                fused(L.down, act, nullptr, x3, x, SYN_OUT_ROWS);
+                fused(L.down, act, nullptr, x3, x_off, x, x_off, SYN_OUT_ROWS);
             } else {
                 activation f;
                 f.f32 = act;
                 if (L.down.quant()) f = quantize(act, ff);
-                matmul(L.down, f, x3, 0, x);
+                matmul(L.down, f, x3, x_off, x, x_off);
             }
         } else {
             const bool gu_any = L.gate.quant() || (!L.fused_gu && L.up.quant());
             const bool gu_f = !L.gate.quant() || (!L.fused_gu && !L.up.quant());
             activation h2 = norm(x, L.ffn_norm, gu_f, gu_any);
-            const int gu = g.new_tensor(size_t(2) * ff * 4);
-            matmul(L.gate, h2, gu, 0, -1);
-            if (!L.fused_gu) matmul(L.up, h2, gu, ff, -1);
+            const int gu = g.new_tensor(size_t(2) * P.n_ff * 4);
+            matmul(L.gate, h2, gu, 0, -1, 0);
+            if (!L.fused_gu) matmul(L.up, h2, gu, size_t(P.n_ff), -1, 0);
             activation f;
             {
                 op o{opk::silu_mul};
                 o.in = gu;
-                o.cols = ff;
-                if (L.down.quant()) f.q8 = o.out2 = g.new_tensor(act_bytes_for(ff));
-                else f.f32 = o.out = g.new_tensor(size_t(ff) * 4);
+                o.cols = P.n_ff;
+                if (tp) {  // floats into the whole-width tensor, gathered, then quantized whole
+                    f.f32 = o.out = g.new_tensor(size_t(ff) * 4);
+                    o.out_off = f_off;
+                } else if (L.down.quant()) {
+                    f.q8 = o.out2 = g.new_tensor(act_bytes_for(ff));
+                } else {
+                    f.f32 = o.out = g.new_tensor(size_t(ff) * 4);
+                }
                 g.add(o);
             }
-            matmul(L.down, f, x3, 0, x);
+            if (tp) {
+                gather(f.f32, P.n_ff);
+                if (L.down.quant()) f = quantize(f.f32, ff);
+            }
+            matmul(L.down, f, x3, x_off, x, x_off);
         }
+        gather(x3, P.n_embd);
         x = x3;
     }
     s.logits_t = g.new_tensor(size_t(c.n_vocab) * 4);
     if (fusable(s.head)) {
-        fused(s.head, x, &s.out_norm, s.logits_t, -1, SYN_OUT_ROWS);
+        fused(s.head, x, &s.out_norm, s.logits_t, size_t(P.vocab0), -1, 0, SYN_OUT_ROWS);
     } else {
         activation hl = norm(x, s.out_norm, !s.head.quant(), s.head.quant());
-        matmul(s.head, hl, s.logits_t, 0, -1);
+        matmul(s.head, hl, s.logits_t, size_t(P.vocab0), -1, 0);
     }
+    gather(s.logits_t, P.n_vocab);
     {
         op o{opk::argmax};
         o.in = s.logits_t;
@@ -369,7 +410,7 @@ int enqueue_body(syn_session& s, cudaStream_t st) {
 
 int enqueue_ops(syn_session& s, cudaStream_t st) {
     const syn_llama_config& c = s.cfg;
-    const int qrows = c.n_head * c.head_dim, kvrows = c.n_head_kv * c.head_dim;
+    const int qrows = s.part.n_head * c.head_dim, kvrows = s.part.n_kv * c.head_dim;  // this rank's heads
     int rc = SYN_OK;
     for (const op& o : s.ops) {
         switch (o.kind) {
@@ -386,7 +427,7 @@ int enqueue_ops(syn_session& s, cudaStream_t st) {
             break;
         case opk::matmul: {
             float* y = s.tf(o.out, o.out_off);
-            const float* res = o.res >= 0 ? s.tf(o.res) : nullptr;
+            const float* res = o.res >= 0 ? s.tf(o.res, o.res_off) : nullptr;
             if (o.in_mode != SYN_IN_Q8 || o.out_mode != SYN_OUT_ROWS) {
                 syn_gemv_args a{};
                 a.type = o.w->type;
@@ -419,12 +460,12 @@ int enqueue_ops(syn_session& s, cudaStream_t st) {
             a.k_cache = s.kv(o.layer, 0);
             a.v_cache = s.kv(o.layer, 1);
             a.pos = s.io() + 1;
-            a.out = s.tf(o.out);
+            a.out = s.tf(o.out, o.out_off);
             a.scratch = s.tb(o.scratch);
             a.cache_stride = 0;
             a.n_q = 1;
-            a.n_head = c.n_head;
-            a.n_kv = c.n_head_kv;
+            a.n_head = s.part.n_head;
+            a.n_kv = s.part.n_kv;
             a.head_dim = c.head_dim;
             a.max_len = s.max_ctx;
             a.append = 1;
@@ -434,12 +475,16 @@ int enqueue_ops(syn_session& s, cudaStream_t st) {
             a.scale = s.scale;
             a.freq_factors = s.has_ff ? s.at<float>(s.ff_off) : nullptr;
             a.rope_table = s.at<float>(s.rope_tab_off);
+            a.split_groups = c.n_head_kv;  // the one-GPU split on every rank
             rc = syn_attention(&a, st);
             break;
         }
         case opk::silu_mul:
-            rc = syn_silu_mul(s.tf(o.in), s.tf(o.in, size_t(o.cols)), 1, o.cols, o.out >= 0 ? s.tf(o.out) : nullptr,
-                              o.out2 >= 0 ? s.tb(o.out2) : nullptr, st);
+            rc = syn_silu_mul(s.tf(o.in), s.tf(o.in, size_t(o.cols)), 1, o.cols,
+                              o.out >= 0 ? s.tf(o.out, o.out_off) : nullptr, o.out2 >= 0 ? s.tb(o.out2) : nullptr, st);
+            break;
+        case opk::allgather:
+            rc = syn_allgather(s.tp, s.tf(o.out), size_t(o.cols) * 4, st);
             break;
         case opk::argmax:
             rc = syn_argmax_ws(s.tf(o.in), 1, c.n_vocab, s.io() + 2, s.arena + s.argmax_ws_off, st);
@@ -613,7 +658,7 @@ int fill_step_plan(syn_session& s) {
 int finish(syn_session& s, layout_builder& lb) {
     const syn_llama_config& c = s.cfg;
     s.weight_bytes = lb.off;
-    s.kv_bytes = size_t(c.n_layer) * 2 * s.max_ctx * c.n_head_kv * c.head_dim * 2;
+    s.kv_bytes = size_t(c.n_layer) * 2 * s.max_ctx * s.part.n_kv * c.head_dim * 2;
     s.kv_off = lb.take(s.kv_bytes);
     build_step(s);
     int rc = plan_step(s);
@@ -624,7 +669,7 @@ int finish(syn_session& s, layout_builder& lb) {
     s.hist_off = lb.take(size_t(s.max_ctx) * 4);
     s.argmax_ws_off = lb.take(syn_argmax_ws_bytes(1));  // persistent: its counters must stay zero between steps
     s.rope_tab_off = lb.take(size_t(s.max_ctx) * c.head_dim * 4);
-    plan_step_kernel(s, lb);
+    if (s.part.world == 1) plan_step_kernel(s, lb);
     s.arena_bytes = lb.off;
     s.theta_scale = std::pow(c.rope_base, -2.0f / float(c.head_dim));  // attention.hpp:47
     s.scale = 1.0f / std::sqrt(float(c.head_dim));                      // llama.hpp:407
@@ -665,9 +710,16 @@ int warm_and_capture(syn_session& s) {
     return SYN_OK;
 }
 
+// Each layer's matrices as this rank holds them (the whole model at world
+// 1): Q/K/V rows of its heads (fused into one matrix when their types
+// match), its rows of O, gate/up (interleaved in pairs for the silu epilogue
+// when that kernel takes the shape) and down, and the norms whole.
 void layer_layout(syn_session& s, const std::vector<std::vector<int>>& types, layout_builder& lb) {
     const syn_llama_config& c = s.cfg;
-    const int d = c.n_embd, qrows = c.n_head * c.head_dim, kvrows = c.n_head_kv * c.head_dim, ff = c.n_ff;
+    const syn_tp_layout& P = s.part;
+    const int d = c.n_embd, hd = c.head_dim, qall = c.n_head * hd;
+    const int qrows = P.n_head * hd, kvrows = P.n_kv * hd, ff = P.n_ff;
+    const int q0 = P.head0 * hd, kv0 = P.kv_head0 * hd;
     s.layers.resize(c.n_layer);
     for (int l = 0; l < c.n_layer; ++l) {
         layer_w& L = s.layers[l];
@@ -677,42 +729,90 @@ void layer_layout(syn_session& s, const std::vector<std::vector<int>>& types, la
         L.fused_qkv = t[1] == t[2] && t[1] == t[3] && (t[1] == SYN_Q4_0 || t[1] == SYN_Q8_0);
         if (L.fused_qkv) {
             define(L.q, t[1], qrows + 2 * kvrows, d, lb);
-            s.sources.push_back({p + "attn_q.weight", &L.q, 0, 1, qrows});
-            s.sources.push_back({p + "attn_k.weight", &L.q, qrows, 1, kvrows});
-            s.sources.push_back({p + "attn_v.weight", &L.q, qrows + kvrows, 1, kvrows});
+            s.sources.push_back({p + "attn_q.weight", &L.q, 0, 1, qrows, q0});
+            s.sources.push_back({p + "attn_k.weight", &L.q, qrows, 1, kvrows, kv0});
+            s.sources.push_back({p + "attn_v.weight", &L.q, qrows + kvrows, 1, kvrows, kv0});
         } else {
             define(L.q, t[1], qrows, d, lb);
             define(L.k, t[2], kvrows, d, lb);
             define(L.v, t[3], kvrows, d, lb);
-            s.sources.push_back({p + "attn_q.weight", &L.q, 0, 1, qrows});
-            s.sources.push_back({p + "attn_k.weight", &L.k, 0, 1, kvrows});
-            s.sources.push_back({p + "attn_v.weight", &L.v, 0, 1, kvrows});
+            s.sources.push_back({p + "attn_q.weight", &L.q, 0, 1, qrows, q0});
+            s.sources.push_back({p + "attn_k.weight", &L.k, 0, 1, kvrows, kv0});
+            s.sources.push_back({p + "attn_v.weight", &L.v, 0, 1, kvrows, kv0});
         }
-        define(L.o, t[4], d, qrows, lb);
-        s.sources.push_back({p + "attn_output.weight", &L.o, 0, 1, d});
+        define(L.o, t[4], P.n_embd, qall, lb);
+        s.sources.push_back({p + "attn_output.weight", &L.o, 0, 1, P.n_embd, P.embd0});
         define(L.ffn_norm, SYN_F32, 1, d, lb);
         L.fused_gu = t[6] == t[7] && (t[6] == SYN_Q4_0 || t[6] == SYN_Q8_0);
         if (L.fused_gu) {
             define(L.gate, t[6], 2 * ff, d, lb);
             L.gu_pairs = syn_gemv_fusable(t[6], SYN_LAYOUT_PLANAR, 2 * ff, d, 1, SYN_OUT_SILU_PAIRS) != 0;
             if (L.gu_pairs) {
-                s.sources.push_back({p + "ffn_gate.weight", &L.gate, 0, 2, ff});
-                s.sources.push_back({p + "ffn_up.weight", &L.gate, 1, 2, ff});
+                s.sources.push_back({p + "ffn_gate.weight", &L.gate, 0, 2, ff, P.ff0});
+                s.sources.push_back({p + "ffn_up.weight", &L.gate, 1, 2, ff, P.ff0});
             } else {
-                s.sources.push_back({p + "ffn_gate.weight", &L.gate, 0, 1, ff});
-                s.sources.push_back({p + "ffn_up.weight", &L.gate, ff, 1, ff});
+                s.sources.push_back({p + "ffn_gate.weight", &L.gate, 0, 1, ff, P.ff0});
+                s.sources.push_back({p + "ffn_up.weight", &L.gate, ff, 1, ff, P.ff0});
             }
         } else {
             define(L.gate, t[6], ff, d, lb);
             define(L.up, t[7], ff, d, lb);
-            s.sources.push_back({p + "ffn_gate.weight", &L.gate, 0, 1, ff});
-            s.sources.push_back({p + "ffn_up.weight", &L.up, 0, 1, ff});
+            s.sources.push_back({p + "ffn_gate.weight", &L.gate, 0, 1, ff, P.ff0});
+            s.sources.push_back({p + "ffn_up.weight", &L.up, 0, 1, ff, P.ff0});
         }
-        define(L.down, t[8], d, ff, lb);
-        s.sources.push_back({p + "ffn_down.weight", &L.down, 0, 1, d});
+        define(L.down, t[8], P.n_embd, c.n_ff, lb);
+        s.sources.push_back({p + "ffn_down.weight", &L.down, 0, 1, P.n_embd, P.embd0});
         s.sources.push_back({p + "attn_norm.weight", &L.attn_norm, 0, 1, 1});
         s.sources.push_back({p + "ffn_norm.weight", &L.ffn_norm, 0, 1, 1});
     }
+}
+
+// The output head as this rank holds it: its rows of output.weight, or of
+// the token embedding when the two are tied (llama.hpp:471-472).
+void head_layout(syn_session& s, layout_builder& lb) {
+    const syn_llama_config& c = s.cfg;
+    const syn_tp_layout& P = s.part;
+    if (c.type_output >= 0) {
+        define(s.head, c.type_output, P.n_vocab, c.n_embd, lb);
+        s.sources.push_back({"output.weight", &s.head, 0, 1, P.n_vocab, P.vocab0});
+    } else {
+        s.head = s.embd;
+        s.head.off += P.vocab0 ? weight_size(s.embd.type, P.vocab0, c.n_embd) : 0;
+        s.head.rows = P.n_vocab;
+        s.head.bytes = weight_size(s.embd.type, P.n_vocab, c.n_embd);
+    }
+}
+
+// Rank's contiguous equal share of every sharded dimension.
+int tp_layout(const syn_llama_config& c, int rank, int world, syn_tp_layout& L) {
+    if (world < 1 || rank < 0 || rank >= world) return SYN_ERR_INVALID;
+    if (c.n_head_kv % world || c.n_embd % world || c.n_ff % world || c.n_vocab % world || c.n_head % c.n_head_kv)
+        return SYN_ERR_UNSUPPORTED;
+    const int G = c.n_head / c.n_head_kv;
+    L.rank = rank;
+    L.world = world;
+    L.n_kv = c.n_head_kv / world;
+    L.kv_head0 = rank * L.n_kv;
+    L.n_head = L.n_kv * G;  // the query heads of those KV groups
+    L.head0 = L.kv_head0 * G;
+    L.n_embd = c.n_embd / world;
+    L.embd0 = rank * L.n_embd;
+    L.n_ff = c.n_ff / world;
+    L.ff0 = rank * L.n_ff;
+    L.n_vocab = c.n_vocab / world;
+    L.vocab0 = rank * L.n_vocab;
+    return SYN_OK;
+}
+
+// The session's group and share; the device must be the group's.
+int set_part(syn_session& s, syn_tp* tp, int device) {
+    int rank = 0, world = 1, tdev = -1;
+    syn_tp_info(tp, &rank, &world, &tdev);
+    if (tp && tdev != device) return set_err(SYN_ERR_INVALID, "session device differs from the tp group's");
+    s.tp = tp;
+    const int rc = tp_layout(s.cfg, rank, world, s.part);
+    if (rc) return set_err(rc, "tensor parallel: world must divide n_head_kv, n_embd, n_ff and n_vocab");
+    return SYN_OK;
 }
 
 void destroy(syn_session* s) {
@@ -739,6 +839,10 @@ bool shape_is(const syn::gguf::tensor_info& t, uint64_t rows, uint64_t cols) {
 }  // namespace
 
 extern "C" int syn_session_open_gguf(const char* path, int max_ctx, int device, syn_session** out) {
+    return syn_session_open_gguf_tp(path, max_ctx, device, nullptr, out);
+}
+
+extern "C" int syn_session_open_gguf_tp(const char* path, int max_ctx, int device, syn_tp* tp, syn_session** out) {
     if (!path || !out || max_ctx <= 0) return SYN_ERR_INVALID;
     *out = nullptr;
     std::unique_ptr<syn::gguf::file> f;
@@ -833,18 +937,14 @@ extern "C" int syn_session_open_gguf(const char* path, int max_ctx, int device, 
     const syn::gguf::tensor_info* rf = f->tensor("rope_freqs.weight");
     if (rf && (rf->type != SYN_F32 || rf->n_elements() != hd / 2)) return set_err(SYN_ERR_FORMAT, "rope_freqs.weight");
 
+    if ((rc = set_part(*s, tp, device))) return rc;
     layout_builder lb;
     define(s->embd, c.type_embd, c.n_vocab, c.n_embd, lb);
     s->sources.push_back({"token_embd.weight", &s->embd, 0, 1, c.n_vocab});
     layer_layout(*s, types, lb);
     define(s->out_norm, SYN_F32, 1, c.n_embd, lb);
     s->sources.push_back({"output_norm.weight", &s->out_norm, 0, 1, 1});
-    if (tout) {
-        define(s->head, c.type_output, c.n_vocab, c.n_embd, lb);
-        s->sources.push_back({"output.weight", &s->head, 0, 1, c.n_vocab});
-    } else {
-        s->head = s->embd;  // tied (llama.hpp:471-472)
-    }
+    head_layout(*s, lb);
     if (rf) {
         s->has_ff = true;
         s->ff_off = lb.take(size_t(hd / 2) * 4);
@@ -858,13 +958,13 @@ extern "C" int syn_session_open_gguf(const char* path, int max_ctx, int device, 
     for (const auto& src : s->sources) {
         const syn::gguf::tensor_info* t = f->tensor(src.name);
         const weight& w = *src.w;
-        const uint8_t* data = f->data(*t);
+        const size_t row_bytes = t->nbytes / size_t(t->rows());
+        const uint8_t* data = f->data(*t) + size_t(src.first) * row_bytes;  // this rank's rows of the tensor
+        const int rows = src.rows;
         if (!w.quant()) {
             rc = cuda(cudaMemcpyAsync(s->arena + w.off + size_t(src.row0) * w.cols * (w.type == SYN_F32 ? 4 : 2), data,
-                                      t->nbytes, cudaMemcpyHostToDevice, s->stream));
+                                      size_t(rows) * row_bytes, cudaMemcpyHostToDevice, s->stream));
         } else {
-            const int rows = int(t->rows());
-            const size_t row_bytes = t->nbytes / size_t(rows);
             const int per = int(staging_bytes / row_bytes);
             for (int r0 = 0; r0 < rows && !rc; r0 += per) {
                 const int n = rows - r0 < per ? rows - r0 : per;
@@ -890,6 +990,11 @@ extern "C" int syn_session_open_gguf(const char* path, int max_ctx, int device, 
 
 extern "C" int syn_session_open_synthetic(const syn_llama_config* cp, int max_ctx, uint64_t seed, int device,
                                           syn_session** out) {
+    return syn_session_open_synthetic_tp(cp, max_ctx, seed, device, nullptr, out);
+}
+
+extern "C" int syn_session_open_synthetic_tp(const syn_llama_config* cp, int max_ctx, uint64_t seed, int device,
+                                             syn_tp* tp, syn_session** out) {
     if (!cp || !out || max_ctx <= 0) return SYN_ERR_INVALID;
     *out = nullptr;
     const syn_llama_config& c0 = *cp;
@@ -907,6 +1012,8 @@ extern "C" int syn_session_open_synthetic(const syn_llama_config* cp, int max_ct
     s->cfg = c0;
     s->cfg.rope_mode = 0;
     const syn_llama_config& c = s->cfg;
+    int rc = set_part(*s, tp, device);
+    if (rc) return rc;
     layout_builder lb;
     define(s->embd, c.type_embd, c.n_vocab, c.n_embd, lb);
     s->sources.push_back({"token_embd.weight", &s->embd, 0, 1, c.n_vocab});
@@ -914,13 +1021,8 @@ extern "C" int syn_session_open_synthetic(const syn_llama_config* cp, int max_ct
     layer_layout(*s, std::vector<std::vector<int>>(c.n_layer, {SYN_F32, T, T, T, T, SYN_F32, T, T, T}), lb);
     define(s->out_norm, SYN_F32, 1, c.n_embd, lb);
     s->sources.push_back({"output_norm.weight", &s->out_norm, 0, 1, 1});
-    if (c.type_output >= 0) {
-        define(s->head, c.type_output, c.n_vocab, c.n_embd, lb);
-        s->sources.push_back({"output.weight", &s->head, 0, 1, c.n_vocab});
-    } else {
-        s->head = s->embd;
-    }
-    int rc = finish(*s, lb);
+    head_layout(*s, lb);
+    rc = finish(*s, lb);
     if (rc) return rc;
     // Every matrix N(0, 0.02) (seeded per tensor name), norms 1.0.
     uint64_t tensor_id = 0;
@@ -931,7 +1033,7 @@ extern "C" int syn_session_open_synthetic(const syn_llama_config* cp, int max_ct
             rc = syn_fill_f32(s->at<float>(w.off), size_t(w.cols), 1.0f, s->stream);
         else
             rc = syn_fill_random(w.type, src.rows, w.cols, s->arena + w.off, w.rows, src.row0, seed, tensor_id, 0.02f,
-                                 s->stream, src.step);
+                                 s->stream, src.step, src.first);
         if (rc) return rc;
     }
     if ((rc = cuda(cudaStreamSynchronize(s->stream)))) return rc;
@@ -941,6 +1043,17 @@ extern "C" int syn_session_open_synthetic(const syn_llama_config* cp, int max_ct
 }
 
 extern "C" void syn_session_close(syn_session* s) { destroy(s); }
+
+extern "C" int syn_tp_layout_of(const syn_llama_config* c, int rank, int world, syn_tp_layout* out) {
+    if (!c || !out || c->n_head_kv <= 0 || c->n_head <= 0) return SYN_ERR_INVALID;
+    return tp_layout(*c, rank, world, *out);
+}
+
+extern "C" int syn_session_tp_layout(const syn_session* s, syn_tp_layout* out) {
+    if (!s || !out) return SYN_ERR_INVALID;
+    *out = s->part;
+    return SYN_OK;
+}
 
 extern "C" int syn_session_config(const syn_session* s, syn_llama_config* out) {
     if (!s || !out) return SYN_ERR_INVALID;
@@ -1008,7 +1121,7 @@ extern "C" int syn_session_generate(syn_session* s, const uint32_t* prompt, int 
 extern "C" int syn_session_launches_per_step(const syn_session* s) {
     if (!s) return 0;
     int n = 1;  // advance
-    for (const op& o : s->ops) n += o.kind == opk::attention ? 2 : 1;
+    for (const op& o : s->ops) n += o.kind == opk::attention ? 2 : o.kind == opk::allgather ? 0 : 1;  // NCCL's own kernels aside
     return n;
 }
 
@@ -1038,6 +1151,7 @@ double op_bytes(const syn_session& s, const op& o, uint32_t pos) {
     }
     case opk::silu_mul: return double(o.cols) * (8 + 1.125);
     case opk::argmax: return double(c.n_vocab) * 4;
+    case opk::allgather: return double(o.cols) * 4 * s.part.world;  // the whole vector lands on every rank
     }
     return 0;
 }
@@ -1051,6 +1165,7 @@ int op_kind_code(opk k) {
     case opk::attention: return SYN_OP_ATTENTION;
     case opk::silu_mul: return SYN_OP_SILU_MUL;
     case opk::argmax: return SYN_OP_ARGMAX;
+    case opk::allgather: return SYN_OP_ALLGATHER;
     }
     return -1;
 }

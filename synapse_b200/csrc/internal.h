@@ -13,9 +13,11 @@ int syn_repack_rows(int type, const void* src, int rows, int cols, void* dst, in
 
 // Random N(0, sigma) values, seeded by (seed, tensor, element), quantized with
 // ggml's reference quantizer (Q4_0 / Q8_0) into rows [row0, row0 + rows) of a
-// planar matrix of total_rows, or written as F32 / F16 (row0 must be 0).
+// planar matrix of total_rows, or written as F32 / F16 rows [row0, row0 + rows).
+// Values are those of rows first_row .. of the tensor (seed, tensor), so a
+// slice of a matrix holds the same weights as the whole matrix's rows.
 int syn_fill_random(int type, int rows, int cols, void* dst, int total_rows, int row0, uint64_t seed,
-                    uint64_t tensor, float sigma, cudaStream_t s, int row_step = 1);
+                    uint64_t tensor, float sigma, cudaStream_t s, int row_step = 1, long first_row = 0);
 // dst[i] = v for n floats.
 int syn_fill_f32(float* dst, size_t n, float v, cudaStream_t s);
 
@@ -40,6 +42,10 @@ extern "C" void syn_set_programmatic_launch(int on);
 
 // Sets the thread's last error message.
 void syn_set_error(const char* msg);
+
+// Rank, world size and device of a tensor-parallel group (tp.cpp).
+struct syn_tp;
+void syn_tp_info(const syn_tp* tp, int* rank, int* world, int* device);
 
 // Self-check of the library's expf (exp_rn): y = exp_rn(x) and, for
 // comparison, y_ref = exp(double(x)) rounded to float, for n device floats.

@@ -82,14 +82,14 @@ __device__ __forceinline__ float normal_at(uint64_t seed, uint64_t tensor, uint6
 // One thread per 32-weight block: generate, then ggml's reference quantizer
 // (quantize_row_q4_0_ref / quantize_row_q8_0_ref; quant/q8.hpp:54-69).
 __global__ void fill_random_q_kernel(int type, int rows, int cols, uint8_t* dst, int row0, int row_step,
-                                     uint64_t seed, uint64_t tensor, float sigma) {
+                                     uint64_t seed, uint64_t tensor, float sigma, uint64_t first_block) {
     const int nb = cols / QK;
     const long i = long(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= long(rows) * nb) return;
     float x[QK];
     float amax = 0.0f, mx = 0.0f;
     for (int j = 0; j < QK; ++j) {
-        x[j] = __fmul_rn(normal_at(seed, tensor, uint64_t(i) * QK + j), sigma);
+        x[j] = __fmul_rn(normal_at(seed, tensor, (first_block + uint64_t(i)) * QK + j), sigma);
         const float a = fabsf(x[j]);
         if (amax < a) { amax = a; mx = x[j]; }
     }
@@ -116,9 +116,10 @@ __global__ void fill_random_q_kernel(int type, int rows, int cols, uint8_t* dst,
     }
 }
 
-__global__ void fill_random_f_kernel(int type, size_t n, void* dst, uint64_t seed, uint64_t tensor, float sigma) {
+__global__ void fill_random_f_kernel(int type, size_t n, void* dst, uint64_t seed, uint64_t tensor, float sigma,
+                                     uint64_t first) {
     for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {
-        const float v = __fmul_rn(normal_at(seed, tensor, i), sigma);
+        const float v = __fmul_rn(normal_at(seed, tensor, first + i), sigma);
         if (type == SYN_F32) static_cast<float*>(dst)[i] = v;
         else static_cast<uint16_t*>(dst)[i] = f16_bits(v);
     }
@@ -146,15 +147,19 @@ int syn_repack_rows(int type, const void* src, int rows, int cols, void* dst, in
 }
 
 int syn_fill_random(int type, int rows, int cols, void* dst, int total_rows, int row0, uint64_t seed,
-                    uint64_t tensor, float sigma, cudaStream_t s, int row_step) {
+                    uint64_t tensor, float sigma, cudaStream_t s, int row_step, long first_row) {
+    if (first_row < 0) return SYN_ERR_INVALID;
     if (quant_type(type)) {
         if (row0 < 0 || row_step < 1 || long(row0) + long(rows - 1) * row_step >= total_rows) return SYN_ERR_INVALID;
         const long n = long(rows) * (cols / QK);
         fill_random_q_kernel<<<(n + 127) / 128, 128, 0, s>>>(type, rows, cols, static_cast<uint8_t*>(dst), row0,
-                                                              row_step, seed, tensor, sigma);
+                                                              row_step, seed, tensor, sigma,
+                                                              uint64_t(first_row) * (cols / QK));
     } else if (type == SYN_F32 || type == SYN_F16) {
-        if (row0 != 0) return SYN_ERR_INVALID;
-        fill_random_f_kernel<<<4096, 256, 0, s>>>(type, size_t(rows) * cols, dst, seed, tensor, sigma);
+        if (row0 < 0 || row_step != 1 || long(row0) + rows > total_rows) return SYN_ERR_INVALID;
+        char* d = static_cast<char*>(dst) + size_t(row0) * cols * (type == SYN_F32 ? 4 : 2);
+        fill_random_f_kernel<<<4096, 256, 0, s>>>(type, size_t(rows) * cols, d, seed, tensor, sigma,
+                                                  uint64_t(first_row) * cols);
     } else {
         return SYN_ERR_UNSUPPORTED;
     }

@@ -1,0 +1,123 @@
+"""Tensor parallelism on 2 or more GPUs of one node, through the session's C
+ABI: each rank holds its heads and rows, NCCL all-gathers in place inside
+the captured step graph, and the logits (and greedy tokens) equal one GPU's
+bit for bit, the reference's D1 contract (tests/unit/llama_threads.cpp:32)
+across GPUs. Skipped on a box with fewer than 2 GPUs."""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+syn = pytest.importorskip("synapse_b200")
+torch = pytest.importorskip("torch")
+
+from synapse_b200 import model  # noqa: E402
+
+SHAPES = {
+    # Llama-3-8B widths, two layers: the fused GEMV and cluster-attention paths
+    "8b_2layer_q4_0": dict(n_layer=2, n_embd=4096, n_ff=14336, n_head=32, n_head_kv=8, head_dim=128, n_vocab=128256,
+                           rms_eps=1e-5, rope_base=500000.0, rope_mode=0, type_embd=model.F32,
+                           type_layers=model.Q4_0, type_output=model.Q8_0),
+    # BASELINE config 1's tiny model (Q8_0 layers, tied F32 embedding head): the unfused fallbacks
+    "tiny_q8_0_tied": dict(n_layer=6, n_embd=288, n_ff=768, n_head=6, n_head_kv=6, head_dim=48, n_vocab=32000,
+                           rms_eps=1e-5, rope_base=10000.0, rope_mode=0, type_embd=model.F32,
+                           type_layers=model.Q8_0, type_output=-1),
+}
+
+
+def _gpus():
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _tokens(cfg, n):
+    return [int(t) for t in np.random.default_rng(11).integers(0, cfg["n_vocab"], n)]
+
+
+def _rank_main(rank, world, port, shape, max_ctx, positions, q):
+    import torch.distributed as dist
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    tp = sess = None
+    try:
+        torch.cuda.set_device(rank)
+        tp = syn.TP.from_torch_distributed(device=rank)
+        cfg = SHAPES[shape]
+        sess = syn.Session.synthetic(cfg, max_ctx=max_ctx, seed=5, device=rank, tp=tp)
+        layout = sess.tp_layout()
+        toks = _tokens(cfg, len(positions))
+        logits, nxt = [], []
+        for t, pos in zip(toks, positions):
+            lg, n = sess.step(t, pos)
+            logits.append(lg)
+            nxt.append(n)
+        sess.reset()
+        gen = sess.generate(toks[:4], 0, 12)
+        q.put((rank, dict(logits=np.stack(logits), next=nxt, gen=gen, layout=layout,
+                          launches=sess.launches_per_step())))
+    except Exception as e:
+        q.put((rank, repr(e)))
+    finally:
+        if sess is not None:
+            sess.close()
+        if tp is not None:
+            tp.close()
+        dist.destroy_process_group()
+
+
+def _run_world(world, shape, max_ctx, positions):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, shape, max_ctx, positions, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=600) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+    for r in range(world):
+        assert not isinstance(got[r], str), f"rank {r}: {got[r]}"
+    return got
+
+
+def _one_gpu(shape, max_ctx, positions):
+    cfg = SHAPES[shape]
+    sess = syn.Session.synthetic(cfg, max_ctx=max_ctx, seed=5, device=0)
+    toks = _tokens(cfg, len(positions))
+    logits = np.stack([sess.step(t, pos)[0] for t, pos in zip(toks, positions)])
+    sess.reset()
+    gen = sess.generate(toks[:4], 0, 12)
+    sess.close()
+    return logits, gen
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("shape", list(SHAPES))
+def test_tp_equals_one_gpu(world, shape):
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    cfg = SHAPES[shape]
+    if cfg["n_head_kv"] % world or cfg["n_vocab"] % world or cfg["n_ff"] % world or cfg["n_embd"] % world:
+        pytest.skip("world does not divide the model")
+    max_ctx = 1024
+    # single-chunk contexts, then positions past kExactChunk where the context is split over a cluster
+    positions = list(range(8)) + [300, 301, 700, 1023]
+    got = _run_world(world, shape, max_ctx, positions)
+    want, want_gen = _one_gpu(shape, max_ctx, positions)
+    for r in range(world):
+        g = got[r]
+        assert g["layout"]["rank"] == r and g["layout"]["world"] == world
+        assert np.array_equal(g["logits"].view(np.uint32), want.view(np.uint32)), f"rank {r}"
+        assert g["next"] == [int(np.argmax(x)) for x in want]
+        assert np.array_equal(g["gen"], want_gen), f"rank {r} greedy tokens"
