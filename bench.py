@@ -22,8 +22,12 @@ cpu_baseline : the C oracle (a restatement of the reference's CPU kernels) on
 --impl reference: the reference's CPU path (the oracle port; the reference's
 own headers need MTL5, absent here) on all host cores, same metric and unit.
 
-Multi-GPU (torchrun, N ranks): each GPU decodes its own sequence (replicas,
-weak scaling); value = tokens of all ranks / max over ranks of the time.
+Multi-GPU (torchrun, N ranks), --parallel tp (default): one sequence,
+tensor-parallel over the N GPUs (KV-head groups and GEMV output rows, NCCL
+all-gathers in the step graph; logits bit-identical to one GPU), strong
+scaling; value = tokens / max over ranks of the device time.
+--parallel replicas: each GPU decodes its own sequence (weak scaling); value
+= tokens of all ranks / max over ranks of the time.
 """
 import argparse
 import json
@@ -51,6 +55,8 @@ def parse():
     p.add_argument("--steps", type=int, default=None, help="timed decode steps (default: to 4096 context)")
     p.add_argument("--warmup", type=int, default=16)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--parallel", default="tp", choices=["tp", "replicas"],
+                   help="N > 1: tensor-parallel one sequence (tp) or one sequence per GPU (replicas)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--profile-out", default=None, help="write the per-op device times of one step (JSON) here")
     p.add_argument("--ncu-step", type=int, default=0,
@@ -267,9 +273,14 @@ def main():
     K = args.steps if args.steps is not None else CTX - PROMPT - W
     max_ctx = max(CTX, PROMPT + W + K)
     cfg = dict(LLAMA8B, type_embd=syn.Q4_0, type_layers=syn.Q4_0, type_output=syn.Q8_0)
-    sess = syn.Session.synthetic(cfg, max_ctx=max_ctx, seed=1234 + rank, device=local)
+    tp_mode = world > 1 and args.parallel == "tp"
+    tp = syn.TP.from_torch_distributed(device=local) if tp_mode else None
+    seed_rank = 0 if tp_mode else rank  # tensor-parallel ranks share one model and one sequence
+    sess = syn.Session.synthetic(cfg, max_ctx=max_ctx, seed=1234 + seed_rank, device=local, tp=tp)
+    layout = sess.tp_layout()
     stream = torch.cuda.ExternalStream(sess.stream_handle(), device=torch.device("cuda", local))
-    prompt = np.random.default_rng(42 + rank).integers(0, LLAMA8B["n_vocab"], PROMPT)
+    prompt = np.random.default_rng(42 + seed_rank).integers(0, LLAMA8B["n_vocab"], PROMPT)
+    seqs = 1 if tp_mode else world  # sequences decoded by the whole job
 
     def run_prompt():
         toks = sess.generate(prompt, 0, PROMPT)  # prompt through the decode graph
@@ -296,7 +307,7 @@ def main():
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_max = float(t.item())
-    value = world * K / (ms_max / 1e3)
+    value = seqs * K / (ms_max / 1e3)
 
     # e2e through the public step API over the same positions (host round trip every step)
     sess.reset()
@@ -315,7 +326,7 @@ def main():
         t = torch.tensor([e_ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e_ms = float(t.item())
-    e2e = world * K / (e_ms / 1e3)
+    e2e = seqs * K / (e_ms / 1e3)
 
     # roofline of the dominant kernel: every GEMV of one step, timed op by op with CUDA events
     prof_pos = min(start_pos + K - 1, max_ctx - 1)
@@ -329,7 +340,8 @@ def main():
     total_ms = sum(per_op)
     n_gemv = sum(1 for o in ops if o["kind"] == "matmul")
     # the dominant kernel: the GEMV on the gate/up rows (the largest share of the step)
-    gu = [(t, o) for t, o in zip(per_op, ops) if o["kind"] == "matmul" and o["rows"] == 2 * LLAMA8B["n_ff"]]
+    gu = [(t, o) for t, o in zip(per_op, ops) if o["kind"] == "matmul" and o["rows"] == 2 * layout["n_ff"]]
+    gather_ms = sum(t for t, o in zip(per_op, ops) if o["kind"] == "allgather")
     gu_ms = sum(t for t, _ in gu) / max(1, len(gu))
     gu_bytes = gu[0][1]["bytes"] if gu else 0.0
     peak, peak_kind = peaks()
@@ -353,27 +365,30 @@ def main():
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": K,
-            "warmup": W, "ms_per_step": round(ms_max / K, 4), "higher_is_better": True, "scaling": "weak",
+            "warmup": W, "ms_per_step": round(ms_max / K, 4), "higher_is_better": True,
+            "scaling": "strong" if tp_mode else "weak",
             "vs_baseline": None, "dtype": "q4_0/q8_0 weights x q8_0 activations (exact int8 dots), f32 accum",
             "data": "synthetic",
             "config": {"workload": "Llama-3-8B-shaped Q4_0 decode (BASELINE config 4): 512-token prompt then "
                                    f"greedy decode positions {start_pos}..{start_pos + K - 1}",
                        "model": "llama3-8b-shape (32L, d4096, 32H/8KV, ff14336, V128256), Q4_0 + Q8_0 head",
-                       "global_batch": world, "seq_len": start_pos + K,
-                       "parallelism": "replicas" if world > 1 else "single",
+                       "global_batch": seqs, "seq_len": start_pos + K,
+                       "parallelism": f"tp{world}" if tp_mode else ("replicas" if world > 1 else "single"),
                        "l2": "weights 4.5 GB per step > 126 MB L2: streamed from HBM every step"},
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
                     "d2h_bytes_per_step": LLAMA8B["n_vocab"] * 4 + 4},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "kernel": f"gemv_stage_kernel<Q4_0> on the gate/up rows (28672x4096, rms_norm in, "
-                                   f"silu*up out), {len(gu)} launches of one step at pos {prof_pos}, "
+                         "kernel": f"gemv_stage_kernel<Q4_0> on the gate/up rows ({2 * layout['n_ff']}x4096 "
+                                   f"per rank, rms_norm in, silu*up out), {len(gu)} launches of one step at pos "
+                                   f"{prof_pos}, "
                                    f"{gu_bytes / 1e6:.2f} MB algorithmic per launch",
                          "all_gemv_gbs": round(gemv_bytes / (gemv_ms / 1e3) / 1e9, 1),
                          "peak_source": peak_kind,
                          "step_frac": round(step_bytes / (ms_max / K / 1e3) / 1e9 / peak, 4),
                          "attention_gbs": round(attn_bytes / (attn_ms / 1e3) / 1e9, 1),
-                         "gemv_share_of_step": round(gemv_ms / total_ms, 3)},
+                         "gemv_share_of_step": round(gemv_ms / total_ms, 3),
+                         "allgather_ms_per_step": round(gather_ms, 4) if tp_mode else None},
             "gpu_launches": sess.launches_per_step() * K,
             "clocks": clocks.summary(),
         }
@@ -381,7 +396,9 @@ def main():
             line["cpu_baseline"] = cpu
         print(json.dumps(line))
         sys.stdout.flush()
-    sess.close()
+    sess.close()  # its graphs hold NCCL calls: released before the communicators
+    if tp is not None:
+        tp.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
