@@ -330,6 +330,12 @@ int syn_session_open_gguf_tp(const char* path, int max_ctx, int device, syn_tp* 
 int syn_session_open_synthetic_tp(const syn_llama_config* c, int max_ctx, uint64_t seed, int device, syn_tp* tp,
                                   syn_session** out);
 int syn_session_tp_layout(const syn_session* s, syn_tp_layout* out);
+/* How a sharded session gathers: *peer_stores 1 when each producing kernel
+ * stores its slice straight into every rank's memory (CUDA IPC over NVLink)
+ * and the reading kernels wait on per-rank flags, 0 when NCCL all-gathers
+ * run between the kernels (SYN_TP_P2P=0, or a peer could not be mapped);
+ * *wait_errors counts flag waits that gave up after 2 s (0 in a healthy run). */
+int syn_session_tp_status(syn_session* s, int* peer_stores, int* wait_errors);
 
 /* Copy device memory to the host (synchronous), e.g. a KV cache for checking. */
 int syn_copy_to_host(void* host_dst, const void* device_src, size_t bytes);

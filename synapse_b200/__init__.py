@@ -117,6 +117,7 @@ def _declare(L):
         "syn_session_open_synthetic_tp": (i32, [ctypes.POINTER(LlamaConfig), i32, ctypes.c_uint64, i32, vp,
                                                 ctypes.POINTER(vp)]),
         "syn_session_tp_layout": (i32, [vp, ctypes.POINTER(TPLayout)]),
+        "syn_session_tp_status": (i32, [vp, ctypes.POINTER(i32), ctypes.POINTER(i32)]),
     })
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -488,6 +489,12 @@ class Session:
         out = TPLayout()
         check(lib().syn_session_tp_layout(self.h, ctypes.byref(out)), "syn_session_tp_layout")
         return out.as_dict()
+
+    def tp_status(self):
+        """{'peer_stores': bool, 'wait_errors': int} of a sharded session."""
+        p, e = ctypes.c_int(), ctypes.c_int()
+        check(lib().syn_session_tp_status(self.h, ctypes.byref(p), ctypes.byref(e)), "syn_session_tp_status")
+        return {"peer_stores": bool(p.value), "wait_errors": e.value}
 
     def step(self, token, pos, logits=True):
         """One token at pos: (logits copy or None, argmax)."""

@@ -63,6 +63,7 @@ struct AttnParams {
     float yarn[5];
     int has_yarn;
     int split_groups;        // groups the cluster size is chosen for (the whole model's under tensor parallelism)
+    TpSync tp;               // push the output to every rank (a tensor-parallel gather point)
 };
 
 size_t scratch_bytes(int n_q, int n_head, int max_len) { return align256(size_t(n_q) * n_head * max_len * 4); }
@@ -587,6 +588,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(AttnParams
     cluster.sync();  // every partial is visible to the cluster
     const int n_out = G * hd, per = (n_out + C - 1) / C;
     float* ob = a.out + (size_t(b) * H + size_t(g) * G) * hd;
+    const unsigned ep = a.tp.peers ? *reinterpret_cast<const volatile unsigned*>(a.tp.epoch) : 0u;
     for (int i = j * per + tid; i < min(n_out, (j + 1) * per); i += kAttnThreads) {
         float v[kMaxCluster];
 #pragma unroll
@@ -595,7 +597,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(AttnParams
 #pragma unroll
         for (int r = 0; r < kMaxCluster; ++r)
             if (r < C) sum = __fadd_rn(sum, v[r]);
-        ob[i] = sum;
+        if (a.tp.peers) tp_store(a.tp, (size_t(b) * H + size_t(g) * G) * hd + i, sum, ep);
+        else ob[i] = sum;
     }
     cluster.sync();  // no CTA leaves while a peer may still read its shared memory
 }
@@ -802,6 +805,26 @@ extern "C" int syn_attention(const syn_attention_args* x, void* stream) {
     AttnParams a = make_params(x);
     a.scores = static_cast<float*>(x->scratch);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    switch (group_tier(x->n_head / x->n_kv)) {
+    case 1: return launch_attention<1>(a, s);
+    case 2: return launch_attention<2>(a, s);
+    case 4: return launch_attention<4>(a, s);
+    case 8: return launch_attention<8>(a, s);
+    case 16: return launch_attention<16>(a, s);
+    }
+    return SYN_ERR_UNSUPPORTED;
+}
+
+int syn_attention_tp(const syn_attention_args* x, const TpSync& t, cudaStream_t s) {
+    int st = check_args(x, true);
+    if (st) return st;
+    if (x->append && x->cache_stride == 0 && x->n_q > 1) return SYN_ERR_INVALID;
+    if (x->append && (!x->k || !x->v)) return SYN_ERR_INVALID;
+    if (t.peers && (t.world < 1 || t.world > kTpMaxWorld || t.rank < 0 || t.rank >= t.world || !t.epoch || !t.out_ll))
+        return SYN_ERR_INVALID;
+    AttnParams a = make_params(x);
+    a.scores = static_cast<float*>(x->scratch);
+    a.tp = t;
     switch (group_tier(x->n_head / x->n_kv)) {
     case 1: return launch_attention<1>(a, s);
     case 2: return launch_attention<2>(a, s);

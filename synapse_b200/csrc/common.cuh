@@ -10,6 +10,7 @@
 #include <stdint.h>
 
 #include "../../include/synapse_b200.h"
+#include "internal.h"
 
 namespace syn {
 
@@ -290,6 +291,79 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     while (!mbar_try_wait(bar, parity))
         if (global_ns() - t0 > limit_ns) return false;
     return true;
+}
+
+// ---- tensor-parallel gathers by peer stores (TpSync, internal.h) ---------------
+constexpr uint64_t kTpWaitNs = 2000000000ull;  // a reader gives up after 2 s and counts an error
+
+__device__ __forceinline__ void st_word_sys(void* p, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_word_sys(const void* p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+// Two words by one 16-byte load (each 8-byte word is written whole). No
+// memory clobber: a thread's loads issue back to back and are checked after.
+__device__ __forceinline__ void ld_words2_sys(const void* p, uint64_t& a, uint64_t& b) {
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p));
+}
+__device__ __forceinline__ uint64_t make_word(float v, unsigned epoch) {
+    return (uint64_t(epoch) << 32) | __float_as_uint(v);
+}
+__device__ __forceinline__ float word_value(uint64_t w) { return __uint_as_float(unsigned(w)); }
+
+// Producer: output element i of this launch, as a word of this step's
+// epoch, into every rank's copy.
+__device__ __forceinline__ void tp_store(const TpSync& t, size_t i, float v, unsigned epoch) {
+    const uint64_t w = make_word(v, epoch);
+#pragma unroll
+    for (int r = 0; r < kTpMaxWorld; ++r)
+        if (r < t.world) st_word_sys(t.peers[r] + t.out_off + 8 * i, w);
+}
+
+// Consumer: n (even) words from p, 16-byte aligned, once each carries this
+// step's epoch: all loads first, then the check, then a wait only for the
+// words still behind.
+template <int N>
+__device__ __forceinline__ void tp_load_n(const TpSync& t, const uint64_t* p, unsigned epoch, float (&v)[N]);
+
+// Consumer: the value of word p once it carries this step's epoch. A read
+// that waits 2 s is counted in *t.err and returns what is there; once one
+// has given up, later reads do not wait (the host reads the count and fails).
+__device__ inline float tp_load(const TpSync& t, const uint64_t* p, unsigned epoch) {
+    uint64_t w = ld_word_sys(p);
+    if (unsigned(w >> 32) == epoch) return word_value(w);
+    const uint64_t t0 = global_ns();
+    while (unsigned(w >> 32) != epoch) {
+        if (*reinterpret_cast<const volatile unsigned*>(t.err) != 0) break;
+        if (global_ns() - t0 > kTpWaitNs) {
+            atomicAdd(t.err, 1u);
+            break;
+        }
+        __nanosleep(20);
+        w = ld_word_sys(p);
+    }
+    return word_value(w);
+}
+
+template <int N>
+__device__ __forceinline__ void tp_load_n(const TpSync& t, const uint64_t* p, unsigned epoch, float (&v)[N]) {
+    static_assert(N % 2 == 0, "pairs of words");
+    uint64_t w[N];
+#pragma unroll
+    for (int k = 0; k < N / 2; ++k) ld_words2_sys(p + 2 * k, w[2 * k], w[2 * k + 1]);
+    bool ready = true;
+#pragma unroll
+    for (int j = 0; j < N; ++j) ready = ready && unsigned(w[j] >> 32) == epoch;
+    if (!ready) {
+#pragma unroll
+        for (int j = 0; j < N; ++j)
+            if (unsigned(w[j] >> 32) != epoch) w[j] = __float_as_uint(tp_load(t, p + j, epoch)) | (uint64_t(epoch) << 32);
+    }
+#pragma unroll
+    for (int j = 0; j < N; ++j) v[j] = word_value(w[j]);
 }
 
 }  // namespace syn

@@ -159,17 +159,28 @@ constexpr int kArgmaxThreads = 512;
 constexpr int kArgmaxSlices = 64;
 
 __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __restrict__ x, int n, int32_t* out,
-                                                                float* part_v, int* part_i, unsigned* count) {
+                                                                float* part_v, int* part_i, unsigned* count,
+                                                                TpSync tp, float* plain) {
     pdl_launch_dependents();
     pdl_wait();
     const int t = blockIdx.y, tid = threadIdx.x, slices = gridDim.x;
     const float* xr = x + size_t(t) * n;
     const int per = (n + slices - 1) / slices;
     const int c0 = blockIdx.x * per, c1 = min(n, c0 + per);
+    // tensor parallelism: x holds every rank's logits as words; read each
+    // once it is this step's and keep the float in plain for the host
+    const bool words = tp.peers && tp.in_ll;
+    const unsigned ep = words ? *reinterpret_cast<const volatile unsigned*>(tp.epoch) : 0u;
     float best = -INFINITY;
     int bi = n;
     for (int c = c0 + tid; c < c1; c += kArgmaxThreads) {
-        const float v = xr[c];
+        float v;
+        if (words) {
+            v = tp_load(tp, reinterpret_cast<const uint64_t*>(x) + c, ep);
+            plain[c] = v;
+        } else {
+            v = xr[c];
+        }
         if (bi >= n || v > best) { best = v; bi = c; }  // ascending c: ties keep the lower index
     }
     __shared__ float sv[kArgmaxThreads];
@@ -281,7 +292,33 @@ int syn_argmax_ws(const float* x, int n_tok, int n, int32_t* out, void* ws, cuda
     float* pv = static_cast<float*>(ws);
     int* pi = reinterpret_cast<int*>(pv + size_t(n_tok) * kArgmaxSlices);
     unsigned* pc = reinterpret_cast<unsigned*>(pi + size_t(n_tok) * kArgmaxSlices);
-    return syn_launch(argmax_kernel, dim3(slices, n_tok), kArgmaxThreads, 0, s, x, n, out, pv, pi, pc);
+    return syn_launch(argmax_kernel, dim3(slices, n_tok), kArgmaxThreads, 0, s, x, n, out, pv, pi, pc, TpSync{},
+                      static_cast<float*>(nullptr));
+}
+
+int syn_argmax_ws_tp(const void* words, int n, int32_t* out, float* plain, void* ws, const TpSync& t,
+                     cudaStream_t s) {
+    if (!words || !out || !plain || !ws || n <= 0 || !t.peers || !t.in_ll || !t.epoch || !t.err)
+        return SYN_ERR_INVALID;
+    const int slices = std::min(kArgmaxSlices, std::max(1, (n + 4095) / 4096));
+    float* pv = static_cast<float*>(ws);
+    int* pi = reinterpret_cast<int*>(pv + kArgmaxSlices);
+    unsigned* pc = reinterpret_cast<unsigned*>(pi + kArgmaxSlices);
+    return syn_launch(argmax_kernel, dim3(slices, 1), kArgmaxThreads, 0, s, static_cast<const float*>(words), n, out,
+                      pv, pi, pc, t, plain);
+}
+
+namespace {
+__global__ void tp_step_begin_kernel(unsigned* epoch) {
+    pdl_launch_dependents();
+    pdl_wait();
+    *epoch += 1u;
+}
+}  // namespace
+
+int syn_tp_step_begin(unsigned* epoch, cudaStream_t s) {
+    if (!epoch) return SYN_ERR_INVALID;
+    return syn_launch(tp_step_begin_kernel, 1, 1, 0, s, epoch);
 }
 
 extern "C" int syn_argmax(const float* x, int n_tok, int n, int32_t* out, void* stream) {

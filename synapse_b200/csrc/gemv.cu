@@ -47,6 +47,7 @@ struct GemvArgs {
     const float* gamma;  // SYN_IN_RMSNORM
     float eps;
     int out_mode;        // SYN_OUT_ROWS / SYN_OUT_SILU_PAIRS
+    TpSync tp;           // staged kernel: gathered input / residual words, output pushed to every rank
 };
 
 // Block b of row r: its quants as 32-bit words and its decoded scale.
@@ -382,12 +383,16 @@ __global__ void __launch_bounds__(W * 32) gemv_stage_kernel(GemvArgs p) {
     __syncwarp();
     pdl_launch_dependents();
     pdl_wait();  // the activations (and the residual) come from the previous kernel
+    const bool push = p.tp.peers && p.tp.out_ll;
+    const unsigned ep = p.tp.peers ? *reinterpret_cast<const volatile unsigned*>(p.tp.epoch) : 0u;
     if (p.in_mode == SYN_IN_Q8) {
         for (int i = threadIdx.x; i < nb * 2; i += blockDim.x)
             reinterpret_cast<int4*>(aq + sact_off(i >> 1))[i & 1] =
                 __ldg(reinterpret_cast<const int4*>(p.act.qs) + i);
         for (int i = threadIdx.x; i < nb; i += blockDim.x)
             dsum[i] = make_float2(__ldg(p.act.d + i), __int_as_float(__ldg(p.act.sum + i)));
+    } else if (p.tp.peers && p.tp.in_ll) {  // a gathered vector: every rank's words of this step
+        quantize_act1<true>(p.x, p.gamma, p.eps, p.in_mode == SYN_IN_RMSNORM, p.cols, aq, dsum, &p.tp, ep);
     } else {
         quantize_act1(p.x, p.gamma, p.eps, p.in_mode == SYN_IN_RMSNORM, p.cols, aq, dsum);
     }
@@ -408,10 +413,20 @@ __global__ void __launch_bounds__(W * 32) gemv_stage_kernel(GemvArgs p) {
         if (p.out_mode == SYN_OUT_SILU_PAIRS) {
             // rows 2i (gate) and 2i+1 (up) are lanes l, l+1 of the batch: out[i] = silu(gate) * up
             const float up = __shfl_down_sync(0xffffffffu, y, 1);
-            if (lane < rows_k && (lane & 1) == 0)
-                p.y[size_t(row / 2)] = silu_mul1(y, up);
+            if (lane < rows_k && (lane & 1) == 0) {
+                const float v = silu_mul1(y, up);
+                if (push) tp_store(p.tp, size_t(row / 2), v, ep);
+                else p.y[size_t(row / 2)] = v;
+            }
         } else if (lane < rows_k) {
-            p.y[row] = p.residual ? __fadd_rn(y, p.residual[row]) : y;
+            float v = y;
+            if (p.residual) {
+                const float r = p.tp.res_ll ? word_value(reinterpret_cast<const uint64_t*>(p.residual)[row])
+                                            : p.residual[row];
+                v = __fadd_rn(y, r);
+            }
+            if (push) tp_store(p.tp, size_t(row), v, ep);
+            else p.y[row] = v;
         }
         __syncwarp();
         if (lane == 0 && k + 2 < nbatch) {
@@ -714,10 +729,10 @@ extern "C" int syn_gemv_fusable(int type, int layout, int rows, int cols, int n_
     return lane_act_bytes(n_tok, cols / QK) <= 200 * 1024;
 }
 
-extern "C" int syn_gemv(const syn_gemv_args* a, void* stream) {
-    if (!a) return SYN_ERR_INVALID;
-    if (a->in_mode == SYN_IN_Q8 && a->out_mode == SYN_OUT_ROWS)
-        return syn_gemv_q(a->type, a->w, a->layout, a->rows, a->cols, a->act, a->n_tok, a->y, a->residual, stream);
+namespace {
+
+// The fused modes' checks and kernel arguments (syn_gemv, syn_gemv_tp).
+int fused_args(const syn_gemv_args* a, GemvArgs& p) {
     if (a->in_mode != SYN_IN_Q8 && a->in_mode != SYN_IN_F32 && a->in_mode != SYN_IN_RMSNORM) return SYN_ERR_INVALID;
     if (a->out_mode != SYN_OUT_ROWS && a->out_mode != SYN_OUT_SILU_PAIRS) return SYN_ERR_INVALID;
     if (!a->w || !a->y) return SYN_ERR_INVALID;
@@ -728,7 +743,7 @@ extern "C" int syn_gemv(const syn_gemv_args* a, void* stream) {
     if ((reinterpret_cast<uintptr_t>(a->w) | reinterpret_cast<uintptr_t>(a->x) |
          reinterpret_cast<uintptr_t>(a->act) | reinterpret_cast<uintptr_t>(a->gamma)) & 15)
         return SYN_ERR_INVALID;
-    GemvArgs p{};
+    p = GemvArgs{};
     p.w = static_cast<const uint8_t*>(a->w);
     p.rows = a->rows;
     p.cols = a->cols;
@@ -742,6 +757,30 @@ extern "C" int syn_gemv(const syn_gemv_args* a, void* stream) {
     p.gamma = a->gamma;
     p.eps = a->eps;
     p.out_mode = a->out_mode;
+    return SYN_OK;
+}
+
+}  // namespace
+
+int syn_gemv_tp(const syn_gemv_args* a, const TpSync& t, cudaStream_t s) {
+    if (!a) return SYN_ERR_INVALID;
+    if (t.peers && (t.world < 1 || t.world > kTpMaxWorld || t.rank < 0 || t.rank >= t.world || !t.epoch || !t.err))
+        return SYN_ERR_INVALID;
+    GemvArgs p;
+    const int st = fused_args(a, p);
+    if (st) return st;
+    if (a->n_tok != 1 || !stage_ok(a->type, a->rows, a->cols, a->out_mode)) return SYN_ERR_UNSUPPORTED;
+    p.tp = t;
+    return a->type == SYN_Q4_0 ? launch_stage<SYN_Q4_0>(p, s) : launch_stage<SYN_Q8_0>(p, s);
+}
+
+extern "C" int syn_gemv(const syn_gemv_args* a, void* stream) {
+    if (!a) return SYN_ERR_INVALID;
+    if (a->in_mode == SYN_IN_Q8 && a->out_mode == SYN_OUT_ROWS)
+        return syn_gemv_q(a->type, a->w, a->layout, a->rows, a->cols, a->act, a->n_tok, a->y, a->residual, stream);
+    GemvArgs p;
+    const int st = fused_args(a, p);
+    if (st) return st;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (a->n_tok == 1 && stage_ok(a->type, a->rows, a->cols, a->out_mode))
         return a->type == SYN_Q4_0 ? launch_stage<SYN_Q4_0>(p, s) : launch_stage<SYN_Q8_0>(p, s);

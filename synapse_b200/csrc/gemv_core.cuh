@@ -154,18 +154,35 @@ __device__ void quantize_act(const float* x, const float* gamma, float eps, bool
 // The same arithmetic as quantize_act: rms_norm (double sum of float squares,
 // mean, 1 / sqrt(mean + eps), (x * scale) * gamma), then quant/q8.hpp:54-69.
 // Every thread of the block calls it (it synchronizes the block).
+// WORDS: x is a gathered vector of tensor-parallel words ({float, epoch},
+// TpSync); each value is read once its word carries this step's epoch.
+template <bool WORDS = false>
 __device__ inline void quantize_act1(const float* x, const float* gamma, float eps, bool norm, int cols, uint8_t* aq,
-                              float2* dsum) {
+                              float2* dsum, const TpSync* tp = nullptr, unsigned epoch = 0) {
     __shared__ double red[32];
     const int nh = cols / 16, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // the 16 values of half-block h
+    auto load16 = [&](int h, float (&v)[16]) {
+        if constexpr (WORDS) {
+            tp_load_n(*tp, reinterpret_cast<const uint64_t*>(x) + size_t(h) * 16, epoch, v);
+        } else {
+            const float4* src = reinterpret_cast<const float4*>(x + size_t(h) * 16);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float4 f = src[k];
+                v[4 * k] = f.x; v[4 * k + 1] = f.y; v[4 * k + 2] = f.z; v[4 * k + 3] = f.w;
+            }
+        }
+    };
     float scale = 1.0f;
     if (norm) {
         double sum = 0.0;
         for (int h = threadIdx.x; h < nh; h += blockDim.x) {
-            const float4* src = reinterpret_cast<const float4*>(x + size_t(h) * 16);
+            float fv[16];
+            load16(h, fv);
             float4 f[4];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) f[k] = src[k];
+            for (int k = 0; k < 4; ++k) f[k] = make_float4(fv[4 * k], fv[4 * k + 1], fv[4 * k + 2], fv[4 * k + 3]);
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 sum += double(__fmul_rn(f[k].x, f[k].x));
@@ -188,13 +205,8 @@ __device__ inline void quantize_act1(const float* x, const float* gamma, float e
         const int live = min(32, max(0, nh - (h0 + warp * 32)));
         if (h >= nh) continue;
         const unsigned mask = live == 32 ? 0xffffffffu : ((1u << live) - 1u);
-        const float4* src = reinterpret_cast<const float4*>(x + size_t(h) * 16);
         float v[16];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const float4 f = src[k];
-            v[4 * k] = f.x; v[4 * k + 1] = f.y; v[4 * k + 2] = f.z; v[4 * k + 3] = f.w;
-        }
+        load16(h, v);
         if (norm) {
             const float4* g4 = reinterpret_cast<const float4*>(gamma + size_t(h) * 16);
 #pragma unroll

@@ -71,6 +71,7 @@ struct op {
     int layer = 0;
     int in_mode = SYN_IN_Q8, out_mode = SYN_OUT_ROWS;  // matmul: fused input / output (syn_gemv)
     const weight* gamma = nullptr;                     // matmul with SYN_IN_RMSNORM
+    bool in_words = false, res_words = false, out_words = false;  // peer gathers: words in / residual / out
 };
 
 struct tensor {
@@ -87,6 +88,13 @@ struct syn_session {
     int max_ctx = 0, device = 0;
     syn_tp* tp = nullptr;   // tensor-parallel group (not owned); NULL = one GPU
     syn_tp_layout part{};   // this rank's share (the whole model when world = 1)
+    // Gathers by peer stores (world > 1): the producers store into every
+    // rank's arena (mapped by CUDA IPC) and raise flags; else NCCL all-gathers.
+    bool p2p = false;
+    int n_gathers = 0;
+    int logits_plain_t = -1;  // the logits as floats (the argmax unpacks the gathered words)
+    size_t tp_off = 0;        // peers[8], epoch at +64, wait errors at +68
+    std::vector<void*> peer_maps;
     cudaStream_t stream = nullptr;
     char* arena = nullptr;
     size_t arena_bytes = 0, weight_bytes = 0, kv_bytes = 0, act_bytes = 0;
@@ -120,7 +128,7 @@ struct syn_session {
     template <typename T>
     T* at(size_t off) { return reinterpret_cast<T*>(arena + off); }
     float* tf(int t, size_t off = 0) { return at<float>(act_off + tensors[t].off) + off; }
-    float* logits() { return mega ? plan.logits : tf(logits_t); }
+    float* logits() { return mega ? plan.logits : tf(p2p ? logits_plain_t : logits_t); }
     void* tb(int t) { return arena + act_off + tensors[t].off; }
     int32_t* io() { return at<int32_t>(io_off); }
     uint16_t* kv(int layer, int which) {
@@ -386,6 +394,55 @@ void build_step(syn_session& s) {
     s.tensors[s.logits_t].last = s.ops.size() - 1;
 }
 
+// Gathers by peer stores, when every gather's producer is the attention
+// kernel or a staged GEMV and every reader of a gathered tensor (as input or
+// residual) is a staged GEMV or the argmax (the Llama shapes), world <=
+// kTpMaxWorld, and SYN_TP_P2P is not "0". A gathered tensor then holds words
+// ({float, epoch}, twice the bytes) and lives for the whole step: peers write
+// it while this rank may still run earlier ops, so no other tensor may share
+// its bytes. Whether the peers' arenas can be mapped is settled later
+// (map_peers); without it the NCCL all-gathers run on the same tensors.
+void plan_p2p(syn_session& s) {
+    s.n_gathers = 0;
+    if (s.part.world <= 1 || s.part.world > kTpMaxWorld) return;
+    const char* env = std::getenv("SYN_TP_P2P");
+    if (env && env[0] == '0') return;
+    auto staged = [](const op& o) {
+        return o.kind == opk::matmul && o.in_mode != SYN_IN_Q8 && o.w->quant() &&
+               syn_gemv_fusable(o.w->type, o.w->layout, o.rows, o.cols, 1, o.out_mode);
+    };
+    std::vector<op> ops = s.ops;
+    std::vector<int> gathered;
+    for (size_t i = 0; i < ops.size(); ++i) {
+        if (ops[i].kind != opk::allgather) continue;
+        const int t = ops[i].out;
+        if (i == 0) return;
+        op& prod = ops[i - 1];
+        if (prod.out != t || !(prod.kind == opk::attention || staged(prod))) return;
+        prod.out_words = true;
+        for (size_t m = i + 1; m < ops.size(); ++m) {
+            op& r = ops[m];
+            if (r.in2 == t || ((r.in == t || r.res == t) && !(staged(r) || (r.kind == opk::argmax && r.in == t))))
+                return;
+            if (r.in == t) r.in_words = true;
+            if (r.res == t) r.res_words = true;
+        }
+        gathered.push_back(t);
+    }
+    s.ops.swap(ops);
+    s.n_gathers = int(gathered.size());
+    for (int t : gathered) {
+        s.tensors[t].bytes *= 2;
+        s.tensors[t].first = 0;
+        s.tensors[t].last = s.ops.size() - 1;
+    }
+    graph_builder g{s};
+    s.logits_plain_t = g.new_tensor(size_t(s.cfg.n_vocab) * 4);
+    s.tensors[s.logits_plain_t].used = true;
+    s.tensors[s.logits_plain_t].first = 0;
+    s.tensors[s.logits_plain_t].last = s.ops.size() - 1;
+}
+
 int plan_step(syn_session& s) {
     std::vector<syn::plan::tensor> ts;
     for (const tensor& t : s.tensors) ts.push_back({t.bytes, t.first, t.last});
@@ -399,6 +456,7 @@ int plan_step(syn_session& s) {
 // ---- execution ---------------------------------------------------------------
 
 int enqueue_ops(syn_session& s, cudaStream_t st);
+TpSync tp_sync(syn_session& s, const op& o);
 
 // One step: the persistent step kernel when the model fits it, else the ops.
 int enqueue_body(syn_session& s, cudaStream_t st) {
@@ -415,8 +473,10 @@ int enqueue_ops(syn_session& s, cudaStream_t st) {
     for (const op& o : s.ops) {
         switch (o.kind) {
         case opk::embed:
-            rc = syn_embed(s.embd.type, s.arena + s.embd.off, s.embd.layout, s.embd.rows, s.embd.cols, s.io(), 1,
-                           s.tf(o.out), st);
+            if (s.p2p) rc = syn_tp_step_begin(s.at<unsigned>(s.tp_off + 64), st);  // this step's epoch
+            if (!rc)
+                rc = syn_embed(s.embd.type, s.arena + s.embd.off, s.embd.layout, s.embd.rows, s.embd.cols, s.io(), 1,
+                               s.tf(o.out), st);
             break;
         case opk::rms_norm:
             rc = syn_rms_norm(s.tf(o.in), s.at<float>(o.w->off), 1, o.cols, c.rms_eps,
@@ -427,7 +487,10 @@ int enqueue_ops(syn_session& s, cudaStream_t st) {
             break;
         case opk::matmul: {
             float* y = s.tf(o.out, o.out_off);
-            const float* res = o.res >= 0 ? s.tf(o.res, o.res_off) : nullptr;
+            const float* res = o.res < 0 ? nullptr
+                               : o.res_words && s.p2p ? reinterpret_cast<const float*>(
+                                                            static_cast<char*>(s.tb(o.res)) + o.res_off * 8)
+                                                      : s.tf(o.res, o.res_off);
             if (o.in_mode != SYN_IN_Q8 || o.out_mode != SYN_OUT_ROWS) {
                 syn_gemv_args a{};
                 a.type = o.w->type;
@@ -443,7 +506,8 @@ int enqueue_ops(syn_session& s, cudaStream_t st) {
                 a.out_mode = o.out_mode;
                 a.y = y;
                 a.residual = res;
-                rc = syn_gemv(&a, st);
+                rc = s.p2p && (o.in_words || o.res_words || o.out_words) ? syn_gemv_tp(&a, tp_sync(s, o), st)
+                                                                         : syn_gemv(&a, st);
             } else if (o.w->quant())
                 rc = syn_gemv_q(o.w->type, s.arena + o.w->off, o.w->layout, o.w->rows, o.w->cols, s.tb(o.in), 1, y,
                                 res, st);
@@ -476,7 +540,7 @@ int enqueue_ops(syn_session& s, cudaStream_t st) {
             a.freq_factors = s.has_ff ? s.at<float>(s.ff_off) : nullptr;
             a.rope_table = s.at<float>(s.rope_tab_off);
             a.split_groups = c.n_head_kv;  // the one-GPU split on every rank
-            rc = syn_attention(&a, st);
+            rc = s.p2p && o.out_words ? syn_attention_tp(&a, tp_sync(s, o), st) : syn_attention(&a, st);
             break;
         }
         case opk::silu_mul:
@@ -484,10 +548,13 @@ int enqueue_ops(syn_session& s, cudaStream_t st) {
                               o.out >= 0 ? s.tf(o.out, o.out_off) : nullptr, o.out2 >= 0 ? s.tb(o.out2) : nullptr, st);
             break;
         case opk::allgather:
-            rc = syn_allgather(s.tp, s.tf(o.out), size_t(o.cols) * 4, st);
+            if (!s.p2p) rc = syn_allgather(s.tp, s.tf(o.out), size_t(o.cols) * 4, st);  // else the producer pushed it
             break;
         case opk::argmax:
-            rc = syn_argmax_ws(s.tf(o.in), 1, c.n_vocab, s.io() + 2, s.arena + s.argmax_ws_off, st);
+            rc = s.p2p && o.in_words
+                     ? syn_argmax_ws_tp(s.tb(o.in), c.n_vocab, s.io() + 2, s.tf(s.logits_plain_t),
+                                        s.arena + s.argmax_ws_off, tp_sync(s, o), st)
+                     : syn_argmax_ws(s.tf(o.in), 1, c.n_vocab, s.io() + 2, s.arena + s.argmax_ws_off, st);
             break;
         }
         if (rc) return rc;
@@ -661,6 +728,7 @@ int finish(syn_session& s, layout_builder& lb) {
     s.kv_bytes = size_t(c.n_layer) * 2 * s.max_ctx * s.part.n_kv * c.head_dim * 2;
     s.kv_off = lb.take(s.kv_bytes);
     build_step(s);
+    plan_p2p(s);
     int rc = plan_step(s);
     if (rc) return rc;
     s.act_off = lb.take(s.act_bytes);
@@ -670,6 +738,7 @@ int finish(syn_session& s, layout_builder& lb) {
     s.argmax_ws_off = lb.take(syn_argmax_ws_bytes(1));  // persistent: its counters must stay zero between steps
     s.rope_tab_off = lb.take(size_t(s.max_ctx) * c.head_dim * 4);
     if (s.part.world == 1) plan_step_kernel(s, lb);
+    if (s.n_gathers) s.tp_off = lb.take(128);  // peers[8], epoch at +64, wait errors at +68
     s.arena_bytes = lb.off;
     s.theta_scale = std::pow(c.rope_base, -2.0f / float(c.head_dim));  // attention.hpp:47
     s.scale = 1.0f / std::sqrt(float(c.head_dim));                      // llama.hpp:407
@@ -683,6 +752,67 @@ int finish(syn_session& s, layout_builder& lb) {
     return SYN_OK;
 }
 
+// Map every peer's arena (CUDA IPC handles exchanged over the group) and put
+// the bases in the arena for the kernels. Collective: every rank learns
+// whether all ranks mapped theirs, and all use peer stores or none does.
+int map_peers(syn_session& s) {
+    s.p2p = false;
+    if (!s.n_gathers) return SYN_OK;
+    const int world = s.part.world, rank = s.part.rank;
+    struct entry {
+        cudaIpcMemHandle_t h;
+        int ok;
+    } mine{}, all[kTpMaxWorld];
+    mine.ok = cudaIpcGetMemHandle(&mine.h, s.arena) == cudaSuccess;
+    if (!mine.ok) cudaGetLastError();
+    int rc = syn_tp_exchange(s.tp, &mine, all, sizeof(entry));
+    if (rc) return rc;
+    char* bases[kTpMaxWorld] = {};
+    bool ok = true;
+    for (int r = 0; r < world; ++r) ok = ok && all[r].ok;
+    for (int r = 0; r < world && ok; ++r) {
+        if (r == rank) {
+            bases[r] = s.arena;
+            continue;
+        }
+        void* p = nullptr;
+        if (cudaIpcOpenMemHandle(&p, all[r].h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            ok = false;
+            break;
+        }
+        s.peer_maps.push_back(p);
+        bases[r] = static_cast<char*>(p);
+    }
+    entry verdict{}, verdicts[kTpMaxWorld];
+    verdict.ok = ok;
+    if ((rc = syn_tp_exchange(s.tp, &verdict, verdicts, sizeof(entry)))) return rc;
+    for (int r = 0; r < world; ++r) ok = ok && verdicts[r].ok;
+    if (!ok) {
+        for (void* p : s.peer_maps) cudaIpcCloseMemHandle(p);
+        s.peer_maps.clear();
+        return SYN_OK;  // NCCL all-gathers on every rank
+    }
+    rc = cuda(cudaMemcpy(s.arena + s.tp_off, bases, sizeof bases, cudaMemcpyHostToDevice));
+    if (!rc) s.p2p = true;
+    return rc;
+}
+
+// The gather hooks of op o (peers mapped).
+TpSync tp_sync(syn_session& s, const op& o) {
+    TpSync t;
+    t.peers = s.at<char*>(s.tp_off);
+    t.epoch = s.at<unsigned>(s.tp_off + 64);
+    t.err = s.at<unsigned>(s.tp_off + 68);
+    t.world = s.part.world;
+    t.rank = s.part.rank;
+    t.in_ll = o.in_words;
+    t.res_ll = o.res_words;
+    t.out_ll = o.out_words;
+    if (o.out_words) t.out_off = s.act_off + s.tensors[o.out].off + o.out_off * 8;
+    return t;
+}
+
 // The RoPE table, one eager step at position 0 (sets per-device kernel
 // attributes outside any capture), then the KV cache and io are cleared and
 // both graphs captured.
@@ -693,6 +823,7 @@ int warm_and_capture(syn_session& s) {
         int rc = fill_step_plan(s);
         if (rc) return rc;
     }
+    if (int rc = map_peers(s)) return rc;
     int rc = syn_rope_table(s.at<float>(s.rope_tab_off), s.max_ctx, s.cfg.head_dim, s.theta_scale,
                             s.has_ff ? s.at<float>(s.ff_off) : nullptr, nullptr, s.stream);
     if (!rc) rc = enqueue_step(s, s.stream);
@@ -823,6 +954,11 @@ void destroy(syn_session* s) {
     if (s->prof_exec) cudaGraphExecDestroy(s->prof_exec);
     for (auto& e : s->prof_events) cudaEventDestroy(e);
     if (s->stream) cudaStreamSynchronize(s->stream);
+    if (!s->peer_maps.empty()) {
+        // no rank still stores into another's arena once all have drained (collective)
+        syn_tp_barrier(s->tp);
+        for (void* p : s->peer_maps) cudaIpcCloseMemHandle(p);
+    }
     if (s->arena) cudaFree(s->arena);
     if (s->h_io) cudaFreeHost(s->h_io);
     if (s->h_logits) cudaFreeHost(s->h_logits);
@@ -1055,6 +1191,21 @@ extern "C" int syn_session_tp_layout(const syn_session* s, syn_tp_layout* out) {
     return SYN_OK;
 }
 
+extern "C" int syn_session_tp_status(syn_session* s, int* peer_stores, int* wait_errors) {
+    if (!s) return SYN_ERR_INVALID;
+    if (peer_stores) *peer_stores = s->p2p ? 1 : 0;
+    if (wait_errors) {
+        unsigned n = 0;
+        if (s->p2p) {
+            int rc = cuda(cudaSetDevice(s->device));
+            if (!rc) rc = cuda(cudaMemcpy(&n, s->arena + s->tp_off + 68, 4, cudaMemcpyDeviceToHost));
+            if (rc) return rc;
+        }
+        *wait_errors = int(n);
+    }
+    return SYN_OK;
+}
+
 extern "C" int syn_session_config(const syn_session* s, syn_llama_config* out) {
     if (!s || !out) return SYN_ERR_INVALID;
     *out = s->cfg;
@@ -1120,7 +1271,7 @@ extern "C" int syn_session_generate(syn_session* s, const uint32_t* prompt, int 
 
 extern "C" int syn_session_launches_per_step(const syn_session* s) {
     if (!s) return 0;
-    int n = 1;  // advance
+    int n = 1 + (s->p2p ? 1 : 0);  // advance (and the epoch under peer gathers)
     for (const op& o : s->ops) n += o.kind == opk::attention ? 2 : o.kind == opk::allgather ? 0 : 1;  // NCCL's own kernels aside
     return n;
 }

@@ -5,6 +5,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include "synapse_b200.h"
+
 // GGUF blocks of `rows` rows (device) -> rows [row0, row0 + rows) of a planar
 // matrix of `total_rows` rows at dst.
 // Source row i lands on destination row row0 + i * row_step.
@@ -46,6 +48,37 @@ void syn_set_error(const char* msg);
 // Rank, world size and device of a tensor-parallel group (tp.cpp).
 struct syn_tp;
 void syn_tp_info(const syn_tp* tp, int* rank, int* world, int* device);
+// Host helpers over the group's communicator (collective, synchronous):
+// every rank's `bytes` of host data gathered in rank order, and a barrier.
+int syn_tp_exchange(syn_tp* tp, const void* mine, void* all, size_t bytes);
+int syn_tp_barrier(syn_tp* tp);
+
+// ---- tensor-parallel gathers by peer stores ------------------------------------
+// Every rank maps every other rank's arena (CUDA IPC); all arenas have the
+// same layout. A gathered vector lives in every arena as 8-byte words, each
+// {float bits, epoch}: a producer kernel stores each element of its slice,
+// with the step's epoch, into every rank's copy by one 64-bit store; a
+// consumer reads a word once its epoch is this step's (each word is written
+// whole, so the value is the producer's). No flag and no fence is needed.
+constexpr int kTpMaxWorld = 8;
+struct TpSync {
+    char* const* peers = nullptr;     // device array [world]: every rank's arena base; nullptr = no peer gathers
+    size_t out_off = 0;               // producer: arena byte offset of the word of this launch's output element 0
+    const unsigned* epoch = nullptr;  // this rank's step counter
+    unsigned* err = nullptr;          // reads that gave up waiting (sticky count)
+    int world = 1, rank = 0;
+    int out_ll = 0;                   // the output goes to every rank as words
+    int in_ll = 0;                    // the input vector is words (wait for this step's)
+    int res_ll = 0;                   // the residual is words (this rank's slice: complete)
+};
+// syn_gemv / syn_attention / the session's argmax with a gather hook (the
+// staged GEMV path only: SYN_ERR_UNSUPPORTED when the shape does not take it).
+int syn_gemv_tp(const syn_gemv_args* a, const TpSync& t, cudaStream_t s);
+int syn_attention_tp(const syn_attention_args* a, const TpSync& t, cudaStream_t s);
+// The argmax of n gathered logits (words), which it also writes as floats to plain.
+int syn_argmax_ws_tp(const void* words, int n, int32_t* out, float* plain, void* ws, const TpSync& t, cudaStream_t s);
+// The step's first launch under peer gathers: epoch += 1.
+int syn_tp_step_begin(unsigned* epoch, cudaStream_t s);
 
 // Self-check of the library's expf (exp_rn): y = exp_rn(x) and, for
 // comparison, y_ref = exp(double(x)) rounded to float, for n device floats.

@@ -42,9 +42,10 @@ def _tokens(cfg, n):
     return [int(t) for t in np.random.default_rng(11).integers(0, cfg["n_vocab"], n)]
 
 
-def _rank_main(rank, world, port, shape, max_ctx, positions, q):
+def _rank_main(rank, world, port, shape, max_ctx, positions, mode, q):
     import torch.distributed as dist
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    os.environ["SYN_TP_P2P"] = "1" if mode == "peer_stores" else "0"
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=120))
     tp = sess = None
@@ -63,7 +64,7 @@ def _rank_main(rank, world, port, shape, max_ctx, positions, q):
         sess.reset()
         gen = sess.generate(toks[:4], 0, 12)
         q.put((rank, dict(logits=np.stack(logits), next=nxt, gen=gen, layout=layout,
-                          launches=sess.launches_per_step())))
+                          launches=sess.launches_per_step(), status=sess.tp_status())))
     except Exception as e:
         q.put((rank, repr(e)))
     finally:
@@ -74,12 +75,12 @@ def _rank_main(rank, world, port, shape, max_ctx, positions, q):
         dist.destroy_process_group()
 
 
-def _run_world(world, shape, max_ctx, positions):
+def _run_world(world, shape, max_ctx, positions, mode):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, shape, max_ctx, positions, q))
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, shape, max_ctx, positions, mode, q))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -102,9 +103,10 @@ def _one_gpu(shape, max_ctx, positions):
     return logits, gen
 
 
+@pytest.mark.parametrize("mode", ["peer_stores", "nccl"])
 @pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("shape", list(SHAPES))
-def test_tp_equals_one_gpu(world, shape):
+def test_tp_equals_one_gpu(world, shape, mode):
     if _gpus() < world:
         pytest.skip(f"needs {world} GPUs")
     cfg = SHAPES[shape]
@@ -113,11 +115,14 @@ def test_tp_equals_one_gpu(world, shape):
     max_ctx = 1024
     # single-chunk contexts, then positions past kExactChunk where the context is split over a cluster
     positions = list(range(8)) + [300, 301, 700, 1023]
-    got = _run_world(world, shape, max_ctx, positions)
+    got = _run_world(world, shape, max_ctx, positions, mode)
     want, want_gen = _one_gpu(shape, max_ctx, positions)
     for r in range(world):
         g = got[r]
         assert g["layout"]["rank"] == r and g["layout"]["world"] == world
+        # the 8B shape gathers by peer stores when asked; the tiny model's unfused ops always use NCCL
+        want_p2p = mode == "peer_stores" and shape.startswith("8b")
+        assert g["status"] == {"peer_stores": want_p2p, "wait_errors": 0}, g["status"]
         assert np.array_equal(g["logits"].view(np.uint32), want.view(np.uint32)), f"rank {r}"
         assert g["next"] == [int(np.argmax(x)) for x in want]
         assert np.array_equal(g["gen"], want_gen), f"rank {r} greedy tokens"
