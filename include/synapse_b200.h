@@ -172,9 +172,6 @@ typedef struct {
     const float* freq_factors;
     const float* yarn;
     const float* rope_table; /* NULL, or syn_rope_table for these rope settings and max_len rows */
-    int split_groups;        /* (query, KV head) groups the context split is sized for; 0 = n_q * n_kv.
-                              * A tensor-parallel rank passes the whole model's count so that it splits
-                              * every context as one GPU does (bit-identical results). */
 } syn_attention_args;
 
 size_t syn_attention_scratch_bytes(int n_q, int n_head, int n_kv, int head_dim, int max_len);

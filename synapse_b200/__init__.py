@@ -269,8 +269,7 @@ class AttentionArgs(ctypes.Structure):
                 ("n_q", ctypes.c_int), ("n_head", ctypes.c_int), ("n_kv", ctypes.c_int), ("head_dim", ctypes.c_int),
                 ("max_len", ctypes.c_int), ("append", ctypes.c_int), ("rope", ctypes.c_int),
                 ("rope_mode", ctypes.c_int), ("theta_scale", ctypes.c_float), ("scale", ctypes.c_float),
-                ("freq_factors", ctypes.c_void_p), ("yarn", ctypes.c_void_p), ("rope_table", ctypes.c_void_p),
-                ("split_groups", ctypes.c_int)]
+                ("freq_factors", ctypes.c_void_p), ("yarn", ctypes.c_void_p), ("rope_table", ctypes.c_void_p)]
 
 
 def attention_scratch_bytes(n_q, n_head, n_kv, head_dim, max_len):

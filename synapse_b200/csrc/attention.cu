@@ -8,27 +8,26 @@
 // scale), rounded after normalisation as the reference rounds it;
 // out = sum_t p_t V_t.
 //
-// One kernel per call. A thread-block cluster of C CTAs serves one (query,
-// KV head) group; CTA j owns positions [j * chunk, (j + 1) * chunk) and reads
-// each of their K and V rows from HBM once, for all G = n_head / n_kv query
-// heads of the group. K and V tiles stream through one four-slot ring of
-// asynchronous copies (the V tiles load while the K tiles are scored).
-//   phase 1: scores of the CTA's positions, and per query head the chunk's
-//            max m_j and double sum s_j of expf(s - m_j);
-//   cluster barrier: every CTA merges all C chunks' statistics from their
-//            shared memory (distributed shared memory): M = max m_j and
-//            sum = sum_j s_j * exp(m_j - M), in chunk order, in double (with
-//            one chunk, the reference's sum of expf(s - M) exactly);
-//   phase 2: p_t = binary16(expf(s_t - M) * (1 / sum)) for the CTA's
-//            positions, and the partial sum of p_t V_t in position order;
-//   cluster barrier: CTA j adds slice j of the outputs over the C partials in
-//            chunk order (deterministic) and stores it.
-// No statistics or partial outputs go through global memory, and no
-// completion counters are needed: the cluster barrier is the grid-wide step.
+// Two kernels per call, one CTA per (chunk of kChunk positions, KV head,
+// query); each CTA reads its chunk's K (then V) rows from HBM once, for all
+// G = n_head / n_kv query heads of the group, all requested at once.
+//   scores kernel: rotates q (and appends the new K, V rows), scores the
+//            chunk, and writes the scores and the chunk's statistics: the
+//            max m_j and the double sum s_j of expf(s - m_j), per query head;
+//   p.V kernel (its V rows requested before it waits on the scores kernel):
+//            merges every chunk's statistics, M = max m_j and sum =
+//            sum_j s_j * exp(m_j - M) (with one chunk, the reference's sum
+//            of expf(s - M) exactly), forms p_t = binary16(expf(s_t - M) *
+//            (1 / sum)) and the chunk's partial sum of p_t V_t in position
+//            order; the group's last CTA to finish adds the partials in
+//            chunk order (deterministic).
+// The split depends on the context only (fixed chunks), never on the grid
+// or the device, so any caller (a tensor-parallel rank included) splits the
+// same context the same way. A context of up to kChunk positions is one
+// chunk: every sum runs in the reference's position order.
 #include "common.cuh"
 #include "internal.h"
 
-#include <cooperative_groups.h>
 
 #include <algorithm>
 #include <array>
@@ -41,20 +40,22 @@ namespace {
 
 constexpr int kThreads = 128;      // RoPE / append kernels
 constexpr int kAttnThreads = 256;  // the decode kernel
-constexpr int kTile = 64;          // K or V rows per ring slot (head_dim <= 128; 32 rows above)
-__host__ __device__ inline int tile_rows(int hd) { return hd <= 128 ? kTile : kTile / 2; }
-constexpr int kSlots = 5;          // ring depth: a slot is refilled one step after it is read
-constexpr int kMaxCluster = 16;
-constexpr int kExactChunk = 256;   // positions per CTA below which the cluster does not split
+constexpr int kChunk = 256;        // positions per CTA: a context of up to kChunk is one chunk (exact order)
+static_assert(kChunk == kAttnThreads, "the p.V kernel gives each thread one position of its chunk");
+constexpr int kPwStride = kChunk + 4;  // floats per head in the p buffer: heads 4 banks apart
 
 struct AttnParams {
     const float *q, *k, *v;
     uint16_t *kc, *vc;
     const int32_t* pos;
     float* out;
-    float* scores;           // [n_q][n_head][max_len] when the chunk's scores do not fit in shared memory
+    float* scores;           // scratch: [n_q][n_head][max_len] scores
+    double* st_s;            // scratch: [n_q][n_head][nch] chunk sums
+    float* st_m;             // scratch: [n_q][n_head][nch] chunk maxima
+    float* parts;            // scratch: [n_q][n_kv][nch][G * head_dim] chunk partials of p.V
+    unsigned* ctr;           // scratch: [n_q][n_kv] arrivals of the p.V kernel's CTAs
+    int nch;                 // chunks at max_len
     const float* rope_tab;   // [max_len][head_dim / 2] (cos, sin), or NULL: computed in the kernel
-    int sc_smem, chunk_cap;  // scores in shared memory, chunk_cap per query head
     size_t cache_stride;
     int n_q, n_head, n_kv, hd, max_len;
     int append, rope, rope_mode;
@@ -62,11 +63,30 @@ struct AttnParams {
     const float* ff;
     float yarn[5];
     int has_yarn;
-    int split_groups;        // groups the cluster size is chosen for (the whole model's under tensor parallelism)
     TpSync tp;               // push the output to every rank (a tensor-parallel gather point)
 };
 
-size_t scratch_bytes(int n_q, int n_head, int max_len) { return align256(size_t(n_q) * n_head * max_len * 4); }
+// The caller's scratch: scores, chunk statistics, chunk partials, counters.
+struct AttnScratch {
+    size_t scores, st_s, st_m, parts, ctr, total;
+};
+AttnScratch scratch_layout(int n_q, int n_head, int n_kv, int hd, int max_len) {
+    AttnScratch l;
+    const size_t nch = size_t(max_len + kChunk - 1) / kChunk;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t o = off;
+        off = align256(off + bytes);
+        return o;
+    };
+    l.scores = take(size_t(n_q) * n_head * max_len * 4);
+    l.st_s = take(size_t(n_q) * n_head * nch * 8);
+    l.st_m = take(size_t(n_q) * n_head * nch * 4);
+    l.parts = take(size_t(n_q) * n_head * nch * hd * 4);
+    l.ctr = take(size_t(n_q) * n_kv * 4);
+    l.total = off;
+    return l;
+}
 
 // 16-byte asynchronous copy global -> shared (the copy engine; no register
 // round trip), and its group fences.
@@ -76,12 +96,6 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
-// Wait until at most kSlots - 2 of this thread's newest copy groups are
-// pending: at step u, tiles up to u + kSlots - 2 have been requested (the
-// slot read at step u - 1 is refilled after this wait), so tile u is in.
-__device__ __forceinline__ void cp_async_wait_ring() { asm volatile("cp.async.wait_group 3;" ::: "memory"); }
-static_assert(kSlots == 5, "cp_async_wait_ring leaves kSlots - 2 groups pending");
-
 // cos and sin of pair i at position p (attention.hpp:102-119): theta built by
 // repeated float multiplication, divided by the frequency factor, then the
 // YaRN ramp (when enabled) and the magnitude scale.
@@ -128,34 +142,66 @@ __device__ __forceinline__ void unpack8(uint4 v, float (&f)[8]) {
     }
 }
 
-// Shared memory of the decode kernel (dynamic part). sc_cap: floats of the
-// score buffer (0 when the scores live in global scratch).
-struct DecodeSmem {
-    size_t cs, qg, part, stat_s, stat_m, krh, vrh, sc, ring, total;
+// Dynamic shared memory of the two kernels: the chunk's K (V) rows padded to
+// hd + 8 halves (16-byte reads stay conflict-free), and the chunk's scores
+// (p) of the G query heads.
+struct ScoreSmem {
+    size_t cs, qg, krh, sc, kt, total;
 };
-
-__host__ __device__ inline DecodeSmem decode_smem(int GT, int hd, size_t sc_cap) {
-    DecodeSmem l;
+__host__ __device__ inline ScoreSmem score_smem(int GT, int hd) {
+    ScoreSmem l;
     size_t off = 0;
     auto take = [&](size_t bytes) {
         const size_t o = off;
         off = (off + bytes + 15) & ~size_t(15);
         return o;
     };
-    l.cs = take(size_t(hd) * 4);                     // cos, sin of the hd / 2 pairs
-    l.qg = take(size_t(GT) * hd * 4);                // rotated q of the group, binary16 values
-    l.part = take(size_t(GT) * hd * 4);              // this CTA's p.V partial (read by the cluster)
-    l.stat_s = take(size_t(GT) * 8);                 // this chunk's sums (double), read by the cluster
-    l.stat_m = take(size_t(GT) * 4);                 // this chunk's maxima, read by the cluster
-    l.krh = take(size_t(hd) * 2);                    // appended K row (binary16)
-    l.vrh = take(size_t(hd) * 2);                    // appended V row
-    l.sc = take(sc_cap * 4);                         // scores, then p, of the chunk
-    l.ring = take(size_t(kSlots) * tile_rows(hd) * (hd + 8) * 2);
+    l.cs = take(size_t(hd) * 4);                   // cos, sin of the hd / 2 pairs
+    l.qg = take(size_t(GT) * hd * 4);              // rotated q of the group, binary16 values
+    l.krh = take(size_t(hd) * 2);                  // appended K row (binary16)
+    l.sc = take(size_t(GT) * kChunk * 4);          // the chunk's scores
+    l.kt = take(size_t(kChunk) * (hd + 8) * 2);    // the chunk's K rows
+    l.total = off;
+    return l;
+}
+struct PvSmem {
+    size_t pw, vt, total;
+};
+__host__ __device__ inline PvSmem pv_smem(int GT, int hd) {
+    PvSmem l;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t o = off;
+        off = (off + bytes + 15) & ~size_t(15);
+        return o;
+    };
+    l.pw = take(size_t(GT) * kPwStride * 4);       // the chunk's p
+    l.vt = take(size_t(kChunk) * (hd + 8) * 2);    // the chunk's V rows
     l.total = off;
     return l;
 }
 
-// Tensor-core tiles for contexts beyond kExactChunk (where the reference's
+// Rows [t0, t1) of KV head g of a cache (row = n_kv * hd halves) into rows
+// 0.. of dst (pitch hd + 8), except row `skip` (-1: none), as one group of
+// asynchronous 16-byte copies.
+__device__ inline void copy_rows(uint16_t* dst, const uint16_t* cache, size_t row, int g, int hd, int t0, int t1,
+                                 int skip) {
+    const int c8n = hd / 8, rowh = hd + 8, m = t1 - t0;
+    const uint16_t* src = cache + size_t(g) * hd;
+    if (kAttnThreads % c8n == 0) {  // every thread copies one fixed 16-byte column of rows tid / c8n, + step, ...
+        const int c8 = threadIdx.x % c8n, step = kAttnThreads / c8n;
+        for (int rr = threadIdx.x / c8n; rr < m; rr += step)
+            if (t0 + rr != skip) cp_async16(dst + rr * rowh + c8 * 8, src + size_t(t0 + rr) * row + c8 * 8);
+    } else {
+        for (int i = threadIdx.x; i < m * c8n; i += kAttnThreads) {
+            const int rr = i / c8n, c8 = i - rr * c8n;
+            if (t0 + rr != skip) cp_async16(dst + rr * rowh + c8 * 8, src + size_t(t0 + rr) * row + c8 * 8);
+        }
+    }
+    cp_async_commit();
+}
+
+// Tensor-core tiles for contexts beyond kChunk (where the reference's
 // summation order is re-associated over chunks anyway): m16n8k16, binary16
 // inputs (q, K, p and V are binary16 values already), fp32 accumulation.
 // Fragment layouts (PTX ISA, mma.m16n8k16 .f16): lane = 4 g + t;
@@ -178,82 +224,35 @@ __device__ __forceinline__ void ldsm_x2_trans(uint32_t& r0, uint32_t& r1, const 
                  : "r"(static_cast<unsigned>(__cvta_generic_to_shared(row_addr))));
 }
 
+// Kernel 1: the chunk's scores and statistics. CTA (j, g, b): positions
+// [j * kChunk, ...) of query b's context, KV head g and its G query heads.
 template <int GT>
-__global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(AttnParams a) {
-    namespace cg = cooperative_groups;
-    cg::cluster_group cluster = cg::this_cluster();
-    const int C = int(cluster.num_blocks());
-    const int j = int(cluster.block_rank()), g = blockIdx.y, b = blockIdx.z;
+__global__ void __launch_bounds__(kAttnThreads) attn_scores_kernel(AttnParams a) {
+    const int j = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
     const int hd = a.hd, G = a.n_head / a.n_kv, H = a.n_head;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     // pos (and the RoPE table) are written before the step's first kernel, or
     // by the caller, never by the kernel this one may overlap: read before the wait.
     const int P = a.pos[b], L = P + 1;
-    if (P < 0 || L > a.max_len) return;  // the whole cluster (same query) leaves together
-    // A context of up to kExactChunk positions stays in CTA 0: p.V in the
-    // reference's position order (the other CTAs idle).
-    const int chunk = L <= kExactChunk ? L : (L + C - 1) / C;
-    const int t0 = min(L, j * chunk), t1 = min(L, t0 + chunk), n = t1 - t0;
-    const bool owns = a.append && t0 <= P && P < t1;
+    if (P < 0 || L > a.max_len) return;
+    const int t0 = j * kChunk;
+    if (t0 >= L) return;  // past the context (the p.V kernel skips it too)
+    const int t1 = min(L, t0 + kChunk), n = t1 - t0;
+    const bool owns = a.append && P < t1;  // the chunk holds the appended row
 
     extern __shared__ __align__(16) unsigned char smem[];
-    const DecodeSmem sl = decode_smem(GT, hd, a.sc_smem ? size_t(GT) * a.chunk_cap : 0);
+    const ScoreSmem sl = score_smem(GT, hd);
     float* cs = reinterpret_cast<float*>(smem + sl.cs);
     float* qg = reinterpret_cast<float*>(smem + sl.qg);
-    float* part = reinterpret_cast<float*>(smem + sl.part);
-    double* stat_s = reinterpret_cast<double*>(smem + sl.stat_s);
-    float* stat_m = reinterpret_cast<float*>(smem + sl.stat_m);
     uint16_t* krh = reinterpret_cast<uint16_t*>(smem + sl.krh);
-    uint16_t* vrh = reinterpret_cast<uint16_t*>(smem + sl.vrh);
-    uint16_t* ring = reinterpret_cast<uint16_t*>(smem + sl.ring);
-    __shared__ float gm[GT], gscale[GT];
+    float* sc = reinterpret_cast<float*>(smem + sl.sc);  // score of head h, chunk row r: sc[h * kChunk + r]
+    uint16_t* kt = reinterpret_cast<uint16_t*>(smem + sl.kt);
     __shared__ float2 etab[64];  // 2^(j/64) for exp_rn_neg
     if (tid < 64) etab[tid] = kExp2J64[tid];
-    // score (then e) of query head jh at position t: sc[jh * sstride + t - soff]
-    float* sc;
-    size_t sstride;
-    int soff;
-    if (a.sc_smem) {
-        sc = reinterpret_cast<float*>(smem + sl.sc);
-        sstride = size_t(a.chunk_cap);
-        soff = t0;
-    } else {
-        sc = a.scores + (size_t(b) * H + size_t(g) * G) * a.max_len;
-        sstride = size_t(a.max_len);
-        soff = 0;
-    }
-
-    const int rowh = hd + 8;  // halves per staged row: 16-byte padding keeps 16-byte reads conflict-free
+    const int rowh = hd + 8, c8n = hd / 8;
     const size_t row = size_t(a.n_kv) * hd;
     uint16_t* kcb = a.kc + size_t(b) * a.cache_stride;
     uint16_t* vcb = a.vc + size_t(b) * a.cache_stride;
-    const int c8n = hd / 8;
-    const int TR = tile_rows(hd);            // rows per ring slot
-    const int nt = (n + TR - 1) / TR;        // tiles per phase; tile u < nt is K tile u, else V tile u - nt
-    // This thread's 16-byte column of the tile rows it copies (fixed when the
-    // block's threads cover whole rows; else the general index split).
-    const bool even_cols = kAttnThreads % c8n == 0;
-    const int my_c8 = tid % c8n, my_r0 = tid / c8n, r_step = kAttnThreads / c8n;
-    auto issue = [&](int u) {
-        if (u < 2 * nt) {
-            const bool is_k = u < nt;
-            const int tb = t0 + (is_k ? u : u - nt) * TR, m = min(TR, t1 - tb);
-            const uint16_t* src = (is_k ? kcb : vcb) + size_t(g) * hd;
-            uint16_t* dst = ring + size_t(u % kSlots) * TR * rowh;
-            if (even_cols) {
-                const uint16_t* sp = src + size_t(tb + my_r0) * row + my_c8 * 8;
-                uint16_t* dp = dst + my_r0 * rowh + my_c8 * 8;
-                for (int rr = my_r0; rr < m; rr += r_step, sp += size_t(r_step) * row, dp += r_step * rowh)
-                    if (!(owns && tb + rr == P)) cp_async16(dp, sp);
-            } else {
-                for (int i = tid; i < m * c8n; i += kAttnThreads) {
-                    const int rr = i / c8n, c8 = i % c8n, t = tb + rr;
-                    if (!(owns && t == P)) cp_async16(dst + rr * rowh + c8 * 8, src + size_t(t) * row + c8 * 8);
-                }
-            }
-        }
-        cp_async_commit();  // an empty group past the end keeps the pending count uniform
-    };
 
     // With append, rows other than P were written by earlier calls: their
     // copies start before the wait. Without it the caller's previous kernel
@@ -262,7 +261,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(AttnParams
     float2 cs_v = make_float2(0.0f, 0.0f);  // this thread's (cos, sin), requested before the copies
     if (a.rope && a.rope_tab && tid < hd / 2)
         cs_v = reinterpret_cast<const float2*>(a.rope_tab)[size_t(P) * (hd / 2) + tid];
-    for (int u = 0; u < kSlots; ++u) issue(u);
+    copy_rows(kt, kcb, row, g, hd, t0, t1, owns ? P : -1);
     if (a.rope) {
         if (a.rope_tab) {
             for (int i = tid; i < hd / 2; i += kAttnThreads) {
@@ -274,8 +273,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(AttnParams
             for (int i = tid; i < hd / 2; i += kAttnThreads) rope_cs(a, P, i, cs[2 * i], cs[2 * i + 1]);
         }
     }
-    pdl_launch_dependents();
+    pdl_launch_dependents();  // the p.V kernel may request its V rows now
     if (a.append) pdl_wait();  // q, k, v come from the previous kernel
+    // the p.V kernel's arrivals for this group, re-armed here: the previous
+    // call's p.V kernel has completed once the wait above has returned
+    if (j == 0 && tid == 0) a.ctr[size_t(b) * a.n_kv + g] = 0u;
     __syncthreads();
 
     const float* qb = a.q + (size_t(b) * H + size_t(g) * G) * hd;
@@ -312,13 +314,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(AttnParams
         } else {
             for (int d = tid; d < hd; d += kAttnThreads) krow[d] = krh[d] = f16_bits(kb[d]);
         }
-        for (int d = tid; d < hd; d += kAttnThreads) vrow[d] = vrh[d] = f16_bits(vb[d]);
+        for (int d = tid; d < hd; d += kAttnThreads) vrow[d] = f16_bits(vb[d]);
     }
     __syncthreads();
 
-    // The tensor-core path (above kExactChunk positions; uniform over the
-    // cluster): q of head g as A fragments, all head_dim / 16 k-steps.
-    const bool tc = L > kExactChunk && hd % 16 == 0 && hd <= 128 && G <= 8;
+    // The tensor-core path (a context of several chunks): q of head g as A
+    // fragments, all head_dim / 16 k-steps.
+    const bool tc = L > kChunk && hd % 16 == 0 && hd <= 128 && G <= 8;
     const int gq = lane >> 2, tq = lane & 3;
     uint32_t qa[16];  // per k-step (head_dim <= 128): a0 (row gq, k 2tq..), a2 (row gq, k 2tq+8..)
 #pragma unroll
@@ -330,56 +332,53 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(AttnParams
             qa[2 * ks + 1] = pack_h2(qr[8], qr[9]);
         }
     }
+    cp_async_wait_all();
+    if (owns && tid < c8n)
+        *reinterpret_cast<uint4*>(kt + (P - t0) * rowh + tid * 8) = *reinterpret_cast<const uint4*>(krh + tid * 8);
+    __syncthreads();
 
-    // Phase 1: scores, one (position, query head) per thread and step; the
-    // dot runs in dimension order (attention.hpp:214-219). The tensor-core
-    // lanes keep the max of the scores they produce (lmx).
+    // Scores: the dot runs in dimension order (attention.hpp:214-219); the
+    // tensor-core lanes keep the max of the scores they produce (lmx).
     float lmx = -INFINITY;
-    for (int u = 0; u < nt; ++u) {
-        cp_async_wait_ring();
-        const int tb = t0 + u * TR, m = min(TR, t1 - tb);
-        uint16_t* tile = ring + size_t(u % kSlots) * TR * rowh;
-        if (owns && P >= tb && P < tb + m && tid < c8n)
-            *reinterpret_cast<uint4*>(tile + (P - tb) * rowh + tid * 8) = *reinterpret_cast<const uint4*>(krh + tid * 8);
-        __syncthreads();  // tile u is visible, and every thread is done with tile u - 1
-        if (u > 0) issue(u - 1 + kSlots);
-        if (tc) {
-            // warp w scores positions tb + 8w .. + 7 of all G heads: C[h][n] = sum_k q[h][k] K[n][k]
-            const int n0 = 8 * warp;
-            if (n0 < m) {
-                float cacc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                const uint16_t* krow = tile + (n0 + gq) * rowh + 2 * tq;  // B: rows past m read stale data, never stored
+    if (tc) {
+        // warp w scores rows 32w .. 32w + 31 as four tiles of 8 positions x all G heads:
+        // C[h][n] = sum_k q[h][k] K[n][k]
+        for (int q4 = 0; q4 < 4; ++q4) {
+            const int n0 = 32 * warp + 8 * q4;
+            if (n0 >= n) break;
+            float cacc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            const uint16_t* krow = kt + (n0 + gq) * rowh + 2 * tq;  // B: rows past n read stale data, never stored
 #pragma unroll
-                for (int ks = 0; ks < 8; ++ks) {
-                    if (ks >= hd / 16) break;
-                    const uint32_t b0 = *reinterpret_cast<const uint32_t*>(krow + 16 * ks);
-                    const uint32_t b1 = *reinterpret_cast<const uint32_t*>(krow + 16 * ks + 8);
-                    const uint32_t af[4] = {qa[2 * ks], 0u, qa[2 * ks + 1], 0u};
-                    mma16816(cacc, af, b0, b1);
+            for (int ks = 0; ks < 8; ++ks) {
+                if (ks >= hd / 16) break;
+                const uint32_t b0 = *reinterpret_cast<const uint32_t*>(krow + 16 * ks);
+                const uint32_t b1 = *reinterpret_cast<const uint32_t*>(krow + 16 * ks + 8);
+                const uint32_t af[4] = {qa[2 * ks], 0u, qa[2 * ks + 1], 0u};
+                mma16816(cacc, af, b0, b1);
+            }
+            if (gq < G) {
+                const int r0 = n0 + 2 * tq;
+                const float v0 = __fmul_rn(cacc[0], a.scale), v1 = __fmul_rn(cacc[1], a.scale);
+                if (r0 < n) {
+                    sc[gq * kChunk + r0] = v0;
+                    lmx = fmaxf(lmx, v0);
                 }
-                if (gq < G) {
-                    const int r0 = n0 + 2 * tq;
-                    const float v0 = __fmul_rn(cacc[0], a.scale), v1 = __fmul_rn(cacc[1], a.scale);
-                    if (r0 < m) {
-                        sc[size_t(gq) * sstride + tb + r0 - soff] = v0;
-                        lmx = fmaxf(lmx, v0);
-                    }
-                    if (r0 + 1 < m) {
-                        sc[size_t(gq) * sstride + tb + r0 + 1 - soff] = v1;
-                        lmx = fmaxf(lmx, v1);
-                    }
+                if (r0 + 1 < n) {
+                    sc[gq * kChunk + r0 + 1] = v1;
+                    lmx = fmaxf(lmx, v1);
                 }
             }
-        } else
-        for (int i = tid; i < m * G; i += kAttnThreads) {
-            const int jh = i / m, r = i % m;
-            const uint16_t* kt = tile + r * rowh;
+        }
+    } else {
+        for (int i = tid; i < n * G; i += kAttnThreads) {
+            const int jh = i / n, r = i % n;
+            const uint16_t* kr = kt + r * rowh;
             const float4* qh = reinterpret_cast<const float4*>(qg + jh * hd);
             float dot = 0.0f;
 #pragma unroll 4
             for (int d8 = 0; d8 < hd / 8; ++d8) {
                 float kf[8];
-                unpack8(*reinterpret_cast<const uint4*>(kt + 8 * d8), kf);
+                unpack8(*reinterpret_cast<const uint4*>(kr + 8 * d8), kf);
                 const float4 q0 = qh[2 * d8], q1 = qh[2 * d8 + 1];
                 dot = fmaf(q0.x, kf[0], dot);  // exact products: each fma is mul then add
                 dot = fmaf(q0.y, kf[1], dot);
@@ -390,41 +389,38 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(AttnParams
                 dot = fmaf(q1.z, kf[6], dot);
                 dot = fmaf(q1.w, kf[7], dot);
             }
-            sc[size_t(jh) * sstride + tb + r - soff] = __fmul_rn(dot, a.scale);
+            sc[jh * kChunk + r] = __fmul_rn(dot, a.scale);
         }
     }
-    __syncthreads();  // the last tile's scores are visible
+    __syncthreads();
 
-    // The softmax over the whole context (elementwise.hpp:174-201).
-    // The chunk's statistics per query head: the max m_j (from the
-    // tensor-core lanes, else by every thread over positions t0 + tid,
-    // + 256, ...), then the double sum s_j of expf(s - m_j) over the same
-    // positions, partials meeting in lane and warp order.
+    // The chunk's statistics per query head (elementwise.hpp:174-201): the
+    // max m_j, then the double sum s_j of expf(s - m_j) over positions
+    // tid, + 256, ..., partials meeting in lane and warp order.
     __shared__ float red_mx[GT][kAttnThreads / 32];
     __shared__ double red_sm[GT][kAttnThreads / 32];
     __shared__ float m_loc[GT];
-    {
-        if (tc) {
-            float w = fmaxf(lmx, __shfl_xor_sync(0xffffffffu, lmx, 1));
-            w = fmaxf(w, __shfl_xor_sync(0xffffffffu, w, 2));
-            if (tq == 0 && gq < G) red_mx[gq][warp] = w;
-        } else {
+    if (tc) {
+        float w = fmaxf(lmx, __shfl_xor_sync(0xffffffffu, lmx, 1));
+        w = fmaxf(w, __shfl_xor_sync(0xffffffffu, w, 2));
+        if (tq == 0 && gq < G) red_mx[gq][warp] = w;
+    } else {
 #pragma unroll 1
-            for (int h = 0; h < G; ++h) {
-                const float* sh = sc + size_t(h) * sstride + t0 - soff;
-                float mx = -INFINITY;
-                for (int t = tid; t < n; t += kAttnThreads) mx = fmaxf(mx, sh[t]);
-                mx = warp_max(mx);
-                if (lane == 0) red_mx[h][warp] = mx;
-            }
+        for (int h = 0; h < G; ++h) {
+            float mx = -INFINITY;
+            for (int t = tid; t < n; t += kAttnThreads) mx = fmaxf(mx, sc[h * kChunk + t]);
+            mx = warp_max(mx);
+            if (lane == 0) red_mx[h][warp] = mx;
         }
-        __syncthreads();
-        if (tid < G) {
-            float m = -INFINITY;
-            for (int w = 0; w < kAttnThreads / 32; ++w) m = fmaxf(m, red_mx[tid][w]);
-            m_loc[tid] = m;
-        }
-        __syncthreads();
+    }
+    __syncthreads();
+    if (tid < G) {
+        float m = -INFINITY;
+        for (int w = 0; w < kAttnThreads / 32; ++w) m = fmaxf(m, red_mx[tid][w]);
+        m_loc[tid] = m;
+    }
+    __syncthreads();
+    {
         double acc[GT];
         float mh[GT];
 #pragma unroll
@@ -432,11 +428,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(AttnParams
             acc[h] = 0.0;
             mh[h] = h < G ? m_loc[h] : 0.0f;
         }
-        const float* sh = sc + t0 - soff;
         for (int t = tid; t < n; t += kAttnThreads) {
 #pragma unroll
             for (int h = 0; h < GT; ++h)
-                if (h < G) acc[h] += double(exp_rn_neg(__fsub_rn(sh[size_t(h) * sstride + t], mh[h]), etab));
+                if (h < G) acc[h] += double(exp_rn_neg(__fsub_rn(sc[h * kChunk + t], mh[h]), etab));
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
@@ -450,132 +445,172 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(AttnParams
                 if (h == lane) v = acc[h];
             red_sm[lane][warp] = v;
         }
-        __syncthreads();
-        if (tid < G) {
-            double sum = 0.0;
-            for (int w = 0; w < kAttnThreads / 32; ++w) sum += red_sm[tid][w];
-            stat_m[tid] = m_loc[tid];
-            stat_s[tid] = sum;
-        }
     }
-    cluster.sync();  // every chunk's statistics are visible to the cluster
+    __syncthreads();
+    const size_t hb = size_t(b) * H + size_t(g) * G;  // first query head of the group
+    if (tid < G) {
+        double sum = 0.0;
+        for (int w = 0; w < kAttnThreads / 32; ++w) sum += red_sm[tid][w];
+        a.st_m[(hb + tid) * a.nch + j] = m_loc[tid];
+        a.st_s[(hb + tid) * a.nch + j] = sum;
+    }
+#pragma unroll 1
+    for (int h = 0; h < G; ++h)
+        for (int t = tid; t < n; t += kAttnThreads) a.scores[(hb + h) * a.max_len + t0 + t] = sc[h * kChunk + t];
+}
+
+// Kernel 2: p and p.V of the chunk, and the group's output.
+template <int GT>
+__global__ void __launch_bounds__(kAttnThreads) attn_pv_kernel(AttnParams a) {
+    const int j = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+    const int hd = a.hd, G = a.n_head / a.n_kv, H = a.n_head;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int P = a.pos[b], L = P + 1;
+    if (P < 0 || L > a.max_len) return;
+    const int t0 = j * kChunk;
+    if (t0 >= L) return;
+    const int t1 = min(L, t0 + kChunk), n = t1 - t0, nchk = (L + kChunk - 1) / kChunk;
+    const bool owns = a.append && P < t1;
+
+    extern __shared__ __align__(16) unsigned char smem[];
+    const PvSmem sl = pv_smem(GT, hd);
+    float* pw = reinterpret_cast<float*>(smem + sl.pw);  // p of head h, chunk row r: pw[h * kPwStride + r]
+    uint16_t* vt = reinterpret_cast<uint16_t*>(smem + sl.vt);
+    __shared__ float gm[GT], gscale[GT];
+    __shared__ float2 etab[64];
+    __shared__ bool last;
+    if (tid < 64) etab[tid] = kExp2J64[tid];
+    const int rowh = hd + 8, c8n = hd / 8;
+    const size_t row = size_t(a.n_kv) * hd;
+    const uint16_t* vcb = a.vc + size_t(b) * a.cache_stride;
+    if (!a.append) pdl_wait();
+    copy_rows(vt, vcb, row, g, hd, t0, t1, owns ? P : -1);  // row P comes from v below
+    pdl_launch_dependents();
+    pdl_wait();  // the scores kernel: scores, statistics, counters, cache rows
+
+    // This thread's position t0 + tid: its scores, requested before the merge.
+    const size_t hb = size_t(b) * H + size_t(g) * G;
+    float sv[GT];
+#pragma unroll
+    for (int h = 0; h < GT; ++h)
+        sv[h] = h < G && tid < n ? a.scores[(hb + h) * a.max_len + t0 + tid] : 0.0f;
+
     // The context's max M and normaliser sum_j s_j * exp(m_j - M), one warp
-    // per query head with lane r holding chunk r. With one chunk (or one
-    // chunk holding every position) the weight is exactly 1 and the sum is
-    // the reference's sum of expf(s - M); with several, the chunks' weights
-    // and their sum order are the approximation of the re-associated sum.
+    // per query head over the chunks (each lane loads its chunks' statistics
+    // once). With one chunk the weight is exactly 1 and the sum is the
+    // reference's sum of expf(s - M); with several, the chunks' weights and
+    // their sum order are the approximation of the re-associated sum.
     for (int h = warp; h < G; h += kAttnThreads / 32) {
-        const float mr = lane < C ? *cluster.map_shared_rank(stat_m + h, lane) : -INFINITY;
-        const double sr = lane < C ? *cluster.map_shared_rank(stat_s + h, lane) : 0.0;
-        const float M = warp_max(mr);
-        const double w = sr > 0.0 ? sr * double(mr == M ? 1.0f : expf(__fsub_rn(mr, M))) : 0.0;
-        const double tot = warp_sum_d(w);
+        const float* mj = a.st_m + (hb + h) * a.nch;
+        const double* sj = a.st_s + (hb + h) * a.nch;
+        constexpr int kHeld = 4;  // chunks per lane held in registers (all of them up to 128 chunks)
+        float mr[kHeld];
+        double sr[kHeld];
+        float M = -INFINITY;
+#pragma unroll
+        for (int u = 0; u < kHeld; ++u) {
+            const int r = lane + 32 * u;
+            mr[u] = r < nchk ? mj[r] : -INFINITY;
+            sr[u] = r < nchk ? sj[r] : 0.0;
+        }
+#pragma unroll
+        for (int u = 0; u < kHeld; ++u) M = fmaxf(M, mr[u]);
+        for (int r = lane + 32 * kHeld; r < nchk; r += 32) M = fmaxf(M, mj[r]);
+        M = warp_max(M);
+        double tot = 0.0;
+#pragma unroll
+        for (int u = 0; u < kHeld; ++u)
+            if (sr[u] > 0.0) tot += sr[u] * double(mr[u] == M ? 1.0f : expf(__fsub_rn(mr[u], M)));
+        for (int r = lane + 32 * kHeld; r < nchk; r += 32) {
+            const float m = mj[r];
+            const double sum = sj[r];
+            if (sum > 0.0) tot += sum * double(m == M ? 1.0f : expf(__fsub_rn(m, M)));
+        }
+        tot = warp_sum_d(tot);
         if (lane == 0) {
             gm[h] = M;
             gscale[h] = float(1.0 / tot);
         }
     }
     __syncthreads();
-    // p_t = binary16(expf(s_t - M) * (1 / sum)) of the chunk, in place of the
-    // scores (the first V tiles are already in flight).
-    {
-        float mh[GT], gs[GT];
+    // p_t = binary16(expf(s_t - M) * (1 / sum)) of the chunk
+    if (tid < n) {
 #pragma unroll
-        for (int h = 0; h < GT; ++h) {
-            mh[h] = h < G ? gm[h] : 0.0f;
-            gs[h] = h < G ? gscale[h] : 0.0f;
-        }
-        float* sh = sc + t0 - soff;
-        for (int t = tid; t < n; t += kAttnThreads) {
-#pragma unroll
-            for (int h = 0; h < GT; ++h)
-                if (h < G) {
-                    float& x = sh[size_t(h) * sstride + t];
-                    x = round_f16(__fmul_rn(exp_rn_neg(__fsub_rn(x, mh[h]), etab), gs[h]));
-                }
-        }
+        for (int h = 0; h < GT; ++h)
+            if (h < G) pw[h * kPwStride + tid] = round_f16(__fmul_rn(exp_rn_neg(__fsub_rn(sv[h], gm[h]), etab), gscale[h]));
+    }
+    const bool tc = L > kChunk && hd % 16 == 0 && hd <= 128 && G <= 8;
+    cp_async_wait_all();
+    if (owns) {  // the appended row, rounded as the scores kernel stored it
+        const float* vb = a.v + size_t(b) * row + size_t(g) * hd;
+        for (int d = tid; d < hd; d += kAttnThreads) vt[(P - t0) * rowh + d] = f16_bits(vb[d]);
+    }
+    if (tc) {  // rows past n up to the next 16: V = 0 (stale bits could be a NaN; their p is 0)
+        const int pad = ((n + 15) & ~15) - n;
+        for (int i = tid; i < pad * c8n; i += kAttnThreads)
+            *reinterpret_cast<uint4*>(vt + (n + i / c8n) * rowh + (i % c8n) * 8) = make_uint4(0u, 0u, 0u, 0u);
     }
     __syncthreads();
 
-    // Phase 2: the position-ordered sum of p_t V_t. Thread slot k owns the
-    // column pair (2 * (o % (hd / 2)), +1) of query head o / (hd / 2).
-    constexpr int KO = GT >= 2 ? GT / 2 : 1;  // pairs per thread: G * hd / 2 <= GT * 128 pairs over 256 threads
-    float acc0[KO], acc1[KO];
-    int pcol[KO], prow[KO];
-    const int n_pairs = G * hd / 2;
+    // The chunk's partial sum of p_t V_t.
+    float* part = a.parts + ((size_t(b) * a.n_kv + g) * a.nch + j) * size_t(G) * hd;
+    if (tc) {
+        // warp w accumulates dims 16w .. 16w + 15 of all G heads: C[h][d] += sum_k p[h][k] V[k][d]
+        const int gq = lane >> 2, tq = lane & 3, d0 = 16 * warp;
+        if (d0 < hd) {
+            float vacc[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+            for (int ks = 0; ks < kChunk / 16; ++ks) {
+                if (16 * ks >= n) break;
+                uint32_t af[4] = {0u, 0u, 0u, 0u};
+                if (gq < G) {
+                    const int r = 16 * ks + 2 * tq;  // p past row n is 0
+                    const float* pr = pw + gq * kPwStride + r;
+                    af[0] = pack_h2(r < n ? pr[0] : 0.0f, r + 1 < n ? pr[1] : 0.0f);
+                    af[2] = pack_h2(r + 8 < n ? pr[8] : 0.0f, r + 9 < n ? pr[9] : 0.0f);
+                }
 #pragma unroll
-    for (int k = 0; k < KO; ++k) {
-        const int o = tid + k * kAttnThreads;
-        acc0[k] = acc1[k] = 0.0f;
-        pcol[k] = o < n_pairs ? 2 * (o % (hd / 2)) : -1;
-        prow[k] = o < n_pairs ? (o / (hd / 2)) * int(sstride) : 0;
-    }
-    float vacc[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
-    for (int u = nt; u < 2 * nt; ++u) {
-        cp_async_wait_ring();
-        const int tb = t0 + (u - nt) * TR, m = min(TR, t1 - tb);
-        uint16_t* tile = ring + size_t(u % kSlots) * TR * rowh;
-        if (owns && P >= tb && P < tb + m && tid < c8n)
-            *reinterpret_cast<uint4*>(tile + (P - tb) * rowh + tid * 8) = *reinterpret_cast<const uint4*>(vrh + tid * 8);
-        const float* pt = sc + (tb - soff);  // p of head h at tile row r: pt[h * sstride + r]
-        if (tc && m < TR) {
-            // V rows past m of the last tile are 0 (stale bits could be a NaN; their p is 0)
-            for (int i = tid; i < (kTile - m) * c8n; i += kAttnThreads)
-                *reinterpret_cast<uint4*>(tile + (m + i / c8n) * rowh + (i % c8n) * 8) = make_uint4(0u, 0u, 0u, 0u);
-        }
-        __syncthreads();  // tile u is visible, and every thread is done with tile u - 1
-        issue(u - 1 + kSlots);
-        if (tc) {
-            // warp w accumulates dims 16w .. 16w + 15 of all G heads: C[h][d] += sum_k p[h][k] V[k][d]
-            const int d0 = 16 * warp;
-            if (d0 < hd) {
-#pragma unroll
-                for (int ks = 0; ks < kTile / 16; ++ks) {
-                    if (16 * ks < m) {
-                        uint32_t af[4] = {0u, 0u, 0u, 0u};
-                        if (gq < G) {
-                            const int r = 16 * ks + 2 * tq;  // p past row m is 0
-                            const float* pr = pt + size_t(gq) * sstride + r;
-                            af[0] = pack_h2(r < m ? pr[0] : 0.0f, r + 1 < m ? pr[1] : 0.0f);
-                            af[2] = pack_h2(r + 8 < m ? pr[8] : 0.0f, r + 9 < m ? pr[9] : 0.0f);
-                        }
-#pragma unroll
-                        for (int nt2 = 0; nt2 < 2; ++nt2) {
-                            uint32_t b0, b1;
-                            // lanes 0-7: rows 16ks..+7 at column d0 + 8nt2; lanes 8-15: rows +8..+15
-                            const int rr = 16 * ks + (lane & 15);
-                            ldsm_x2_trans(b0, b1, tile + rr * rowh + d0 + 8 * nt2);
-                            mma16816(vacc[nt2], af, b0, b1);
-                        }
-                    }
+                for (int nt2 = 0; nt2 < 2; ++nt2) {
+                    uint32_t b0, b1;
+                    // lanes 0-7: rows 16ks..+7 at column d0 + 8nt2; lanes 8-15: rows +8..+15
+                    ldsm_x2_trans(b0, b1, vt + (16 * ks + (lane & 15)) * rowh + d0 + 8 * nt2);
+                    mma16816(vacc[nt2], af, b0, b1);
                 }
             }
-        } else
+            if (gq < G) {
+#pragma unroll
+                for (int nt2 = 0; nt2 < 2; ++nt2) {
+                    const int o = gq * hd + d0 + 8 * nt2 + 2 * tq;
+                    part[o] = vacc[nt2][0];
+                    part[o + 1] = vacc[nt2][1];
+                }
+            }
+        }
+    } else {
+        // thread slot k owns the column pair (2 * (o % (hd / 2)), +1) of query head o / (hd / 2)
+        constexpr int KO = GT >= 2 ? GT / 2 : 1;  // pairs per thread: G * hd / 2 <= GT * 128 pairs over 256 threads
+        float acc0[KO], acc1[KO];
+        int pcol[KO], prow[KO];
+        const int n_pairs = G * hd / 2;
+#pragma unroll
+        for (int k = 0; k < KO; ++k) {
+            const int o = tid + k * kAttnThreads;
+            acc0[k] = acc1[k] = 0.0f;
+            pcol[k] = o < n_pairs ? 2 * (o % (hd / 2)) : -1;
+            prow[k] = o < n_pairs ? (o / (hd / 2)) * kPwStride : 0;
+        }
 #pragma unroll 4
-        for (int r = 0; r < m; ++r) {
-            const uint16_t* vr = tile + r * rowh;
+        for (int r = 0; r < n; ++r) {
+            const uint16_t* vr = vt + r * rowh;
 #pragma unroll
             for (int k = 0; k < KO; ++k) {
                 if (pcol[k] >= 0) {
-                    const float p = pt[prow[k] + r];
+                    const float p = pw[prow[k] + r];
                     const uint32_t v2 = *reinterpret_cast<const uint32_t*>(vr + pcol[k]);
                     acc0[k] = fmaf(p, f16_from_bits(uint16_t(v2 & 0xffff)), acc0[k]);  // exact products
                     acc1[k] = fmaf(p, f16_from_bits(uint16_t(v2 >> 16)), acc1[k]);
                 }
             }
         }
-    }
-    cp_async_wait_all();  // nothing is left in flight (the trailing groups are empty)
-    if (tc) {
-        if (16 * warp < hd && gq < G) {
-#pragma unroll
-            for (int nt2 = 0; nt2 < 2; ++nt2) {
-                const int o = gq * hd + 16 * warp + 8 * nt2 + 2 * tq;
-                part[o] = vacc[nt2][0];
-                part[o + 1] = vacc[nt2][1];
-            }
-        }
-    } else {
 #pragma unroll
         for (int k = 0; k < KO; ++k) {
             if (pcol[k] >= 0) {
@@ -585,22 +620,32 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(AttnParams
             }
         }
     }
-    cluster.sync();  // every partial is visible to the cluster
-    const int n_out = G * hd, per = (n_out + C - 1) / C;
-    float* ob = a.out + (size_t(b) * H + size_t(g) * G) * hd;
+
+    // The group's last CTA to finish adds the chunks' partials in chunk order.
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last = atomicAdd(&a.ctr[size_t(b) * a.n_kv + g], 1u) == unsigned(nchk - 1);
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    const int n_out = G * hd;
+    const float* pb = a.parts + (size_t(b) * a.n_kv + g) * a.nch * size_t(n_out);
+    float* ob = a.out + hb * hd;
     const unsigned ep = a.tp.peers ? *reinterpret_cast<const volatile unsigned*>(a.tp.epoch) : 0u;
-    for (int i = j * per + tid; i < min(n_out, (j + 1) * per); i += kAttnThreads) {
-        float v[kMaxCluster];
-#pragma unroll
-        for (int r = 0; r < kMaxCluster; ++r) v[r] = r < C ? *cluster.map_shared_rank(part + i, r) : 0.0f;
+    for (int i = tid; i < n_out; i += kAttnThreads) {
         float sum = 0.0f;
+        int r = 0;
+        for (; r + 8 <= nchk; r += 8) {  // eight loads in flight, added in chunk order
+            float v[8];
 #pragma unroll
-        for (int r = 0; r < kMaxCluster; ++r)
-            if (r < C) sum = __fadd_rn(sum, v[r]);
-        if (a.tp.peers) tp_store(a.tp, (size_t(b) * H + size_t(g) * G) * hd + i, sum, ep);
+            for (int u = 0; u < 8; ++u) v[u] = __ldcg(pb + size_t(r + u) * n_out + i);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) sum = __fadd_rn(sum, v[u]);
+        }
+        for (; r < nchk; ++r) sum = __fadd_rn(sum, __ldcg(pb + size_t(r) * n_out + i));
+        if (a.tp.peers) tp_store(a.tp, hb * hd + i, sum, ep);
         else ob[i] = sum;
     }
-    cluster.sync();  // no CTA leaves while a peer may still read its shared memory
 }
 
 // RoPE of k and F16 append of (k, v) at row pos[b], one CTA per token.
@@ -685,7 +730,6 @@ AttnParams make_params(const syn_attention_args* x) {
     a.theta_scale = x->theta_scale; a.scale = x->scale;
     a.ff = x->freq_factors;
     a.rope_tab = x->rope_table;
-    a.split_groups = x->split_groups > 0 ? x->split_groups : x->n_q * x->n_kv;
     a.has_yarn = x->yarn != nullptr;
     for (int i = 0; i < 5; ++i) a.yarn[i] = x->yarn ? x->yarn[i] : 0.0f;
     return a;
@@ -705,96 +749,49 @@ int check_args(const syn_attention_args* x, bool need_scratch) {
     return SYN_OK;
 }
 
-// Scores of a chunk stay in shared memory up to this size per CTA.
-constexpr size_t kScoreSmemBytes = 96 * 1024;
-
-// Cluster size for a call: 1 to 16 CTAs per (query, KV head) group, at least
-// kExactChunk positions each at max_len, chosen by the number of clusters of
-// each size the device keeps resident with this kernel's largest shared
-// memory (checked once per device, group tier and head size): a 16-CTA
-// cluster needs 16 free SMs of one GPC, so fewer of those fit at once than
-// 148 / 16.
-template <int GT>
-int pick_cluster(const AttnParams& a, int* out) {
-    // Per (device, head size): how many clusters of 1 .. kMaxCluster CTAs can
-    // be resident at once (0 = that size cannot be scheduled).
-    struct Fit { int dev, hd; int active[kMaxCluster + 1]; };
+// The dynamic shared memory opt-in of a kernel, set once per device to the
+// most any head size (<= 256) asks for, so a smaller shape configured later
+// never lowers it.
+int opt_in(const void* kernel, size_t most) {
     static std::mutex mu;
-    static std::vector<Fit> known;
+    static std::vector<std::pair<const void*, int>> done;
     int dev = 0;
     int st = syn_cuda_status(cudaGetDevice(&dev));
     if (st) return st;
-    Fit fit = {dev, a.hd, {}};
-    {
-        std::lock_guard<std::mutex> lock(mu);
-        bool found = false;
-        for (const auto& k : known)
-            if (k.dev == dev && k.hd == a.hd) fit = k, found = true;
-        if (!found) {
-            auto kern = attn_decode_kernel<GT>;
-            const size_t smem = decode_smem(GT, a.hd, kScoreSmemBytes / 4).total;
-            // The opt-in covers the largest head size, so configuring a smaller
-            // one later never lowers it below what an earlier one needs.
-            const size_t most = decode_smem(GT, 256, kScoreSmemBytes / 4).total;
-            st = syn_cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(most)));
-            if (!st) st = syn_cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-            if (st) return st;
-            for (int c = 1; c <= kMaxCluster; ++c) {
-                cudaLaunchConfig_t cfg = {};
-                cfg.gridDim = dim3(c, 1, 1);
-                cfg.blockDim = dim3(kAttnThreads);
-                cfg.dynamicSmemBytes = smem;
-                cudaLaunchAttribute attr[1];
-                attr[0].id = cudaLaunchAttributeClusterDimension;
-                attr[0].val.clusterDim.x = c;
-                attr[0].val.clusterDim.y = 1;
-                attr[0].val.clusterDim.z = 1;
-                cfg.attrs = attr;
-                cfg.numAttrs = 1;
-                int nc = 0;
-                if (cudaOccupancyMaxActiveClusters(&nc, kern, &cfg) != cudaSuccess) {
-                    cudaGetLastError();
-                    nc = 0;
-                }
-                fit.active[c] = nc;
-            }
-            if (!fit.active[1]) return SYN_ERR_UNSUPPORTED;
-            known.push_back(fit);
-        }
-    }
-    // Cluster sizes with at least kExactChunk positions per CTA at max_len (a
-    // context that fits one chunk sums p.V in the reference's order); of
-    // those, the fewest waves x positions per CTA, a tie keeping the smaller
-    // cluster, which merges fewer partials.
-    const long groups = a.split_groups;
-    int best = 1;
-    long best_cost = -1;
-    for (int c = 1; c <= kMaxCluster; ++c) {
-        if (!fit.active[c] || (c > 1 && long(c) * kExactChunk > a.max_len)) continue;
-        const long waves = (groups + fit.active[c] - 1) / fit.active[c];
-        const long cost = waves * ((a.max_len + c - 1) / c);
-        if (best_cost < 0 || cost < best_cost) best = c, best_cost = cost;
-    }
-    *out = best;
-    return SYN_OK;
+    std::lock_guard<std::mutex> lock(mu);
+    for (const auto& d : done)
+        if (d.first == kernel && d.second == dev) return SYN_OK;
+    st = syn_cuda_status(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(most)));
+    if (!st) done.push_back({kernel, dev});
+    return st;
 }
 
+// The two kernels of a call over grid (chunks at max_len, n_kv, n_q): a CTA
+// whose chunk starts past its query's context leaves at once.
 template <int GT>
-int launch_attention(AttnParams a, cudaStream_t s) {
-    int c = 1;
-    int st = pick_cluster<GT>(a, &c);
+int launch_attention(AttnParams a, void* scratch, cudaStream_t s) {
+    const AttnScratch l = scratch_layout(a.n_q, a.n_head, a.n_kv, a.hd, a.max_len);
+    char* base = static_cast<char*>(scratch);
+    a.scores = reinterpret_cast<float*>(base + l.scores);
+    a.st_s = reinterpret_cast<double*>(base + l.st_s);
+    a.st_m = reinterpret_cast<float*>(base + l.st_m);
+    a.parts = reinterpret_cast<float*>(base + l.parts);
+    a.ctr = reinterpret_cast<unsigned*>(base + l.ctr);
+    a.nch = (a.max_len + kChunk - 1) / kChunk;
+    int st = opt_in(reinterpret_cast<const void*>(attn_scores_kernel<GT>), score_smem(GT, 256).total);
+    if (!st) st = opt_in(reinterpret_cast<const void*>(attn_pv_kernel<GT>), pv_smem(GT, 256).total);
     if (st) return st;
-    a.chunk_cap = (a.max_len + c - 1) / c;
-    a.sc_smem = size_t(GT) * a.chunk_cap * 4 <= kScoreSmemBytes;
-    const size_t smem = decode_smem(GT, a.hd, a.sc_smem ? size_t(GT) * a.chunk_cap : 0).total;
-    return syn_launch_cluster(attn_decode_kernel<GT>, dim3(c, a.n_kv, a.n_q), kAttnThreads, smem, c, s, a);
+    const dim3 grid(a.nch, a.n_kv, a.n_q);
+    st = syn_launch(attn_scores_kernel<GT>, grid, kAttnThreads, score_smem(GT, a.hd).total, s, a);
+    if (!st) st = syn_launch(attn_pv_kernel<GT>, grid, kAttnThreads, pv_smem(GT, a.hd).total, s, a);
+    return st;
 }
 
 }  // namespace
 
 extern "C" size_t syn_attention_scratch_bytes(int n_q, int n_head, int n_kv, int head_dim, int max_len) {
     if (n_q <= 0 || n_head <= 0 || n_kv <= 0 || head_dim <= 0 || max_len <= 0) return 0;
-    return scratch_bytes(n_q, n_head, max_len);
+    return scratch_layout(n_q, n_head, n_kv, head_dim, max_len).total;
 }
 
 extern "C" int syn_attention(const syn_attention_args* x, void* stream) {
@@ -803,14 +800,13 @@ extern "C" int syn_attention(const syn_attention_args* x, void* stream) {
     if (x->append && x->cache_stride == 0 && x->n_q > 1) return SYN_ERR_INVALID;  // rows would race
     if (x->append && (!x->k || !x->v)) return SYN_ERR_INVALID;
     AttnParams a = make_params(x);
-    a.scores = static_cast<float*>(x->scratch);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     switch (group_tier(x->n_head / x->n_kv)) {
-    case 1: return launch_attention<1>(a, s);
-    case 2: return launch_attention<2>(a, s);
-    case 4: return launch_attention<4>(a, s);
-    case 8: return launch_attention<8>(a, s);
-    case 16: return launch_attention<16>(a, s);
+    case 1: return launch_attention<1>(a, x->scratch, s);
+    case 2: return launch_attention<2>(a, x->scratch, s);
+    case 4: return launch_attention<4>(a, x->scratch, s);
+    case 8: return launch_attention<8>(a, x->scratch, s);
+    case 16: return launch_attention<16>(a, x->scratch, s);
     }
     return SYN_ERR_UNSUPPORTED;
 }
@@ -823,14 +819,13 @@ int syn_attention_tp(const syn_attention_args* x, const TpSync& t, cudaStream_t 
     if (t.peers && (t.world < 1 || t.world > kTpMaxWorld || t.rank < 0 || t.rank >= t.world || !t.epoch || !t.out_ll))
         return SYN_ERR_INVALID;
     AttnParams a = make_params(x);
-    a.scores = static_cast<float*>(x->scratch);
     a.tp = t;
     switch (group_tier(x->n_head / x->n_kv)) {
-    case 1: return launch_attention<1>(a, s);
-    case 2: return launch_attention<2>(a, s);
-    case 4: return launch_attention<4>(a, s);
-    case 8: return launch_attention<8>(a, s);
-    case 16: return launch_attention<16>(a, s);
+    case 1: return launch_attention<1>(a, x->scratch, s);
+    case 2: return launch_attention<2>(a, x->scratch, s);
+    case 4: return launch_attention<4>(a, x->scratch, s);
+    case 8: return launch_attention<8>(a, x->scratch, s);
+    case 16: return launch_attention<16>(a, x->scratch, s);
     }
     return SYN_ERR_UNSUPPORTED;
 }
@@ -883,8 +878,9 @@ extern "C" int syn_attention_noalloc(const syn_attention_args* x, void* stream) 
     void* scratch = nullptr;
     const int st = noalloc_scratch(&scratch);
     if (st) return st;
-    // The kernel writes every score it reads later in the same call, so
-    // nothing left from an earlier call needs clearing here.
+    // The kernels write every score, statistic and partial they read later
+    // in the same call, and the first re-arms the counters the second uses,
+    // so nothing left from an earlier call needs clearing here.
     syn_attention_args a = *x;
     a.scratch = scratch;
     return syn_attention(&a, stream);

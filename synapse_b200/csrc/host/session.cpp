@@ -539,7 +539,6 @@ int enqueue_ops(syn_session& s, cudaStream_t st) {
             a.scale = s.scale;
             a.freq_factors = s.has_ff ? s.at<float>(s.ff_off) : nullptr;
             a.rope_table = s.at<float>(s.rope_tab_off);
-            a.split_groups = c.n_head_kv;  // the one-GPU split on every rank
             rc = s.p2p && o.out_words ? syn_attention_tp(&a, tp_sync(s, o), st) : syn_attention(&a, st);
             break;
         }

@@ -284,8 +284,8 @@ def attention_case(n_head, n_kv, hd, L, n_q, seed, base=10000.0, freq_factors=No
     return out
 
 
-@pytest.mark.parametrize("n_head,n_kv,hd", [(32, 8, 128), (6, 6, 48), (4, 2, 16), (64, 8, 128)])
-@pytest.mark.parametrize("L", [1, 2, 33, 1000])
+@pytest.mark.parametrize("n_head,n_kv,hd", [(32, 8, 128), (6, 6, 48), (4, 2, 16), (64, 8, 128), (8, 2, 32)])
+@pytest.mark.parametrize("L", [1, 2, 33, 256, 257, 287, 1000])
 def test_attention_small(n_head, n_kv, hd, L):
     attention_case(n_head, n_kv, hd, L, 1, seed=L * 13 + hd + n_head)
 

