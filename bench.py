@@ -61,6 +61,8 @@ def parse():
     p.add_argument("--profile-out", default=None, help="write the per-op device times of one step (JSON) here")
     p.add_argument("--ncu-step", type=int, default=0,
                    help="profiling mode: an 8-token prompt, then N graph steps inside the NVTX range decode_step")
+    p.add_argument("--ncu-pos", type=int, default=8,
+                   help="profiling mode: the position of the first profiled step (the cache rows before it hold zeros)")
     return p.parse_args()
 
 
@@ -232,7 +234,7 @@ def reference_arm(args, rank, world):
 
 def ncu_step(args, local):
     """A short run for ncu launch lists: the 8B session, an 8-token prompt, then
-    args.ncu_step graph steps inside the NVTX range "decode_step"."""
+    args.ncu_step graph steps from position args.ncu_pos inside the NVTX range "decode_step"."""
     import torch
 
     import synapse_b200 as syn
@@ -242,9 +244,10 @@ def ncu_step(args, local):
     toks = sess.generate(list(range(1, 9)), 0, 8)
     torch.cuda.synchronize()
     torch.cuda.nvtx.range_push("decode_step")
-    out = sess.generate([int(toks[-1])], 8, args.ncu_step)
+    pos = max(8, min(args.ncu_pos, CTX - args.ncu_step))
+    out = sess.generate([int(toks[-1])], pos, args.ncu_step)
     torch.cuda.nvtx.range_pop()
-    print(json.dumps({"ncu_step": args.ncu_step, "launches_per_step": sess.launches_per_step(),
+    print(json.dumps({"ncu_step": args.ncu_step, "position": pos, "launches_per_step": sess.launches_per_step(),
                       "tokens": [int(t) for t in out]}))
     sess.close()
 
