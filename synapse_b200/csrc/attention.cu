@@ -341,24 +341,33 @@ __global__ void __launch_bounds__(kAttnThreads) attn_scores_kernel(AttnParams a)
     // tensor-core lanes keep the max of the scores they produce (lmx).
     float lmx = -INFINITY;
     if (tc) {
-        // warp w scores rows 32w .. 32w + 31 as four tiles of 8 positions x all G heads:
-        // C[h][n] = sum_k q[h][k] K[n][k]
-        for (int q4 = 0; q4 < 4; ++q4) {
-            const int n0 = 32 * warp + 8 * q4;
-            if (n0 >= n) break;
-            float cacc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            const uint16_t* krow = kt + (n0 + gq) * rowh + 2 * tq;  // B: rows past n read stale data, never stored
+        // warp w scores rows 32w .. 32w + 31 as four tiles of 8 positions x all G heads,
+        // interleaved (four independent accumulators): C[h][n] = sum_k q[h][k] K[n][k]
+        float cacc[4][4];
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) cacc[q4][0] = cacc[q4][1] = cacc[q4][2] = cacc[q4][3] = 0.0f;
+        if (32 * warp < n) {
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
-                if (ks >= hd / 16) break;
-                const uint32_t b0 = *reinterpret_cast<const uint32_t*>(krow + 16 * ks);
-                const uint32_t b1 = *reinterpret_cast<const uint32_t*>(krow + 16 * ks + 8);
-                const uint32_t af[4] = {qa[2 * ks], 0u, qa[2 * ks + 1], 0u};
-                mma16816(cacc, af, b0, b1);
+                if (ks < hd / 16) {
+                    const uint32_t af[4] = {qa[2 * ks], 0u, qa[2 * ks + 1], 0u};
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        // B: rows past n read stale data (inside the buffer), never stored
+                        const uint16_t* krow = kt + (32 * warp + 8 * q4 + gq) * rowh + 2 * tq + 16 * ks;
+                        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(krow);
+                        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(krow + 8);
+                        mma16816(cacc[q4], af, b0, b1);
+                    }
+                }
             }
-            if (gq < G) {
+        }
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+            const int n0 = 32 * warp + 8 * q4;
+            if (gq < G && n0 < n) {
                 const int r0 = n0 + 2 * tq;
-                const float v0 = __fmul_rn(cacc[0], a.scale), v1 = __fmul_rn(cacc[1], a.scale);
+                const float v0 = __fmul_rn(cacc[q4][0], a.scale), v1 = __fmul_rn(cacc[q4][1], a.scale);
                 if (r0 < n) {
                     sc[gq * kChunk + r0] = v0;
                     lmx = fmaxf(lmx, v0);
@@ -555,35 +564,55 @@ __global__ void __launch_bounds__(kAttnThreads) attn_pv_kernel(AttnParams a) {
     // The chunk's partial sum of p_t V_t.
     float* part = a.parts + ((size_t(b) * a.n_kv + g) * a.nch + j) * size_t(G) * hd;
     if (tc) {
-        // warp w accumulates dims 16w .. 16w + 15 of all G heads: C[h][d] += sum_k p[h][k] V[k][d]
-        const int gq = lane >> 2, tq = lane & 3, d0 = 16 * warp;
-        if (d0 < hd) {
-            float vacc[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
-            for (int ks = 0; ks < kChunk / 16; ++ks) {
-                if (16 * ks >= n) break;
+        // warp w takes positions 32w .. 32w + 31 (two k-steps) of every head_dim column
+        // (hd / 8 tiles of 8, independent accumulators): C[h][d] += sum_k p[h][k] V[k][d];
+        // then the eight warps' sums are added in warp order through shared memory
+        const int gq = lane >> 2, tq = lane & 3, r0 = 32 * warp;
+        float vacc[16][4];
+#pragma unroll
+        for (int nt = 0; nt < 16; ++nt) vacc[nt][0] = vacc[nt][1] = vacc[nt][2] = vacc[nt][3] = 0.0f;
+#pragma unroll
+        for (int ks2 = 0; ks2 < 2; ++ks2) {
+            const int rk = r0 + 16 * ks2;
+            if (rk < n) {  // rows past n up to the next 16 are zero; later k-steps are skipped
                 uint32_t af[4] = {0u, 0u, 0u, 0u};
                 if (gq < G) {
-                    const int r = 16 * ks + 2 * tq;  // p past row n is 0
+                    const int r = rk + 2 * tq;  // p past row n is 0
                     const float* pr = pw + gq * kPwStride + r;
                     af[0] = pack_h2(r < n ? pr[0] : 0.0f, r + 1 < n ? pr[1] : 0.0f);
                     af[2] = pack_h2(r + 8 < n ? pr[8] : 0.0f, r + 9 < n ? pr[9] : 0.0f);
                 }
+                // lanes 0-7: rows rk..rk+7 at column 8nt; lanes 8-15: rows rk+8..rk+15
+                const uint16_t* vrow = vt + (rk + (lane & 15)) * rowh;
 #pragma unroll
-                for (int nt2 = 0; nt2 < 2; ++nt2) {
-                    uint32_t b0, b1;
-                    // lanes 0-7: rows 16ks..+7 at column d0 + 8nt2; lanes 8-15: rows +8..+15
-                    ldsm_x2_trans(b0, b1, vt + (16 * ks + (lane & 15)) * rowh + d0 + 8 * nt2);
-                    mma16816(vacc[nt2], af, b0, b1);
+                for (int nt = 0; nt < 16; ++nt) {
+                    if (nt < hd / 8) {
+                        uint32_t b0, b1;
+                        ldsm_x2_trans(b0, b1, vrow + 8 * nt);
+                        mma16816(vacc[nt], af, b0, b1);
+                    }
                 }
             }
-            if (gq < G) {
+        }
+        __syncthreads();  // every warp is done with the V rows: their buffer holds the warps' sums next
+        float* red = reinterpret_cast<float*>(vt);  // [warp][G * hd]
+        const int n_out = G * hd;
+        if (gq < G) {
 #pragma unroll
-                for (int nt2 = 0; nt2 < 2; ++nt2) {
-                    const int o = gq * hd + d0 + 8 * nt2 + 2 * tq;
-                    part[o] = vacc[nt2][0];
-                    part[o + 1] = vacc[nt2][1];
+            for (int nt = 0; nt < 16; ++nt) {
+                if (nt < hd / 8) {
+                    const int o = gq * hd + 8 * nt + 2 * tq;
+                    red[warp * n_out + o] = vacc[nt][0];
+                    red[warp * n_out + o + 1] = vacc[nt][1];
                 }
             }
+        }
+        __syncthreads();
+        for (int o = tid; o < n_out; o += kAttnThreads) {
+            float sum = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kAttnThreads / 32; ++w) sum = __fadd_rn(sum, red[w * n_out + o]);
+            part[o] = sum;
         }
     } else {
         // thread slot k owns the column pair (2 * (o % (hd / 2)), +1) of query head o / (hd / 2)
@@ -635,12 +664,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_pv_kernel(AttnParams a) {
     for (int i = tid; i < n_out; i += kAttnThreads) {
         float sum = 0.0f;
         int r = 0;
-        for (; r + 8 <= nchk; r += 8) {  // eight loads in flight, added in chunk order
-            float v[8];
+        for (; r + 16 <= nchk; r += 16) {  // sixteen loads in flight, added in chunk order
+            float v[16];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) v[u] = __ldcg(pb + size_t(r + u) * n_out + i);
+            for (int u = 0; u < 16; ++u) v[u] = __ldcg(pb + size_t(r + u) * n_out + i);
 #pragma unroll
-            for (int u = 0; u < 8; ++u) sum = __fadd_rn(sum, v[u]);
+            for (int u = 0; u < 16; ++u) sum = __fadd_rn(sum, v[u]);
         }
         for (; r < nchk; ++r) sum = __fadd_rn(sum, __ldcg(pb + size_t(r) * n_out + i));
         if (a.tp.peers) tp_store(a.tp, hb * hd + i, sum, ep);
