@@ -21,6 +21,8 @@
 #include "gemv_core.cuh"
 
 #include <algorithm>
+#include <cstdio>
+#include <cstdlib>
 #include <mutex>
 #include <utility>
 #include <vector>
@@ -351,7 +353,7 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
 // W warps per CTA, batches of about BB bytes of rows.
 template <int TYPE, int W, int BB>
-__global__ void __launch_bounds__(W * 32) gemv_stage_kernel(GemvArgs p) {
+__global__ void __launch_bounds__(W * 32, 1) gemv_stage_kernel(GemvArgs p) {  // one CTA per SM (its shared memory)
     extern __shared__ __align__(128) unsigned char smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const StageShape sh = stage_shape(TYPE, p.cols, W, BB);
@@ -528,7 +530,16 @@ int configure(const void* kernel, size_t smem) {
     std::lock_guard<std::mutex> lock(mu);
     for (const auto& d : done)
         if (d.first == kernel && d.second == dev) return SYN_OK;
-    st = syn_cuda_status(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    // the device's per-block opt-in less the kernel's static shared memory (the batched
+    // kernel's Q8_0 x 16 tokens takes up to 222 KB)
+    int optin = 0;
+    cudaFuncAttributes fa{};
+    st = syn_cuda_status(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    if (!st) st = syn_cuda_status(cudaFuncGetAttributes(&fa, kernel));
+    if (st) return st;
+    const size_t most = size_t(optin) - fa.sharedSizeBytes;
+    if (smem > most) return SYN_ERR_UNSUPPORTED;
+    st = syn_cuda_status(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(most)));
     if (!st) done.push_back({kernel, dev});
     return st;
 }
@@ -580,9 +591,25 @@ struct StageCfg {
     int warps;
     int batch;
 };
+// The configurations the staged kernel is built for: warps per CTA, batch bytes.
+constexpr StageCfg kStageCfgs[] = {{8, 9728}, {8, 16384}, {12, 4864}, {16, 4864}, {4, 16384}, {5, 16384}};
+
 StageCfg stage_cfg(int type, int rows, int cols) {
-    (void)type;
     (void)rows;
+    // SYN_GEMV_CFG="warps,batch" picks a built configuration (tuning sweeps); 8 warps
+    // of ~9.7 KB batches measured best on every Llama-3-8B shape
+    static const StageCfg forced = [] {
+        StageCfg c{0, 0};
+        if (const char* e = std::getenv("SYN_GEMV_CFG")) {
+            int w = 0, b = 0;
+            if (std::sscanf(e, "%d,%d", &w, &b) == 2)
+                for (const StageCfg& k : kStageCfgs)
+                    if (k.warps == w && k.batch == b) c = k;
+        }
+        return c;
+    }();
+    if (forced.warps) return forced;
+    (void)type;
     (void)cols;
     return {8, 9728};
 }
@@ -615,7 +642,200 @@ int launch_stage(const GemvArgs& p, cudaStream_t s) {
     if (c.warps == 16 && c.batch == 4864) return launch_stage_cfg<TYPE, 16, 4864>(p, s);
     if (c.warps == 12 && c.batch == 4864) return launch_stage_cfg<TYPE, 12, 4864>(p, s);
     if (c.warps == 8 && c.batch == 16384) return launch_stage_cfg<TYPE, 8, 16384>(p, s);
+    if (c.warps == 4 && c.batch == 16384) return launch_stage_cfg<TYPE, 4, 16384>(p, s);
+    if (c.warps == 5 && c.batch == 16384) return launch_stage_cfg<TYPE, 5, 16384>(p, s);
     return launch_stage_cfg<TYPE, 8, 9728>(p, s);
+}
+
+// ---- batched tokens on integer tensor cores --------------------------------------
+// n_tok >= 3 tokens, planar Q4_0 / Q8_0 rows (gemm.hpp:143-221 gemm_rows, G1:
+// every token's row equals the one-token GEMV's). mma.m16n8k32 .s8 takes one
+// 32-weight block as its k-step: the int32 product of 16 rows x 8 tokens is
+// each (row, token) block dot exactly (Q4_0 weights enter as q - 8, the value
+// the reference multiplies). The lane holding C[row][token] then runs that
+// pair's fma chain in block order, acc = fma(float(isum), d_w * d_a, acc),
+// over one 32-block chunk (dot.hpp:277-287), and the chunk sums of a row are
+// added in order (dot.hpp:398).
+// Fragment layouts (PTX ISA, mma.m16n8k32 .s8): lane = 4 g + t;
+//   A: a0 = A[g][4t..4t+3], a1 = A[g+8][4t..], a2 = A[g][16+4t..], a3 = A[g+8][16+4t..]
+//   B: b0 = B[4t..4t+3][g], b1 = B[16+4t..16+4t+3][g]
+//   C: c0, c1 = C[g][2t], C[g][2t+1]; c2, c3 = C[g+8][2t], C[g+8][2t+1]
+// A Q4_0 block holds element j in the low nibble of byte j and element j+16 in
+// its high nibble, so one 32-bit word of bytes 4t..4t+3 gives both a0 and a2.
+__device__ __forceinline__ void mma_s8(int (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void cp_async16_g(void* smem, const void* gmem) {
+    const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+
+constexpr int kImmaWarps = 4;      // warps per CTA: the chunk slots of one 16-row tile
+constexpr int kImmaChunk = 32;     // blocks per chunk (the reference's fma-chain unit)
+constexpr int kImmaSeg = kImmaWarps * kImmaChunk;  // blocks of activations staged per pass: one chunk per warp
+constexpr int kImmaTokPitch = kImmaSeg * 32 + 16;  // bytes per token: consecutive tokens 4 banks apart
+__host__ __device__ constexpr int imma_chunk_bytes(int type) {
+    return 16 * kImmaChunk * (type == SYN_Q4_0 ? 16 : 32) + 16 * kImmaChunk * 2;  // 16 rows' quants, then scales
+}
+__host__ __device__ constexpr size_t imma_act_bytes(int ntt) {
+    return size_t(8 * ntt) * kImmaTokPitch + size_t(8 * ntt) * kImmaSeg * 4;  // quants, then the decoded scales
+}
+__host__ __device__ inline size_t imma_smem(int type, int ntt, int nch) {
+    return imma_act_bytes(ntt) + size_t(nch) * 16 * 8 * ntt * 4 +  // chunk sums of the tile
+           size_t(kImmaWarps) * 2 * imma_chunk_bytes(type);      // each warp's chunk, double-buffered
+}
+
+// CTA (x, y): the 16-row tile x for tokens 8 NTT y ..; warp w computes chunks
+// w, w + 4, ... of every row of the tile (their weights requested one chunk
+// ahead), against the tokens' activations the CTA stages one segment of four
+// chunks at a time between two block barriers; the chunk sums then meet in
+// shared memory and are added in chunk order.
+template <int TYPE, int NTT>
+__global__ void __launch_bounds__(kImmaWarps * 32) gemm_imma_kernel(GemvArgs p) {
+    constexpr int QB = TYPE == SYN_Q4_0 ? 16 : 32;
+    constexpr int QS = 16 * kImmaChunk * QB, CB = imma_chunk_bytes(TYPE), NTOK = 8 * NTT;
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, t = lane & 3;
+    const int r0 = blockIdx.x * 16, tok0 = blockIdx.y * NTOK;
+    const int nb = p.nb, nch = (nb + kImmaChunk - 1) / kImmaChunk, nseg = (nb + kImmaSeg - 1) / kImmaSeg;
+    int8_t* sq = reinterpret_cast<int8_t*>(smem);                                  // [NTOK][kImmaTokPitch]
+    float* sd = reinterpret_cast<float*>(smem + size_t(NTOK) * kImmaTokPitch);    // [NTOK][kImmaSeg]
+    float* cs = reinterpret_cast<float*>(smem + imma_act_bytes(NTT));             // [nch][16 rows][NTOK]
+    unsigned char* wbuf = smem + imma_act_bytes(NTT) + size_t(nch) * 16 * NTOK * 4 + size_t(warp) * 2 * CB;
+    const size_t row_b = planar_row_bytes(TYPE, p.cols), qbytes = planar_quant_bytes(TYPE, p.cols);
+    // chunk c of the tile's 16 rows into buffer k (rows past the matrix re-read its last row, never stored)
+    auto issue_chunk = [&](int c, int k) {
+        if (c < nch) {
+            unsigned char* dst = wbuf + k * CB;
+            const int b0 = c * kImmaChunk, cnt = min(kImmaChunk, nb - b0);
+            const int qpr = cnt * QB / 16, spr = (cnt * 2 + 15) / 16;  // 16-byte pieces per row (scales padded)
+            for (int i = lane; i < 16 * qpr; i += 32) {
+                const int rr = i / qpr, q = i - rr * qpr;
+                const size_t r = size_t(min(r0 + rr, p.rows - 1));
+                cp_async16_g(dst + rr * (kImmaChunk * QB) + q * 16, p.w + r * row_b + size_t(b0) * QB + q * 16);
+            }
+            for (int i = lane; i < 16 * spr; i += 32) {
+                const int rr = i / spr, q = i - rr * spr;
+                const size_t r = size_t(min(r0 + rr, p.rows - 1));
+                cp_async16_g(dst + QS + rr * (kImmaChunk * 2) + q * 16, p.w + r * row_b + qbytes + size_t(b0) * 2 + q * 16);
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    // activations of blocks [seg0, seg0 + kImmaSeg) for the CTA's tokens (zero past n_tok)
+    auto stage_act = [&](int seg0) {
+        const int nblk = min(kImmaSeg, nb - seg0);
+        const int per_tok = nblk * 2;  // 16-byte pieces
+        for (int i = threadIdx.x; i < NTOK * per_tok; i += kImmaWarps * 32) {
+            const int tl = i / per_tok, c = i - tl * per_tok, tk = tok0 + tl;
+            int4 v = make_int4(0, 0, 0, 0);
+            if (tk < p.n_tok) v = __ldg(reinterpret_cast<const int4*>(p.act.qs + size_t(tk) * p.cols + size_t(seg0) * 32) + c);
+            *reinterpret_cast<int4*>(sq + tl * kImmaTokPitch + c * 16) = v;
+        }
+        for (int i = threadIdx.x; i < NTOK * nblk; i += kImmaWarps * 32) {
+            const int tl = i / nblk, j = i - tl * nblk, tk = tok0 + tl;
+            sd[tl * kImmaSeg + j] = tk < p.n_tok ? __ldg(p.act.d + size_t(tk) * nb + seg0 + j) : 0.0f;
+        }
+    };
+    issue_chunk(warp, 0);  // weights never depend on the previous kernel
+    pdl_launch_dependents();
+    pdl_wait();  // the activations do
+
+    for (int seg = 0; seg < nseg; ++seg) {
+        __syncthreads();  // every warp is done with the previous segment
+        stage_act(seg * kImmaSeg);
+        __syncthreads();
+        const int c = seg * kImmaWarps + warp;
+        issue_chunk(c + kImmaWarps, (seg + 1) & 1);  // this warp's next chunk, one segment ahead
+        asm volatile("cp.async.wait_group 1;" ::: "memory");  // chunk c (the older group) is in
+        __syncwarp();
+        if (c >= nch) continue;
+        const unsigned char* st = wbuf + (seg & 1) * CB;
+        const int cnt = min(kImmaChunk, nb - c * kImmaChunk);
+        float acc[NTT][4];
+#pragma unroll
+        for (int n = 0; n < NTT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
+#pragma unroll 4
+        for (int j = 0; j < cnt; ++j) {
+            uint32_t a[4];
+            const unsigned char* qlo = st + g * (kImmaChunk * QB) + j * QB;
+            const unsigned char* qhi = qlo + 8 * (kImmaChunk * QB);
+            if (TYPE == SYN_Q4_0) {
+                const uint32_t wl = *reinterpret_cast<const uint32_t*>(qlo + 4 * t);
+                const uint32_t wh = *reinterpret_cast<const uint32_t*>(qhi + 4 * t);
+                a[0] = __vsub4(wl & 0x0f0f0f0fu, 0x08080808u);
+                a[2] = __vsub4((wl >> 4) & 0x0f0f0f0fu, 0x08080808u);
+                a[1] = __vsub4(wh & 0x0f0f0f0fu, 0x08080808u);
+                a[3] = __vsub4((wh >> 4) & 0x0f0f0f0fu, 0x08080808u);
+            } else {
+                a[0] = *reinterpret_cast<const uint32_t*>(qlo + 4 * t);
+                a[2] = *reinterpret_cast<const uint32_t*>(qlo + 16 + 4 * t);
+                a[1] = *reinterpret_cast<const uint32_t*>(qhi + 4 * t);
+                a[3] = *reinterpret_cast<const uint32_t*>(qhi + 16 + 4 * t);
+            }
+            const float dlo = f16_from_bits(*reinterpret_cast<const uint16_t*>(st + QS + g * (kImmaChunk * 2) + j * 2));
+            const float dhi =
+                f16_from_bits(*reinterpret_cast<const uint16_t*>(st + QS + (g + 8) * (kImmaChunk * 2) + j * 2));
+            const int bs = warp * kImmaChunk + j;  // the block in the staged segment
+#pragma unroll
+            for (int n = 0; n < NTT; ++n) {
+                // this lane's B column is local token 8n + g (zeros past n_tok)
+                const int8_t* aq = sq + (8 * n + g) * kImmaTokPitch + bs * 32;
+                const uint32_t bq0 = *reinterpret_cast<const uint32_t*>(aq + 4 * t);
+                const uint32_t bq1 = *reinterpret_cast<const uint32_t*>(aq + 16 + 4 * t);
+                int cc[4] = {0, 0, 0, 0};
+                mma_s8(cc, a, bq0, bq1);
+                const int tl = 8 * n + 2 * t;  // local tokens of c0 / c2 (c1 / c3: + 1)
+                const float da0 = sd[tl * kImmaSeg + bs], da1 = sd[(tl + 1) * kImmaSeg + bs];
+                acc[n][0] = fmaf(float(cc[0]), __fmul_rn(dlo, da0), acc[n][0]);
+                acc[n][1] = fmaf(float(cc[1]), __fmul_rn(dlo, da1), acc[n][1]);
+                acc[n][2] = fmaf(float(cc[2]), __fmul_rn(dhi, da0), acc[n][2]);
+                acc[n][3] = fmaf(float(cc[3]), __fmul_rn(dhi, da1), acc[n][3]);
+            }
+        }
+        float* cc_out = cs + size_t(c) * 16 * NTOK;  // [row][token]
+#pragma unroll
+        for (int n = 0; n < NTT; ++n) {
+            const int tl = 8 * n + 2 * t;
+            cc_out[g * NTOK + tl] = acc[n][0];
+            cc_out[g * NTOK + tl + 1] = acc[n][1];
+            cc_out[(g + 8) * NTOK + tl] = acc[n][2];
+            cc_out[(g + 8) * NTOK + tl + 1] = acc[n][3];
+        }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");  // nothing left in flight (trailing groups are empty)
+    __syncthreads();
+    // y = ((0 + chunk 0) + chunk 1) + ... (dot.hpp:398), plus the residual
+    for (int i = threadIdx.x; i < 16 * NTOK; i += kImmaWarps * 32) {
+        const int rr = i / NTOK, tl = i - rr * NTOK, r = r0 + rr, tk = tok0 + tl;
+        if (r >= p.rows || tk >= p.n_tok) continue;
+        float y = 0.0f;
+        for (int c = 0; c < nch; ++c) y = __fadd_rn(y, cs[size_t(c) * 16 * NTOK + i]);
+        const size_t o = size_t(tk) * p.rows + r;
+        p.y[o] = p.residual ? __fadd_rn(y, p.residual[o]) : y;
+    }
+}
+
+template <int TYPE>
+int launch_imma(const GemvArgs& p, cudaStream_t s) {
+    const int nch = (p.nb + kImmaChunk - 1) / kImmaChunk;
+    const unsigned gx = unsigned((p.rows + 15) / 16);
+    if (p.n_tok > 8) {
+        auto k = gemm_imma_kernel<TYPE, 2>;
+        const size_t smem = imma_smem(TYPE, 2, nch);
+        int st = configure(reinterpret_cast<const void*>(k), smem);
+        if (st) return st;
+        return syn_launch(k, dim3(gx, (p.n_tok + 15) / 16, 1), unsigned(kImmaWarps * 32), smem, s, p);
+    }
+    auto k = gemm_imma_kernel<TYPE, 1>;
+    const size_t smem = imma_smem(TYPE, 1, nch);
+    int st = configure(reinterpret_cast<const void*>(k), smem);
+    if (st) return st;
+    return syn_launch(k, dim3(gx, 1, 1), unsigned(kImmaWarps * 32), smem, s, p);
 }
 
 template <int TYPE, int LAYOUT, int NT>
@@ -692,6 +912,21 @@ extern "C" int syn_gemv_q(int type, const void* w, int layout, int rows, int col
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const ActPlanes all = act_planes(const_cast<void*>(act), n_tok, cols);
     const int nb = cols / QK;
+    if (layout == SYN_LAYOUT_PLANAR && n_tok >= 3) {  // integer tensor cores, every token in one launch
+        GemvArgs p{};
+        p.w = static_cast<const uint8_t*>(w);
+        p.rows = rows;
+        p.cols = cols;
+        p.nb = nb;
+        p.n_tok = n_tok;
+        p.act = all;
+        p.y = y;
+        p.residual = residual;
+        p.in_mode = SYN_IN_Q8;
+        p.out_mode = SYN_OUT_ROWS;
+        const int st = type == SYN_Q4_0 ? launch_imma<SYN_Q4_0>(p, s) : launch_imma<SYN_Q8_0>(p, s);
+        if (st != SYN_ERR_UNSUPPORTED) return st;  // else a row too wide for its shared memory: the lane kernels
+    }
     for (int t0 = 0; t0 < n_tok; t0 += 8) {
         const int n = n_tok - t0 < 8 ? n_tok - t0 : 8;
         GemvArgs p{};

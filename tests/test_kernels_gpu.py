@@ -74,7 +74,7 @@ def check_gemv(ty, layout, rows, cols, n_tok, seed, row_subset=None):
 @pytest.mark.parametrize("ty", [syn.Q4_0, syn.Q8_0])
 @pytest.mark.parametrize("layout", [syn.LAYOUT_PLANAR, syn.LAYOUT_GGUF])
 @pytest.mark.parametrize("rows,cols,n_tok", [(8, 1024, 1), (288, 288, 1), (768, 288, 2), (300, 4096, 4),
-                                             (64, 14336, 16), (1000, 2048, 3)])
+                                             (64, 14336, 16), (1000, 2048, 3), (300, 4096, 20), (37, 1056, 9)])
 def test_gemv_small(ty, layout, rows, cols, n_tok):
     check_gemv(ty, layout, rows, cols, n_tok, seed=rows * 7 + cols + n_tok)
 
@@ -82,10 +82,11 @@ def test_gemv_small(ty, layout, rows, cols, n_tok):
 @pytest.mark.parametrize("ty", [syn.Q4_0, syn.Q8_0])
 @pytest.mark.parametrize("rows,cols", [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)])
 def test_gemv_sweep_shapes(ty, rows, cols):
-    # the BASELINE sweep shapes at batch 1 and 4; the oracle checks a row sample of the largest
+    # the BASELINE sweep shapes at batch 1, 4 and 16; the oracle checks a row sample of the largest
     subset = None if rows * cols <= 14336 * 4096 else np.random.default_rng(1).choice(rows, 512, replace=False)
     check_gemv(ty, syn.LAYOUT_PLANAR, rows, cols, 1, seed=rows + cols, row_subset=subset)
     check_gemv(ty, syn.LAYOUT_PLANAR, rows, cols, 4, seed=rows + cols + 1, row_subset=subset)
+    check_gemv(ty, syn.LAYOUT_PLANAR, rows, cols, 16, seed=rows + cols + 2, row_subset=subset)
 
 
 @pytest.mark.parametrize("fmt,ty", [("q4_0", syn.Q4_0), ("q8_0", syn.Q8_0)])
