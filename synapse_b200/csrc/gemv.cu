@@ -353,7 +353,7 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
 // W warps per CTA, batches of about BB bytes of rows.
 template <int TYPE, int W, int BB>
-__global__ void __launch_bounds__(W * 32, 1) gemv_stage_kernel(GemvArgs p) {  // one CTA per SM (its shared memory)
+__global__ void __launch_bounds__(W * 32) gemv_stage_kernel(GemvArgs p) {
     extern __shared__ __align__(128) unsigned char smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const StageShape sh = stage_shape(TYPE, p.cols, W, BB);

@@ -174,22 +174,48 @@ __device__ inline void quantize_act1(const float* x, const float* gamma, float e
             }
         }
     };
-    // gamma of half h (norm only)
-    auto gamma16 = [&](int h, float4 (&g)[4]) {
-        const float4* g4 = reinterpret_cast<const float4*>(gamma + size_t(h) * 16);
+    float scale = 1.0f;
+    if (norm) {
+        double sum = 0.0;
+        for (int h = threadIdx.x; h < nh; h += blockDim.x) {
+            float fv[16];
+            load16(h, fv);
+            float4 f[4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) g[k] = __ldg(g4 + k);
-    };
-    // half h scaled by the norm (when asked), quantized, its quants and (d, sum) staged;
-    // mask: the lanes of this pass (a prefix of the warp; block pairs never straddle it)
-    auto quantize_half = [&](int h, float (&v)[16], const float4 (&g)[4], float scale, unsigned mask) {
-        if (norm) {
+            for (int k = 0; k < 4; ++k) f[k] = make_float4(fv[4 * k], fv[4 * k + 1], fv[4 * k + 2], fv[4 * k + 3]);
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                v[4 * k] = __fmul_rn(__fmul_rn(v[4 * k], scale), g[k].x);
-                v[4 * k + 1] = __fmul_rn(__fmul_rn(v[4 * k + 1], scale), g[k].y);
-                v[4 * k + 2] = __fmul_rn(__fmul_rn(v[4 * k + 2], scale), g[k].z);
-                v[4 * k + 3] = __fmul_rn(__fmul_rn(v[4 * k + 3], scale), g[k].w);
+                sum += double(__fmul_rn(f[k].x, f[k].x));
+                sum += double(__fmul_rn(f[k].y, f[k].y));
+                sum += double(__fmul_rn(f[k].z, f[k].z));
+                sum += double(__fmul_rn(f[k].w, f[k].w));
+            }
+        }
+        sum = warp_sum_d(sum);
+        if (lane == 0) red[warp] = sum;
+        __syncthreads();
+        double tot = 0.0;
+        for (int w = 0; w < int(blockDim.x >> 5); ++w) tot += red[w];
+        const float mean = float(tot / double(cols));
+        scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    }
+    for (int h0 = 0; h0 < nh; h0 += blockDim.x) {
+        const int h = h0 + int(threadIdx.x);
+        // lanes of this pass (a prefix of the warp; block pairs never straddle it)
+        const int live = min(32, max(0, nh - (h0 + warp * 32)));
+        if (h >= nh) continue;
+        const unsigned mask = live == 32 ? 0xffffffffu : ((1u << live) - 1u);
+        float v[16];
+        load16(h, v);
+        if (norm) {
+            const float4* g4 = reinterpret_cast<const float4*>(gamma + size_t(h) * 16);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float4 g = __ldg(g4 + k);
+                v[4 * k] = __fmul_rn(__fmul_rn(v[4 * k], scale), g.x);
+                v[4 * k + 1] = __fmul_rn(__fmul_rn(v[4 * k + 1], scale), g.y);
+                v[4 * k + 2] = __fmul_rn(__fmul_rn(v[4 * k + 2], scale), g.z);
+                v[4 * k + 3] = __fmul_rn(__fmul_rn(v[4 * k + 3], scale), g.w);
             }
         }
         float amax = 0.0f;
@@ -214,74 +240,6 @@ __device__ inline void quantize_act1(const float* x, const float* gamma, float e
         const int b = h >> 1;
         *reinterpret_cast<uint4*>(aq + sact_off(b) + 16 * (h & 1)) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
         if ((h & 1) == 0) dsum[b] = make_float2(f16_from_bits(f16_bits(d)), __int_as_float(qsum));
-    };
-    // 1 / sqrt(mean + eps) from this thread's partial sum (its halves in order, then
-    // lanes in tree order, then warps in order)
-    auto norm_scale = [&](double sum) {
-        sum = warp_sum_d(sum);
-        if (lane == 0) red[warp] = sum;
-        __syncthreads();
-        double tot = 0.0;
-        for (int w = 0; w < int(blockDim.x >> 5); ++w) tot += red[w];
-        const float mean = float(tot / double(cols));
-        return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
-    };
-    auto pass_mask = [&](int h0) {
-        const int live = min(32, max(0, nh - (h0 + warp * 32)));
-        return live == 32 ? 0xffffffffu : ((1u << live) - 1u);
-    };
-    constexpr int kHeld = 4;      // halves per thread kept in registers between the two passes
-    constexpr int kHeldNorm = 2;  // with the norm (gamma held too)
-    if (nh <= (norm ? kHeldNorm : kHeld) * int(blockDim.x)) {
-        // every load in flight at once (x and gamma); x is read once
-        float hv[kHeld][16];
-        float4 gv[kHeldNorm][4];
-#pragma unroll
-        for (int k = 0; k < kHeld; ++k) {
-            const int h = int(threadIdx.x) + k * int(blockDim.x);
-            if (h < nh) {
-                if (k < kHeldNorm && norm) gamma16(h, gv[k < kHeldNorm ? k : 0]);
-                load16(h, hv[k]);
-            }
-        }
-        float scale = 1.0f;
-        if (norm) {
-            double sum = 0.0;
-#pragma unroll
-            for (int k = 0; k < kHeld; ++k) {
-                if (int(threadIdx.x) + k * int(blockDim.x) < nh) {
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) sum += double(__fmul_rn(hv[k][j], hv[k][j]));
-                }
-            }
-            scale = norm_scale(sum);
-        }
-#pragma unroll
-        for (int k = 0; k < kHeld; ++k) {
-            const int h0 = k * int(blockDim.x), h = h0 + int(threadIdx.x);
-            if (h < nh) quantize_half(h, hv[k], gv[k < kHeldNorm ? k : 0], scale, pass_mask(h0));
-        }
-        return;
-    }
-    float scale = 1.0f;
-    if (norm) {
-        double sum = 0.0;
-        for (int h = threadIdx.x; h < nh; h += blockDim.x) {
-            float fv[16];
-            load16(h, fv);
-#pragma unroll
-            for (int j = 0; j < 16; ++j) sum += double(__fmul_rn(fv[j], fv[j]));
-        }
-        scale = norm_scale(sum);
-    }
-    for (int h0 = 0; h0 < nh; h0 += blockDim.x) {
-        const int h = h0 + int(threadIdx.x);
-        if (h >= nh) continue;
-        float v[16];
-        float4 g[4];
-        if (norm) gamma16(h, g);
-        load16(h, v);
-        quantize_half(h, v, g, scale, pass_mask(h0));
     }
 }
 
