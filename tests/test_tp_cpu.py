@@ -1,8 +1,8 @@
 """Tensor-parallel sharding on the CPU (no GPU).
 
 The product's rank layouts (syn_tp_layout_of, the same function the session
-shards with) must partition every sharded dimension; and a world-2 gloo run
-of the oracle's per-op functions over those shares, all-gathering at the five
+shards with) must partition every sharded dimension; and a gloo run over 2 or
+4 ranks of the oracle's per-op functions over those shares, all-gathering at the five
 points the sharded session gathers (attention output, residual after O,
 silu * up, residual after down, logits), must reproduce the one-process
 oracle's logits bit for bit. That is the reference's D1 contract
@@ -21,6 +21,9 @@ from synapse_b200 import model
 
 TINY = dict(n_layer=2, n_embd=64, n_ff=128, n_head=4, n_head_kv=2, head_dim=16, n_vocab=64, rms_eps=1e-5,
             rope_base=10000.0)
+# four KV heads: shards over 2 and 4 ranks
+TINY_KV4 = dict(n_layer=2, n_embd=64, n_ff=128, n_head=8, n_head_kv=4, head_dim=8, n_vocab=64, rms_eps=1e-5,
+                rope_base=10000.0)
 LLAMA_8B = dict(n_layer=32, n_embd=4096, n_ff=14336, n_head=32, n_head_kv=8, head_dim=128, n_vocab=128256,
                 rms_eps=1e-5, rope_base=500000.0)
 LLAMA_70B = dict(n_layer=80, n_embd=8192, n_ff=28672, n_head=64, n_head_kv=8, head_dim=128, n_vocab=128256,
@@ -112,7 +115,7 @@ def _tokens(cfg, n):
     return [int(t) for t in np.random.default_rng(3).integers(0, cfg["n_vocab"], n)]
 
 
-def _rank_main(rank, world, port, type_layers, n_steps, q):
+def _rank_main(rank, world, port, type_layers, n_steps, cfg_name, q):
     import torch
     import torch.distributed as dist
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
@@ -123,8 +126,9 @@ def _rank_main(rank, world, port, type_layers, n_steps, q):
             parts = [torch.empty_like(t) for _ in range(world)]
             dist.all_gather(parts, t)
             return torch.cat(parts).numpy()
-        w = _model(TINY, type_layers)
-        logits = sharded_decode(TINY, w, _tokens(TINY, n_steps), n_steps, rank, world, gather)
+        cfg = CONFIGS[cfg_name]
+        w = _model(cfg, type_layers)
+        logits = sharded_decode(cfg, w, _tokens(cfg, n_steps), n_steps, rank, world, gather)
         q.put((rank, np.stack(logits)))
     except Exception as e:  # reported to the parent, which fails the test
         q.put((rank, repr(e)))
@@ -138,14 +142,21 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("type_layers", [model.Q8_0, model.Q4_0], ids=["q8_0", "q4_0"])
-def test_world2_sharded_logits_equal_one_process(type_layers):
+CONFIGS = {"tiny": TINY, "tiny_kv4": TINY_KV4}
+
+
+@pytest.mark.parametrize("world,cfg_name,type_layers", [(2, "tiny", model.Q8_0), (2, "tiny", model.Q4_0),
+                                                        (4, "tiny_kv4", model.Q4_0)],
+                         ids=["w2-q8_0", "w2-q4_0", "w4-q4_0"])
+def test_sharded_logits_equal_one_process(world, cfg_name, type_layers):
     import torch.multiprocessing as mp
-    n_steps, world = 6, 2
+    n_steps = 6
+    cfg = CONFIGS[cfg_name]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, type_layers, n_steps, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, type_layers, n_steps, cfg_name, q))
+             for r in range(world)]
     for p in procs:
         p.start()
     got = dict(q.get(timeout=300) for _ in range(world))
@@ -154,8 +165,9 @@ def test_world2_sharded_logits_equal_one_process(type_layers):
     for r in range(world):
         assert not isinstance(got[r], str), got[r]
     # every rank holds the same gathered logits
-    assert np.array_equal(got[0].view(np.uint32), got[1].view(np.uint32))
-    w = _model(TINY, type_layers)
-    ref = orc.Llama(TINY, w, max_ctx=n_steps)
-    want = np.stack([ref.step(t, pos) for pos, t in enumerate(_tokens(TINY, n_steps))])
+    for r in range(1, world):
+        assert np.array_equal(got[0].view(np.uint32), got[r].view(np.uint32))
+    w = _model(cfg, type_layers)
+    ref = orc.Llama(cfg, w, max_ctx=n_steps)
+    want = np.stack([ref.step(t, pos) for pos, t in enumerate(_tokens(cfg, n_steps))])
     assert np.array_equal(got[0].view(np.uint32), want.view(np.uint32))
