@@ -14,9 +14,12 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_build", "liboracle.so")
 
-F32, F16, Q4_0, Q8_0 = 0, 1, 2, 8
+F32, F16, Q4_0, Q8_0, Q4_K, Q6_K = 0, 1, 2, 8, 12, 14
 QK = 32
-BLOCK_BYTES = {Q4_0: 18, Q8_0: 34}
+QK_K = 256
+BLOCK_BYTES = {Q4_0: 18, Q8_0: 34, Q4_K: 144, Q6_K: 210}
+BLOCK_ELEMS = {Q4_0: QK, Q8_0: QK, Q4_K: QK_K, Q6_K: QK_K}
+Q8_K_BYTES = 292
 
 _lib = None
 
@@ -37,11 +40,12 @@ def lib():
         L.orc_fp16_to_float.argtypes = [ctypes.c_uint16]
         L.orc_float_to_fp16.restype = ctypes.c_uint16
         L.orc_float_to_fp16.argtypes = [ctypes.c_float]
-        for name in ("orc_quantize_row_q8_0", "orc_quantize_row_q4_0"):
+        for name in ("orc_quantize_row_q8_0", "orc_quantize_row_q4_0", "orc_quantize_row_q8_k"):
             getattr(L, name).argtypes = [vp, sz, vp]
         L.orc_dequantize_row.argtypes = [ctypes.c_int, vp, sz, vp]
         L.orc_gemv.argtypes = [ctypes.c_int, vp, sz, sz, vp, vp]
         L.orc_gemv_q8act.argtypes = [ctypes.c_int, vp, sz, sz, vp, vp]
+        L.orc_gemv_q8k.argtypes = [ctypes.c_int, vp, sz, sz, vp, vp]
         L.orc_gemm.argtypes = [ctypes.c_int, vp, sz, sz, vp, sz, vp]
         L.orc_rope_theta_scale.restype = ctypes.c_float
         L.orc_rope_theta_scale.argtypes = [ctypes.c_float, sz]
@@ -112,7 +116,7 @@ def row_bytes(type_, cols):
         return cols * 4
     if type_ == F16:
         return cols * 2
-    return cols // QK * BLOCK_BYTES[type_]
+    return cols // BLOCK_ELEMS[type_] * BLOCK_BYTES[type_]
 
 
 def quantize_q8_0(x):
@@ -124,6 +128,35 @@ def quantize_q8_0(x):
     for i in range(xs.shape[0]):
         lib().orc_quantize_row_q8_0(_p(xs[i]), cols, _p(os_[i]))
     return out
+
+
+def quantize_q8_k(x):
+    """x: (..., cols) f32 -> uint8 blocks (..., cols/256*292), ggml's block_q8_k."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    cols = x.shape[-1]
+    out = np.empty(x.shape[:-1] + (cols // QK_K * Q8_K_BYTES,), dtype=np.uint8)
+    xs, os_ = x.reshape(-1, cols), out.reshape(-1, cols // QK_K * Q8_K_BYTES)
+    for i in range(xs.shape[0]):
+        lib().orc_quantize_row_q8_k(_p(xs[i]), cols, _p(os_[i]))
+    return out
+
+
+def random_k_blocks(type_, rows, cols, seed):
+    """Seeded random Q4_K / Q6_K rows: every byte pattern of the quants and
+    sub-block scales is a valid block; the binary16 super-block scales are
+    drawn from [2^-14, 2^-8) so no value is inf or nan."""
+    rng = np.random.default_rng(seed)
+    nb = cols // QK_K
+    out = rng.integers(0, 256, (rows, nb, BLOCK_BYTES[type_]), dtype=np.uint8)
+    scale = lambda n: (2.0 ** rng.uniform(-14, -8, n)).astype(np.float16).view(np.uint8).reshape(-1, 2)
+    if type_ == Q4_K:
+        out[:, :, 0:2] = scale(rows * nb).reshape(rows, nb, 2)  # d
+        out[:, :, 2:4] = scale(rows * nb).reshape(rows, nb, 2)  # dmin
+    elif type_ == Q6_K:
+        out[:, :, 208:210] = scale(rows * nb).reshape(rows, nb, 2)
+    else:
+        raise ValueError(type_)
+    return out.reshape(rows, -1)
 
 
 def quantize_q4_0(x):
@@ -182,6 +215,15 @@ def gemv_q8act(type_, w, rows, cols, act):
     act = np.ascontiguousarray(act, dtype=np.uint8)
     y = np.empty(rows, dtype=np.float32)
     lib().orc_gemv_q8act(type_, _p(w), rows, cols, _p(act), _p(y))
+    return y
+
+
+def gemv_q8k(type_, w, rows, cols, act):
+    """Q4_K / Q6_K rows on ggml block_q8_k activations."""
+    w = np.ascontiguousarray(w).view(np.uint8)
+    act = np.ascontiguousarray(act, dtype=np.uint8)
+    y = np.empty(rows, dtype=np.float32)
+    lib().orc_gemv_q8k(type_, _p(w), rows, cols, _p(act), _p(y))
     return y
 
 

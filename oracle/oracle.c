@@ -14,6 +14,10 @@
 #include <stdlib.h>
 #include <string.h>
 
+_Static_assert(sizeof(orc_block_q4_k) == 144, "block_q4_k");
+_Static_assert(sizeof(orc_block_q6_k) == 210, "block_q6_k");
+_Static_assert(sizeof(orc_block_q8_k) == 292, "block_q8_k");
+
 static int g_threads = 1;
 
 void orc_set_threads(int n) { g_threads = n < 1 ? 1 : (n > 256 ? 256 : n); }
@@ -137,12 +141,57 @@ void orc_quantize_row_q4_0(const float* x, size_t n, orc_block_q4_0* y) {
     }
 }
 
+/* ---- quant/q8.hpp:44-48 nearest_int: round half to even through the
+ * 1.5 * 2^23 magic (valid for |v| <= 2^22) ----------------------------- */
+static inline int nearest_int(float v) {
+    const float t = v + 12582912.0f;
+    return (int)(f2u(t) & 0x007fffffu) - 0x00400000;
+}
+
+/* ---- quant/q8.hpp:73-104: quantize_row_q8_k ------------------------------ */
+void orc_quantize_row_q8_k(const float* x, size_t n, orc_block_q8_k* y) {
+    for (size_t i = 0; i < n / ORC_QK_K; ++i) {
+        const float* xb = x + i * ORC_QK_K;
+        float max = 0.0f, amax = 0.0f; /* the first element of largest magnitude, signed */
+        for (int j = 0; j < ORC_QK_K; ++j) {
+            const float ax = fabsf(xb[j]);
+            if (ax > amax) { amax = ax; max = xb[j]; }
+        }
+        if (amax == 0.0f) { memset(&y[i], 0, sizeof y[i]); continue; }
+        const float iscale = -127.0f / max;
+        for (int j = 0; j < ORC_QK_K; ++j) {
+            const int q = nearest_int(iscale * xb[j]);
+            y[i].qs[j] = (int8_t)(q < 127 ? q : 127);
+        }
+        for (int j = 0; j < ORC_QK_K / 16; ++j) {
+            int sum = 0;
+            for (int l = 0; l < 16; ++l) sum += y[i].qs[j * 16 + l];
+            y[i].bsums[j] = (int16_t)sum;
+        }
+        y[i].d = 1.0f / iscale;
+    }
+}
+
+/* ---- quant/blocks.hpp:114-124 get_scale_min_k4: the 6-bit scale and min of
+ * sub-block j of a Q4_K block ------------------------------------------- */
+static void q4_k_scale_min(int j, const uint8_t* q, int* sc, int* m) {
+    if (j < 4) {
+        *sc = q[j] & 63;
+        *m = q[j + 4] & 63;
+    } else {
+        *sc = (q[j + 4] & 0x0f) | ((q[j - 4] >> 6) << 4);
+        *m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+    }
+}
+
 size_t orc_row_bytes(int type, size_t cols) {
     switch (type) {
     case ORC_F32: return cols * 4;
     case ORC_F16: return cols * 2;
     case ORC_Q4_0: return cols / ORC_QK * sizeof(orc_block_q4_0);
     case ORC_Q8_0: return cols / ORC_QK * sizeof(orc_block_q8_0);
+    case ORC_Q4_K: return cols / ORC_QK_K * sizeof(orc_block_q4_k);
+    case ORC_Q6_K: return cols / ORC_QK_K * sizeof(orc_block_q6_k);
     default: return 0;
     }
 }
@@ -171,6 +220,47 @@ void orc_dequantize_row(int type, const void* row, size_t n, float* y) {
         for (size_t i = 0; i < n / ORC_QK; ++i) {
             const float d = orc_fp16_to_float(b[i].d);
             for (int j = 0; j < 32; ++j) y[i * 32 + j] = (float)b[i].qs[j] * d;
+        }
+    }
+    if (type == ORC_Q4_K) { /* quant/blocks.hpp:127-149 */
+        for (size_t i = 0; i < n / ORC_QK_K; ++i) {
+            orc_block_q4_k b;
+            memcpy(&b, (const uint8_t*)row + i * sizeof b, sizeof b);
+            const float d = orc_fp16_to_float(b.d), dmin = orc_fp16_to_float(b.dmin);
+            float* o = y + i * ORC_QK_K;
+            for (int k = 0; k < 4; ++k) { /* 32 bytes of qs: sub-block 2k low nibbles, 2k+1 high */
+                int sc, m;
+                q4_k_scale_min(2 * k, b.scales, &sc, &m);
+                const float d1 = d * (float)sc, m1 = dmin * (float)m;
+                q4_k_scale_min(2 * k + 1, b.scales, &sc, &m);
+                const float d2 = d * (float)sc, m2 = dmin * (float)m;
+                for (int l = 0; l < 32; ++l) o[64 * k + l] = d1 * (float)(b.qs[32 * k + l] & 0x0f) - m1;
+                for (int l = 0; l < 32; ++l) o[64 * k + 32 + l] = d2 * (float)(b.qs[32 * k + l] >> 4) - m2;
+            }
+        }
+    }
+    if (type == ORC_Q6_K) { /* quant/blocks.hpp:152-174 */
+        for (size_t i = 0; i < n / ORC_QK_K; ++i) {
+            orc_block_q6_k b;
+            memcpy(&b, (const uint8_t*)row + i * sizeof b, sizeof b);
+            const float d = orc_fp16_to_float(b.d);
+            for (int h = 0; h < 2; ++h) { /* halves of 128 */
+                const uint8_t* ql = b.ql + 64 * h;
+                const uint8_t* qh = b.qh + 32 * h;
+                const int8_t* sc = b.scales + 8 * h;
+                float* o = y + i * ORC_QK_K + 128 * h;
+                for (int l = 0; l < 32; ++l) {
+                    const int is = l / 16;
+                    const int q1 = ((ql[l] & 0x0f) | (((qh[l] >> 0) & 3) << 4)) - 32;
+                    const int q2 = ((ql[l + 32] & 0x0f) | (((qh[l] >> 2) & 3) << 4)) - 32;
+                    const int q3 = ((ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4)) - 32;
+                    const int q4 = ((ql[l + 32] >> 4) | (((qh[l] >> 6) & 3) << 4)) - 32;
+                    o[l] = d * (float)sc[is + 0] * (float)q1;
+                    o[l + 32] = d * (float)sc[is + 2] * (float)q2;
+                    o[l + 64] = d * (float)sc[is + 4] * (float)q3;
+                    o[l + 96] = d * (float)sc[is + 6] * (float)q4;
+                }
+            }
         }
     }
 }
@@ -245,6 +335,77 @@ static float row_dot_plain(int type, const uint8_t* row, const float* x, size_t 
     return y;
 }
 
+/* ---- K formats on Q8_K activations (dot.hpp:166-239 unpack, :359-399
+ * dot_tile, :268-322 block_scaled_dots) --------------------------------------
+ * Chunks of chunk_elements = 1024 weights are 4 super-blocks. Block b's
+ * weight operand is sc_j * q (Q4_K) or sc_j * (q - 32) (Q6_K) per 32- or
+ * 16-element sub-block j, so its dot with the Q8_K quants is one exact
+ * integer; the chunk's float accumulator takes fma(float(isum_b), d_w * d_a,
+ * acc) in block order. Q4_K also subtracts its min term: per block the exact
+ * integer sum_j m_{j/2} * bsums_j (16 sub-block sums) accumulated as
+ * fma(float(msum_b), dmin_w * d_a, acc_m); the chunk adds acc - acc_m to the
+ * row result (:396 sums -= mins, then :398). One lane, as for Q4_0. */
+#define ORC_CHUNK_SUPER 4
+
+static int32_t q4_k_block_dot(const orc_block_q4_k* b, const orc_block_q8_k* a, int32_t* msum) {
+    int sc[8], m[8];
+    for (int j = 0; j < 8; ++j) q4_k_scale_min(j, b->scales, &sc[j], &m[j]);
+    int32_t s = 0;
+    for (int k = 0; k < 4; ++k)
+        for (int l = 0; l < 32; ++l) {
+            s += (int32_t)(sc[2 * k] * (b->qs[32 * k + l] & 0x0f)) * a->qs[64 * k + l];
+            s += (int32_t)(sc[2 * k + 1] * (b->qs[32 * k + l] >> 4)) * a->qs[64 * k + 32 + l];
+        }
+    int32_t ms = 0;
+    for (int j = 0; j < 16; ++j) ms += m[j / 2] * a->bsums[j];
+    *msum = ms;
+    return s;
+}
+
+static int32_t q6_k_block_dot(const orc_block_q6_k* b, const orc_block_q8_k* a) {
+    int32_t s = 0;
+    for (int h = 0; h < 2; ++h) {
+        const uint8_t* ql = b->ql + 64 * h;
+        const uint8_t* qh = b->qh + 32 * h;
+        const int8_t* sc = b->scales + 8 * h;
+        const int8_t* x = a->qs + 128 * h;
+        for (int l = 0; l < 32; ++l) {
+            const int is = l / 16;
+            const int q1 = ((ql[l] & 0x0f) | (((qh[l] >> 0) & 3) << 4)) - 32;
+            const int q2 = ((ql[l + 32] & 0x0f) | (((qh[l] >> 2) & 3) << 4)) - 32;
+            const int q3 = ((ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4)) - 32;
+            const int q4 = ((ql[l + 32] >> 4) | (((qh[l] >> 6) & 3) << 4)) - 32;
+            s += sc[is + 0] * q1 * x[l] + sc[is + 2] * q2 * x[l + 32] + sc[is + 4] * q3 * x[l + 64] +
+                 sc[is + 6] * q4 * x[l + 96];
+        }
+    }
+    return s;
+}
+
+static float row_dot_k(int type, const uint8_t* row, const orc_block_q8_k* act, size_t nb) {
+    float y = 0.0f;
+    for (size_t b0 = 0; b0 < nb; b0 += ORC_CHUNK_SUPER) {
+        const size_t end = b0 + ORC_CHUNK_SUPER < nb ? b0 + ORC_CHUNK_SUPER : nb;
+        float acc = 0.0f, accm = 0.0f;
+        for (size_t b = b0; b < end; ++b) {
+            if (type == ORC_Q4_K) {
+                orc_block_q4_k w;
+                memcpy(&w, row + b * sizeof w, sizeof w);
+                int32_t ms;
+                const int32_t s = q4_k_block_dot(&w, &act[b], &ms);
+                acc = fmaf((float)s, orc_fp16_to_float(w.d) * act[b].d, acc);
+                accm = fmaf((float)ms, orc_fp16_to_float(w.dmin) * act[b].d, accm);
+            } else {
+                orc_block_q6_k w;
+                memcpy(&w, row + b * sizeof w, sizeof w);
+                acc = fmaf((float)q6_k_block_dot(&w, &act[b]), orc_fp16_to_float(w.d) * act[b].d, acc);
+            }
+        }
+        y += type == ORC_Q4_K ? acc - accm : acc;
+    }
+    return y;
+}
+
 typedef struct {
     int type;
     const uint8_t* W;
@@ -254,6 +415,17 @@ typedef struct {
     const float* x;
     float* y;
 } orc_gemv_ctx;
+
+static void gemv_k_row(size_t r, void* p) {
+    orc_gemv_ctx* c = (orc_gemv_ctx*)p;
+    c->y[r] = row_dot_k(c->type, c->W + r * c->rb, (const orc_block_q8_k*)c->act, c->nb);
+}
+
+void orc_gemv_q8k(int type, const void* w, size_t rows, size_t cols, const orc_block_q8_k* act, float* y) {
+    orc_gemv_ctx c = {type, (const uint8_t*)w, orc_row_bytes(type, cols), cols / ORC_QK_K, cols,
+                      (const orc_block_q8_0*)(const void*)act, NULL, NULL, y};
+    orc_parallel_for(rows, 64, gemv_k_row, &c);
+}
 
 static void gemv_q_row(size_t r, void* p) {
     orc_gemv_ctx* c = (orc_gemv_ctx*)p;
@@ -278,6 +450,13 @@ void orc_gemv(int type, const void* w, size_t rows, size_t cols, const float* x,
     if (type == ORC_F32 || type == ORC_F16) {
         orc_gemv_ctx c = {type, (const uint8_t*)w, orc_row_bytes(type, cols), 0, cols, NULL, NULL, x, y};
         orc_parallel_for(rows, 64, gemv_plain_row, &c);
+        return;
+    }
+    if (type == ORC_Q4_K || type == ORC_Q6_K) { /* gemv.hpp:149-161 with Q8_K activations */
+        orc_block_q8_k* ak = (orc_block_q8_k*)malloc(cols / ORC_QK_K * sizeof(orc_block_q8_k));
+        orc_quantize_row_q8_k(x, cols, ak);
+        orc_gemv_q8k(type, w, rows, cols, ak, y);
+        free(ak);
         return;
     }
     orc_block_q8_0* act = (orc_block_q8_0*)malloc(cols / ORC_QK * sizeof(orc_block_q8_0));

@@ -15,7 +15,8 @@
  * tests/golden/make_golden.py from the reference's tests/data GGUF files):
  *   - kernel_golden.gguf: Q4_0/Q8_0 activations bit-identical, gemv y within
  *     1e-5 of ggml's vec_dot;
- *   - quant_golden.gguf: Q4_0/Q8_0/F16 dequantizers bit-identical;
+ *   - kernel_golden.gguf: Q4_K/Q6_K on Q8_K activations, the same checks;
+ *   - quant_golden.gguf: Q4_0/Q8_0/F16/Q4_K/Q6_K dequantizers bit-identical;
  *   - llama_tiny_f32(_golden).gguf: 16 decode steps of logits within 1e-4
  *     relative max of llama.cpp (RoPE with frequency factors, GQA, F16 KV
  *     cache, softmax, RMSNorm, residuals, tied F32 head);
@@ -34,12 +35,17 @@ extern "C" {
 
 /* GGUF tensor type tags (ggml_type values), as in the reference's
  * gguf/tensor_type.hpp:25-46. */
-enum { ORC_F32 = 0, ORC_F16 = 1, ORC_Q4_0 = 2, ORC_Q8_0 = 8 };
+enum { ORC_F32 = 0, ORC_F16 = 1, ORC_Q4_0 = 2, ORC_Q8_0 = 8, ORC_Q4_K = 12, ORC_Q6_K = 14 };
 
 #define ORC_QK 32
+#define ORC_QK_K 256
 
 typedef struct { uint16_t d; uint8_t qs[16]; } orc_block_q4_0;   /* 18 B */
 typedef struct { uint16_t d; int8_t qs[32]; } orc_block_q8_0;    /* 34 B */
+/* quant/blocks.hpp:56-70 and quant/q8.hpp:33-38 */
+typedef struct { uint16_t d, dmin; uint8_t scales[12]; uint8_t qs[128]; } orc_block_q4_k;           /* 144 B */
+typedef struct { uint8_t ql[128]; uint8_t qh[64]; int8_t scales[16]; uint16_t d; } orc_block_q6_k;  /* 210 B */
+typedef struct { float d; int8_t qs[256]; int16_t bsums[16]; } orc_block_q8_k;                     /* 292 B */
 
 /* numeric/half.hpp */
 float orc_fp16_to_float(uint16_t h);
@@ -48,6 +54,7 @@ uint16_t orc_float_to_fp16(float f);
 /* quant/q8.hpp, quant/blocks.hpp */
 void orc_quantize_row_q8_0(const float* x, size_t n, orc_block_q8_0* y);
 void orc_quantize_row_q4_0(const float* x, size_t n, orc_block_q4_0* y);
+void orc_quantize_row_q8_k(const float* x, size_t n, orc_block_q8_k* y);
 void orc_dequantize_row(int type, const void* row, size_t n, float* y);
 size_t orc_row_bytes(int type, size_t cols);
 
@@ -56,6 +63,8 @@ size_t orc_row_bytes(int type, size_t cols);
 void orc_gemv(int type, const void* w, size_t rows, size_t cols, const float* x, float* y);
 /* The same product on already-quantized activations (cols/32 blocks). */
 void orc_gemv_q8act(int type, const void* w, size_t rows, size_t cols, const orc_block_q8_0* act, float* y);
+/* Q4_K / Q6_K rows on Q8_K activations (cols/256 blocks). */
+void orc_gemv_q8k(int type, const void* w, size_t rows, size_t cols, const orc_block_q8_k* act, float* y);
 /* kernels/gemm.hpp: Y[n x rows] = X[n x cols] W^T, each row as orc_gemv (G1). */
 void orc_gemm(int type, const void* w, size_t rows, size_t cols, const float* x, size_t n, float* y);
 

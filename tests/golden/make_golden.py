@@ -9,9 +9,10 @@ by the reference's scripts/gen_*_fixture.py from ggml / llama.cpp @ e6f2ec01f):
 
 - kernel_golden.gguf : x (1024 f32, N(0,1)), <fmt>.w (8 x 1024 weights),
   <fmt>.act (ggml's Q8_0 activation blocks), <fmt>.y (ggml's vec_dot);
-  used by tests/sdk/kernels_golden.cpp:81-156.  Q4_0 and Q8_0 entries only.
+  used by tests/sdk/kernels_golden.cpp:81-156.  Q4_0, Q8_0 (Q8_0 activations)
+  and Q4_K, Q6_K (Q8_K activations) entries.
 - quant_golden.gguf  : <fmt>.q blocks and gguf-py's dequantized .expected;
-  used by tests/sdk/quant_golden.cpp:66-87.  F16, Q4_0, Q8_0 entries.
+  used by tests/sdk/quant_golden.cpp:66-87.  F16, Q4_0, Q8_0, Q4_K, Q6_K entries.
 - llama_tiny_f32.gguf + llama_tiny_f32_golden.gguf : a 2-layer all-F32 Llama
   (d 64, ff 128, 4 heads / 2 KV, hd 16, vocab 128, rope_freqs) and
   llama.cpp's logits after each of 16 tokens; tests/sdk/llama_golden.cpp:70-83.
@@ -41,7 +42,7 @@ def main(ref_root):
     r = gguf.GGUFReader(os.path.join(data, "kernel_golden.gguf"))
     t = tensors(r)
     kg = {"x": np.asarray(t["x"].data, dtype=np.float32).reshape(-1).copy()}
-    for fmt in ("q4_0", "q8_0"):
+    for fmt in ("q4_0", "q8_0", "q4_K", "q6_K"):
         w = t[fmt + ".w"]
         kg[fmt + "_w"] = raw(w)
         kg[fmt + "_shape"] = np.array([int(w.shape[1]), int(w.shape[0])], dtype=np.int64)  # rows, cols
@@ -53,7 +54,7 @@ def main(ref_root):
     r = gguf.GGUFReader(os.path.join(data, "quant_golden.gguf"))
     t = tensors(r)
     qg = {}
-    for fmt in ("f16", "q4_0", "q8_0"):
+    for fmt in ("f16", "q4_0", "q8_0", "q4_k", "q6_k"):
         q = t[fmt + ".q"]
         qg[fmt + "_q"] = raw(q)
         qg[fmt + "_shape"] = np.array([int(q.shape[1]), int(q.shape[0])], dtype=np.int64)

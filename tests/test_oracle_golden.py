@@ -40,7 +40,59 @@ def test_kernel_golden(fmt, ty):
     assert np.all(np.abs(y - ref) <= bound + slack)
 
 
-@pytest.mark.parametrize("fmt,ty", [("f16", orc.F16), ("q4_0", orc.Q4_0), ("q8_0", orc.Q8_0)])
+def q8_k_values(act, cols):
+    """ggml block_q8_k bytes -> the float values they stand for (q * d)."""
+    b = np.ascontiguousarray(act, np.uint8).reshape(-1, orc.Q8_K_BYTES)
+    d = b[:, 0:4].copy().view(np.float32)
+    qs = b[:, 4:260].copy().view(np.int8).astype(np.float32)
+    return (qs * d).reshape(-1)[:cols]
+
+
+@pytest.mark.parametrize("fmt,ty", [("q4_K", orc.Q4_K), ("q6_K", orc.Q6_K)])
+def test_kernel_golden_k_quants(fmt, ty):
+    # kernels_golden.cpp:81-156 for the K formats: Q8_K activations
+    g = load("kernel_golden.npz")
+    x = g["x"]
+    rows, cols = (int(v) for v in g[fmt + "_shape"])
+    act = orc.quantize_q8_k(x)
+    assert np.array_equal(act, g[fmt + "_act"])  # bit-identical, bsums included (:103)
+    y = orc.gemv(ty, g[fmt + "_w"], rows, cols, x)
+    assert np.array_equal(y.view(np.uint32), orc.gemv_q8k(ty, g[fmt + "_w"], rows, cols, act).view(np.uint32))
+    yg = g[fmt + "_y"]
+    assert np.all(np.abs(y - yg) <= 1e-5 * np.maximum(1.0, np.abs(yg)))  # (:114)
+    w = orc.dequantize(ty, g[fmt + "_w"], rows, cols).astype(np.float64)
+    xq = q8_k_values(act, cols).astype(np.float64)
+    ref = w @ x.astype(np.float64)
+    bound = np.abs(w) @ np.abs(x.astype(np.float64) - xq)
+    slack = 1e-6 * (np.abs(w) @ np.abs(xq)) + 1e-6
+    assert np.all(np.abs(y - ref) <= bound + slack)  # (:117-133)
+
+
+def test_q8_k_edge_cases():
+    # quant/q8.hpp:73-104: an all-zero block is all zero (bsums too); the
+    # element of largest magnitude maps to -127 (never -128, :88), and of two
+    # with equal magnitude the first one is that element
+    x = np.zeros(512, np.float32)
+    x[256 + 5], x[256 + 9] = -2.0, 2.0
+    x[256 + 7] = 0.5
+    b = orc.quantize_q8_k(x).reshape(2, orc.Q8_K_BYTES)
+    assert not b[0].any()
+    d = b[1, 0:4].copy().view(np.float32)[0]
+    qs = b[1, 4:260].copy().view(np.int8)
+    bsums = b[1, 260:292].copy().view(np.int16)
+    assert d == np.float32(1.0) / (np.float32(-127.0) / np.float32(-2.0))
+    assert qs[5] == -127 and qs[9] == 127 and qs[7] == 32  # iscale 63.5: 0.5 -> 31.75 -> 32
+    assert bsums[0] == -127 + 127 + 32 and not bsums[1:].any()
+    # iscale 1: halves round to even
+    y = np.zeros(256, np.float32)
+    y[0] = -127.0
+    y[1], y[2], y[3] = 2.5, 3.5, -2.5
+    q = orc.quantize_q8_k(y)[4:260].view(np.int8)
+    assert q[0] == -127 and q[1] == 2 and q[2] == 4 and q[3] == -2
+
+
+@pytest.mark.parametrize("fmt,ty", [("f16", orc.F16), ("q4_0", orc.Q4_0), ("q8_0", orc.Q8_0),
+                                    ("q4_k", orc.Q4_K), ("q6_k", orc.Q6_K)])
 def test_quant_golden_dequantize(fmt, ty):
     g = load("quant_golden.npz")
     rows, cols = (int(v) for v in g[fmt + "_shape"])
