@@ -40,7 +40,8 @@ typedef enum {
     SYN_ERR_RANGE = 8         /* token or position out of range: session::run returns false */
 } syn_status;
 
-enum { SYN_F32 = 0, SYN_F16 = 1, SYN_Q4_0 = 2, SYN_Q8_0 = 8 };
+/* GGUF tensor types (ggml_type values, gguf/tensor_type.hpp:25-46). */
+enum { SYN_F32 = 0, SYN_F16 = 1, SYN_Q4_0 = 2, SYN_Q8_0 = 8, SYN_Q4_K = 12, SYN_Q6_K = 14 };
 
 /* Weight layouts in device memory.
  *   SYN_LAYOUT_GGUF   : the GGUF bytes unchanged (rows of 18 B / 34 B blocks).
@@ -48,7 +49,12 @@ enum { SYN_F32 = 0, SYN_F16 = 1, SYN_Q4_0 = 2, SYN_Q8_0 = 8 };
  *                       a row's quants (blocks x 16 B for Q4_0, x 32 B for
  *                       Q8_0), then its binary16 scales, padded to 16 bytes.
  *                       A range of rows is one contiguous byte range.
- * Plain F32/F16 weights have one layout (row-major). */
+ *                       Q4_K: the GGUF rows unchanged (144 B blocks).
+ *                       Q6_K: a row's blocks as 208 B each (the GGUF block
+ *                       without its binary16 scale), then its scales,
+ *                       padded to 16 bytes.
+ * Plain F32/F16 weights have one layout (row-major). Q6_K weights must be
+ * planar for syn_gemv_q (GGUF Q6_K blocks are 210 B, not 16-byte aligned). */
 enum { SYN_LAYOUT_GGUF = 0, SYN_LAYOUT_PLANAR = 1 };
 
 /* Build-time identity: "sm_100a" and the library version. */
@@ -75,6 +81,16 @@ int syn_quantize_q8_0(const float* x, int n_tok, int cols, void* act, void* stre
 /* act -> ggml block_q8_0 bytes [n_tok][cols/32][34] (checking / interchange). */
 int syn_q8_act_to_blocks(const void* act, int n_tok, int cols, void* blocks, void* stream);
 
+/* Q8_K activations for the K formats (quant/q8.hpp:73-104 quantize_row_q8_k):
+ * planar int8 quants [n_tok][cols], float scales [n_tok][cols/256], int16
+ * sums of 16 quants [n_tok][cols/16], each plane 256-byte aligned; cols a
+ * multiple of 256. Bit-identical to the reference's block_q8_k
+ * (quant/q8.hpp:33-38), which syn_q8k_act_to_blocks writes
+ * ([n_tok][cols/256][292]). */
+size_t syn_q8k_act_bytes(int n_tok, int cols);
+int syn_quantize_q8_k(const float* x, int n_tok, int cols, void* act, void* stream);
+int syn_q8k_act_to_blocks(const void* act, int n_tok, int cols, void* blocks, void* stream);
+
 /* ------------------------------------------------------------------------
  * Weights: device bytes of a rows x cols matrix in a layout, and the
  * GGUF -> planar repack the loader runs once per tensor (gguf/tensor_view.hpp:
@@ -100,6 +116,10 @@ int syn_fill_random_planar(int type, int rows, int cols, void* dst, uint64_t see
  *   Q4_0 / Q8_0 weights take Q8_0 activations (syn_quantize_q8_0); each block
  *   is an exact integer dot scaled by d_w * d_a (kernels/dot.hpp:103-164,
  *   :268-322); rows may be in either layout.
+ *   Q4_K / Q6_K weights take Q8_K activations (syn_quantize_q8_k); each
+ *   256-weight block is an exact integer dot with its sub-block scales folded
+ *   in, less the Q4_K min term (kernels/dot.hpp:166-239, :359-399); Q6_K
+ *   rows must be planar.
  *   F32 / F16 weights take float activations (kernels/dot.hpp:404-433).
  * residual (may be NULL): Y[t][r] += residual[t][r] after the dot, the
  *   reference's following op_add (elementwise.hpp:29); it may alias y.

@@ -15,9 +15,10 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libsynapse_b200.so")
 
-F32, F16, Q4_0, Q8_0 = 0, 1, 2, 8
+F32, F16, Q4_0, Q8_0, Q4_K, Q6_K = 0, 1, 2, 8, 12, 14
 LAYOUT_GGUF, LAYOUT_PLANAR = 0, 1
 QK = 32
+QK_K = 256
 
 STATUS = {0: "ok", 1: "invalid argument", 2: "unsupported", 3: "cuda error", 4: "out of device memory",
           5: "timeout", 6: "nccl error", 7: "bad format", 8: "out of range"}
@@ -71,6 +72,9 @@ def _declare(L):
         "syn_q8_act_bytes": (sz, [i32, i32]),
         "syn_quantize_q8_0": (i32, [vp, i32, i32, vp, vp]),
         "syn_q8_act_to_blocks": (i32, [vp, i32, i32, vp, vp]),
+        "syn_q8k_act_bytes": (sz, [i32, i32]),
+        "syn_quantize_q8_k": (i32, [vp, i32, i32, vp, vp]),
+        "syn_q8k_act_to_blocks": (i32, [vp, i32, i32, vp, vp]),
         "syn_weight_bytes": (sz, [i32, i32, i32, i32]),
         "syn_repack_planar": (i32, [i32, vp, i32, i32, vp, vp]),
         "syn_upload_weight": (i32, [i32, vp, i32, i32, vp, i32, vp, sz, vp]),
@@ -182,6 +186,31 @@ def act_to_blocks(act, n_tok, cols, stream=None):
     torch = _torch()
     out = torch.empty(n_tok * (cols // QK) * 34, dtype=torch.uint8, device=act.device)
     check(lib().syn_q8_act_to_blocks(_ptr(act), n_tok, cols, _ptr(out), _stream(stream)), "syn_q8_act_to_blocks")
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Q8_K activations (the K formats' activation blocks)
+
+def q8k_act_bytes(n_tok, cols):
+    return lib().syn_q8k_act_bytes(n_tok, cols)
+
+
+def quantize_q8_k(x, act=None, stream=None):
+    """x: (n_tok, cols) f32 CUDA tensor, cols a multiple of 256 -> device Q8_K activation buffer (uint8)."""
+    x = x.contiguous()
+    n_tok, cols = (1, x.numel()) if x.dim() == 1 else x.shape
+    if act is None:
+        act = empty_bytes(q8k_act_bytes(n_tok, cols), x.device)
+    check(lib().syn_quantize_q8_k(_ptr(x), n_tok, cols, _ptr(act), _stream(stream)), "syn_quantize_q8_k")
+    return act
+
+
+def q8k_act_to_blocks(act, n_tok, cols, stream=None):
+    """Device Q8_K activations -> ggml block_q8_k bytes (292 per 256 values)."""
+    torch = _torch()
+    out = torch.empty(n_tok * (cols // QK_K) * 292, dtype=torch.uint8, device=act.device)
+    check(lib().syn_q8k_act_to_blocks(_ptr(act), n_tok, cols, _ptr(out), _stream(stream)), "syn_q8k_act_to_blocks")
     return out
 
 

@@ -903,6 +903,8 @@ int dispatch_f(const void* w, int rows, int cols, const float* x, int n, float* 
 
 extern "C" int syn_gemv_q(int type, const void* w, int layout, int rows, int cols, const void* act, int n_tok,
                           float* y, const float* residual, void* stream) {
+    if (syn_k_type(type))
+        return syn_gemv_k(type, w, layout, rows, cols, act, n_tok, y, residual, static_cast<cudaStream_t>(stream));
     if (type != SYN_Q4_0 && type != SYN_Q8_0) return SYN_ERR_UNSUPPORTED;
     if (layout != SYN_LAYOUT_GGUF && layout != SYN_LAYOUT_PLANAR) return SYN_ERR_INVALID;
     if (!w || !act || !y || rows <= 0 || cols <= 0 || cols % QK || n_tok <= 0) return SYN_ERR_INVALID;

@@ -1,0 +1,378 @@
+// Q4_K / Q6_K matrix-vector products on Q8_K activations: the K formats of
+// GGUF files such as Q4_K_M (quant/blocks.hpp:56-70, quant/q8.hpp:33-104,
+// kernels/dot.hpp:166-239 and :359-399).
+//
+// Numerics follow the reference's one-lane configuration, as the Q4_0 / Q8_0
+// path does: a super-block's dot with the activation quants is one exact
+// integer, sum_j sc_j * dot(q_j, a_j) (Q4_K) or sum_j sc_j * dot(q_j - 32,
+// a_j) (Q6_K); a chunk of four super-blocks (chunk_elements 1024,
+// dot.hpp:91) accumulates fma(float(isum), d_w * d_a, acc) in block order;
+// Q4_K subtracts a second accumulator over its mins, fma(float(msum),
+// dmin_w * d_a, acc_m) with msum = sum_j m_{j/2} * bsums_j; the chunk sums
+// are added to the row in order. Integer order is free (sums are exact), so
+// the kernel splits each super-block across eight lanes, one chunk per warp
+// instruction, and reduces the lanes' integers with shuffles before the
+// float chain, which every lane of the warp then runs identically.
+//
+// Device layouts.
+//   Q8_K activations, planar (16-byte loads): int8 quants [n_tok][cols], then
+//     the float scales [n_tok][cols/256], then the int16 sub-block sums
+//     [n_tok][cols/16], each plane 256-byte aligned. syn_q8k_act_to_blocks
+//     writes ggml's block_q8_k bytes from them.
+//   Q4_K weights: GGUF rows unchanged (144-byte blocks keep 16-byte alignment).
+//   Q6_K weights, planar: a row's blocks as 208 bytes each (ql 128, qh 64,
+//     scales 16: the GGUF block without its scale, so 16-byte aligned), then
+//     the row's binary16 scales, padded to 16 bytes.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace syn {
+namespace {
+
+constexpr int QKK = 256;         // weights per super-block (quant/blocks.hpp:33)
+constexpr int kChunkBlocks = 4;  // chunk_elements / 256 (kernels/dot.hpp:91)
+constexpr int kQ4KBytes = 144;
+constexpr int kQ6KBytes = 210;
+constexpr int kQ6KQuant = 208;
+constexpr int kMaxTok = 8;       // tokens per launch (weights read once for all of them)
+
+struct KAct {
+    int8_t* qs;      // [n_tok][cols]
+    float* d;        // [n_tok][cols / 256]
+    int16_t* bsums;  // [n_tok][cols / 16]
+};
+
+__host__ __device__ inline size_t kact_qs_bytes(int n_tok, int cols) { return align256(size_t(n_tok) * cols); }
+__host__ __device__ inline size_t kact_d_bytes(int n_tok, int cols) { return align256(size_t(n_tok) * (cols / QKK) * 4); }
+__host__ __device__ inline size_t kact_bs_bytes(int n_tok, int cols) { return align256(size_t(n_tok) * (cols / 16) * 2); }
+
+inline KAct kact_planes(void* act, int n_tok, int cols) {
+    char* p = static_cast<char*>(act);
+    KAct a;
+    a.qs = reinterpret_cast<int8_t*>(p);
+    p += kact_qs_bytes(n_tok, cols);
+    a.d = reinterpret_cast<float*>(p);
+    p += kact_d_bytes(n_tok, cols);
+    a.bsums = reinterpret_cast<int16_t*>(p);
+    return a;
+}
+
+__host__ __device__ inline size_t k_gguf_row_bytes(int type, int cols) {
+    return size_t(cols / QKK) * (type == SYN_Q4_K ? kQ4KBytes : kQ6KBytes);
+}
+__host__ __device__ inline size_t k_planar_row_bytes(int type, int cols) {
+    const size_t nb = size_t(cols / QKK);
+    if (type == SYN_Q4_K) return nb * kQ4KBytes;
+    return (nb * kQ6KQuant + nb * 2 + 15) & ~size_t(15);
+}
+
+// ---- Q8_K activations (quant/q8.hpp:73-104) ---------------------------------
+// One CTA per (token, super-block), one thread per value. The scale comes from
+// the first value of largest magnitude (ties: the lower index); quants are
+// nearest_int(iscale * x) capped at 127, through the 1.5 * 2^23 magic
+// (q8.hpp:44-48), with every rounding explicit.
+__global__ void __launch_bounds__(QKK) quantize_q8k_kernel(const float* __restrict__ x, int cols, KAct a) {
+    __shared__ float xs[QKK];
+    __shared__ float wkey[QKK / 32];
+    __shared__ int widx[QKK / 32];
+    const int nbk = cols / QKK;
+    const int t = blockIdx.x / nbk, b = blockIdx.x % nbk, i = threadIdx.x;
+    const size_t e = size_t(t) * cols + size_t(b) * QKK + i;
+    const float v = x[e];
+    xs[i] = v;
+    const float ax = fabsf(v);
+    float key = ax > 0.0f ? ax : 0.0f;  // a NaN never becomes the maximum (q8.hpp:83 ax > amax)
+    int idx = i;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const float ok = __shfl_xor_sync(0xffffffffu, key, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (ok > key || (ok == key && oi < idx)) {
+            key = ok;
+            idx = oi;
+        }
+    }
+    if ((i & 31) == 0) {
+        wkey[i >> 5] = key;
+        widx[i >> 5] = idx;
+    }
+    __syncthreads();
+    float amax = wkey[0];
+    int imax = widx[0];
+#pragma unroll
+    for (int w = 1; w < QKK / 32; ++w)
+        if (wkey[w] > amax) {  // warps in index order: equal keys keep the earlier warp
+            amax = wkey[w];
+            imax = widx[w];
+        }
+    int q = 0;
+    float iscale = 0.0f;
+    if (amax != 0.0f) {
+        iscale = __fdiv_rn(-127.0f, xs[imax]);
+        const float m = __fadd_rn(__fmul_rn(iscale, v), 12582912.0f);
+        q = min(127, (__float_as_int(m) & 0x007fffff) - 0x00400000);
+    }
+    a.qs[e] = static_cast<int8_t>(q);
+    int s = q;  // sums of 16 consecutive quants: half-warps
+#pragma unroll
+    for (int o = 8; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((i & 15) == 0) a.bsums[e / 16] = static_cast<int16_t>(s);
+    if (i == 0) a.d[size_t(t) * nbk + b] = amax != 0.0f ? __fdiv_rn(1.0f, iscale) : 0.0f;
+}
+
+// planes -> ggml block_q8_k bytes (d, qs[256], bsums[16]; 292 bytes)
+__global__ void q8k_to_blocks_kernel(KAct a, int cols, uint8_t* __restrict__ out) {
+    const int nbk = cols / QKK;
+    const int t = blockIdx.x / nbk, b = blockIdx.x % nbk, i = threadIdx.x;
+    uint8_t* o = out + size_t(blockIdx.x) * 292;
+    o[4 + i] = static_cast<uint8_t>(a.qs[size_t(t) * cols + size_t(b) * QKK + i]);
+    if (i < 16) {
+        const uint16_t s = static_cast<uint16_t>(a.bsums[(size_t(t) * cols + size_t(b) * QKK) / 16 + i]);
+        o[260 + 2 * i] = uint8_t(s & 0xff);
+        o[261 + 2 * i] = uint8_t(s >> 8);
+    }
+    if (i < 4) o[i] = uint8_t(__float_as_uint(a.d[size_t(t) * nbk + b]) >> (8 * i));
+}
+
+// GGUF Q6_K rows -> planar rows (layout above). One CTA per (row, block).
+__global__ void repack_q6k_kernel(const uint8_t* __restrict__ src, int nb, size_t pitch, uint8_t* __restrict__ dst) {
+    const size_t r = blockIdx.x / nb;
+    const int b = blockIdx.x % nb;
+    const uint8_t* s = src + (r * nb + b) * kQ6KBytes;
+    uint8_t* row = dst + r * pitch;
+    for (int i = threadIdx.x; i < kQ6KQuant; i += blockDim.x) row[size_t(b) * kQ6KQuant + i] = s[i];
+    if (threadIdx.x < 2) row[size_t(nb) * kQ6KQuant + 2 * b + threadIdx.x] = s[kQ6KQuant + threadIdx.x];
+    if (b == 0)  // the row's padding bytes, so the matrix is fully defined
+        for (size_t p = size_t(nb) * (kQ6KQuant + 2) + threadIdx.x; p < pitch; p += blockDim.x) row[p] = 0;
+}
+
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+    uint4 v;
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ int dot16(const uint4 w, const uint4 x) {
+    int s = __dp4a(int(w.x), int(x.x), 0);
+    s = __dp4a(int(w.y), int(x.y), s);
+    s = __dp4a(int(w.z), int(x.z), s);
+    return __dp4a(int(w.w), int(x.w), s);
+}
+
+__device__ __forceinline__ uint4 low_nibbles(uint4 v) {
+    return {v.x & 0x0f0f0f0fu, v.y & 0x0f0f0f0fu, v.z & 0x0f0f0f0fu, v.w & 0x0f0f0f0fu};
+}
+__device__ __forceinline__ uint4 high_nibbles(uint4 v) {
+    return {(v.x >> 4) & 0x0f0f0f0fu, (v.y >> 4) & 0x0f0f0f0fu, (v.z >> 4) & 0x0f0f0f0fu, (v.w >> 4) & 0x0f0f0f0fu};
+}
+
+// The 6-bit scale and min of sub-block j of a Q4_K block, from its 12 scale
+// bytes held as three little-endian words (quant/blocks.hpp:114-124).
+__device__ __forceinline__ void q4k_scale_min(int j, uint32_t s0, uint32_t s1, uint32_t s2, int& sc, int& m) {
+    const auto byte = [&](int k) -> int {
+        const uint32_t w = k < 4 ? s0 : (k < 8 ? s1 : s2);
+        return int((w >> (8 * (k & 3))) & 0xff);
+    };
+    if (j < 4) {
+        sc = byte(j) & 63;
+        m = byte(j + 4) & 63;
+    } else {
+        sc = (byte(j + 4) & 0x0f) | ((byte(j - 4) >> 6) << 4);
+        m = (byte(j + 4) >> 4) | ((byte(j) >> 6) << 4);
+    }
+}
+
+// One warp per row; lane = 8 * g + j takes part j of super-block 4c + g of
+// each chunk c. Q4_K part j: qs bytes 16j..16j+15, i.e. 16 weights of
+// sub-block 2k (low nibbles) and of 2k+1 (high), k = j/2, at element
+// 64k + 16(j%2) (+32); and the min term of sub-block j. Q6_K part j: half
+// h = j/4, quad pair p = (j/2)%2, positions ll = 16(j%2): ql bytes
+// 64h + 32p + ll (low nibbles: quad p, high: quad p + 2) and qh bytes
+// 32h + ll (bits 2p and 2p + 4).
+template <int TYPE>
+__global__ void __launch_bounds__(256) gemv_k_kernel(const uint8_t* __restrict__ w, size_t pitch, int rows, int cols,
+                                                     KAct a, int n_tok, float* __restrict__ y,
+                                                     const float* residual) {
+    const int lane = threadIdx.x & 31;
+    const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r >= rows) return;
+    const int g = lane >> 3, j = lane & 7;
+    const int nb = cols / QKK;
+    const uint8_t* row = w + size_t(r) * pitch;
+    float yacc[kMaxTok];
+#pragma unroll
+    for (int t = 0; t < kMaxTok; ++t) yacc[t] = 0.0f;
+
+    for (int c = 0; c * kChunkBlocks < nb; ++c) {
+        const int b = c * kChunkBlocks + g;
+        const bool valid = b < nb;
+        uint4 wlo = {0, 0, 0, 0}, whi = {0, 0, 0, 0};
+        int sc_lo = 0, sc_hi = 0, mj = 0;
+        float dw = 0.0f, dmin = 0.0f;
+        int e_lo = 0, e_hi = 0;  // element offsets of this lane's two 16-value runs
+        if (valid) {
+            if (TYPE == SYN_Q4_K) {
+                const uint8_t* blk = row + size_t(b) * kQ4KBytes;
+                const uint4 hdr = __ldg(reinterpret_cast<const uint4*>(blk));
+                const uint4 qs = ld_stream(blk + 16 + 16 * j);
+                const int k = j >> 1;
+                int m_unused;
+                q4k_scale_min(2 * k, hdr.y, hdr.z, hdr.w, sc_lo, m_unused);
+                q4k_scale_min(2 * k + 1, hdr.y, hdr.z, hdr.w, sc_hi, m_unused);
+                int sc_unused;
+                q4k_scale_min(j, hdr.y, hdr.z, hdr.w, sc_unused, mj);
+                dw = __half2float(__ushort_as_half(uint16_t(hdr.x & 0xffff)));
+                dmin = __half2float(__ushort_as_half(uint16_t(hdr.x >> 16)));
+                wlo = low_nibbles(qs);
+                whi = high_nibbles(qs);
+                e_lo = 64 * k + 16 * (j & 1);
+                e_hi = e_lo + 32;
+            } else {
+                const uint8_t* blk = row + size_t(b) * kQ6KQuant;
+                const int h = j >> 2, p = (j >> 1) & 1, ll = 16 * (j & 1);
+                const uint4 ql = ld_stream(blk + 64 * h + 32 * p + ll);
+                const uint4 qh = ld_stream(blk + 128 + 32 * h + ll);
+                const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192 + 8 * h);
+                sc_lo = __ldg(sc + (j & 1) + 2 * p);      // scales[is + 2p], is = ll / 16
+                sc_hi = __ldg(sc + (j & 1) + 2 * p + 4);  // scales[is + 2p + 4]
+                dw = __half2float(__ushort_as_half(
+                    __ldg(reinterpret_cast<const unsigned short*>(row + size_t(nb) * kQ6KQuant) + b)));
+                const uint32_t sh_lo = 2 * p, sh_hi = 2 * p + 4;
+                const uint32_t* l4 = &ql.x;
+                const uint32_t* h4 = &qh.x;
+                uint32_t lo[4], hi[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    lo[i] = __vsub4((l4[i] & 0x0f0f0f0fu) | (((h4[i] >> sh_lo) & 0x03030303u) << 4), 0x20202020u);
+                    hi[i] = __vsub4(((l4[i] >> 4) & 0x0f0f0f0fu) | (((h4[i] >> sh_hi) & 0x03030303u) << 4),
+                                    0x20202020u);
+                }
+                wlo = {lo[0], lo[1], lo[2], lo[3]};
+                whi = {hi[0], hi[1], hi[2], hi[3]};
+                e_lo = 128 * h + 32 * p + ll;
+                e_hi = e_lo + 64;
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < kMaxTok; ++t) {
+            if (t >= n_tok) break;
+            int s = 0, ms = 0;
+            float da = 0.0f;
+            if (valid) {
+                const int8_t* aq = a.qs + size_t(t) * cols + size_t(b) * QKK;
+                const uint4 xlo = __ldg(reinterpret_cast<const uint4*>(aq + e_lo));
+                const uint4 xhi = __ldg(reinterpret_cast<const uint4*>(aq + e_hi));
+                s = sc_lo * dot16(wlo, xlo) + sc_hi * dot16(whi, xhi);
+                if (TYPE == SYN_Q4_K) {
+                    const uint32_t bs = __ldg(reinterpret_cast<const uint32_t*>(
+                        a.bsums + (size_t(t) * cols + size_t(b) * QKK) / 16 + 2 * j));
+                    ms = mj * (int(int16_t(bs & 0xffff)) + int(int16_t(bs >> 16)));
+                }
+                da = __ldg(a.d + size_t(t) * nb + b);
+            }
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) {
+                s += __shfl_xor_sync(0xffffffffu, s, o);
+                if (TYPE == SYN_Q4_K) ms += __shfl_xor_sync(0xffffffffu, ms, o);
+            }
+            const float scl = __fmul_rn(dw, da);
+            const float sclm = __fmul_rn(dmin, da);
+            float acc = 0.0f, accm = 0.0f;
+#pragma unroll
+            for (int q = 0; q < kChunkBlocks; ++q) {
+                const int sq = __shfl_sync(0xffffffffu, s, 8 * q);
+                const float cq = __shfl_sync(0xffffffffu, scl, 8 * q);
+                if (TYPE == SYN_Q4_K) {
+                    const int mq = __shfl_sync(0xffffffffu, ms, 8 * q);
+                    const float cm = __shfl_sync(0xffffffffu, sclm, 8 * q);
+                    if (c * kChunkBlocks + q < nb) accm = fmaf(float(mq), cm, accm);
+                }
+                if (c * kChunkBlocks + q < nb) acc = fmaf(float(sq), cq, acc);
+            }
+            yacc[t] = __fadd_rn(yacc[t], TYPE == SYN_Q4_K ? __fsub_rn(acc, accm) : acc);
+        }
+    }
+    if (lane == 0) {
+#pragma unroll
+        for (int t = 0; t < kMaxTok; ++t) {
+            if (t >= n_tok) break;
+            const size_t o = size_t(t) * rows + r;
+            y[o] = residual ? __fadd_rn(yacc[t], residual[o]) : yacc[t];
+        }
+    }
+}
+
+}  // namespace
+}  // namespace syn
+
+using namespace syn;
+
+bool syn_k_type(int type) { return type == SYN_Q4_K || type == SYN_Q6_K; }
+
+size_t syn_k_weight_bytes(int type, int rows, int cols, int layout) {
+    if (!syn_k_type(type) || rows <= 0 || cols <= 0 || cols % QKK) return 0;
+    return size_t(rows) * (layout == SYN_LAYOUT_GGUF ? k_gguf_row_bytes(type, cols) : k_planar_row_bytes(type, cols));
+}
+
+int syn_k_repack_rows(int type, const void* src, int rows, int cols, void* dst, cudaStream_t s) {
+    if (type == SYN_Q4_K)
+        return syn_cuda_status(cudaMemcpyAsync(dst, src, size_t(rows) * k_gguf_row_bytes(type, cols),
+                                               cudaMemcpyDeviceToDevice, s));
+    const int nb = cols / QKK;
+    repack_q6k_kernel<<<unsigned(size_t(rows) * nb), 128, 0, s>>>(static_cast<const uint8_t*>(src), nb,
+                                                                   k_planar_row_bytes(type, cols),
+                                                                   static_cast<uint8_t*>(dst));
+    return syn_cuda_status(cudaGetLastError());
+}
+
+int syn_gemv_k(int type, const void* w, int layout, int rows, int cols, const void* act, int n_tok, float* y,
+               const float* residual, cudaStream_t s) {
+    if (!syn_k_type(type)) return SYN_ERR_UNSUPPORTED;
+    if (!w || !act || !y || rows <= 0 || cols <= 0 || cols % QKK || n_tok <= 0) return SYN_ERR_INVALID;
+    if (type == SYN_Q6_K && layout != SYN_LAYOUT_PLANAR) return SYN_ERR_UNSUPPORTED;  // 210-byte blocks: repack first
+    if (layout != SYN_LAYOUT_GGUF && layout != SYN_LAYOUT_PLANAR) return SYN_ERR_INVALID;
+    if ((reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(act) & 15)) return SYN_ERR_INVALID;
+    const KAct all = kact_planes(const_cast<void*>(act), n_tok, cols);
+    const size_t pitch = k_planar_row_bytes(type, cols);  // Q4_K: the GGUF pitch
+    const unsigned grid = unsigned((rows + 7) / 8);
+    const int nbk = cols / QKK;
+    for (int t0 = 0; t0 < n_tok; t0 += kMaxTok) {
+        const int n = std::min(kMaxTok, n_tok - t0);
+        KAct a{all.qs + size_t(t0) * cols, all.d + size_t(t0) * nbk, all.bsums + size_t(t0) * (cols / 16)};
+        const float* res = residual ? residual + size_t(t0) * rows : nullptr;
+        float* yo = y + size_t(t0) * rows;
+        const uint8_t* wp = static_cast<const uint8_t*>(w);
+        if (type == SYN_Q4_K)
+            gemv_k_kernel<SYN_Q4_K><<<grid, 256, 0, s>>>(wp, pitch, rows, cols, a, n, yo, res);
+        else
+            gemv_k_kernel<SYN_Q6_K><<<grid, 256, 0, s>>>(wp, pitch, rows, cols, a, n, yo, res);
+        const int st = syn_cuda_status(cudaGetLastError());
+        if (st) return st;
+    }
+    return SYN_OK;
+}
+
+extern "C" size_t syn_q8k_act_bytes(int n_tok, int cols) {
+    if (n_tok <= 0 || cols <= 0 || cols % QKK) return 0;
+    return kact_qs_bytes(n_tok, cols) + kact_d_bytes(n_tok, cols) + kact_bs_bytes(n_tok, cols);
+}
+
+extern "C" int syn_quantize_q8_k(const float* x, int n_tok, int cols, void* act, void* stream) {
+    if (!x || !act || n_tok <= 0 || cols <= 0 || cols % QKK) return SYN_ERR_INVALID;
+    if (reinterpret_cast<uintptr_t>(act) & 15) return SYN_ERR_INVALID;
+    const KAct a = kact_planes(act, n_tok, cols);
+    quantize_q8k_kernel<<<unsigned(size_t(n_tok) * (cols / QKK)), QKK, 0, static_cast<cudaStream_t>(stream)>>>(
+        x, cols, a);
+    return syn_cuda_status(cudaGetLastError());
+}
+
+extern "C" int syn_q8k_act_to_blocks(const void* act, int n_tok, int cols, void* blocks, void* stream) {
+    if (!act || !blocks || n_tok <= 0 || cols <= 0 || cols % QKK) return SYN_ERR_INVALID;
+    const KAct a = kact_planes(const_cast<void*>(act), n_tok, cols);
+    q8k_to_blocks_kernel<<<unsigned(size_t(n_tok) * (cols / QKK)), QKK, 0, static_cast<cudaStream_t>(stream)>>>(
+        a, cols, static_cast<uint8_t*>(blocks));
+    return syn_cuda_status(cudaGetLastError());
+}

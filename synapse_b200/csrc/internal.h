@@ -36,6 +36,15 @@ int syn_argmax_ws(const float* x, int n_tok, int n, int32_t* out, void* ws, cuda
 // blocks per row (the loader's chunk rotation).
 int syn_planar_block_pos(int nb, size_t r, int b);
 
+// Q4_K / Q6_K (gemv_k.cu): bytes of a matrix in a layout (0 if not a K type
+// or cols is not a multiple of 256), the GGUF -> planar repack of `rows`
+// rows into dst, and the matrix-vector product on Q8_K activations.
+bool syn_k_type(int type);
+size_t syn_k_weight_bytes(int type, int rows, int cols, int layout);
+int syn_k_repack_rows(int type, const void* src, int rows, int cols, void* dst, cudaStream_t s);
+int syn_gemv_k(int type, const void* w, int layout, int rows, int cols, const void* act, int n_tok, float* y,
+               const float* residual, cudaStream_t s);
+
 // Programmatic dependent launch for this thread's launches.
 void syn_set_pdl(int on);
 // The same, exported for microbenchmarks that time kernels captured the way

@@ -209,11 +209,17 @@ extern "C" size_t syn_weight_bytes(int type, int rows, int cols, int layout) {
         if (cols % QK) return 0;
         if (layout == SYN_LAYOUT_GGUF) return size_t(rows) * (cols / QK) * gguf_block_bytes(type);
         return size_t(rows) * planar_row_bytes(type, cols);
+    case SYN_Q4_K:
+    case SYN_Q6_K: return syn_k_weight_bytes(type, rows, cols, layout);
     default: return 0;
     }
 }
 
 extern "C" int syn_repack_planar(int type, const void* src, int rows, int cols, void* dst, void* stream) {
+    if (syn_k_type(type)) {
+        if (!src || !dst || rows <= 0 || cols <= 0 || cols % 256) return SYN_ERR_INVALID;
+        return syn_k_repack_rows(type, src, rows, cols, dst, static_cast<cudaStream_t>(stream));
+    }
     if (!quant_type(type)) return SYN_ERR_UNSUPPORTED;
     if (!src || !dst || rows <= 0 || cols <= 0 || cols % QK) return SYN_ERR_INVALID;
     return syn_repack_rows(type, src, rows, cols, dst, rows, 0, static_cast<cudaStream_t>(stream));
@@ -225,12 +231,28 @@ extern "C" int syn_upload_weight(int type, const void* host_src, int rows, int c
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const size_t total = syn_weight_bytes(type, rows, cols, SYN_LAYOUT_GGUF);
     if (total == 0) return SYN_ERR_UNSUPPORTED;
-    if (!quant_type(type) || layout == SYN_LAYOUT_GGUF) {
+    if ((!quant_type(type) && !syn_k_type(type)) || layout == SYN_LAYOUT_GGUF || type == SYN_Q4_K) {
         int st = syn_cuda_status(cudaMemcpyAsync(dst, host_src, total, cudaMemcpyHostToDevice, s));
         if (st) return st;
         return syn_cuda_status(cudaStreamSynchronize(s));
     }
     if (!staging || staging_bytes < (1u << 20)) return SYN_ERR_INVALID;
+    if (syn_k_type(type)) {  // Q6_K: rows through the staging buffer, repacked into place
+        const size_t row_g = total / size_t(rows), row_p = syn_k_weight_bytes(type, 1, cols, SYN_LAYOUT_PLANAR);
+        if (row_g > staging_bytes) return SYN_ERR_INVALID;
+        const int per = int(std::min<size_t>(size_t(rows), staging_bytes / row_g));
+        const uint8_t* h = static_cast<const uint8_t*>(host_src);
+        for (int r0 = 0; r0 < rows; r0 += per) {
+            const int n = rows - r0 < per ? rows - r0 : per;
+            int st = syn_cuda_status(cudaMemcpyAsync(staging, h + size_t(r0) * row_g, size_t(n) * row_g,
+                                                     cudaMemcpyHostToDevice, s));
+            if (st) return st;
+            if ((st = syn_k_repack_rows(type, staging, n, cols, static_cast<uint8_t*>(dst) + size_t(r0) * row_p, s)))
+                return st;
+            if ((st = syn_cuda_status(cudaStreamSynchronize(s)))) return st;
+        }
+        return SYN_OK;
+    }
     const size_t row_b = size_t(cols / QK) * gguf_block_bytes(type);
     const int per = int(std::max<size_t>(1, staging_bytes / row_b));
     if (row_b > staging_bytes) return SYN_ERR_INVALID;

@@ -2,11 +2,14 @@
 
   python -m synapse_b200.kernel_bench gemv [--type q4_0|q8_0] [--rows R --cols C] [--batch N] [--iters I]
   python -m synapse_b200.kernel_bench attention [--ctx L] [--batch B] [--iters I]
+  python -m synapse_b200.kernel_bench gemv_k [--type q4_k|q6_k] [--rows R --cols C] [--batch N]
 
 gemv: the quantized GEMV (syn_gemv_q, planar weights) at the sweep shapes
 (4096x4096, 14336x4096, 4096x14336, 128256x4096) and batches 1/4/16, weights
 N(0, 0.02) quantized on the device; enough weight copies rotate that their
 total exceeds twice the 126 MB L2, so every launch streams from HBM.
+gemv_k: the K-format GEMV (Q4_K / Q6_K on Q8_K activations) at the same
+shapes, weights of random bytes with finite binary16 super-block scales.
 attention: the fused RoPE + F16 append + split-KV attention (syn_attention)
 with H 32 / KV 8 / hd 128, theta 500000, caches of N(0,1) F16 at context L,
 batch 1/8/32.
@@ -21,9 +24,9 @@ import math
 
 import numpy as np
 
-from . import IN_F32, IN_Q8, IN_RMSNORM, LAYOUT_PLANAR, OUT_ROWS, OUT_SILU_PAIRS, Q4_0, Q8_0, GemvArgs, _ptr, \
-    _stream, attention, attention_scratch_bytes, check, empty_bytes, gemv_q, lib, q8_act_bytes, quantize_q8_0, \
-    rope_table, weight_bytes
+from . import IN_F32, IN_Q8, IN_RMSNORM, LAYOUT_PLANAR, OUT_ROWS, OUT_SILU_PAIRS, Q4_0, Q4_K, Q6_K, Q8_0, \
+    GemvArgs, _ptr, _stream, attention, attention_scratch_bytes, check, empty_bytes, gemv_q, lib, q8_act_bytes, \
+    quantize_q8_0, quantize_q8_k, rope_table, weight_bytes
 
 L2_BYTES = 126 << 20
 TYPES = {"q4_0": Q4_0, "q8_0": Q8_0}
@@ -111,6 +114,49 @@ def bench_gemv(type_name, rows, cols, batch, iters=50, mode="q8"):
             "GBps": round(alg / (ms * 1e-3) / 1e9, 1), "rotating_copies": copies}
 
 
+K_TYPES = {"q4_k": Q4_K, "q6_k": Q6_K}
+
+
+def _random_k_weights(ty, rows, cols, seed):
+    """Random bytes as planar K-format rows, every binary16 super-block scale set to 2^-10."""
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    wb = weight_bytes(ty, rows, cols, LAYOUT_PLANAR)
+    w = torch.randint(0, 256, (wb,), dtype=torch.uint8, device="cuda", generator=g)
+    nb = cols // 256
+    scale = torch.tensor([0x00, 0x14], dtype=torch.uint8, device="cuda")  # 0x1400 little-endian
+    if ty == Q4_K:
+        blk = w.view(rows * nb, 144)
+        blk[:, 0:2] = scale
+        blk[:, 2:4] = scale
+    else:
+        r = w.view(rows, wb // rows)
+        r[:, nb * 208:nb * 210] = scale.repeat(nb)
+    return w
+
+
+def bench_gemv_k(type_name, rows, cols, batch, iters=50):
+    import torch
+    ty = K_TYPES[type_name]
+    wb = weight_bytes(ty, rows, cols, LAYOUT_PLANAR)
+    copies = max(1, math.ceil(2 * L2_BYTES / wb) + 1)
+    ws = [_random_k_weights(ty, rows, cols, 1000 + i) for i in range(copies)]
+    x = torch.randn(batch, cols, device="cuda")
+    act = quantize_q8_k(x)
+    y = torch.empty(batch, rows, device="cuda")
+
+    def launch(i):
+        gemv_q(ty, ws[i % copies], LAYOUT_PLANAR, rows, cols, act, batch, y=y)
+    for i in range(3 * copies):
+        launch(i)
+    ms = _graph_time(launch, iters)
+    nb = cols // 256
+    alg = rows * nb * (144 if ty == Q4_K else 210) + batch * (cols + nb * 4 + cols // 16 * 2) + batch * rows * 4
+    return {"kernel": "gemv_k", "type": type_name, "rows": rows, "cols": cols, "batch": batch,
+            "us_per_launch": round(ms * 1e3, 3), "bytes_per_launch": alg, "GBps": round(alg / (ms * 1e-3) / 1e9, 1),
+            "rotating_copies": copies}
+
+
 def bench_attention(ctx, batch, iters=20, n_head=32, n_kv=8, hd=128):
     import torch
     row = n_kv * hd
@@ -142,7 +188,7 @@ def bench_attention(ctx, batch, iters=20, n_head=32, n_kv=8, hd=128):
 
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("what", choices=["gemv", "attention", "all"])
+    p.add_argument("what", choices=["gemv", "gemv_k", "attention", "all"])
     p.add_argument("--type", default=None)
     p.add_argument("--rows", type=int, default=None)
     p.add_argument("--cols", type=int, default=None)
@@ -167,6 +213,12 @@ def main():
             for r, c in shapes:
                 for n in ([a.batch] if a.batch else [1, 4, 16]):
                     print(json.dumps(bench_gemv(t, r, c, n, a.iters or 50, a.mode)), flush=True)
+    if a.what in ("gemv_k", "all"):
+        shapes = [(a.rows, a.cols)] if a.rows else [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)]
+        for t in ([a.type] if a.type else ["q4_k", "q6_k"]):
+            for r, c in shapes:
+                for n in ([a.batch] if a.batch else [1, 4, 16]):
+                    print(json.dumps(bench_gemv_k(t, r, c, n, a.iters or 50)), flush=True)
     if a.what in ("attention", "all"):
         for L in ([a.ctx] if a.ctx else [1024, 4096, 16384, 32768]):
             for b in ([a.batch] if a.batch else [1, 8, 32]):
