@@ -141,14 +141,15 @@ def quantize_q8_k(x):
     return out
 
 
-def random_k_blocks(type_, rows, cols, seed):
+def random_k_blocks(type_, rows, cols, seed, log2_scale=(-14, -8)):
     """Seeded random Q4_K / Q6_K rows: every byte pattern of the quants and
     sub-block scales is a valid block; the binary16 super-block scales are
-    drawn from [2^-14, 2^-8) so no value is inf or nan."""
+    drawn from [2^lo, 2^hi) of log2_scale so no value is inf or nan."""
     rng = np.random.default_rng(seed)
     nb = cols // QK_K
     out = rng.integers(0, 256, (rows, nb, BLOCK_BYTES[type_]), dtype=np.uint8)
-    scale = lambda n: (2.0 ** rng.uniform(-14, -8, n)).astype(np.float16).view(np.uint8).reshape(-1, 2)
+    lo, hi = log2_scale
+    scale = lambda n: (2.0 ** rng.uniform(lo, hi, n)).astype(np.float16).view(np.uint8).reshape(-1, 2)
     if type_ == Q4_K:
         out[:, :, 0:2] = scale(rows * nb).reshape(rows, nb, 2)  # d
         out[:, :, 2:4] = scale(rows * nb).reshape(rows, nb, 2)  # dmin

@@ -192,8 +192,43 @@ __device__ __forceinline__ void q4k_scale_min(int j, uint32_t s0, uint32_t s1, u
 // h = j/4, quad pair p = (j/2)%2, positions ll = 16(j%2): ql bytes
 // 64h + 32p + ll (low nibbles: quad p, high: quad p + 2) and qh bytes
 // 32h + ll (bits 2p and 2p + 4).
+// A lane's raw bytes of one super-block part, loaded a chunk ahead of use.
+struct RawPart {
+    uint4 a, b;      // Q4_K: header (d, dmin, scales), 16 quant bytes; Q6_K: 16 ql bytes, 16 qh bytes
+    int sc_lo, sc_hi;  // Q6_K sub-block scales
+    uint32_t dbits;    // Q6_K binary16 scale
+};
+
 template <int TYPE>
-__global__ void __launch_bounds__(256) gemv_k_kernel(const uint8_t* __restrict__ w, size_t pitch, int rows, int cols,
+__device__ __forceinline__ RawPart load_part(const uint8_t* row, int nb, int b, int j) {
+    RawPart p{};
+    if (TYPE == SYN_Q4_K) {
+        const uint8_t* blk = row + size_t(b) * kQ4KBytes;
+        p.a = __ldg(reinterpret_cast<const uint4*>(blk));
+        p.b = ld_stream(blk + 16 + 16 * j);
+    } else {
+        const uint8_t* blk = row + size_t(b) * kQ6KQuant;
+        const int h = j >> 2, q = (j >> 1) & 1, ll = 16 * (j & 1);
+        p.a = ld_stream(blk + 64 * h + 32 * q + ll);
+        p.b = ld_stream(blk + 128 + 32 * h + ll);
+        const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192 + 8 * h);
+        p.sc_lo = __ldg(sc + (j & 1) + 2 * q);      // scales[is + 2q], is = ll / 16
+        p.sc_hi = __ldg(sc + (j & 1) + 2 * q + 4);  // scales[is + 2q + 4]
+        p.dbits = __ldg(reinterpret_cast<const unsigned short*>(row + size_t(nb) * kQ6KQuant) + b);
+    }
+    return p;
+}
+
+// One warp per row; lane = 8 * g + j takes part j of super-block 4c + g of
+// each chunk c. Q4_K part j: qs bytes 16j..16j+15, i.e. 16 weights of
+// sub-block 2k (low nibbles) and of 2k+1 (high), k = j/2, at element
+// 64k + 16(j%2) (+32); and the min term of sub-block j. Q6_K part j: half
+// h = j/4, quad pair p = (j/2)%2, positions ll = 16(j%2): ql bytes
+// 64h + 32p + ll (low nibbles: quad p, high: quad p + 2) and qh bytes
+// 32h + ll (bits 2p and 2p + 4). The next chunk's bytes are requested
+// before this chunk is computed.
+template <int TYPE>
+__global__ void __launch_bounds__(256, 4) gemv_k_kernel(const uint8_t* __restrict__ w, size_t pitch, int rows, int cols,
                                                      KAct a, int n_tok, float* __restrict__ y,
                                                      const float* residual) {
     const int lane = threadIdx.x & 31;
@@ -206,18 +241,20 @@ __global__ void __launch_bounds__(256) gemv_k_kernel(const uint8_t* __restrict__
 #pragma unroll
     for (int t = 0; t < kMaxTok; ++t) yacc[t] = 0.0f;
 
+    RawPart nxt{};
+    if (g < nb) nxt = load_part<TYPE>(row, nb, g, j);
     for (int c = 0; c * kChunkBlocks < nb; ++c) {
         const int b = c * kChunkBlocks + g;
         const bool valid = b < nb;
+        const RawPart raw = nxt;
+        if (b + kChunkBlocks < nb) nxt = load_part<TYPE>(row, nb, b + kChunkBlocks, j);
         uint4 wlo = {0, 0, 0, 0}, whi = {0, 0, 0, 0};
         int sc_lo = 0, sc_hi = 0, mj = 0;
         float dw = 0.0f, dmin = 0.0f;
         int e_lo = 0, e_hi = 0;  // element offsets of this lane's two 16-value runs
         if (valid) {
             if (TYPE == SYN_Q4_K) {
-                const uint8_t* blk = row + size_t(b) * kQ4KBytes;
-                const uint4 hdr = __ldg(reinterpret_cast<const uint4*>(blk));
-                const uint4 qs = ld_stream(blk + 16 + 16 * j);
+                const uint4 hdr = raw.a;
                 const int k = j >> 1;
                 int m_unused;
                 q4k_scale_min(2 * k, hdr.y, hdr.z, hdr.w, sc_lo, m_unused);
@@ -226,23 +263,18 @@ __global__ void __launch_bounds__(256) gemv_k_kernel(const uint8_t* __restrict__
                 q4k_scale_min(j, hdr.y, hdr.z, hdr.w, sc_unused, mj);
                 dw = __half2float(__ushort_as_half(uint16_t(hdr.x & 0xffff)));
                 dmin = __half2float(__ushort_as_half(uint16_t(hdr.x >> 16)));
-                wlo = low_nibbles(qs);
-                whi = high_nibbles(qs);
+                wlo = low_nibbles(raw.b);
+                whi = high_nibbles(raw.b);
                 e_lo = 64 * k + 16 * (j & 1);
                 e_hi = e_lo + 32;
             } else {
-                const uint8_t* blk = row + size_t(b) * kQ6KQuant;
                 const int h = j >> 2, p = (j >> 1) & 1, ll = 16 * (j & 1);
-                const uint4 ql = ld_stream(blk + 64 * h + 32 * p + ll);
-                const uint4 qh = ld_stream(blk + 128 + 32 * h + ll);
-                const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192 + 8 * h);
-                sc_lo = __ldg(sc + (j & 1) + 2 * p);      // scales[is + 2p], is = ll / 16
-                sc_hi = __ldg(sc + (j & 1) + 2 * p + 4);  // scales[is + 2p + 4]
-                dw = __half2float(__ushort_as_half(
-                    __ldg(reinterpret_cast<const unsigned short*>(row + size_t(nb) * kQ6KQuant) + b)));
+                sc_lo = raw.sc_lo;
+                sc_hi = raw.sc_hi;
+                dw = __half2float(__ushort_as_half(uint16_t(raw.dbits)));
                 const uint32_t sh_lo = 2 * p, sh_hi = 2 * p + 4;
-                const uint32_t* l4 = &ql.x;
-                const uint32_t* h4 = &qh.x;
+                const uint32_t* l4 = &raw.a.x;
+                const uint32_t* h4 = &raw.b.x;
                 uint32_t lo[4], hi[4];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {

@@ -39,6 +39,7 @@ struct weight {
     int type = -1, layout = SYN_LAYOUT_PLANAR, rows = 0, cols = 0;
     size_t off = 0, bytes = 0;
     bool quant() const { return type == SYN_Q4_0 || type == SYN_Q8_0; }
+    bool kquant() const { return type == SYN_Q4_K || type == SYN_Q6_K; }  // on Q8_K activations
 };
 
 // A file tensor (rows first .. first + rows - 1 of it) inside a (possibly
@@ -60,7 +61,7 @@ struct layer_w {
     bool gu_pairs = false;  // gate/up rows interleaved (gate i at 2i, up i at 2i+1) for the silu-pair epilogue
 };
 
-enum class opk { embed, rms_norm, quantize, matmul, attention, silu_mul, argmax, allgather };
+enum class opk { embed, rms_norm, quantize, quantize_k, matmul, attention, silu_mul, argmax, allgather };
 
 struct op {
     opk kind;
@@ -151,9 +152,12 @@ int cuda(cudaError_t e) {
 }
 
 bool supported_type(int t) { return t == SYN_F32 || t == SYN_F16 || t == SYN_Q4_0 || t == SYN_Q8_0; }
+// matrices that only multiply (not the embedding table): the K formats too
+bool supported_matrix_type(int t) { return supported_type(t) || t == SYN_Q4_K || t == SYN_Q6_K; }
+bool planar_type(int t) { return t == SYN_Q4_0 || t == SYN_Q8_0 || t == SYN_Q4_K || t == SYN_Q6_K; }
 
 size_t weight_size(int type, int rows, int cols) {
-    return syn_weight_bytes(type, rows, cols, type == SYN_Q4_0 || type == SYN_Q8_0 ? SYN_LAYOUT_PLANAR : SYN_LAYOUT_GGUF);
+    return syn_weight_bytes(type, rows, cols, planar_type(type) ? SYN_LAYOUT_PLANAR : SYN_LAYOUT_GGUF);
 }
 
 // ---- arena layout -------------------------------------------------------------
@@ -171,7 +175,7 @@ void define(weight& w, int type, int rows, int cols, layout_builder& lb) {
     w.type = type;
     w.rows = rows;
     w.cols = cols;
-    w.layout = w.quant() ? SYN_LAYOUT_PLANAR : SYN_LAYOUT_GGUF;
+    w.layout = planar_type(type) ? SYN_LAYOUT_PLANAR : SYN_LAYOUT_GGUF;
     w.bytes = weight_size(type, rows, cols);
     w.off = lb.take(w.bytes);
 }
@@ -201,10 +205,14 @@ struct graph_builder {
 
 size_t act_bytes_for(int cols) { return syn_q8_act_bytes(1, cols); }
 
-// Activation input of a matmul: the Q8_0 form for quantized weights, else f32.
+size_t act_k_bytes_for(int cols) { return syn_q8k_act_bytes(1, cols); }
+
+// Activation input of a matmul: the Q8_0 form for Q4_0 / Q8_0 weights, the
+// Q8_K form for the K formats (made from the floats on first use), else f32.
 struct activation {
     int f32 = -1;  // tensor with float values
     int q8 = -1;   // tensor with Q8_0 activations
+    int qk = -1;   // tensor with Q8_K activations
 };
 
 bool fusable(const weight& w, int out_mode = SYN_OUT_ROWS) {
@@ -256,10 +264,17 @@ void build_step(syn_session& s) {
         g.add(o);
         return a;
     };
-    auto matmul = [&](const weight& w, const activation& a, int out, size_t out_off, int res, size_t res_off) {
+    auto matmul = [&](const weight& w, activation& a, int out, size_t out_off, int res, size_t res_off) {
+        if (w.kquant() && a.qk < 0) {  // quantize_row_q8_k of the floats, once per activation
+            op q{opk::quantize_k};
+            q.in = a.f32;
+            q.out = a.qk = g.new_tensor(act_k_bytes_for(w.cols));
+            q.cols = w.cols;
+            g.add(q);
+        }
         op o{opk::matmul};
         o.w = &w;
-        o.in = w.quant() ? a.q8 : a.f32;
+        o.in = w.quant() ? a.q8 : w.kquant() ? a.qk : a.f32;
         o.out = out;
         o.out_off = out_off;
         o.res = res;
@@ -485,6 +500,9 @@ int enqueue_ops(syn_session& s, cudaStream_t st) {
         case opk::quantize:
             rc = syn_quantize_q8_0(s.tf(o.in), 1, o.cols, s.tb(o.out), st);
             break;
+        case opk::quantize_k:
+            rc = syn_quantize_q8_k(s.tf(o.in), 1, o.cols, s.tb(o.out), st);
+            break;
         case opk::matmul: {
             float* y = s.tf(o.out, o.out_off);
             const float* res = o.res < 0 ? nullptr
@@ -508,7 +526,7 @@ int enqueue_ops(syn_session& s, cudaStream_t st) {
                 a.residual = res;
                 rc = s.p2p && (o.in_words || o.res_words || o.out_words) ? syn_gemv_tp(&a, tp_sync(s, o), st)
                                                                          : syn_gemv(&a, st);
-            } else if (o.w->quant())
+            } else if (o.w->quant() || o.w->kquant())
                 rc = syn_gemv_q(o.w->type, s.arena + o.w->off, o.w->layout, o.w->rows, o.w->cols, s.tb(o.in), 1, y,
                                 res, st);
             else
@@ -1055,7 +1073,7 @@ extern "C" int syn_session_open_gguf_tp(const char* path, int max_ctx, int devic
             const bool norm = i == 0 || i == 5;
             if (!(norm ? t->n_elements() == n_embd : shape_is(*t, layer_wants[i].rows, layer_wants[i].cols)))
                 return set_err(SYN_ERR_FORMAT, "bad shape " + name);
-            if (!supported_type(int(t->type)) || (norm && t->type != SYN_F32))
+            if (!supported_matrix_type(int(t->type)) || (norm && t->type != SYN_F32))
                 return set_err(SYN_ERR_UNSUPPORTED, "type of " + name);
             types[l][i] = int(t->type);
         }
@@ -1066,7 +1084,7 @@ extern "C" int syn_session_open_gguf_tp(const char* path, int max_ctx, int devic
     }
     const syn::gguf::tensor_info* on = f->tensor("output_norm.weight");
     if (!on || on->n_elements() != n_embd || on->type != SYN_F32) return set_err(SYN_ERR_FORMAT, "output_norm.weight");
-    if (tout && (!shape_is(*tout, uint64_t(c.n_vocab), n_embd) || !supported_type(int(tout->type))))
+    if (tout && (!shape_is(*tout, uint64_t(c.n_vocab), n_embd) || !supported_matrix_type(int(tout->type))))
         return set_err(SYN_ERR_UNSUPPORTED, "output.weight");
     if (f->tensor("output.bias")) return set_err(SYN_ERR_UNSUPPORTED, "output.bias");
     const syn::gguf::tensor_info* rf = f->tensor("rope_freqs.weight");
@@ -1096,7 +1114,19 @@ extern "C" int syn_session_open_gguf_tp(const char* path, int max_ctx, int devic
         const size_t row_bytes = t->nbytes / size_t(t->rows());
         const uint8_t* data = f->data(*t) + size_t(src.first) * row_bytes;  // this rank's rows of the tensor
         const int rows = src.rows;
-        if (!w.quant()) {
+        if (w.kquant()) {  // rows through the staging buffer, repacked in place (src.step is 1: never fused)
+            const size_t pitch = syn_weight_bytes(w.type, 1, w.cols, SYN_LAYOUT_PLANAR);
+            const int per = int(staging_bytes / row_bytes);
+            for (int r0 = 0; r0 < rows && !rc; r0 += per) {
+                const int n = rows - r0 < per ? rows - r0 : per;
+                rc = cuda(cudaMemcpyAsync(staging, data + size_t(r0) * row_bytes, size_t(n) * row_bytes,
+                                          cudaMemcpyHostToDevice, s->stream));
+                if (!rc)
+                    rc = syn_k_repack_rows(w.type, staging, n, w.cols,
+                                           s->arena + w.off + size_t(src.row0 + r0) * pitch, s->stream);
+                if (!rc) rc = cuda(cudaStreamSynchronize(s->stream));
+            }
+        } else if (!w.quant()) {
             rc = cuda(cudaMemcpyAsync(s->arena + w.off + size_t(src.row0) * w.cols * (w.type == SYN_F32 ? 4 : 2), data,
                                       size_t(rows) * row_bytes, cudaMemcpyHostToDevice, s->stream));
         } else {
@@ -1285,12 +1315,15 @@ double op_bytes(const syn_session& s, const op& o, uint32_t pos) {
     case opk::embed: return double(c.n_embd) * 4 * 2;
     case opk::rms_norm: return double(o.cols) * 4 * 3 + (o.out2 >= 0 ? double(o.cols) * 1.125 : 0);
     case opk::quantize: return double(o.cols) * (4 + 1.125);
+    case opk::quantize_k: return double(o.cols) * (4 + 1 + 4.0 / 256 + 2.0 / 16);
     case opk::matmul: {
         const weight& w = *o.w;
         const double nb = double(w.cols) / 32;
         double wb = w.quant() ? double(w.rows) * nb * (w.type == SYN_Q4_0 ? 18 : 34)
-                              : double(w.rows) * w.cols * (w.type == SYN_F32 ? 4 : 2);
-        double in = w.quant() ? double(w.cols) + nb * 8 : double(w.cols) * 4;
+                    : w.kquant() ? double(syn_weight_bytes(w.type, w.rows, w.cols, SYN_LAYOUT_GGUF))
+                                 : double(w.rows) * w.cols * (w.type == SYN_F32 ? 4 : 2);
+        double in = w.quant() ? double(w.cols) + nb * 8
+                    : w.kquant() ? double(w.cols) * (1 + 4.0 / 256 + 2.0 / 16) : double(w.cols) * 4;
         if (o.in_mode != SYN_IN_Q8) in = double(w.cols) * 4 * (o.in_mode == SYN_IN_RMSNORM ? 2 : 1);  // x (+ gamma)
         const double out = o.out_mode == SYN_OUT_SILU_PAIRS ? double(w.rows) / 2 : double(w.rows);
         return wb + in + out * 4 * (o.res >= 0 ? 2 : 1);
@@ -1310,7 +1343,8 @@ int op_kind_code(opk k) {
     switch (k) {
     case opk::embed: return SYN_OP_EMBED;
     case opk::rms_norm: return SYN_OP_RMS_NORM;
-    case opk::quantize: return SYN_OP_QUANTIZE;
+    case opk::quantize:
+    case opk::quantize_k: return SYN_OP_QUANTIZE;
     case opk::matmul: return SYN_OP_MATMUL;
     case opk::attention: return SYN_OP_ATTENTION;
     case opk::silu_mul: return SYN_OP_SILU_MUL;
@@ -1408,6 +1442,27 @@ extern "C" int syn_session_weight(syn_session* s, const char* name, void* host_o
         if (bytes < need) return SYN_ERR_INVALID;
         int rc = cuda(cudaSetDevice(s->device));
         if (rc) return rc;
+        if (w.kquant()) {  // planar rows -> GGUF blocks (Q6_K: each block's 208 quant bytes, then its scale)
+            const int nb = w.cols / 256, bb = w.type == SYN_Q4_K ? 144 : 210;
+            const size_t pitch = syn_weight_bytes(w.type, 1, w.cols, SYN_LAYOUT_PLANAR);
+            std::vector<uint8_t> rowbuf(pitch);
+            uint8_t* o = static_cast<uint8_t*>(host_out);
+            for (int rr = 0; rr < r; ++rr) {
+                const size_t dr = size_t(src.row0) + size_t(rr) * src.step;
+                rc = cuda(cudaMemcpy(rowbuf.data(), s->arena + w.off + dr * pitch, pitch, cudaMemcpyDeviceToHost));
+                if (rc) return rc;
+                uint8_t* orow = o + size_t(rr) * nb * bb;
+                if (w.type == SYN_Q4_K) {
+                    std::memcpy(orow, rowbuf.data(), size_t(nb) * bb);
+                    continue;
+                }
+                for (int b = 0; b < nb; ++b) {
+                    std::memcpy(orow + size_t(b) * bb, rowbuf.data() + size_t(b) * 208, 208);
+                    std::memcpy(orow + size_t(b) * bb + 208, rowbuf.data() + size_t(nb) * 208 + size_t(b) * 2, 2);
+                }
+            }
+            return SYN_OK;
+        }
         if (!w.quant()) {
             const size_t es = w.type == SYN_F32 ? 4 : 2;
             return cuda(cudaMemcpy(host_out, s->arena + w.off + size_t(src.row0) * w.cols * es, need,

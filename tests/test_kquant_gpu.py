@@ -132,3 +132,60 @@ def test_gemv_k_rejects_bad_args():
                         syn._stream()) == 1
     assert L.syn_q8k_act_bytes(1, 288) == 0
     assert L.syn_weight_bytes(syn.Q4_K, 8, 288, syn.LAYOUT_GGUF) == 0
+
+
+# ---------------------------------------------------------------- a K-format model end to end
+
+KM_CFG = dict(n_layer=2, n_embd=256, n_ff=512, n_head=4, n_head_kv=2, head_dim=64, n_vocab=512, rms_eps=1e-5,
+              rope_base=10000.0)
+KM_TYPES = {"attn_q": orc.Q4_K, "attn_k": orc.Q4_K, "attn_v": orc.Q6_K, "attn_output": orc.Q4_K,
+            "ffn_gate": orc.Q4_K, "ffn_up": orc.Q4_K, "ffn_down": orc.Q6_K}
+
+
+def q4_k_m_model(cfg, seed=21):
+    """A Q4_K_M-style mix (Q4_K matrices, Q6_K for V, down and the head) with one
+    Q8_0 matrix in the second layer, F32 embedding and norms."""
+    from synapse_b200 import model
+    rng = np.random.default_rng(seed)
+    shapes = model.llama_shapes(cfg)
+    w = {"token_embd": (model.F32, rng.standard_normal((cfg["n_vocab"], cfg["n_embd"]), dtype=np.float32) * 0.02)}
+    for l in range(cfg["n_layer"]):
+        for n in model.LAYER_NAMES:
+            rows, cols = shapes[n]
+            if n.endswith("norm"):
+                w[f"blk.{l}.{n}"] = (model.F32, np.ones(cols, np.float32))
+            elif l == 1 and n == "attn_k":
+                w[f"blk.{l}.{n}"] = (model.Q8_0, model.encode(rng.standard_normal((rows, cols), dtype=np.float32)
+                                                              * np.float32(0.02), model.Q8_0))
+            else:
+                w[f"blk.{l}.{n}"] = (KM_TYPES[n], orc.random_k_blocks(KM_TYPES[n], rows, cols, seed + l * 16 +
+                                                                      len(n), log2_scale=(-18, -14)))
+    w["output_norm"] = (model.F32, np.ones(cfg["n_embd"], np.float32))
+    w["output"] = (orc.Q6_K, orc.random_k_blocks(orc.Q6_K, cfg["n_vocab"], cfg["n_embd"], seed + 99,
+                                                 log2_scale=(-16, -12)))
+    return w
+
+
+def test_k_model_session_matches_oracle_bit_for_bit(tmp_path):
+    from synapse_b200 import model
+    cfg = KM_CFG
+    w = q4_k_m_model(cfg)
+    p = tmp_path / "q4_k_m.gguf"
+    model.write_llama_gguf(str(p), cfg, w, context_length=64)
+    sess = syn.Session.open(p, max_ctx=64)
+    ref = orc.Llama(cfg, w, max_ctx=64)
+    tok = 7
+    for pos in range(40):  # one attention chunk: every op in the reference's order, so logits are identical
+        got, nxt = sess.step(tok, pos)
+        want = ref.step(tok, pos)
+        assert np.all(np.isfinite(want)) and np.std(want) > 0
+        assert same_bits(got, want), (pos, float(np.max(np.abs(got - want))))
+        assert nxt == int(np.argmax(want))
+        tok = nxt
+    # the K matrices read back from the device as the file's GGUF bytes
+    for name in ("blk.0.attn_q.weight", "blk.0.attn_v.weight", "blk.1.ffn_down.weight", "output.weight"):
+        ty, rows, cols, data = sess.weight(name)
+        key = name[:-len(".weight")]
+        assert ty == w[key][0]
+        assert np.array_equal(data, np.ascontiguousarray(w[key][1]).reshape(-1))
+    sess.close()
