@@ -3,8 +3,9 @@
 //
 // load: GGUF metadata is read with the reference's rules (llama.hpp:206-319),
 //   every weight is bound with its shape checked (models/common.hpp:146-160),
-//   and uploaded into ONE device arena: Q4_0/Q8_0 matrices repacked to the
-//   planar layout, Q/K/V (and gate/up) of equal type concatenated by rows so
+//   and streamed into ONE device arena (pinned double buffers, host copies
+//   overlapping the transfers and repacks): Q4_0/Q8_0/K matrices repacked to
+//   the planar layout, Q/K/V (and gate/up) of equal type concatenated by rows so
 //   one GEMV launch streams them together. The f16 KV cache and the step's
 //   activations live in the same arena; activations are placed by the
 //   reference's static planner (planner.hpp) over the step's node order.
@@ -18,12 +19,14 @@
 //   device memory, so the same graph serves every position.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "../internal.h"
@@ -991,6 +994,99 @@ bool shape_is(const syn::gguf::tensor_info& t, uint64_t rows, uint64_t cols) {
 
 }  // namespace
 
+// ---- streaming upload -------------------------------------------------------
+// The file's bytes reach the arena through two pinned host buffers and two
+// device staging buffers of kStageBytes: while the GPU copies piece k in and
+// repacks it (planar rows, Q/K/V and gate/up placement), host threads copy
+// piece k + 1 out of the mapped file into the other pinned buffer. A piece is
+// up to kStageBytes of whole rows of one source; plain F32/F16 rows go from
+// the pinned buffer straight to their place in the arena.
+constexpr size_t kStageBytes = size_t(64) << 20;
+
+struct upload_piece {
+    const source* src;
+    const uint8_t* data;  // host (mapped file)
+    size_t bytes;
+    int r0, n;  // rows of the source
+};
+
+// dst[0, n) = src[0, n) on up to `threads` host threads (page faults of a
+// cold file are taken in parallel too).
+void parallel_copy(void* dst, const void* src, size_t n, unsigned threads) {
+    const size_t min_part = size_t(4) << 20;
+    unsigned t = unsigned(std::min<size_t>(threads, std::max<size_t>(1, n / min_part)));
+    if (t <= 1) {
+        std::memcpy(dst, src, n);
+        return;
+    }
+    const size_t part = (n + t - 1) / t;
+    std::vector<std::thread> pool;
+    pool.reserve(t - 1);
+    for (unsigned i = 1; i < t; ++i) {
+        const size_t b = std::min(n, size_t(i) * part), e = std::min(n, b + part);
+        pool.emplace_back([=] { std::memcpy(static_cast<char*>(dst) + b, static_cast<const char*>(src) + b, e - b); });
+    }
+    std::memcpy(dst, src, std::min(n, part));
+    for (auto& th : pool) th.join();
+}
+
+int upload_sources(syn_session& s, const syn::gguf::file& f) {
+    std::vector<upload_piece> pieces;
+    for (const auto& src : s.sources) {
+        const syn::gguf::tensor_info* t = f.tensor(src.name);
+        const size_t row_bytes = t->nbytes / size_t(t->rows());
+        if (row_bytes > kStageBytes) return set_err(SYN_ERR_UNSUPPORTED, "row wider than the staging buffer: " + src.name);
+        const uint8_t* data = f.data(*t) + size_t(src.first) * row_bytes;  // this rank's rows of the tensor
+        const int per = int(kStageBytes / row_bytes);
+        for (int r0 = 0; r0 < src.rows; r0 += per) {
+            const int n = std::min(per, src.rows - r0);
+            pieces.push_back({&src, data + size_t(r0) * row_bytes, size_t(n) * row_bytes, r0, n});
+        }
+    }
+    const unsigned threads = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+    void* host[2] = {nullptr, nullptr};
+    void* stage[2] = {nullptr, nullptr};
+    cudaEvent_t free_ev[2] = {nullptr, nullptr};
+    bool pending[2] = {false, false};
+    int rc = SYN_OK;
+    for (int b = 0; b < 2 && !rc; ++b) {
+        rc = cuda(cudaHostAlloc(&host[b], kStageBytes, cudaHostAllocDefault));
+        if (!rc) rc = cuda(cudaMalloc(&stage[b], kStageBytes));
+        if (!rc) rc = cuda(cudaEventCreateWithFlags(&free_ev[b], cudaEventDisableTiming));
+    }
+    for (size_t k = 0; k < pieces.size() && !rc; ++k) {
+        const int b = int(k & 1);
+        const upload_piece& pc = pieces[k];
+        const weight& w = *pc.src->w;
+        if (pending[b] && (rc = cuda(cudaEventSynchronize(free_ev[b])))) break;  // piece k - 2 has left buffer b
+        parallel_copy(host[b], pc.data, pc.bytes, threads);
+        const int row = pc.src->row0 + pc.r0 * pc.src->step;  // first destination row
+        if (w.kquant()) {  // src.step is 1: K matrices are never fused
+            const size_t pitch = syn_weight_bytes(w.type, 1, w.cols, SYN_LAYOUT_PLANAR);
+            rc = cuda(cudaMemcpyAsync(stage[b], host[b], pc.bytes, cudaMemcpyHostToDevice, s.stream));
+            if (!rc) rc = syn_k_repack_rows(w.type, stage[b], pc.n, w.cols, s.arena + w.off + size_t(row) * pitch,
+                                            s.stream);
+        } else if (!w.quant()) {
+            rc = cuda(cudaMemcpyAsync(s.arena + w.off + size_t(row) * w.cols * (w.type == SYN_F32 ? 4 : 2), host[b],
+                                      pc.bytes, cudaMemcpyHostToDevice, s.stream));
+        } else {
+            rc = cuda(cudaMemcpyAsync(stage[b], host[b], pc.bytes, cudaMemcpyHostToDevice, s.stream));
+            if (!rc) rc = syn_repack_rows(w.type, stage[b], pc.n, w.cols, s.arena + w.off, w.rows, row, s.stream,
+                                          pc.src->step);
+        }
+        if (!rc) rc = cuda(cudaEventRecord(free_ev[b], s.stream));
+        pending[b] = true;
+    }
+    const int sync_rc = cuda(cudaStreamSynchronize(s.stream));
+    if (!rc) rc = sync_rc;
+    for (int b = 0; b < 2; ++b) {
+        if (free_ev[b]) cudaEventDestroy(free_ev[b]);
+        if (stage[b]) cudaFree(stage[b]);
+        if (host[b]) cudaFreeHost(host[b]);
+    }
+    return rc;
+}
+
 extern "C" int syn_session_open_gguf(const char* path, int max_ctx, int device, syn_session** out) {
     return syn_session_open_gguf_tp(path, max_ctx, device, nullptr, out);
 }
@@ -1104,49 +1200,9 @@ extern "C" int syn_session_open_gguf_tp(const char* path, int max_ctx, int devic
     }
     if ((rc = finish(*s, lb))) return rc;
 
-    // upload: host -> staging (GGUF bytes) -> repack into the arena
-    const size_t staging_bytes = size_t(64) << 20;
-    void* staging = nullptr;
-    if ((rc = cuda(cudaMalloc(&staging, staging_bytes)))) return rc;
-    for (const auto& src : s->sources) {
-        const syn::gguf::tensor_info* t = f->tensor(src.name);
-        const weight& w = *src.w;
-        const size_t row_bytes = t->nbytes / size_t(t->rows());
-        const uint8_t* data = f->data(*t) + size_t(src.first) * row_bytes;  // this rank's rows of the tensor
-        const int rows = src.rows;
-        if (w.kquant()) {  // rows through the staging buffer, repacked in place (src.step is 1: never fused)
-            const size_t pitch = syn_weight_bytes(w.type, 1, w.cols, SYN_LAYOUT_PLANAR);
-            const int per = int(staging_bytes / row_bytes);
-            for (int r0 = 0; r0 < rows && !rc; r0 += per) {
-                const int n = rows - r0 < per ? rows - r0 : per;
-                rc = cuda(cudaMemcpyAsync(staging, data + size_t(r0) * row_bytes, size_t(n) * row_bytes,
-                                          cudaMemcpyHostToDevice, s->stream));
-                if (!rc)
-                    rc = syn_k_repack_rows(w.type, staging, n, w.cols,
-                                           s->arena + w.off + size_t(src.row0 + r0) * pitch, s->stream);
-                if (!rc) rc = cuda(cudaStreamSynchronize(s->stream));
-            }
-        } else if (!w.quant()) {
-            rc = cuda(cudaMemcpyAsync(s->arena + w.off + size_t(src.row0) * w.cols * (w.type == SYN_F32 ? 4 : 2), data,
-                                      size_t(rows) * row_bytes, cudaMemcpyHostToDevice, s->stream));
-        } else {
-            const int per = int(staging_bytes / row_bytes);
-            for (int r0 = 0; r0 < rows && !rc; r0 += per) {
-                const int n = rows - r0 < per ? rows - r0 : per;
-                rc = cuda(cudaMemcpyAsync(staging, data + size_t(r0) * row_bytes, size_t(n) * row_bytes,
-                                          cudaMemcpyHostToDevice, s->stream));
-                if (!rc)
-                    rc = syn_repack_rows(w.type, staging, n, w.cols, s->arena + w.off, w.rows,
-                                         src.row0 + r0 * src.step, s->stream, src.step);
-                if (!rc) rc = cuda(cudaStreamSynchronize(s->stream));
-            }
-        }
-        if (!rc) rc = cuda(cudaStreamSynchronize(s->stream));
-        if (rc) break;
-    }
+    rc = upload_sources(*s, *f);
     if (!rc && rf)
         rc = cuda(cudaMemcpy(s->arena + s->ff_off, f->data(*rf), size_t(hd / 2) * 4, cudaMemcpyHostToDevice));
-    cudaFree(staging);
     if (rc) return rc;
     if ((rc = warm_and_capture(*s))) return rc;
     *out = s.release();

@@ -3,6 +3,7 @@
   python -m synapse_b200.kernel_bench gemv [--type q4_0|q8_0] [--rows R --cols C] [--batch N] [--iters I]
   python -m synapse_b200.kernel_bench attention [--ctx L] [--batch B] [--iters I]
   python -m synapse_b200.kernel_bench gemv_k [--type q4_k|q6_k] [--rows R --cols C] [--batch N]
+  python -m synapse_b200.kernel_bench load [--path DIR]
 
 gemv: the quantized GEMV (syn_gemv_q, planar weights) at the sweep shapes
 (4096x4096, 14336x4096, 4096x14336, 128256x4096) and batches 1/4/16, weights
@@ -10,6 +11,10 @@ N(0, 0.02) quantized on the device; enough weight copies rotate that their
 total exceeds twice the 126 MB L2, so every launch streams from HBM.
 gemv_k: the K-format GEMV (Q4_K / Q6_K on Q8_K activations) at the same
 shapes, weights of random bytes with finite binary16 super-block scales.
+load: a Llama-3-8B-shaped Q4_0 GGUF (Q8_0 head; 5.0 GB of tensor bytes with
+valid block scales) written to DIR, then opened with syn_session_open_gguf
+twice (the file is in the page cache both times); GB/s = tensor bytes over
+the open time, beside the pinned host-to-device copy rate of this box.
 attention: the fused RoPE + F16 append + split-KV attention (syn_attention)
 with H 32 / KV 8 / hd 128, theta 500000, caches of N(0,1) F16 at context L,
 batch 1/8/32.
@@ -157,6 +162,74 @@ def bench_gemv_k(type_name, rows, cols, batch, iters=50):
             "rotating_copies": copies}
 
 
+def _patterned(n_bytes, block, seed):
+    """Random bytes laid out as `block`-byte GGUF blocks whose binary16 scale (the
+    first two bytes) is 2^-10."""
+    rng = np.random.default_rng(seed)
+    n_blocks = -(-n_bytes // block)
+    buf = rng.integers(0, 256, n_blocks * block, dtype=np.uint8)
+    buf.reshape(n_blocks, block)[:, 0:2] = np.array([0x00, 0x14], np.uint8)
+    return buf
+
+
+def bench_load(directory=None, opens=2):
+    """Load bandwidth of the session's GGUF loader on a synthetic 8B Q4_0 file."""
+    import os
+    import tempfile
+    import time
+
+    import torch
+
+    from . import Session
+    from . import model as m
+    cfg = dict(n_layer=32, n_embd=4096, n_ff=14336, n_head=32, n_head_kv=8, head_dim=128, n_vocab=128256,
+               rms_eps=1e-5, rope_base=500000.0)
+    shapes = m.llama_shapes(cfg)
+    q4 = _patterned(cfg["n_vocab"] * cfg["n_embd"] // 32 * 18, 18, 1)
+    q8 = _patterned(cfg["n_vocab"] * cfg["n_embd"] // 32 * 34, 34, 2)
+    w = {"token_embd": (Q4_0, q4.reshape(cfg["n_vocab"], -1)),
+         "output": (Q8_0, q8.reshape(cfg["n_vocab"], -1)),
+         "output_norm": (m.F32, np.ones(cfg["n_embd"], np.float32))}
+    total = q4.size + q8.size + cfg["n_embd"] * 4
+    for l in range(cfg["n_layer"]):
+        for n in m.LAYER_NAMES:
+            rows, cols = shapes[n]
+            if n.endswith("norm"):
+                w[f"blk.{l}.{n}"] = (m.F32, np.ones(cols, np.float32))
+                total += cols * 4
+            else:
+                nb = rows * cols // 32 * 18
+                w[f"blk.{l}.{n}"] = (Q4_0, q4[:nb].reshape(rows, -1))
+                total += nb
+    d = directory or tempfile.mkdtemp(prefix="synload")
+    path = os.path.join(d, "llama8b_q4_0.gguf")
+    m.write_llama_gguf(path, cfg, w, context_length=4096)
+    # the pinned host -> device rate of this box, for scale
+    h = torch.empty(256 << 20, dtype=torch.uint8).pin_memory()
+    dv = torch.empty_like(h, device="cuda")
+    dv.copy_(h, non_blocking=True)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    ev[0].record()
+    for _ in range(4):
+        dv.copy_(h, non_blocking=True)
+    ev[1].record()
+    ev[1].synchronize()
+    h2d = 4 * h.numel() / (ev[0].elapsed_time(ev[1]) * 1e-3) / 1e9
+    del h, dv
+    times = []
+    for _ in range(opens):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        sess = Session.open(path, max_ctx=4096)
+        times.append(time.perf_counter() - t0)
+        sess.close()
+    os.remove(path)
+    best = min(times)
+    return {"kernel": "load", "file": "llama-3-8B-shaped Q4_0 (Q8_0 head)", "tensor_bytes": total,
+            "open_s": [round(t, 3) for t in times], "GBps": round(total / best / 1e9, 2),
+            "pinned_h2d_GBps": round(h2d, 1), "host_threads": os.cpu_count()}
+
+
 def bench_attention(ctx, batch, iters=20, n_head=32, n_kv=8, hd=128):
     import torch
     row = n_kv * hd
@@ -188,7 +261,8 @@ def bench_attention(ctx, batch, iters=20, n_head=32, n_kv=8, hd=128):
 
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("what", choices=["gemv", "gemv_k", "attention", "all"])
+    p.add_argument("what", choices=["gemv", "gemv_k", "attention", "load", "all"])
+    p.add_argument("--path", default=None, help="load: directory for the synthetic GGUF file")
     p.add_argument("--type", default=None)
     p.add_argument("--rows", type=int, default=None)
     p.add_argument("--cols", type=int, default=None)
@@ -219,6 +293,8 @@ def main():
             for r, c in shapes:
                 for n in ([a.batch] if a.batch else [1, 4, 16]):
                     print(json.dumps(bench_gemv_k(t, r, c, n, a.iters or 50)), flush=True)
+    if a.what == "load":
+        print(json.dumps(bench_load(a.path)), flush=True)
     if a.what in ("attention", "all"):
         for L in ([a.ctx] if a.ctx else [1024, 4096, 16384, 32768]):
             for b in ([a.batch] if a.batch else [1, 8, 32]):
