@@ -24,6 +24,7 @@
 //     scales 16: the GGUF block without its scale, so 16-byte aligned), then
 //     the row's binary16 scales, padded to 16 bytes.
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 
@@ -337,6 +338,246 @@ __global__ void __launch_bounds__(256, 4) gemv_k_kernel(const uint8_t* __restric
     }
 }
 
+// ---- one lane per super-block ----------------------------------------------------
+// Each lane owns whole 256-weight super-blocks, so a block's exact integer dot
+// needs no cross-lane reduction; LPR lanes (a multiple of 4) cover LPR
+// consecutive blocks of one row per pass, 32 / LPR rows per warp. The
+// activation quants of every token of the launch are staged once per CTA in
+// shared memory, transposed to [token][16-byte piece][block] so that lanes
+// reading consecutive blocks hit consecutive banks; sub-block sums and scales
+// likewise. The fma chain of a chunk runs over its four lanes by three
+// shuffles (lane 4c + q adds block 4c + q), and the chunk sums of a row are
+// broadcast and added in order, so every value is computed exactly as the
+// reference's one-lane order computes it. A lane's 16-byte loads stride its
+// block, so each load uses half of every 32-byte sector it touches: they
+// allocate in L1, where the next load finds the other half.
+constexpr int kKbSmemBudget = 96 * 1024;  // two CTAs per SM
+constexpr int kKbBytesPerBlockTok = 256 + 32 + 4;
+
+// The eight 6-bit scales and mins of a Q4_K block from its 12 scale bytes,
+// as words s0 (bytes 0-3), s1 (4-7), s2 (8-11) (quant/blocks.hpp:114-124):
+// byte j of sc_lo / m_lo is scale / min j, byte j of sc_hi / m_hi is j + 4.
+__device__ __forceinline__ void q4k_scales_all(uint32_t s0, uint32_t s1, uint32_t s2, uint32_t& sc_lo,
+                                               uint32_t& sc_hi, uint32_t& m_lo, uint32_t& m_hi) {
+    sc_lo = s0 & 0x3f3f3f3fu;
+    m_lo = s1 & 0x3f3f3f3fu;
+    sc_hi = (s2 & 0x0f0f0f0fu) | ((s0 >> 2) & 0x30303030u);
+    m_hi = ((s2 >> 4) & 0x0f0f0f0fu) | ((s1 >> 2) & 0x30303030u);
+}
+
+__device__ __forceinline__ int byte_at(uint32_t w, int i) { return int((w >> (8 * i)) & 0xffu); }
+__device__ __forceinline__ int sbyte_at(uint32_t w, int i) { return int(int8_t((w >> (8 * i)) & 0xffu)); }
+
+template <int TYPE, int LPR>
+__global__ void __launch_bounds__(256, 2) gemv_kb_kernel(const uint8_t* __restrict__ w, size_t pitch, int rows,
+                                                         int cols, KAct a, int n_tok, float* __restrict__ y,
+                                                         const float* residual) {
+    extern __shared__ uint4 smem[];
+    const int nb = cols / QKK;
+    uint4* act_s = smem;                                                    // [(t * 16 + i) * nb + b]
+    uint4* bs_s = act_s + size_t(n_tok) * 16 * nb;                         // [(t * 2 + j) * nb + b]
+    float* d_s = reinterpret_cast<float*>(bs_s + size_t(n_tok) * 2 * nb);  // [t * nb + b]
+    {
+        const int nq = n_tok * nb * 16;
+        const uint4* src = reinterpret_cast<const uint4*>(a.qs);  // [n_tok][cols] = [(t * nb + b) * 16 + i]
+        for (int u = threadIdx.x; u < nq; u += blockDim.x) {
+            const int i = u & 15, tb = u >> 4, t = tb / nb, b = tb - t * nb;
+            act_s[(t * 16 + i) * nb + b] = __ldg(src + u);
+        }
+        const int ns = n_tok * nb * 2;
+        const uint4* bsrc = reinterpret_cast<const uint4*>(a.bsums);  // [(t * nb + b) * 2 + j]
+        for (int u = threadIdx.x; u < ns; u += blockDim.x) {
+            const int j = u & 1, tb = u >> 1, t = tb / nb, b = tb - t * nb;
+            bs_s[(t * 2 + j) * nb + b] = __ldg(bsrc + u);
+        }
+        for (int u = threadIdx.x; u < n_tok * nb; u += blockDim.x) d_s[u] = __ldg(a.d + u);
+    }
+    __syncthreads();
+
+    constexpr int RPW = 32 / LPR;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int sub = lane % LPR, q = lane & 3, rbase = lane & ~(LPR - 1);
+    const int n_groups = (rows + 8 * RPW - 1) / (8 * RPW);
+    for (int rg = blockIdx.x; rg < n_groups; rg += gridDim.x) {
+        const int r = (rg * 8 + warp) * RPW + lane / LPR;
+        const bool row_ok = r < rows;  // lanes of an absent row still take part in the shuffles
+        const uint8_t* row = w + size_t(row_ok ? r : 0) * pitch;
+        float yacc[kMaxTok];
+#pragma unroll
+        for (int t = 0; t < kMaxTok; ++t) yacc[t] = 0.0f;
+        for (int b0 = 0; b0 < nb; b0 += LPR) {
+            const int b = b0 + sub;
+            const bool valid = row_ok && b < nb;
+            const int bb = valid ? b : 0;
+            // token-invariant weight operands
+            // Q4_K: low nibbles (0..31), high nibbles (32..63); Q6_K: the unsigned 6-bit quants, quads 1..4 of halves 0, 1
+            uint32_t wq[64];
+            int sc[16];
+            float dw = 0.0f, dmin = 0.0f;
+            if (TYPE == SYN_Q4_K) {
+                const uint8_t* blk = row + size_t(bb) * kQ4KBytes;
+                uint4 hdr = {0, 0, 0, 0}, qv[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) qv[i] = {0, 0, 0, 0};
+                if (valid) {
+                    hdr = __ldg(reinterpret_cast<const uint4*>(blk));
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) qv[i] = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 16 * i));
+                }
+                dw = __half2float(__ushort_as_half(uint16_t(hdr.x & 0xffff)));
+                dmin = __half2float(__ushort_as_half(uint16_t(hdr.x >> 16)));
+                uint32_t sc_lo, sc_hi, m_lo, m_hi;
+                q4k_scales_all(hdr.y, hdr.z, hdr.w, sc_lo, sc_hi, m_lo, m_hi);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    sc[j] = byte_at(sc_lo, j);
+                    sc[j + 4] = byte_at(sc_hi, j);
+                    sc[j + 8] = byte_at(m_lo, j);  // the mins ride in sc[8..15]
+                    sc[j + 12] = byte_at(m_hi, j);
+                }
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const uint32_t* v = &qv[i].x;
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        wq[4 * i + e] = v[e] & 0x0f0f0f0fu;
+                        wq[32 + 4 * i + e] = (v[e] >> 4) & 0x0f0f0f0fu;
+                    }
+                }
+            } else {
+                const uint8_t* blk = row + size_t(bb) * kQ6KQuant;
+                uint4 v[13];
+#pragma unroll
+                for (int i = 0; i < 13; ++i) v[i] = {0, 0, 0, 0};
+                uint32_t dbits = 0;
+                if (valid) {
+#pragma unroll
+                    for (int i = 0; i < 13; ++i) v[i] = __ldg(reinterpret_cast<const uint4*>(blk) + i);
+                    dbits = __ldg(reinterpret_cast<const unsigned short*>(row + size_t(nb) * kQ6KQuant) + bb);
+                }
+                dw = __half2float(__ushort_as_half(uint16_t(dbits)));
+                const uint32_t* sw = &v[12].x;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) sc[j] = sbyte_at(sw[j >> 2], j & 3);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const uint32_t* ql = &v[4 * h].x;    // 16 words: ql[64h .. 64h + 63]
+                    const uint32_t* qh = &v[8 + 2 * h].x;  // 8 words: qh[32h .. 32h + 31]
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const uint32_t A = ql[k], B = ql[8 + k], H = qh[k];
+                        wq[32 * h + k] = (A & 0x0f0f0f0fu) | ((H << 4) & 0x30303030u);
+                        wq[32 * h + 8 + k] = (B & 0x0f0f0f0fu) | ((H << 2) & 0x30303030u);
+                        wq[32 * h + 16 + k] = ((A >> 4) & 0x0f0f0f0fu) | (H & 0x30303030u);
+                        wq[32 * h + 24 + k] = ((B >> 4) & 0x0f0f0f0fu) | ((H >> 2) & 0x30303030u);
+                    }
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < kMaxTok; ++t) {
+                if (t >= n_tok) break;
+                const uint4* at = act_s + size_t(t) * 16 * nb + bb;  // piece i at at[i * nb]
+                int s = 0, ms = 0;
+                if (TYPE == SYN_Q4_K) {
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const uint4 w0 = {wq[8 * k], wq[8 * k + 1], wq[8 * k + 2], wq[8 * k + 3]};
+                        const uint4 w1 = {wq[8 * k + 4], wq[8 * k + 5], wq[8 * k + 6], wq[8 * k + 7]};
+                        const uint4 h0 = {wq[32 + 8 * k], wq[33 + 8 * k], wq[34 + 8 * k], wq[35 + 8 * k]};
+                        const uint4 h1 = {wq[36 + 8 * k], wq[37 + 8 * k], wq[38 + 8 * k], wq[39 + 8 * k]};
+                        const int lo = dot16(w0, at[(4 * k) * nb]) + dot16(w1, at[(4 * k + 1) * nb]);
+                        const int hi = dot16(h0, at[(4 * k + 2) * nb]) + dot16(h1, at[(4 * k + 3) * nb]);
+                        s += sc[2 * k] * lo + sc[2 * k + 1] * hi;
+                    }
+                    const uint4 p0 = bs_s[size_t(t) * 2 * nb + bb], p1 = bs_s[(size_t(t) * 2 + 1) * nb + bb];
+                    const uint32_t pw[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        ms += sc[8 + j] * (int(int16_t(pw[j] & 0xffffu)) + (int(pw[j]) >> 16));
+                } else {
+                    // sum (q - 32) a = sum q a - 32 sum a, the second from the Q8_K sums of 16
+                    const uint4 p0 = bs_s[size_t(t) * 2 * nb + bb], p1 = bs_s[(size_t(t) * 2 + 1) * nb + bb];
+                    const uint32_t pw[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+#pragma unroll
+                        for (int quad = 0; quad < 4; ++quad)
+#pragma unroll
+                            for (int is = 0; is < 2; ++is) {
+                                const int o = 32 * h + 8 * quad + 4 * is;
+                                const int j = 8 * h + 2 * quad + is;  // the sub-block of 16
+                                const uint4 wv = {wq[o], wq[o + 1], wq[o + 2], wq[o + 3]};
+                                const int bsum = j & 1 ? int(pw[j >> 1]) >> 16 : int(int16_t(pw[j >> 1] & 0xffffu));
+                                s += sc[8 * h + is + 2 * quad] * (dot16(wv, at[j * nb]) - 32 * bsum);
+                            }
+                }
+                const float da = d_s[t * nb + bb];
+                const float scl = __fmul_rn(dw, da), sclm = __fmul_rn(dmin, da);
+                float acc = q == 0 && valid ? fmaf(float(s), scl, 0.0f) : 0.0f;
+                float accm = q == 0 && valid ? fmaf(float(ms), sclm, 0.0f) : 0.0f;
+#pragma unroll
+                for (int step = 1; step < 4; ++step) {
+                    const float prev = __shfl_up_sync(0xffffffffu, acc, 1);
+                    const float prevm = TYPE == SYN_Q4_K ? __shfl_up_sync(0xffffffffu, accm, 1) : 0.0f;
+                    if (q == step) {
+                        acc = valid ? fmaf(float(s), scl, prev) : prev;
+                        if (TYPE == SYN_Q4_K) accm = valid ? fmaf(float(ms), sclm, prevm) : prevm;
+                    }
+                }
+                const float chunk = TYPE == SYN_Q4_K ? __fsub_rn(acc, accm) : acc;  // at lane 4c + 3
+#pragma unroll
+                for (int c = 0; c < LPR / 4; ++c) {
+                    const float v = __shfl_sync(0xffffffffu, chunk, rbase + 4 * c + 3);
+                    if (b0 + 4 * c < nb) yacc[t] = __fadd_rn(yacc[t], v);
+                }
+            }
+        }
+        if (row_ok && sub == 0) {
+#pragma unroll
+            for (int t = 0; t < kMaxTok; ++t) {
+                if (t >= n_tok) break;
+                const size_t o = size_t(t) * rows + r;
+                y[o] = residual ? __fadd_rn(yacc[t], residual[o]) : yacc[t];
+            }
+        }
+    }
+}
+
+template <int TYPE, int LPR>
+int launch_kb(const uint8_t* w, size_t pitch, int rows, int cols, const KAct& a, int n, float* y, const float* res,
+              size_t smem, cudaStream_t s) {
+    static bool opted = false;  // the opt-in is per kernel and process; setting it twice is harmless
+    if (!opted) {
+        const int st = syn_cuda_status(
+            cudaFuncSetAttribute(gemv_kb_kernel<TYPE, LPR>, cudaFuncAttributeMaxDynamicSharedMemorySize, kKbSmemBudget));
+        if (st) return st;
+        opted = true;
+    }
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (sms <= 0) sms = 148;
+    }
+    const int rpw = 32 / LPR;
+    const int groups = (rows + 8 * rpw - 1) / (8 * rpw);
+    const unsigned grid = unsigned(std::min(groups, 2 * sms));
+    gemv_kb_kernel<TYPE, LPR><<<grid, 256, smem, s>>>(w, pitch, rows, cols, a, n, y, res);
+    return syn_cuda_status(cudaGetLastError());
+}
+
+template <int TYPE>
+int launch_kb_lpr(int lpr, const uint8_t* w, size_t pitch, int rows, int cols, const KAct& a, int n, float* y,
+                  const float* res, size_t smem, cudaStream_t s) {
+    switch (lpr) {
+    case 4: return launch_kb<TYPE, 4>(w, pitch, rows, cols, a, n, y, res, smem, s);
+    case 8: return launch_kb<TYPE, 8>(w, pitch, rows, cols, a, n, y, res, smem, s);
+    case 16: return launch_kb<TYPE, 16>(w, pitch, rows, cols, a, n, y, res, smem, s);
+    default: return launch_kb<TYPE, 32>(w, pitch, rows, cols, a, n, y, res, smem, s);
+    }
+}
+
 }  // namespace
 }  // namespace syn
 
@@ -371,6 +612,26 @@ int syn_gemv_k(int type, const void* w, int layout, int rows, int cols, const vo
     const size_t pitch = k_planar_row_bytes(type, cols);  // Q4_K: the GGUF pitch
     const unsigned grid = unsigned((rows + 7) / 8);
     const int nbk = cols / QKK;
+    // one lane per super-block when a token's activations fit the shared-memory budget
+    const int kb_tok = std::min(kMaxTok, kKbSmemBudget / (nbk * kKbBytesPerBlockTok));
+    const char* env = std::getenv("SYN_GEMV_K_WARP");  // 1: the warp-per-row kernel only (comparisons)
+    if (kb_tok >= 1 && !(env && env[0] == '1')) {
+        const int lpr = nbk >= 24 ? 32 : nbk >= 12 ? 16 : nbk >= 6 ? 8 : 4;
+        for (int t0 = 0; t0 < n_tok; t0 += kb_tok) {
+            const int n = std::min(kb_tok, n_tok - t0);
+            KAct a{all.qs + size_t(t0) * cols, all.d + size_t(t0) * nbk, all.bsums + size_t(t0) * (cols / 16)};
+            const float* res = residual ? residual + size_t(t0) * rows : nullptr;
+            const size_t smem = size_t(n) * nbk * kKbBytesPerBlockTok;
+            const uint8_t* wp = static_cast<const uint8_t*>(w);
+            const int st = type == SYN_Q4_K
+                               ? launch_kb_lpr<SYN_Q4_K>(lpr, wp, pitch, rows, cols, a, n, y + size_t(t0) * rows, res,
+                                                         smem, s)
+                               : launch_kb_lpr<SYN_Q6_K>(lpr, wp, pitch, rows, cols, a, n, y + size_t(t0) * rows, res,
+                                                         smem, s);
+            if (st) return st;
+        }
+        return SYN_OK;
+    }
     for (int t0 = 0; t0 < n_tok; t0 += kMaxTok) {
         const int n = std::min(kMaxTok, n_tok - t0);
         KAct a{all.qs + size_t(t0) * cols, all.d + size_t(t0) * nbk, all.bsums + size_t(t0) * (cols / 16)};

@@ -69,9 +69,14 @@ K_SHAPES = [(8, 256, 1), (37, 1280, 1), (300, 4096, 3), (64, 14336, 2), (129, 76
             (1000, 14336, 16)]
 
 
+@pytest.mark.parametrize("kernel", ["lane", "warp"])
 @pytest.mark.parametrize("ty", [syn.Q4_K, syn.Q6_K])
 @pytest.mark.parametrize("rows,cols,n_tok", K_SHAPES)
-def test_gemv_k_matches_oracle(ty, rows, cols, n_tok):
+def test_gemv_k_matches_oracle(ty, rows, cols, n_tok, kernel, monkeypatch):
+    # lane: one lane per super-block (the default); warp: the warp-per-row kernel that
+    # rows too wide for the lane kernel's shared memory take
+    if kernel == "warp":
+        monkeypatch.setenv("SYN_GEMV_K_WARP", "1")
     rng = np.random.default_rng(rows * 7 + cols + n_tok)
     w = orc.random_k_blocks(ty, rows, cols, seed=rows + cols)
     x = rng.standard_normal((n_tok, cols), dtype=np.float32)
