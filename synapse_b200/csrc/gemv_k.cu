@@ -9,10 +9,11 @@
 // dot.hpp:91) accumulates fma(float(isum), d_w * d_a, acc) in block order;
 // Q4_K subtracts a second accumulator over its mins, fma(float(msum),
 // dmin_w * d_a, acc_m) with msum = sum_j m_{j/2} * bsums_j; the chunk sums
-// are added to the row in order. Integer order is free (sums are exact), so
-// the kernel splits each super-block across eight lanes, one chunk per warp
-// instruction, and reduces the lanes' integers with shuffles before the
-// float chain, which every lane of the warp then runs identically.
+// are added to the row in order. Integer order is free (sums are exact):
+// gemv_kb_kernel gives each lane whole super-blocks and chains a chunk over
+// four lanes; gemv_k_kernel (for rows too wide for the first's shared
+// memory) splits each super-block across eight lanes and reduces their
+// integers with shuffles before the float chain.
 //
 // Device layouts.
 //   Q8_K activations, planar (16-byte loads): int8 quants [n_tok][cols], then
