@@ -369,8 +369,10 @@ __device__ __forceinline__ void q4k_scales_all(uint32_t s0, uint32_t s1, uint32_
 __device__ __forceinline__ int byte_at(uint32_t w, int i) { return int((w >> (8 * i)) & 0xffu); }
 __device__ __forceinline__ int sbyte_at(uint32_t w, int i) { return int(int8_t((w >> (8 * i)) & 0xffu)); }
 
-template <int TYPE, int LPR>
-__global__ void __launch_bounds__(256, 2) gemv_kb_kernel(const uint8_t* __restrict__ w, size_t pitch, int rows,
+// MAXT: tokens per launch at most (1: the decode case, fewer live registers,
+// three CTAs per SM; 8: the decoded weights are kept for every token).
+template <int TYPE, int LPR, int MAXT>
+__global__ void __launch_bounds__(256, MAXT == 1 ? 3 : 2) gemv_kb_kernel(const uint8_t* __restrict__ w, size_t pitch, int rows,
                                                          int cols, KAct a, int n_tok, float* __restrict__ y,
                                                          const float* residual) {
     extern __shared__ uint4 smem[];
@@ -403,9 +405,9 @@ __global__ void __launch_bounds__(256, 2) gemv_kb_kernel(const uint8_t* __restri
         const int r = (rg * 8 + warp) * RPW + lane / LPR;
         const bool row_ok = r < rows;  // lanes of an absent row still take part in the shuffles
         const uint8_t* row = w + size_t(row_ok ? r : 0) * pitch;
-        float yacc[kMaxTok];
+        float yacc[MAXT];
 #pragma unroll
-        for (int t = 0; t < kMaxTok; ++t) yacc[t] = 0.0f;
+        for (int t = 0; t < MAXT; ++t) yacc[t] = 0.0f;
         for (int b0 = 0; b0 < nb; b0 += LPR) {
             const int b = b0 + sub;
             const bool valid = row_ok && b < nb;
@@ -475,7 +477,7 @@ __global__ void __launch_bounds__(256, 2) gemv_kb_kernel(const uint8_t* __restri
                 }
             }
 #pragma unroll
-            for (int t = 0; t < kMaxTok; ++t) {
+            for (int t = 0; t < MAXT; ++t) {
                 if (t >= n_tok) break;
                 const uint4* at = act_s + size_t(t) * 16 * nb + bb;  // piece i at at[i * nb]
                 int s = 0, ms = 0;
@@ -535,7 +537,7 @@ __global__ void __launch_bounds__(256, 2) gemv_kb_kernel(const uint8_t* __restri
         }
         if (row_ok && sub == 0) {
 #pragma unroll
-            for (int t = 0; t < kMaxTok; ++t) {
+            for (int t = 0; t < MAXT; ++t) {
                 if (t >= n_tok) break;
                 const size_t o = size_t(t) * rows + r;
                 y[o] = residual ? __fadd_rn(yacc[t], residual[o]) : yacc[t];
@@ -544,38 +546,39 @@ __global__ void __launch_bounds__(256, 2) gemv_kb_kernel(const uint8_t* __restri
     }
 }
 
-template <int TYPE, int LPR>
+template <int TYPE, int LPR, int MAXT>
 int launch_kb(const uint8_t* w, size_t pitch, int rows, int cols, const KAct& a, int n, float* y, const float* res,
               size_t smem, cudaStream_t s) {
-    static bool opted = false;  // the opt-in is per kernel and process; setting it twice is harmless
-    if (!opted) {
-        const int st = syn_cuda_status(
-            cudaFuncSetAttribute(gemv_kb_kernel<TYPE, LPR>, cudaFuncAttributeMaxDynamicSharedMemorySize, kKbSmemBudget));
-        if (st) return st;
-        opted = true;
-    }
+    static int per_sm = 0;  // resident CTAs per SM at the full budget (the opt-in is per kernel and process)
     static int sms = 0;
-    if (!sms) {
+    auto kernel = gemv_kb_kernel<TYPE, LPR, MAXT>;
+    if (!per_sm) {
+        int st = syn_cuda_status(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                      kKbSmemBudget));
+        if (st) return st;
         int dev = 0;
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (sms <= 0) sms = 148;
+        int b = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, 256, smem) != cudaSuccess || b < 1) b = 1;
+        per_sm = b;
     }
     const int rpw = 32 / LPR;
     const int groups = (rows + 8 * rpw - 1) / (8 * rpw);
-    const unsigned grid = unsigned(std::min(groups, 2 * sms));
-    gemv_kb_kernel<TYPE, LPR><<<grid, 256, smem, s>>>(w, pitch, rows, cols, a, n, y, res);
+    const unsigned grid = unsigned(std::min(groups, per_sm * sms));
+    kernel<<<grid, 256, smem, s>>>(w, pitch, rows, cols, a, n, y, res);
     return syn_cuda_status(cudaGetLastError());
 }
 
-template <int TYPE>
+template <int TYPE, int MAXT>
 int launch_kb_lpr(int lpr, const uint8_t* w, size_t pitch, int rows, int cols, const KAct& a, int n, float* y,
                   const float* res, size_t smem, cudaStream_t s) {
     switch (lpr) {
-    case 4: return launch_kb<TYPE, 4>(w, pitch, rows, cols, a, n, y, res, smem, s);
-    case 8: return launch_kb<TYPE, 8>(w, pitch, rows, cols, a, n, y, res, smem, s);
-    case 16: return launch_kb<TYPE, 16>(w, pitch, rows, cols, a, n, y, res, smem, s);
-    default: return launch_kb<TYPE, 32>(w, pitch, rows, cols, a, n, y, res, smem, s);
+    case 4: return launch_kb<TYPE, 4, MAXT>(w, pitch, rows, cols, a, n, y, res, smem, s);
+    case 8: return launch_kb<TYPE, 8, MAXT>(w, pitch, rows, cols, a, n, y, res, smem, s);
+    case 16: return launch_kb<TYPE, 16, MAXT>(w, pitch, rows, cols, a, n, y, res, smem, s);
+    default: return launch_kb<TYPE, 32, MAXT>(w, pitch, rows, cols, a, n, y, res, smem, s);
     }
 }
 
@@ -624,11 +627,15 @@ int syn_gemv_k(int type, const void* w, int layout, int rows, int cols, const vo
             const float* res = residual ? residual + size_t(t0) * rows : nullptr;
             const size_t smem = size_t(n) * nbk * kKbBytesPerBlockTok;
             const uint8_t* wp = static_cast<const uint8_t*>(w);
-            const int st = type == SYN_Q4_K
-                               ? launch_kb_lpr<SYN_Q4_K>(lpr, wp, pitch, rows, cols, a, n, y + size_t(t0) * rows, res,
-                                                         smem, s)
-                               : launch_kb_lpr<SYN_Q6_K>(lpr, wp, pitch, rows, cols, a, n, y + size_t(t0) * rows, res,
-                                                         smem, s);
+            float* yo = y + size_t(t0) * rows;
+            int st;
+            if (n == 1)
+                st = type == SYN_Q4_K ? launch_kb_lpr<SYN_Q4_K, 1>(lpr, wp, pitch, rows, cols, a, n, yo, res, smem, s)
+                                      : launch_kb_lpr<SYN_Q6_K, 1>(lpr, wp, pitch, rows, cols, a, n, yo, res, smem, s);
+            else
+                st = type == SYN_Q4_K
+                         ? launch_kb_lpr<SYN_Q4_K, kMaxTok>(lpr, wp, pitch, rows, cols, a, n, yo, res, smem, s)
+                         : launch_kb_lpr<SYN_Q6_K, kMaxTok>(lpr, wp, pitch, rows, cols, a, n, yo, res, smem, s);
             if (st) return st;
         }
         return SYN_OK;
