@@ -309,7 +309,7 @@ int syn_session_profile(syn_session* s, uint32_t token, uint32_t pos, syn_op_pro
  * Tensor parallelism over the GPUs of one node, one process (or thread) per
  * GPU. The reference computes every output element of a GEMV with one
  * thread's arithmetic whatever the thread count (its D1 contract,
- * tests/unit/llama_threads.cpp:32, over kernels/gemv.hpp:72-161 row ranges);
+ * tests/sdk/llama_threads.cpp:32, over kernels/gemv.hpp:72-161 row ranges);
  * the sharding here keeps that across GPUs: attention by KV-head groups, every
  * matrix by output rows, and the four per-layer activations (attention output,
  * residual after O, silu*up, residual after down) plus the logits all-gathered

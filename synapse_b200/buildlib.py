@@ -53,8 +53,7 @@ def build(verbose=False, force=False):
         cmd = ["nvcc", *ARCH, "-O3", "-lineinfo", "--fmad=false", "-std=c++20", "-Xcompiler", "-fPIC",
                "-I", os.path.join(ROOT, "include"), "-I", inc, "-c", src, "-o", obj]
         if src.endswith(".cpp"):
-            cmd = ["nvcc", "-x", "cu", *cmd[1:]] if False else \
-                ["g++", "-O2", "-std=c++20", "-fPIC", "-Wall", "-I", os.path.join(ROOT, "include"),
+            cmd = ["g++", "-O2", "-std=c++20", "-fPIC", "-Wall", "-I", os.path.join(ROOT, "include"),
                  "-I", inc, "-I", "/usr/local/cuda/include", "-c", src, "-o", obj]
         if verbose:
             print(" ".join(cmd))

@@ -396,27 +396,3 @@ int syn_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cud
     }
     return syn_cuda_status(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
 }
-
-// syn_launch with thread-block clusters of cluster_x CTAs along x.
-template <typename... KArgs, typename... Args>
-int syn_launch_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, int cluster_x, cudaStream_t s,
-                       Args&&... args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = unsigned(cluster_x);
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    if (syn_pdl_enabled()) {
-        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[1].val.programmaticStreamSerializationAllowed = 1;
-        cfg.numAttrs = 2;
-    }
-    return syn_cuda_status(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
-}

@@ -1,5 +1,4 @@
-// Shared pieces of the one-token GEMV (gemv.cu) and of the persistent decode
-// step (decode_step.cu): the exact block dot, the in-kernel Q8_0 quantization
+// Pieces of the one-token GEMV (gemv.cu): the exact block dot, the in-kernel Q8_0 quantization
 // of the input (with or without rms_norm), and the staged batch: lane-parallel
 // block dots staged in shared memory, then one fma chain per 32-block chunk in
 // the reference's order, then the row sums.

@@ -111,12 +111,6 @@ struct syn_session {
     size_t act_off = 0;
     size_t io_off = 0, forced_off = 0, hist_off = 0, argmax_ws_off = 0;
     size_t rope_tab_off = 0;  // (cos, sin) of every RoPE pair at every position < max_ctx
-    // the persistent step kernel (decode_step.cu), when the model fits it
-    bool mega = false;
-    int mega_lt = 0, mega_ht = 0, mega_grid = 0;
-    size_t mega_smem = 0;
-    size_t plan_off = 0, players_off = 0, mega_act_off = 0, mega_sync_off = 0, mega_err_off = 0;
-    StepPlan plan{};
     std::vector<tensor> tensors;
     std::vector<op> ops;
     int logits_t = -1;
@@ -132,7 +126,7 @@ struct syn_session {
     template <typename T>
     T* at(size_t off) { return reinterpret_cast<T*>(arena + off); }
     float* tf(int t, size_t off = 0) { return at<float>(act_off + tensors[t].off) + off; }
-    float* logits() { return mega ? plan.logits : tf(p2p ? logits_plain_t : logits_t); }
+    float* logits() { return tf(p2p ? logits_plain_t : logits_t); }
     void* tb(int t) { return arena + act_off + tensors[t].off; }
     int32_t* io() { return at<int32_t>(io_off); }
     uint16_t* kv(int layer, int which) {
@@ -476,14 +470,6 @@ int plan_step(syn_session& s) {
 int enqueue_ops(syn_session& s, cudaStream_t st);
 TpSync tp_sync(syn_session& s, const op& o);
 
-// One step: the persistent step kernel when the model fits it, else the ops.
-int enqueue_body(syn_session& s, cudaStream_t st) {
-    if (!s.mega) return enqueue_ops(s, st);
-    int rc = cuda(cudaMemsetAsync(s.arena + s.mega_sync_off, 0, size_t(2 + s.cfg.n_head_kv) * 4, st));
-    if (!rc) rc = syn_step_launch(s.at<StepPlan>(s.plan_off), s.mega_lt, s.mega_ht, s.mega_smem, s.mega_grid, st);
-    return rc;
-}
-
 int enqueue_ops(syn_session& s, cudaStream_t st) {
     const syn_llama_config& c = s.cfg;
     const int qrows = s.part.n_head * c.head_dim, kvrows = s.part.n_kv * c.head_dim;  // this rank's heads
@@ -584,7 +570,7 @@ int enqueue_ops(syn_session& s, cudaStream_t st) {
 
 int enqueue_step(syn_session& s, cudaStream_t st) {
     int rc = cuda(cudaMemcpyAsync(s.io(), s.h_io, 2 * sizeof(int32_t), cudaMemcpyHostToDevice, st));
-    if (!rc) rc = enqueue_body(s, st);
+    if (!rc) rc = enqueue_ops(s, st);
     if (!rc) rc = cuda(cudaMemcpyAsync(s.h_logits, s.logits(), size_t(s.cfg.n_vocab) * 4,
                                        cudaMemcpyDeviceToHost, st));
     if (!rc) rc = cuda(cudaMemcpyAsync(s.h_next, s.io() + 2, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
@@ -592,7 +578,7 @@ int enqueue_step(syn_session& s, cudaStream_t st) {
 }
 
 int enqueue_gen(syn_session& s, cudaStream_t st) {
-    int rc = enqueue_body(s, st);
+    int rc = enqueue_ops(s, st);
     if (!rc) rc = syn_advance(s.io(), s.at<int32_t>(s.forced_off), s.at<int32_t>(s.hist_off), st);
     return rc;
 }
@@ -628,118 +614,6 @@ int capture(syn_session& s, int (*fn)(syn_session&, cudaStream_t), cudaGraphExec
     return rc;
 }
 
-// ---- the persistent step kernel ------------------------------------------------
-
-// The persistent step kernel is opt-in (SYN_STEP_KERNEL=1): it computes the
-// same values as the ops, but the op graph with programmatic dependent launch
-// is faster today.
-bool step_kernel_wanted() {
-    const char* env = std::getenv("SYN_STEP_KERNEL");
-    return env && env[0] == '1';
-}
-
-// Whether the model fits the step kernel, and its buffers in the arena.
-void plan_step_kernel(syn_session& s, layout_builder& lb) {
-    const syn_llama_config& c = s.cfg;
-    s.mega = false;
-    if (!step_kernel_wanted() || c.rope_mode != 0 || c.head_dim > 128 || c.head_dim % 8) return;
-    const int G = c.n_head / c.n_head_kv;
-    if (G > 8 || s.layers.empty()) return;
-    const int lt = s.layers[0].q.type;
-    if (lt != SYN_Q4_0 && lt != SYN_Q8_0) return;
-    for (const layer_w& L : s.layers) {
-        if (!L.fused_qkv || !L.gu_pairs || L.q.type != lt || L.o.type != lt || L.gate.type != lt || L.down.type != lt)
-            return;
-    }
-    if (!s.head.quant() || s.head.layout != SYN_LAYOUT_PLANAR) return;
-    StepPlan& P = s.plan;
-    P = StepPlan{};
-    P.n_layer = c.n_layer;
-    P.d = c.n_embd;
-    P.qrows = c.n_head * c.head_dim;
-    P.kvrows = c.n_head_kv * c.head_dim;
-    P.ff = c.n_ff;
-    P.vocab = c.n_vocab;
-    P.n_head = c.n_head;
-    P.n_kv = c.n_head_kv;
-    P.hd = c.head_dim;
-    P.max_ctx = s.max_ctx;
-    const size_t smem = syn_step_smem(&P, lt, s.head.type);
-    if (!smem) return;
-    const int grid = syn_step_grid(lt, s.head.type, smem);
-    if (grid <= 0) return;
-    P.max_split = std::max(1, grid / c.n_head_kv);
-    if (size_t(s.max_ctx) > size_t(P.max_split) * 8 * 256) return;  // per-warp score buffer
-    s.mega = true;
-    s.mega_lt = lt;
-    s.mega_ht = s.head.type;
-    s.mega_smem = smem;
-    s.mega_grid = grid;
-    s.plan_off = lb.take(sizeof(StepPlan));
-    s.players_off = lb.take(sizeof(StepLayer) * size_t(c.n_layer));
-    const size_t f = 4;
-    const size_t floats = size_t(c.n_embd) * 2 + size_t(P.qrows + 2 * P.kvrows) + size_t(P.qrows) + size_t(c.n_ff) +
-                          size_t(c.n_vocab) + size_t(c.n_head) * P.max_split +
-                          size_t(c.n_head_kv) * P.max_split * G * c.head_dim + size_t(grid) * 2;
-    s.mega_act_off = lb.take(floats * f + size_t(c.n_head) * P.max_split * 8 + 16 * 1024);  // + per-buffer rounding
-    s.mega_sync_off = lb.take(size_t(64 + c.n_head_kv) * 4);
-    s.mega_err_off = lb.take(64);
-}
-
-// The plan's pointers (the arena exists now), copied to the device.
-int fill_step_plan(syn_session& s) {
-    const syn_llama_config& c = s.cfg;
-    StepPlan& P = s.plan;
-    P.etype = s.embd.type;
-    P.elayout = s.embd.layout;
-    P.eps = c.rms_eps;
-    P.scale = s.scale;
-    P.embd = reinterpret_cast<const uint8_t*>(s.arena + s.embd.off);
-    P.head = reinterpret_cast<const uint8_t*>(s.arena + s.head.off);
-    P.out_norm = s.at<float>(s.out_norm.off);
-    P.rope_tab = s.at<float>(s.rope_tab_off);
-    P.layers = s.at<StepLayer>(s.players_off);
-    P.io = s.io();
-    const int G = c.n_head / c.n_head_kv;
-    float* f = s.at<float>(s.mega_act_off);
-    auto take = [&](size_t n) {
-        float* p = f;
-        f += (n + 63) / 64 * 64;
-        return p;
-    };
-    P.x = take(c.n_embd);
-    P.x2 = take(c.n_embd);
-    P.qkv = take(size_t(P.qrows + 2 * P.kvrows));
-    P.attn = take(size_t(P.qrows));
-    P.act = take(size_t(c.n_ff));
-    P.logits = take(size_t(c.n_vocab));
-    P.att_m = take(size_t(c.n_head) * P.max_split);
-    P.att_part = take(size_t(c.n_head_kv) * P.max_split * G * c.head_dim);
-    P.am_v = take(size_t(s.mega_grid));
-    P.am_i = reinterpret_cast<int*>(take(size_t(s.mega_grid)));
-    P.att_s = reinterpret_cast<double*>(take(size_t(c.n_head) * P.max_split * 2));
-    P.sync = s.at<unsigned>(s.mega_sync_off);
-    P.err = s.at<unsigned>(s.mega_err_off);
-    std::vector<StepLayer> layers(c.n_layer);
-    for (int l = 0; l < c.n_layer; ++l) {
-        const layer_w& L = s.layers[l];
-        StepLayer& d = layers[l];
-        d.qkv = reinterpret_cast<const uint8_t*>(s.arena + L.q.off);
-        d.o = reinterpret_cast<const uint8_t*>(s.arena + L.o.off);
-        d.gu = reinterpret_cast<const uint8_t*>(s.arena + L.gate.off);
-        d.down = reinterpret_cast<const uint8_t*>(s.arena + L.down.off);
-        d.attn_norm = s.at<float>(L.attn_norm.off);
-        d.ffn_norm = s.at<float>(L.ffn_norm.off);
-        d.kc = s.kv(l, 0);
-        d.vc = s.kv(l, 1);
-    }
-    int rc = cuda(cudaMemcpy(s.arena + s.players_off, layers.data(), sizeof(StepLayer) * layers.size(),
-                             cudaMemcpyHostToDevice));
-    if (!rc) rc = cuda(cudaMemcpy(s.arena + s.plan_off, &P, sizeof(StepPlan), cudaMemcpyHostToDevice));
-    if (!rc) rc = cuda(cudaMemset(s.arena + s.mega_err_off, 0, 64));
-    return rc;
-}
-
 // ---- config + weights ---------------------------------------------------------
 
 int finish(syn_session& s, layout_builder& lb) {
@@ -757,7 +631,6 @@ int finish(syn_session& s, layout_builder& lb) {
     s.hist_off = lb.take(size_t(s.max_ctx) * 4);
     s.argmax_ws_off = lb.take(syn_argmax_ws_bytes(1));  // persistent: its counters must stay zero between steps
     s.rope_tab_off = lb.take(size_t(s.max_ctx) * c.head_dim * 4);
-    if (s.part.world == 1) plan_step_kernel(s, lb);
     if (s.n_gathers) s.tp_off = lb.take(128);  // peers[8], epoch at +64, wait errors at +68
     s.arena_bytes = lb.off;
     s.theta_scale = std::pow(c.rope_base, -2.0f / float(c.head_dim));  // attention.hpp:47
@@ -839,10 +712,6 @@ TpSync tp_sync(syn_session& s, const op& o) {
 int warm_and_capture(syn_session& s) {
     s.h_io[0] = 0;
     s.h_io[1] = 0;
-    if (s.mega) {
-        int rc = fill_step_plan(s);
-        if (rc) return rc;
-    }
     if (int rc = map_peers(s)) return rc;
     int rc = syn_rope_table(s.at<float>(s.rope_tab_off), s.max_ctx, s.cfg.head_dim, s.theta_scale,
                             s.has_ff ? s.at<float>(s.ff_off) : nullptr, nullptr, s.stream);

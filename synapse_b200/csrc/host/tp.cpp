@@ -1,7 +1,7 @@
 // Tensor-parallel groups: one NCCL communicator per rank, created from an id
 // the ranks share, and the in-place all-gather the sharded session runs after
 // every row-sharded op. The reference runs one process; its D1 contract
-// (tests/unit/llama_threads.cpp:32: any thread count gives the one-thread
+// (tests/sdk/llama_threads.cpp:32: any thread count gives the one-thread
 // bits) is what the row sharding keeps across GPUs.
 #include <cuda_runtime.h>
 #include <nccl.h>

@@ -93,40 +93,3 @@ int syn_tp_step_begin(unsigned* epoch, cudaStream_t s);
 // comparison, y_ref = exp(double(x)) rounded to float, for n device floats.
 extern "C" int syn_check_exp(const float* x, float* y, float* y_ref, int n, void* stream);
 
-// ---- the persistent decode step (decode_step.cu) ------------------------------
-// Device pointers of one layer: planar fused QKV rows, O, interleaved gate/up
-// rows (gate i at 2i, up i at 2i+1), down; F32 norms; the F16 K / V caches.
-struct StepLayer {
-    const uint8_t *qkv, *o, *gu, *down;
-    const float *attn_norm, *ffn_norm;
-    uint16_t *kc, *vc;
-};
-
-// Everything the step kernel reads, in device memory.
-struct StepPlan {
-    int n_layer, d, qrows, kvrows, ff, vocab, n_head, n_kv, hd, max_ctx;
-    int etype, elayout;        // embedding table
-    float eps, scale;
-    const uint8_t* embd;
-    const uint8_t* head;
-    const float* out_norm;
-    const float* rope_tab;     // [max_ctx][hd / 2] (cos, sin)
-    const StepLayer* layers;   // device array
-    int32_t* io;               // token, pos, next token
-    float *x, *x2, *qkv, *attn, *act, *logits;
-    float* att_m;              // [n_head][max_split] chunk maxima
-    double* att_s;             // [n_head][max_split] chunk sums
-    float* att_part;           // [n_kv][max_split][G * hd] chunk p.V
-    int max_split;
-    unsigned* sync;            // [0] arrivals, [1] abort, [2 + g] per-KV-head counters (zero before a launch)
-    unsigned* err;             // steps that aborted (sticky)
-    float* am_v;               // [grid] argmax partials
-    int* am_i;
-    // shared memory layout (syn_step_smem)
-    int nb_max;
-    size_t act_bytes, warp_base, warp_bytes;
-};
-
-size_t syn_step_smem(StepPlan* plan, int ltype, int htype);
-int syn_step_grid(int ltype, int htype, size_t smem);
-int syn_step_launch(const StepPlan* dplan, int ltype, int htype, size_t smem, int grid, cudaStream_t s);

@@ -6,7 +6,7 @@ shards with) must partition every sharded dimension; and a gloo run over 2 or
 points the sharded session gathers (attention output, residual after O,
 silu * up, residual after down, logits), must reproduce the one-process
 oracle's logits bit for bit. That is the reference's D1 contract
-(tests/unit/llama_threads.cpp:32) carried across ranks: row sharding never
+(tests/sdk/llama_threads.cpp:32) carried across ranks: row sharding never
 changes how an output element is computed."""
 import datetime
 import os

@@ -1,7 +1,7 @@
 """Tensor parallelism on 2 or more GPUs of one node, through the session's C
 ABI: each rank holds its heads and rows, NCCL all-gathers in place inside
 the captured step graph, and the logits (and greedy tokens) equal one GPU's
-bit for bit, the reference's D1 contract (tests/unit/llama_threads.cpp:32)
+bit for bit, the reference's D1 contract (tests/sdk/llama_threads.cpp:32)
 across GPUs. Skipped on a box with fewer than 2 GPUs."""
 import datetime
 import os
@@ -17,7 +17,7 @@ torch = pytest.importorskip("torch")
 from synapse_b200 import model  # noqa: E402
 
 SHAPES = {
-    # Llama-3-8B widths, two layers: the fused GEMV and cluster-attention paths
+    # Llama-3-8B widths, two layers: the fused GEMV and fused attention paths
     "8b_2layer_q4_0": dict(n_layer=2, n_embd=4096, n_ff=14336, n_head=32, n_head_kv=8, head_dim=128, n_vocab=128256,
                            rms_eps=1e-5, rope_base=500000.0, rope_mode=0, type_embd=model.F32,
                            type_layers=model.Q4_0, type_output=model.Q8_0),
@@ -113,7 +113,7 @@ def test_tp_equals_one_gpu(world, shape, mode):
     if cfg["n_head_kv"] % world or cfg["n_vocab"] % world or cfg["n_ff"] % world or cfg["n_embd"] % world:
         pytest.skip("world does not divide the model")
     max_ctx = 1024
-    # single-chunk contexts, then positions past kExactChunk where the context is split over a cluster
+    # single-chunk contexts, then positions past one 256-position chunk (several score CTAs per KV head)
     positions = list(range(8)) + [300, 301, 700, 1023]
     got = _run_world(world, shape, max_ctx, positions, mode)
     want, want_gen = _one_gpu(shape, max_ctx, positions)
