@@ -3,31 +3,35 @@
 reference's headline path: quantized GEMV + RoPE/KV-cache attention).
 
 One step = one greedy decode token of the 32-layer model (Q4_0 layers and
-embedding, Q8_0 head, F16 KV cache), after a seeded 512-token prompt, at
-positions 512+W .. 512+W+K (4k context by default). Weights are random
-N(0, 0.02), quantized on the device (synthetic data of the named shape).
+embedding, Q8_0 head, F16 KV cache) at 4k context: a seeded 512-token prompt
+and greedy decode to position 4095 - K run untimed on the device (W of those
+steps are the warm-up), then the K timed steps decode positions 4096 - K ..
+4095 ("at 4k context"). Weights are random N(0, 0.02),
+quantized on the device (synthetic data of the named shape).
 
-value : K / device time of K steps (CUDA events on the session stream; the
-        steps are CUDA-graph replays with the argmax fed back on the device).
-e2e   : the same metric through the public step API: per step the token and
-        position go host->device from pinned memory and the logits + argmax
-        come back device->host.
+value : K / device time of the K steps (CUDA events on the session stream;
+        the steps are CUDA-graph replays with the argmax fed back on the
+        device). full_range: the same over every position 512 .. 4095.
+e2e   : the same metric through the public step API over the same positions:
+        per step the token and position go host->device from pinned memory
+        and the logits + argmax come back device->host.
 roofline : the dominant kernel (the quantized GEMV on the gate/up rows):
-        algorithmic bytes per launch / its CUDA-event time inside one step
-        (each op of the step captured between events), vs MEASURED_PEAKS
-        hbm_gbs; traffic: DRAM bytes per launch of the same shape from ncu.
+        algorithmic bytes per launch / its CUDA-event time inside one step at
+        position 4095 (each op of the step captured between events), vs
+        MEASURED_PEAKS hbm_gbs; traffic: DRAM bytes per launch of the same
+        shape from ncu.
 cpu_baseline : the C oracle (a restatement of the reference's CPU kernels) on
-        this host's cores, a bounded sample (see `sample`).
+        this host's cores, a bounded sample (see `sample`), and on one core
+        (cpu_baseline_1core).
 
 --impl reference: the reference's CPU path (the oracle port; the reference's
 own headers need MTL5, absent here) on all host cores, same metric and unit.
 
 Multi-GPU (torchrun, N ranks), --parallel tp (default): one sequence,
-tensor-parallel over the N GPUs (KV-head groups and GEMV output rows, NCCL
-all-gathers in the step graph; logits bit-identical to one GPU), strong
-scaling; value = tokens / max over ranks of the device time.
---parallel replicas: each GPU decodes its own sequence (weak scaling); value
-= tokens of all ranks / max over ranks of the time.
+tensor-parallel over the N GPUs (KV-head groups and GEMV output rows;
+logits bit-identical to one GPU), strong scaling; value = tokens / max over
+ranks of the device time. --parallel replicas: each GPU decodes its own
+sequence (weak scaling); value = tokens of all ranks / max over ranks.
 """
 import argparse
 import json
@@ -52,7 +56,7 @@ METRIC = "decode tok/s (Llama-3-8B Q4_0 shape)"
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=None, help="timed decode steps (default: to 4096 context)")
+    p.add_argument("--steps", type=int, default=20, help="timed decode steps: positions 4096-K .. 4095")
     p.add_argument("--warmup", type=int, default=16)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--parallel", default="tp", choices=["tp", "replicas"],
@@ -89,7 +93,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.FIELDS,
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
@@ -189,16 +193,24 @@ class CpuDecoder:
                 f"pre-filled) + the Q8_0 head once; tok/s = 1/(32*{layer_s * 1e3:.2f} ms + {head_s * 1e3:.2f} ms)")
 
 
-def cpu_baseline(budget_s, threads):
-    dec = CpuDecoder(threads)
-    dec.layer_step(record=False)
-    t_end = time.perf_counter() + budget_s
-    while time.perf_counter() < t_end or len(dec.times) < 2:
-        dec.layer_step()
-    head = dec.head()
-    value, layer = dec.result(head)
-    return {"value": round(value, 4), "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": dec.sample(head, layer)}
+def cpu_baselines(budget_all_s, budget_one_s):
+    """The oracle timed on every host core, then on one core (the same decoder and position)."""
+    import oracle as orc
+
+    out = []
+    dec = CpuDecoder(os.cpu_count() or 1)
+    for threads, budget in ((os.cpu_count() or 1, budget_all_s), (1, budget_one_s)):
+        orc.set_threads(threads)
+        dec.threads, dec.times = threads, []
+        dec.layer_step(record=False)
+        t_end = time.perf_counter() + budget
+        while time.perf_counter() < t_end or len(dec.times) < 2:
+            dec.layer_step()
+        head = dec.head()
+        value, layer = dec.result(head)
+        out.append({"value": round(value, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+                    "sample": dec.sample(head, layer)})
+    return out
 
 
 def reference_arm(args, rank, world):
@@ -273,8 +285,9 @@ def main():
     if args.ncu_step:
         return ncu_step(args, local)
     W = max(3, args.warmup)
-    K = args.steps if args.steps is not None else CTX - PROMPT - W
-    max_ctx = max(CTX, PROMPT + W + K)
+    K = max(1, min(args.steps, CTX - PROMPT - W))
+    start_pos = CTX - K  # the timed steps decode positions CTX-K .. CTX-1 (4k context)
+    max_ctx = CTX
     cfg = dict(LLAMA8B, type_embd=syn.Q4_0, type_layers=syn.Q4_0, type_output=syn.Q8_0)
     tp_mode = world > 1 and args.parallel == "tp"
     tp = syn.TP.from_torch_distributed(device=local) if tp_mode else None
@@ -285,36 +298,49 @@ def main():
     prompt = np.random.default_rng(42 + seed_rank).integers(0, LLAMA8B["n_vocab"], PROMPT)
     seqs = 1 if tp_mode else world  # sequences decoded by the whole job
 
-    def run_prompt():
-        toks = sess.generate(prompt, 0, PROMPT)  # prompt through the decode graph
-        warm = sess.generate([int(toks[-1])], PROMPT, W)
-        return int(warm[-1])
+    def device_max(ms):
+        if world == 1:
+            return ms
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
 
-    last = run_prompt()
-    start_pos = PROMPT + W
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    def to_start():
+        """The prompt, then greedy decode to position start_pos - 1 (on the device, untimed); the last W of
+        these steps are the warm-up. Returns the next input token and the device time of positions
+        PROMPT .. start_pos - 1."""
+        toks = sess.generate(prompt, 0, PROMPT)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        out = sess.generate([int(toks[-1])], PROMPT, start_pos - PROMPT)
+        e1.record(stream)
+        e1.synchronize()
+        return int(out[-1]), e0.elapsed_time(e1)
+
     if world > 1:
         dist.barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(local) as clocks:
+    with ClockSampler(local) as clocks:  # the pre-decode runs the same step graph: the clocks under this load
+        last, pre_ms = to_start()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
         ev0.record(stream)
         sess.generate([last], start_pos, K, wait=False)
         ev1.record(stream)
         ev1.synchronize()
-    torch.cuda.synchronize()
+        torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    ms = ev0.elapsed_time(ev1)
-    ms_max = ms
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_max = float(t.item())
+    ms_max = device_max(ev0.elapsed_time(ev1))
     value = seqs * K / (ms_max / 1e3)
+    full_ms = device_max(pre_ms + ev0.elapsed_time(ev1))
+    full_range = {"positions": f"{PROMPT}..{CTX - 1}", "value": round(seqs * (CTX - PROMPT) / (full_ms / 1e3), 2),
+                  "unit": "tok/s"}
 
     # e2e through the public step API over the same positions (host round trip every step)
     sess.reset()
-    last = run_prompt()
+    last, _ = to_start()
     tok = last
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
@@ -324,15 +350,10 @@ def main():
         _, tok = sess.step(tok, start_pos + i, logits=True)
     e1.record(stream)
     e1.synchronize()
-    e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e_ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e_ms = float(t.item())
-    e2e = seqs * K / (e_ms / 1e3)
+    e2e = seqs * K / (device_max(e0.elapsed_time(e1)) / 1e3)
 
-    # roofline of the dominant kernel: every GEMV of one step, timed op by op with CUDA events
-    prof_pos = min(start_pos + K - 1, max_ctx - 1)
+    # roofline of the dominant kernel: every op of one step at position CTX-1, timed op by op with CUDA events
+    prof_pos = CTX - 1
     runs = [sess.profile(tok, prof_pos) for _ in range(3)]
     per_op = [min(r[i]["ms"] for r in runs) for i in range(len(runs[0]))]
     ops = runs[0]
@@ -341,10 +362,10 @@ def main():
     attn_ms = sum(t for t, o in zip(per_op, ops) if o["kind"] == "attention")
     attn_bytes = sum(o["bytes"] for o in ops if o["kind"] == "attention")
     total_ms = sum(per_op)
-    n_gemv = sum(1 for o in ops if o["kind"] == "matmul")
     # the dominant kernel: the GEMV on the gate/up rows (the largest share of the step)
     gu = [(t, o) for t, o in zip(per_op, ops) if o["kind"] == "matmul" and o["rows"] == 2 * layout["n_ff"]]
     gather_ms = sum(t for t, o in zip(per_op, ops) if o["kind"] == "allgather")
+    peer_stores = tp_mode and sess.tp_status()["peer_stores"]
     gu_ms = sum(t for t, _ in gu) / max(1, len(gu))
     gu_bytes = gu[0][1]["bytes"] if gu else 0.0
     peak, peak_kind = peaks()
@@ -361,9 +382,9 @@ def main():
             json.dump([dict(o, ms=t, gbps=o["bytes"] / (t / 1e3) / 1e9 if t > 0 else None)
                        for o, t in zip(ops, per_op)], f, indent=0)
 
-    cpu = None
+    cpu = cpu1 = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(12.0, os.cpu_count() or 1)
+        cpu, cpu1 = cpu_baselines(12.0, 8.0)
 
     if rank == 0:
         line = {
@@ -372,12 +393,15 @@ def main():
             "scaling": "strong" if tp_mode else "weak",
             "vs_baseline": None, "dtype": "q4_0/q8_0 weights x q8_0 activations (exact int8 dots), f32 accum",
             "data": "synthetic",
-            "config": {"workload": "Llama-3-8B-shaped Q4_0 decode (BASELINE config 4): 512-token prompt then "
-                                   f"greedy decode positions {start_pos}..{start_pos + K - 1}",
+            "config": {"workload": "Llama-3-8B-shaped Q4_0 decode at 4k context (BASELINE config 4): 512-token "
+                                   f"prompt and greedy decode to position {start_pos - 1} untimed (the last {W} "
+                                   f"steps the warm-up), then timed positions {start_pos}..{CTX - 1}",
                        "model": "llama3-8b-shape (32L, d4096, 32H/8KV, ff14336, V128256), Q4_0 + Q8_0 head",
-                       "global_batch": seqs, "seq_len": start_pos + K,
+                       "global_batch": seqs, "seq_len": CTX,
                        "parallelism": f"tp{world}" if tp_mode else ("replicas" if world > 1 else "single"),
+                       "attention_order": "reference" if os.environ.get("SYN_ATTN_ORDER", "") != "split" else "split",
                        "l2": "weights 4.5 GB per step > 126 MB L2: streamed from HBM every step"},
+            "full_range": full_range,
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
                     "d2h_bytes_per_step": LLAMA8B["n_vocab"] * 4 + 4},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -390,13 +414,16 @@ def main():
                          "peak_source": peak_kind,
                          "step_frac": round(step_bytes / (ms_max / K / 1e3) / 1e9 / peak, 4),
                          "attention_gbs": round(attn_bytes / (attn_ms / 1e3) / 1e9, 1),
+                         "attention_us_per_layer": round(attn_ms * 1e3 / max(1, LLAMA8B["n_layer"]), 2),
                          "gemv_share_of_step": round(gemv_ms / total_ms, 3),
-                         "allgather_ms_per_step": round(gather_ms, 4) if tp_mode else None},
+                         # NCCL all-gathers only: peer-store gathers run inside the producing and reading kernels
+                         "allgather_ms_per_step": round(gather_ms, 4) if tp_mode and not peer_stores else None},
             "gpu_launches": sess.launches_per_step() * K,
             "clocks": clocks.summary(),
         }
         if cpu:
             line["cpu_baseline"] = cpu
+            line["cpu_baseline_1core"] = cpu1
         print(json.dumps(line))
         sys.stdout.flush()
     sess.close()  # its graphs hold NCCL calls: released before the communicators

@@ -172,7 +172,16 @@ int syn_gemv_fusable(int type, int layout, int rows, int cols, int n_tok, int ou
  * rope_mode: 0 normal (Llama), 1 neox. freq_factors: NULL or head_dim/2 floats
  * (device). yarn: NULL or 5 floats {freq_scale, ext_factor, attn_factor,
  * corr_low, corr_high} (host), attention.hpp:60-66.
+ * order: SYN_ORDER_REFERENCE (0, the default) adds every float sum in the
+ *   reference's order at any context length: the score dots in dimension
+ *   order, the normaliser in double, and out = sum_t p_t V_t in position
+ *   order, one fma per position and output element (attention.hpp:214-243);
+ *   bit-identical to the reference's attend_group on the same binary16
+ *   inputs. SYN_ORDER_SPLIT (1) splits the context over 256-position chunks
+ *   whose partial p.V sums run on tensor cores and are added in chunk order:
+ *   the same up to 256 positions, about 1e-6 relative beyond.
  * ---------------------------------------------------------------------- */
+enum { SYN_ORDER_REFERENCE = 0, SYN_ORDER_SPLIT = 1 };
 typedef struct {
     const float* q;        /* [n_q][n_head * head_dim], before RoPE */
     const float* k;        /* [n_q][n_kv * head_dim], before RoPE (append only) */
@@ -192,6 +201,7 @@ typedef struct {
     const float* freq_factors;
     const float* yarn;
     const float* rope_table; /* NULL, or syn_rope_table for these rope settings and max_len rows */
+    int order;             /* SYN_ORDER_REFERENCE / SYN_ORDER_SPLIT */
 } syn_attention_args;
 
 size_t syn_attention_scratch_bytes(int n_q, int n_head, int n_kv, int head_dim, int max_len);
@@ -208,7 +218,9 @@ int syn_attention(const syn_attention_args* a, void* stream);
  * capture. No call allocates. Every call on a device uses the same array, so
  * calls whose GPU work overlaps (different streams, or different host
  * threads) race and must be serialised by the caller; the array keeps the
- * last call's contents, none of which a later call depends on. */
+ * last call's contents, none of which a later call depends on. The device
+ * address is cached per device for the life of the process: do not call it
+ * again on a device after cudaDeviceReset there. */
 int syn_attention_noalloc(const syn_attention_args* a, void* stream);
 /* The (cos, sin) of every RoPE pair at every position p < max_len, as
  * table[p][i] = {cos, sin} of pair i (max_len * head_dim floats), with the
@@ -242,7 +254,9 @@ int syn_embed(int type, const void* table, int layout, int rows, int cols, const
  * std::max_element: ties go to the lowest index). n_tok <= 64. Its partial
  * results live in a small static device array shared by every call on a
  * device, so calls that overlap on the GPU must be serialised by the caller
- * (a session uses its own workspace instead). */
+ * (a session uses its own workspace instead). The workspace's device address
+ * is cached per device for the life of the process: do not call it again on
+ * a device after cudaDeviceReset there. */
 int syn_argmax(const float* x, int n_tok, int n, int32_t* out, void* stream);
 
 /* ------------------------------------------------------------------------

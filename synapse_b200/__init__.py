@@ -298,7 +298,11 @@ class AttentionArgs(ctypes.Structure):
                 ("n_q", ctypes.c_int), ("n_head", ctypes.c_int), ("n_kv", ctypes.c_int), ("head_dim", ctypes.c_int),
                 ("max_len", ctypes.c_int), ("append", ctypes.c_int), ("rope", ctypes.c_int),
                 ("rope_mode", ctypes.c_int), ("theta_scale", ctypes.c_float), ("scale", ctypes.c_float),
-                ("freq_factors", ctypes.c_void_p), ("yarn", ctypes.c_void_p), ("rope_table", ctypes.c_void_p)]
+                ("freq_factors", ctypes.c_void_p), ("yarn", ctypes.c_void_p), ("rope_table", ctypes.c_void_p),
+                ("order", ctypes.c_int)]
+
+
+ORDER_REFERENCE, ORDER_SPLIT = 0, 1
 
 
 def attention_scratch_bytes(n_q, n_head, n_kv, head_dim, max_len):
@@ -307,8 +311,9 @@ def attention_scratch_bytes(n_q, n_head, n_kv, head_dim, max_len):
 
 def attention(q, k, v, k_cache, v_cache, pos, n_head, n_kv, head_dim, max_len, theta_scale, scale,
               cache_stride=None, append=True, rope=True, rope_mode=0, freq_factors=None, out=None, scratch=None,
-              rope_table=None, stream=None):
-    """Fused RoPE + F16 append + decode attention for n_q queries (see syn_attention)."""
+              rope_table=None, order=ORDER_REFERENCE, stream=None):
+    """Fused RoPE + F16 append + decode attention for n_q queries (see syn_attention); order:
+    ORDER_REFERENCE (the reference's summation order) or ORDER_SPLIT (split p.V, re-associated)."""
     torch = _torch()
     n_q = pos.numel()
     if out is None:
@@ -322,7 +327,7 @@ def attention(q, k, v, k_cache, v_cache, pos, n_head, n_kv, head_dim, max_len, t
                       pos.data_ptr(), out.data_ptr(), scratch.data_ptr(), cache_stride, n_q, n_head, n_kv, head_dim,
                       max_len, int(append), int(rope), rope_mode, theta_scale, scale,
                       freq_factors.data_ptr() if freq_factors is not None else None, None,
-                      rope_table.data_ptr() if rope_table is not None else None)
+                      rope_table.data_ptr() if rope_table is not None else None, int(order))
     check(lib().syn_attention(ctypes.byref(a), _stream(stream)), "syn_attention")
     return out
 

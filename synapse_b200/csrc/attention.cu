@@ -8,9 +8,34 @@
 // scale), rounded after normalisation as the reference rounds it;
 // out = sum_t p_t V_t.
 //
-// Two kernels per call, one CTA per (chunk of kChunk positions, KV head,
-// query); each CTA reads its chunk's K (then V) rows from HBM once, for all
-// G = n_head / n_kv query heads of the group, all requested at once.
+// Two summation orders (syn_attention_args.order):
+//
+// SYN_ORDER_REFERENCE (the default): every float sum in the reference's order
+// at any context length. Three stream-ordered kernels:
+//   scores: one CTA per (chunk of kChunk positions, KV head, query); the
+//           chunk's K rows land in shared memory by one bulk copy each; each
+//           thread scores one position for the G query heads, every dot a
+//           dimension-order chain of mixed-precision fmas (binary16 inputs,
+//           float accumulator: the reference's exact products and one
+//           rounding per add); the chunk's max per head;
+//   exp:    the context's max M per head from the chunk maxima, e_t =
+//           expf(s_t - M) in place of the scores, the chunk's double sum;
+//   p.V:    one CTA per (KV head, up to four of its query heads, 32 output
+//           columns); a producer warp streams the V tile of every 64
+//           positions (a tensor TMA copy) and the heads' e_t (bulk copies)
+//           through a ring of shared-memory slots; each consumer lane owns one
+//           output element and adds p_t V_t in position order, one fma per
+//           position (attention.hpp:231-243). The normaliser is the chunks'
+//           double sums added in chunk order (a re-association of double
+//           additions of float terms: exact whenever every term is a
+//           multiple of 2^-53 of the sum, and otherwise within a few double
+//           ulps, far inside one float ulp of 1 / sum).
+//
+// SYN_ORDER_SPLIT: the p.V sums split over 256-position chunks on tensor
+// cores and re-associated (about 1e-6 relative from the reference past one
+// chunk, bit-exact up to kChunk positions). Two kernels, one CTA per (chunk,
+// KV head, query); each CTA reads its chunk's K (then V) rows from HBM once,
+// for all G = n_head / n_kv query heads of the group, all requested at once.
 //   scores kernel: rotates q (and appends the new K, V rows), scores the
 //            chunk, and writes the scores and the chunk's statistics: the
 //            max m_j and the double sum s_j of expf(s - m_j), per query head;
@@ -21,13 +46,14 @@
 //            (1 / sum)) and the chunk's partial sum of p_t V_t in position
 //            order; the group's last CTA to finish adds the partials in
 //            chunk order (deterministic).
-// The split depends on the context only (fixed chunks), never on the grid
-// or the device, so any caller (a tensor-parallel rank included) splits the
-// same context the same way. A context of up to kChunk positions is one
-// chunk: every sum runs in the reference's position order.
+// Either way the split depends on the context only (fixed chunks), never on
+// the grid or the device, so any caller (a tensor-parallel rank included)
+// splits the same context the same way.
 #include "common.cuh"
 #include "internal.h"
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <array>
@@ -43,18 +69,27 @@ constexpr int kAttnThreads = 256;  // the decode kernel
 constexpr int kChunk = 256;        // positions per CTA: a context of up to kChunk is one chunk (exact order)
 static_assert(kChunk == kAttnThreads, "the p.V kernel gives each thread one position of its chunk");
 constexpr int kPwStride = kChunk + 4;  // floats per head in the p buffer: heads 4 banks apart
+constexpr int kSlotPos = 64;           // positions per slot of the exact p.V kernel's ring
+constexpr int kSlots = 16;             // slots in the ring (1024 positions in flight)
+constexpr int kXvHeads = 4;            // query heads (consumer warps) per exact p.V CTA
+constexpr uint64_t kAttnWaitNs = 2000000000ull;  // bounded waits on bulk copies give up after 2 s
+
+__device__ unsigned g_attn_timeouts = 0;  // bounded waits that gave up (syn_device_errors)
 
 struct AttnParams {
     const float *q, *k, *v;
     uint16_t *kc, *vc;
     const int32_t* pos;
     float* out;
-    float* scores;           // scratch: [n_q][n_head][max_len] scores
+    float* scores;           // scratch: [n_q][n_head][ld] scores (the exact order: then expf(s - M))
     double* st_s;            // scratch: [n_q][n_head][nch] chunk sums
     float* st_m;             // scratch: [n_q][n_head][nch] chunk maxima
     float* parts;            // scratch: [n_q][n_kv][nch][G * head_dim] chunk partials of p.V
     unsigned* ctr;           // scratch: [n_q][n_kv] arrivals of the p.V kernel's CTAs
     int nch;                 // chunks at max_len
+    int ld;                  // floats per head in the score scratch (max_len rounded up to 64)
+    int order;               // SYN_ORDER_REFERENCE / SYN_ORDER_SPLIT
+    int v3d;                 // the exact p.V kernel's V tensor map has a query dimension (cache_stride != 0)
     const float* rope_tab;   // [max_len][head_dim / 2] (cos, sin), or NULL: computed in the kernel
     size_t cache_stride;
     int n_q, n_head, n_kv, hd, max_len;
@@ -70,6 +105,7 @@ struct AttnParams {
 struct AttnScratch {
     size_t scores, st_s, st_m, parts, ctr, total;
 };
+__host__ __device__ inline int score_ld(int max_len) { return (max_len + kSlotPos - 1) / kSlotPos * kSlotPos; }
 AttnScratch scratch_layout(int n_q, int n_head, int n_kv, int hd, int max_len) {
     AttnScratch l;
     const size_t nch = size_t(max_len + kChunk - 1) / kChunk;
@@ -79,7 +115,7 @@ AttnScratch scratch_layout(int n_q, int n_head, int n_kv, int hd, int max_len) {
         off = align256(off + bytes);
         return o;
     };
-    l.scores = take(size_t(n_q) * n_head * max_len * 4);
+    l.scores = take(size_t(n_q) * n_head * score_ld(max_len) * 4);
     l.st_s = take(size_t(n_q) * n_head * nch * 8);
     l.st_m = take(size_t(n_q) * n_head * nch * 4);
     l.parts = take(size_t(n_q) * n_head * nch * hd * 4);
@@ -465,7 +501,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_scores_kernel(AttnParams a)
     }
 #pragma unroll 1
     for (int h = 0; h < G; ++h)
-        for (int t = tid; t < n; t += kAttnThreads) a.scores[(hb + h) * a.max_len + t0 + t] = sc[h * kChunk + t];
+        for (int t = tid; t < n; t += kAttnThreads) a.scores[(hb + h) * a.ld + t0 + t] = sc[h * kChunk + t];
 }
 
 // Kernel 2: p and p.V of the chunk, and the group's output.
@@ -502,7 +538,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_pv_kernel(AttnParams a) {
     float sv[GT];
 #pragma unroll
     for (int h = 0; h < GT; ++h)
-        sv[h] = h < G && tid < n ? a.scores[(hb + h) * a.max_len + t0 + tid] : 0.0f;
+        sv[h] = h < G && tid < n ? a.scores[(hb + h) * a.ld + t0 + tid] : 0.0f;
 
     // The context's max M and normaliser sum_j s_j * exp(m_j - M), one warp
     // per query head over the chunks (each lane loads its chunks' statistics
@@ -677,6 +713,431 @@ __global__ void __launch_bounds__(kAttnThreads) attn_pv_kernel(AttnParams a) {
     }
 }
 
+// ---- the reference's order at any length (SYN_ORDER_REFERENCE) ------------------
+
+// c + a * b for binary16 a, b (exact product), rounded once to float: the
+// mixed-precision fma of sm_100. Pairs: the low halves first, then the high.
+__device__ __forceinline__ float fma_hh(uint16_t a, uint16_t b, float c) {
+    asm("fma.rn.f32.f16 %0, %1, %2, %0;" : "+f"(c) : "h"(a), "h"(b));
+    return c;
+}
+__device__ __forceinline__ float fma_h2(uint32_t a2, uint32_t b2, float c) {
+    asm("{\n .reg .b16 al, ah, bl, bh;\n mov.b32 {al, ah}, %1;\n mov.b32 {bl, bh}, %2;\n"
+        " fma.rn.f32.f16 %0, al, bl, %0;\n fma.rn.f32.f16 %0, ah, bh, %0;\n}"
+        : "+f"(c)
+        : "r"(a2), "r"(b2));
+    return c;
+}
+
+// Shared memory of the exact scores kernel: cos/sin, the group's rotated q as
+// binary16, the appended K row, the chunk's K rows (pitch hd + 8 halves, so
+// consecutive threads' 16-byte reads of their rows spread over the banks).
+struct XsSmem {
+    size_t cs, qh, krh, kt, total;
+};
+__host__ __device__ inline XsSmem xs_smem(int GT, int hd) {
+    XsSmem l;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t o = off;
+        off = (off + bytes + 15) & ~size_t(15);
+        return o;
+    };
+    l.cs = take(size_t(hd) * 4);
+    l.qh = take(size_t(GT) * hd * 2);
+    l.krh = take(size_t(hd) * 2);
+    l.kt = take(size_t(kChunk) * (hd + 8) * 2);
+    l.total = off;
+    return l;
+}
+
+// Exact scores of one chunk: CTA (j, g, b), thread r = position t0 + r.
+template <int GT>
+__global__ void __launch_bounds__(kAttnThreads) attn_xs_kernel(AttnParams a) {
+    const int j = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+    const int hd = a.hd, G = a.n_head / a.n_kv, H = a.n_head;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int P = a.pos[b], L = P + 1;
+    if (P < 0 || L > a.max_len) return;
+    const int t0 = j * kChunk;
+    if (t0 >= L) return;
+    const int t1 = min(L, t0 + kChunk), n = t1 - t0;
+    const bool owns = a.append && P < t1;  // the chunk holds the appended row
+
+    extern __shared__ __align__(16) unsigned char smem[];
+    const XsSmem sl = xs_smem(GT, hd);
+    float* cs = reinterpret_cast<float*>(smem + sl.cs);
+    uint16_t* qh = reinterpret_cast<uint16_t*>(smem + sl.qh);
+    uint16_t* krh = reinterpret_cast<uint16_t*>(smem + sl.krh);
+    uint16_t* kt = reinterpret_cast<uint16_t*>(smem + sl.kt);
+    __shared__ __align__(8) uint64_t bar[kAttnThreads / 64];  // one per 64 rows
+    __shared__ float red[GT][kAttnThreads / 32];
+    __shared__ int bad;
+    const int rowh = hd + 8;
+    const size_t row = size_t(a.n_kv) * hd;
+    uint16_t* kcb = a.kc + size_t(b) * a.cache_stride;
+    uint16_t* vcb = a.vc + size_t(b) * a.cache_stride;
+    if (tid < kAttnThreads / 64) mbar_init(&bar[tid], 1);
+    if (tid == 0) bad = 0;
+    mbar_init_fence();
+    __syncthreads();
+
+    // With append, rows other than P were written by earlier calls: their
+    // copies start before the wait. Without it the caller's previous kernel
+    // may have written them (syn_rope_kv_append), so everything waits.
+    if (!a.append) pdl_wait();
+    float2 cs_v = make_float2(0.0f, 0.0f);
+    if (a.rope && a.rope_tab && tid < hd / 2)
+        cs_v = reinterpret_cast<const float2*>(a.rope_tab)[size_t(P) * (hd / 2) + tid];
+    {
+        const int r = tid, q = tid >> 6;
+        const bool copy = r < n && !(owns && t0 + r == P);
+        if ((tid & 63) == 0) {  // the quarter's bytes: its rows in the chunk, less the appended one
+            const int r0 = 64 * q, r1 = min(n, r0 + 64);
+            int rows = max(0, r1 - r0);
+            if (owns && P >= t0 + r0 && P < t0 + r1) --rows;
+            mbar_expect_tx(&bar[q], uint32_t(rows) * uint32_t(hd) * 2u);
+        }
+        if (copy)
+            bulk_copy_g2s(kt + r * rowh, kcb + size_t(t0 + r) * row + size_t(g) * hd, uint32_t(hd) * 2u, &bar[q]);
+    }
+    if (a.rope) {
+        if (a.rope_tab) {
+            for (int i = tid; i < hd / 2; i += kAttnThreads) {
+                const float2 v = i == tid ? cs_v : reinterpret_cast<const float2*>(a.rope_tab)[size_t(P) * (hd / 2) + i];
+                cs[2 * i] = v.x;
+                cs[2 * i + 1] = v.y;
+            }
+        } else {
+            for (int i = tid; i < hd / 2; i += kAttnThreads) rope_cs(a, P, i, cs[2 * i], cs[2 * i + 1]);
+        }
+    }
+    pdl_launch_dependents();
+    if (a.append) pdl_wait();  // q, k, v come from the previous kernel
+    __syncthreads();
+
+    // q of the group rotated and rounded to binary16 (attention.hpp:205-207)
+    const float* qb = a.q + (size_t(b) * H + size_t(g) * G) * hd;
+    if (a.rope) {
+        for (int i = tid; i < G * hd / 2; i += kAttnThreads) {
+            const int jh = i / (hd / 2), pi = i % (hd / 2);
+            int i0, i1;
+            pair_index(a.rope_mode, hd, pi, i0, i1);
+            float o0, o1;
+            rotate(qb[jh * hd + i0], qb[jh * hd + i1], cs[2 * pi], cs[2 * pi + 1], o0, o1);
+            qh[jh * hd + i0] = f16_bits(o0);
+            qh[jh * hd + i1] = f16_bits(o1);
+        }
+    } else {
+        for (int i = tid; i < G * hd; i += kAttnThreads) qh[i] = f16_bits(qb[i]);
+    }
+    if (owns) {  // kv_append (attention.hpp:165-175): the rotated k and v as binary16 into row P
+        const float* kb = a.k + size_t(b) * row + size_t(g) * hd;
+        const float* vb = a.v + size_t(b) * row + size_t(g) * hd;
+        uint16_t* krow = kcb + size_t(P) * row + size_t(g) * hd;
+        uint16_t* vrow = vcb + size_t(P) * row + size_t(g) * hd;
+        if (a.rope) {
+            for (int pi = tid; pi < hd / 2; pi += kAttnThreads) {
+                int i0, i1;
+                pair_index(a.rope_mode, hd, pi, i0, i1);
+                float o0, o1;
+                rotate(kb[i0], kb[i1], cs[2 * pi], cs[2 * pi + 1], o0, o1);
+                const uint16_t h0 = f16_bits(o0), h1 = f16_bits(o1);
+                krow[i0] = h0;
+                krow[i1] = h1;
+                krh[i0] = h0;
+                krh[i1] = h1;
+            }
+        } else {
+            for (int d = tid; d < hd; d += kAttnThreads) krow[d] = krh[d] = f16_bits(kb[d]);
+        }
+        for (int d = tid; d < hd; d += kAttnThreads) vrow[d] = f16_bits(vb[d]);
+    }
+    __syncthreads();
+    if (owns && tid < hd / 8)  // no copy was issued for this row
+        *reinterpret_cast<uint4*>(kt + (P - t0) * rowh + tid * 8) = *reinterpret_cast<const uint4*>(krh + tid * 8);
+    __syncthreads();
+    if (!mbar_wait_bounded(&bar[tid >> 6], 0, kAttnWaitNs)) {
+        atomicAdd(&g_attn_timeouts, 1u);
+        bad = 1;
+    }
+    __syncthreads();
+    if (bad) return;
+
+    // s_t = (q . K_t) * scale, each head's dot in dimension order (attention.hpp:214-220)
+    const size_t hb = size_t(b) * H + size_t(g) * G;
+    float acc[GT];
+#pragma unroll
+    for (int h = 0; h < GT; ++h) acc[h] = 0.0f;
+    if (tid < n) {
+        const uint4* kr = reinterpret_cast<const uint4*>(kt + tid * rowh);
+#pragma unroll 2
+        for (int d8 = 0; d8 < hd / 8; ++d8) {
+            const uint4 kv = kr[d8];
+#pragma unroll
+            for (int h = 0; h < GT; ++h) {
+                if (h < G) {
+                    const uint4 qv = reinterpret_cast<const uint4*>(qh + h * hd)[d8];
+                    float c = acc[h];
+                    c = fma_h2(qv.x, kv.x, c);
+                    c = fma_h2(qv.y, kv.y, c);
+                    c = fma_h2(qv.z, kv.z, c);
+                    c = fma_h2(qv.w, kv.w, c);
+                    acc[h] = c;
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int h = 0; h < GT; ++h) {
+        if (h < G) {
+            const float sv = __fmul_rn(acc[h], a.scale);
+            if (tid < n) a.scores[(hb + h) * a.ld + t0 + tid] = sv;
+            const float m = warp_max(tid < n ? sv : -INFINITY);
+            if (lane == 0) red[h][warp] = m;
+        }
+    }
+    __syncthreads();
+    if (tid < G) {
+        float m = -INFINITY;
+        for (int w = 0; w < kAttnThreads / 32; ++w) m = fmaxf(m, red[tid][w]);
+        a.st_m[(hb + tid) * a.nch + j] = m;
+    }
+}
+
+// e_t = expf(s_t - M) of one chunk (in place) and the chunk's double sums:
+// CTA (j, g, b), thread r = position t0 + r (elementwise.hpp:174-191).
+template <int GT>
+__global__ void __launch_bounds__(kAttnThreads) attn_xe_kernel(AttnParams a) {
+    const int j = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+    const int G = a.n_head / a.n_kv, H = a.n_head;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int P = a.pos[b], L = P + 1;
+    if (P < 0 || L > a.max_len) return;
+    const int t0 = j * kChunk;
+    if (t0 >= L) return;
+    const int n = min(L, t0 + kChunk) - t0, nchk = (L + kChunk - 1) / kChunk;
+    __shared__ float gm[GT];
+    __shared__ double red[GT][kAttnThreads / 32];
+    __shared__ float2 etab[64];
+    if (tid < 64) etab[tid] = kExp2J64[tid];
+    pdl_launch_dependents();
+    pdl_wait();  // the scores and chunk maxima
+    const size_t hb = size_t(b) * H + size_t(g) * G;
+    float sv[GT];
+#pragma unroll
+    for (int h = 0; h < GT; ++h) sv[h] = h < G && tid < n ? a.scores[(hb + h) * a.ld + t0 + tid] : 0.0f;
+    for (int h = warp; h < G; h += kAttnThreads / 32) {  // M = the largest score (exact in any order)
+        float m = -INFINITY;
+        for (int c = lane; c < nchk; c += 32) m = fmaxf(m, a.st_m[(hb + h) * a.nch + c]);
+        m = warp_max(m);
+        if (lane == 0) gm[h] = m;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int h = 0; h < GT; ++h) {
+        if (h < G) {
+            double e = 0.0;
+            if (tid < n) {
+                const float ev = exp_rn_neg(__fsub_rn(sv[h], gm[h]), etab);
+                a.scores[(hb + h) * a.ld + t0 + tid] = ev;
+                e = double(ev);
+            }
+            e = warp_sum_d(e);
+            if (lane == 0) red[h][warp] = e;
+        }
+    }
+    __syncthreads();
+    if (tid < G) {
+        double sum = 0.0;
+        for (int w = 0; w < kAttnThreads / 32; ++w) sum += red[tid][w];
+        a.st_s[(hb + tid) * a.nch + j] = sum;
+    }
+}
+
+// Shared memory of the exact p.V kernel: the ring's V tiles (64 positions x 32
+// columns of binary16), the heads' e rows of each slot, the consumers' p
+// (binary16), and the barriers.
+struct XvSmem {
+    size_t vt, es, ph, bars, total;
+};
+__host__ __device__ inline XvSmem xv_smem() {
+    XvSmem l;
+    l.vt = 0;                                                      // [kSlots][64][32] halves, 4 KB per slot
+    l.es = l.vt + size_t(kSlots) * kSlotPos * 32 * 2;              // [kSlots][4][64] floats
+    l.ph = l.es + size_t(kSlots) * kXvHeads * kSlotPos * 4;        // [4][64] halves
+    l.bars = l.ph + size_t(kXvHeads) * kSlotPos * 2;               // vfull, efull, empty: [kSlots] each
+    l.total = l.bars + size_t(3) * kSlots * 8 + 1024;  // + the alignment of the ring
+    return l;
+}
+
+__device__ __forceinline__ void tma_load_v(void* dst, const CUtensorMap* map, int x, int y, int z, bool three,
+                                           uint64_t* bar) {
+    if (three)
+        asm volatile(
+            "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+            "%4}], [%5];" ::"r"(smem_addr(dst)),
+            "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
+            : "memory");
+    else
+        asm volatile(
+            "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+            "%3}], [%4];" ::"r"(smem_addr(dst)),
+            "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+            : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// p.V in position order: CTA (g, head quad hq, 32-column slice s) of query b;
+// warps 0..nw-1 consume (warp w = query head g*G + 4*hq + w, lane = column
+// 32*s + lane), warp nw produces.
+__global__ void __launch_bounds__(32 * (kXvHeads + 1)) attn_xv_kernel(AttnParams a,
+                                                                     const __grid_constant__ CUtensorMap vmap) {
+    const int G = a.n_head / a.n_kv, H = a.n_head, hd = a.hd;
+    const int ns = (hd + 31) / 32, nq = (G + kXvHeads - 1) / kXvHeads;
+    const int s = blockIdx.x % ns, hq = (blockIdx.x / ns) % nq, g = blockIdx.x / (ns * nq), b = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nw = int(blockDim.x >> 5) - 1;          // consumer warps
+    const int nh = min(kXvHeads, G - kXvHeads * hq);  // of which hold a head
+    const int P = a.pos[b], L = P + 1;
+    if (P < 0 || L > a.max_len) return;
+    const int nslot = (L + kSlotPos - 1) / kSlotPos, nchk = (L + kChunk - 1) / kChunk;
+
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    // tensor copies land 128-byte aligned: the ring starts at the next 1 KB boundary
+    unsigned char* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    const XvSmem sl = xv_smem();
+    uint16_t* vt = reinterpret_cast<uint16_t*>(smem + sl.vt);
+    float* es = reinterpret_cast<float*>(smem + sl.es);
+    uint16_t* ph = reinterpret_cast<uint16_t*>(smem + sl.ph);
+    uint64_t* vfull = reinterpret_cast<uint64_t*>(smem + sl.bars);
+    uint64_t* efull = vfull + kSlots;
+    uint64_t* empty = efull + kSlots;
+    __shared__ int abort_flag, issued;
+    if (tid < kSlots) {
+        mbar_init(&vfull[tid], 1);
+        mbar_init(&efull[tid], 1);
+        mbar_init(&empty[tid], uint32_t(nw));
+    }
+    if (tid == 0) abort_flag = issued = 0;
+    mbar_init_fence();
+    __syncthreads();
+
+    const size_t hb = size_t(b) * H + size_t(g) * G + size_t(kXvHeads) * hq;  // this CTA's first query head
+    const int vx = g * hd + 32 * s, vz = a.v3d ? b : 0;
+    const bool producer = warp == nw;
+    auto issue_v = [&](int k) {
+        uint64_t* bar = &vfull[k % kSlots];
+        mbar_expect_tx(bar, uint32_t(kSlotPos) * 32u * 2u);
+        tma_load_v(vt + size_t(k % kSlots) * kSlotPos * 32, &vmap, vx, k * kSlotPos, vz, a.v3d != 0, bar);
+    };
+    auto issue_e = [&](int k) {
+        uint64_t* bar = &efull[k % kSlots];
+        mbar_expect_tx(bar, uint32_t(nh) * kSlotPos * 4u);
+        for (int h = 0; h < nh; ++h)
+            bulk_copy_g2s(es + (size_t(k % kSlots) * kXvHeads + h) * kSlotPos,
+                          a.scores + (hb + h) * a.ld + size_t(k) * kSlotPos, kSlotPos * 4u, bar);
+    };
+    // V rows below P were written by earlier calls: their tiles start before the wait
+    const int first = min(kSlots, nslot);
+    if (producer && lane == 0)
+        for (int k = 0; k < first; ++k)
+            if ((k + 1) * kSlotPos <= P) issue_v(k);
+    pdl_launch_dependents();
+    pdl_wait();  // e, the chunk sums and the appended V row
+
+    if (producer) {
+        if (lane == 0) {
+            int k = 0;
+            for (; k < first; ++k) {
+                if ((k + 1) * kSlotPos > P) issue_v(k);
+                issue_e(k);
+            }
+            for (; k < nslot; ++k) {
+                const int slot = k % kSlots;
+                if (!mbar_wait_bounded(&empty[slot], uint32_t((k / kSlots - 1) & 1), kAttnWaitNs) ||
+                    *reinterpret_cast<volatile int*>(&abort_flag)) {
+                    if (!*reinterpret_cast<volatile int*>(&abort_flag)) atomicAdd(&g_attn_timeouts, 1u);
+                    atomicExch(&abort_flag, 1);
+                    break;
+                }
+                issue_v(k);
+                issue_e(k);
+            }
+            issued = k;
+        }
+    } else {
+        const int w = warp;
+        const bool active = w < nh;
+        // the normaliser: the chunks' double sums in chunk order; scale = float(1 / sum) (elementwise.hpp:192-193)
+        float scale = 0.0f;
+        if (active && lane == 0) {
+            double sum = 0.0;
+            for (int c = 0; c < nchk; ++c) sum += a.st_s[(hb + w) * a.nch + c];
+            scale = float(1.0 / sum);
+        }
+        scale = __shfl_sync(0xffffffffu, scale, 0);
+        uint16_t* pw = ph + size_t(w) * kSlotPos;
+        float acc = 0.0f;
+        for (int k = 0; k < nslot; ++k) {
+            const int slot = k % kSlots;
+            const uint32_t par = uint32_t((k / kSlots) & 1);
+            const int n = min(kSlotPos, L - k * kSlotPos);
+            bool ok = mbar_wait_bounded(&efull[slot], par, kAttnWaitNs);
+            ok = ok && mbar_wait_bounded(&vfull[slot], par, kAttnWaitNs);
+            if (!__all_sync(0xffffffffu, ok) || *reinterpret_cast<volatile int*>(&abort_flag)) {
+                if (lane == 0 && !*reinterpret_cast<volatile int*>(&abort_flag)) {
+                    atomicAdd(&g_attn_timeouts, 1u);
+                    atomicExch(&abort_flag, 1);
+                }
+                break;
+            }
+            if (active) {
+                // p_t = binary16(e_t * scale) of positions 2 lane, 2 lane + 1 (attention.hpp:224-227)
+                const float2 e2 = reinterpret_cast<const float2*>(es + (size_t(slot) * kXvHeads + w) * kSlotPos)[lane];
+                const uint16_t p0 = 2 * lane < n ? f16_bits(__fmul_rn(e2.x, scale)) : uint16_t(0);
+                const uint16_t p1 = 2 * lane + 1 < n ? f16_bits(__fmul_rn(e2.y, scale)) : uint16_t(0);
+                reinterpret_cast<uint32_t*>(pw)[lane] = uint32_t(p0) | (uint32_t(p1) << 16);
+                __syncwarp();
+                // out_d += p_t * V_t,d for t in order (attention.hpp:231-243)
+                const uint16_t* vcol = vt + size_t(slot) * kSlotPos * 32 + lane;
+                if (n == kSlotPos) {
+#pragma unroll
+                    for (int t8 = 0; t8 < kSlotPos / 8; ++t8) {
+                        const uint4 p8 = reinterpret_cast<const uint4*>(pw)[t8];
+                        const uint32_t pp[4] = {p8.x, p8.y, p8.z, p8.w};
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            acc = fma_hh(uint16_t(pp[u] & 0xffffu), vcol[(8 * t8 + 2 * u) * 32], acc);
+                            acc = fma_hh(uint16_t(pp[u] >> 16), vcol[(8 * t8 + 2 * u + 1) * 32], acc);
+                        }
+                    }
+                } else {
+                    for (int t = 0; t < n; ++t) acc = fma_hh(pw[t], vcol[t * 32], acc);
+                }
+                __syncwarp();
+            }
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+        const int d = 32 * s + lane;
+        if (active && d < hd && !*reinterpret_cast<volatile int*>(&abort_flag)) {
+            const size_t o = (hb + w) * hd + d;
+            if (a.tp.peers) tp_store(a.tp, o, acc, *reinterpret_cast<const volatile unsigned*>(a.tp.epoch));
+            else a.out[o] = acc;
+        }
+    }
+    // A CTA that gave up lets its copies still in flight land before it leaves (bounded).
+    __syncthreads();
+    if (abort_flag && tid == 0) {
+        for (int k = max(0, issued - kSlots); k < issued; ++k) {
+            mbar_wait_bounded(&vfull[k % kSlots], uint32_t((k / kSlots) & 1), kAttnWaitNs);
+            mbar_wait_bounded(&efull[k % kSlots], uint32_t((k / kSlots) & 1), kAttnWaitNs);
+        }
+    }
+}
+
 // RoPE of k and F16 append of (k, v) at row pos[b], one CTA per token.
 __global__ void __launch_bounds__(kThreads) rope_append_kernel(AttnParams a) {
     pdl_launch_dependents();
@@ -759,6 +1220,7 @@ AttnParams make_params(const syn_attention_args* x) {
     a.theta_scale = x->theta_scale; a.scale = x->scale;
     a.ff = x->freq_factors;
     a.rope_tab = x->rope_table;
+    a.order = x->order;
     a.has_yarn = x->yarn != nullptr;
     for (int i = 0; i < 5; ++i) a.yarn[i] = x->yarn ? x->yarn[i] : 0.0f;
     return a;
@@ -775,6 +1237,7 @@ int check_args(const syn_attention_args* x, bool need_scratch) {
         return SYN_ERR_INVALID;
     if (x->cache_stride % 8) return SYN_ERR_INVALID;  // rows stay 16-byte aligned
     if (reinterpret_cast<uintptr_t>(x->rope_table) & 7) return SYN_ERR_INVALID;
+    if (x->order != SYN_ORDER_REFERENCE && x->order != SYN_ORDER_SPLIT) return SYN_ERR_INVALID;
     return SYN_OK;
 }
 
@@ -795,8 +1258,47 @@ int opt_in(const void* kernel, size_t most) {
     return st;
 }
 
-// The two kernels of a call over grid (chunks at max_len, n_kv, n_q): a CTA
-// whose chunk starts past its query's context leaves at once.
+// cuTensorMapEncodeTiled from the driver (looked up once; no libcuda link).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        else
+            cudaGetLastError();
+    });
+    return fn;
+}
+
+// The V cache as a tensor of binary16: x = column (n_kv * head_dim), y = position
+// (max_len rows), z = query (cache_stride apart; absent when the queries share
+// one cache); boxes of 32 columns x kSlotPos positions.
+int v_tensor_map(const AttnParams& a, CUtensorMap* m) {
+    const auto encode = tensor_map_encoder();
+    if (!encode) {
+        syn_set_error("cuTensorMapEncodeTiled is not available from the driver");
+        return SYN_ERR_CUDA;
+    }
+    const cuuint64_t dims[3] = {cuuint64_t(a.n_kv) * a.hd, cuuint64_t(a.max_len), cuuint64_t(a.n_q)};
+    const cuuint64_t strides[2] = {cuuint64_t(a.n_kv) * a.hd * 2, cuuint64_t(a.cache_stride) * 2};
+    const cuuint32_t box[3] = {32, kSlotPos, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, a.v3d ? 3 : 2, a.vc, dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        syn_set_error("cuTensorMapEncodeTiled rejected the V cache geometry");
+        return SYN_ERR_INVALID;
+    }
+    return SYN_OK;
+}
+
+// The kernels of a call over grid (chunks at max_len, n_kv, n_q): a CTA whose
+// chunk starts past its query's context leaves at once.
 template <int GT>
 int launch_attention(AttnParams a, void* scratch, cudaStream_t s) {
     const AttnScratch l = scratch_layout(a.n_q, a.n_head, a.n_kv, a.hd, a.max_len);
@@ -807,16 +1309,41 @@ int launch_attention(AttnParams a, void* scratch, cudaStream_t s) {
     a.parts = reinterpret_cast<float*>(base + l.parts);
     a.ctr = reinterpret_cast<unsigned*>(base + l.ctr);
     a.nch = (a.max_len + kChunk - 1) / kChunk;
-    int st = opt_in(reinterpret_cast<const void*>(attn_scores_kernel<GT>), score_smem(GT, 256).total);
-    if (!st) st = opt_in(reinterpret_cast<const void*>(attn_pv_kernel<GT>), pv_smem(GT, 256).total);
-    if (st) return st;
+    a.ld = score_ld(a.max_len);
     const dim3 grid(a.nch, a.n_kv, a.n_q);
-    st = syn_launch(attn_scores_kernel<GT>, grid, kAttnThreads, score_smem(GT, a.hd).total, s, a);
-    if (!st) st = syn_launch(attn_pv_kernel<GT>, grid, kAttnThreads, pv_smem(GT, a.hd).total, s, a);
+    int st;
+    if (a.order == SYN_ORDER_SPLIT) {
+        st = opt_in(reinterpret_cast<const void*>(attn_scores_kernel<GT>), score_smem(GT, 256).total);
+        if (!st) st = opt_in(reinterpret_cast<const void*>(attn_pv_kernel<GT>), pv_smem(GT, 256).total);
+        if (st) return st;
+        st = syn_launch(attn_scores_kernel<GT>, grid, kAttnThreads, score_smem(GT, a.hd).total, s, a);
+        if (!st) st = syn_launch(attn_pv_kernel<GT>, grid, kAttnThreads, pv_smem(GT, a.hd).total, s, a);
+        return st;
+    }
+    st = opt_in(reinterpret_cast<const void*>(attn_xs_kernel<GT>), xs_smem(GT, 256).total);
+    if (!st) st = opt_in(reinterpret_cast<const void*>(attn_xv_kernel), xv_smem().total);
+    if (st) return st;
+    a.v3d = a.cache_stride != 0;
+    CUtensorMap vmap;
+    if ((st = v_tensor_map(a, &vmap))) return st;
+    const int G = a.n_head / a.n_kv, nw = std::min(kXvHeads, G);
+    const int ns = (a.hd + 31) / 32, nq = (G + kXvHeads - 1) / kXvHeads;
+    st = syn_launch(attn_xs_kernel<GT>, grid, kAttnThreads, xs_smem(GT, a.hd).total, s, a);
+    if (!st) st = syn_launch(attn_xe_kernel<GT>, grid, kAttnThreads, 0, s, a);
+    if (!st)
+        st = syn_launch(attn_xv_kernel, dim3(unsigned(a.n_kv * nq * ns), unsigned(a.n_q)), unsigned(32 * (nw + 1)),
+                        xv_smem().total, s, a, vmap);
     return st;
 }
 
 }  // namespace
+
+// Bounded waits of the attention kernels that gave up on this device (syn_device_errors).
+int syn_attn_timeouts() {
+    unsigned n = 0;
+    if (cudaMemcpyFromSymbol(&n, g_attn_timeouts, sizeof n) != cudaSuccess) return -1;
+    return int(n);
+}
 
 extern "C" size_t syn_attention_scratch_bytes(int n_q, int n_head, int n_kv, int head_dim, int max_len) {
     if (n_q <= 0 || n_head <= 0 || n_kv <= 0 || head_dim <= 0 || max_len <= 0) return 0;

@@ -1030,7 +1030,8 @@ extern "C" int syn_gemv(const syn_gemv_args* a, void* stream) {
 extern "C" int syn_device_errors(void) {
     unsigned n = 0;
     if (cudaMemcpyFromSymbol(&n, g_gemv_timeouts, sizeof n) != cudaSuccess) return -1;
-    return int(n);
+    const int a = syn_attn_timeouts();
+    return a < 0 ? -1 : int(n) + a;
 }
 
 extern "C" int syn_gemv_f(int type, const void* w, int rows, int cols, const float* x, int n_tok, float* y,

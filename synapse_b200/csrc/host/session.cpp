@@ -115,6 +115,7 @@ struct syn_session {
     std::vector<op> ops;
     int logits_t = -1;
     float theta_scale = 0, scale = 0;
+    int attn_order = SYN_ORDER_REFERENCE;  // SYN_ATTN_ORDER=split: the split p.V sums
     // host side
     int32_t* h_io = nullptr;   // pinned: token, pos
     float* h_logits = nullptr; // pinned
@@ -546,6 +547,7 @@ int enqueue_ops(syn_session& s, cudaStream_t st) {
             a.scale = s.scale;
             a.freq_factors = s.has_ff ? s.at<float>(s.ff_off) : nullptr;
             a.rope_table = s.at<float>(s.rope_tab_off);
+            a.order = s.attn_order;
             rc = s.p2p && o.out_words ? syn_attention_tp(&a, tp_sync(s, o), st) : syn_attention(&a, st);
             break;
         }
@@ -633,6 +635,7 @@ int finish(syn_session& s, layout_builder& lb) {
     s.rope_tab_off = lb.take(size_t(s.max_ctx) * c.head_dim * 4);
     if (s.n_gathers) s.tp_off = lb.take(128);  // peers[8], epoch at +64, wait errors at +68
     s.arena_bytes = lb.off;
+    if (const char* e = std::getenv("SYN_ATTN_ORDER")) s.attn_order = std::strcmp(e, "split") == 0 ? SYN_ORDER_SPLIT : SYN_ORDER_REFERENCE;
     s.theta_scale = std::pow(c.rope_base, -2.0f / float(c.head_dim));  // attention.hpp:47
     s.scale = 1.0f / std::sqrt(float(c.head_dim));                      // llama.hpp:407
     if ((rc = cuda(cudaSetDevice(s.device)))) return rc;

@@ -89,6 +89,9 @@ int syn_argmax_ws_tp(const void* words, int n, int32_t* out, float* plain, void*
 // The step's first launch under peer gathers: epoch += 1.
 int syn_tp_step_begin(unsigned* epoch, cudaStream_t s);
 
+// Bounded waits of the attention kernels that gave up on the current device (-1: unreadable).
+int syn_attn_timeouts();
+
 // Self-check of the library's expf (exp_rn): y = exp_rn(x) and, for
 // comparison, y_ref = exp(double(x)) rounded to float, for n device floats.
 extern "C" int syn_check_exp(const float* x, float* y, float* y_ref, int n, void* stream);

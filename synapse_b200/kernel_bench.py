@@ -15,9 +15,9 @@ load: a Llama-3-8B-shaped Q4_0 GGUF (Q8_0 head; 5.0 GB of tensor bytes with
 valid block scales) written to DIR, then opened with syn_session_open_gguf
 twice (the file is in the page cache both times); GB/s = tensor bytes over
 the open time, beside the pinned host-to-device copy rate of this box.
-attention: the fused RoPE + F16 append + split-KV attention (syn_attention)
-with H 32 / KV 8 / hd 128, theta 500000, caches of N(0,1) F16 at context L,
-batch 1/8/32.
+attention: the fused RoPE + F16 append + attention (syn_attention) in either
+summation order (--order), with H 32 / KV 8 / hd 128, theta 500000, caches of
+N(0,1) F16 at context L, batch 1/8/32.
 Each line: JSON with the average CUDA-event time per launch, the algorithmic
 bytes per launch and GB/s. Launches are captured with programmatic dependent
 launch as in the session's graphs (--no-pdl: without).
@@ -230,7 +230,7 @@ def bench_load(directory=None, opens=2):
             "pinned_h2d_GBps": round(h2d, 1), "host_threads": os.cpu_count()}
 
 
-def bench_attention(ctx, batch, iters=20, n_head=32, n_kv=8, hd=128):
+def bench_attention(ctx, batch, iters=20, n_head=32, n_kv=8, hd=128, order=0):
     import torch
     row = n_kv * hd
     per_seq = ctx * row
@@ -249,12 +249,13 @@ def bench_attention(ctx, batch, iters=20, n_head=32, n_kv=8, hd=128):
     scratch = empty_bytes(attention_scratch_bytes(batch, n_head, n_kv, hd, ctx))
     tab = rope_table(ctx, hd, ts)
     run = lambda i: attention(q, k, v, kcs[i % copies], vcs[i % copies], pos, n_head, n_kv, hd, ctx, ts, scale,
-                              cache_stride=per_seq, out=out, scratch=scratch, rope_table=tab)
+                              cache_stride=per_seq, out=out, scratch=scratch, rope_table=tab, order=order)
     for i in range(2 * copies):
         run(i)
     ms = _graph_time(run, iters)
     alg = batch * (2 * ctx * row * 2 + n_head * hd * 8 + 2 * row * 4)
-    return {"kernel": "attention", "ctx": ctx, "batch": batch, "heads": f"{n_head}/{n_kv}x{hd}",
+    return {"kernel": "attention", "order": ["reference", "split"][order], "ctx": ctx, "batch": batch,
+            "heads": f"{n_head}/{n_kv}x{hd}",
             "us_per_launch": round(ms * 1e3, 3), "bytes_per_launch": alg, "GBps": round(alg / (ms * 1e-3) / 1e9, 1),
             "rotating_copies": copies}
 
@@ -270,6 +271,8 @@ def main():
     p.add_argument("--ctx", type=int, default=None)
     p.add_argument("--iters", type=int, default=None)
     p.add_argument("--no-pdl", action="store_true", help="capture without programmatic dependent launch")
+    p.add_argument("--order", default="both", choices=["reference", "split", "both"],
+                   help="attention: the summation order (syn_attention_args.order)")
     p.add_argument("--mode", default="q8", choices=["q8", "f32", "rmsnorm", "silu", "step"],
                    help="gemv input/output fusion; step: the four fused GEMVs of an 8B layer")
     a = p.parse_args()
@@ -298,7 +301,8 @@ def main():
     if a.what in ("attention", "all"):
         for L in ([a.ctx] if a.ctx else [1024, 4096, 16384, 32768]):
             for b in ([a.batch] if a.batch else [1, 8, 32]):
-                print(json.dumps(bench_attention(L, b, a.iters or 20)), flush=True)
+                for o in ({"reference": [0], "split": [1], "both": [0, 1]}[a.order]):
+                    print(json.dumps(bench_attention(L, b, a.iters or 20, order=o)), flush=True)
 
 
 if __name__ == "__main__":

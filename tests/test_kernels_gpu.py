@@ -251,49 +251,100 @@ def assert_f16_rows_close(got, want):
     assert np.count_nonzero(diff) <= max(2, diff.size // 1000), np.count_nonzero(diff)
 
 
-def attention_case(n_head, n_kv, hd, L, n_q, seed, base=10000.0, freq_factors=None, fill=True):
-    """Caches filled with N(0,1) F16 rows 0..L-2 per query, then one fused step at pos = L-1."""
+def fill_f16(rng, shape):
+    """N(0, 1) values as binary16 bits, made a row block at a time (bounded host memory)."""
+    out = np.empty(shape, np.uint16)
+    flat = out.reshape(-1)
+    step = 1 << 24
+    for i in range(0, flat.size, step):
+        n = min(step, flat.size - i)
+        flat[i:i + n] = rng.standard_normal(n, dtype=np.float32).astype(np.float16).view(np.uint16)
+    return out
+
+
+def attention_case(n_head, n_kv, hd, L, n_q, seed, base=10000.0, freq_factors=None, fill=True,
+                   order=0, rope=True):
+    """Caches filled with N(0,1) F16 rows 0..L-2 per query, then one fused step at pos = L-1.
+
+    rope=True: the kernel rotates q and k (its cos/sin may differ from the C runtime's by an ulp, so the
+    check is a tolerance); rope=False: q and k arrive rotated by the oracle, so both sides hold the same
+    binary16 inputs and the reference order must give the oracle's bits exactly."""
     rng = np.random.default_rng(seed)
     max_ctx = L
     row = n_kv * hd
     kc = np.zeros((n_q, max_ctx * row), np.uint16)
     vc = np.zeros((n_q, max_ctx * row), np.uint16)
     if fill and L > 1:
-        kc[:, :(L - 1) * row] = rng.standard_normal((n_q, (L - 1) * row), dtype=np.float32).astype(np.float16).view(np.uint16)
-        vc[:, :(L - 1) * row] = rng.standard_normal((n_q, (L - 1) * row), dtype=np.float32).astype(np.float16).view(np.uint16)
+        for b in range(n_q):
+            kc[b, :(L - 1) * row] = fill_f16(rng, (L - 1) * row)
+            vc[b, :(L - 1) * row] = fill_f16(rng, (L - 1) * row)
     q = rng.standard_normal((n_q, n_head * hd), dtype=np.float32)
     k = rng.standard_normal((n_q, row), dtype=np.float32)
     v = rng.standard_normal((n_q, row), dtype=np.float32)
     pos = np.full(n_q, L - 1, np.int32)
     ts = orc.rope_theta_scale(base, hd)
     scale = np.float32(1.0) / np.float32(math.sqrt(hd))
+    qr = np.stack([orc.rope(q[b], hd, L - 1, ts, freq_factors) for b in range(n_q)])
+    kr = np.stack([orc.rope(k[b], hd, L - 1, ts, freq_factors) for b in range(n_q)])
     kcd, vcd = dev(kc), dev(vc)
     ffd = dev(np.asarray(freq_factors, np.float32)) if freq_factors is not None else None
-    out = syn.attention(dev(q), dev(k), dev(v), kcd, vcd, dev(pos), n_head, n_kv, hd, max_ctx, ts, float(scale),
-                        cache_stride=max_ctx * row, freq_factors=ffd).cpu().numpy()
+    out = syn.attention(dev(q if rope else qr), dev(k if rope else kr), dev(v), kcd, vcd, dev(pos), n_head, n_kv,
+                        hd, max_ctx, ts, float(scale), cache_stride=max_ctx * row, freq_factors=ffd, rope=rope,
+                        order=order).cpu().numpy()
     kc_after, vc_after = kcd.cpu().numpy(), vcd.cpu().numpy()
     for b in range(n_q):
-        qr = orc.rope(q[b], hd, L - 1, ts, freq_factors)
-        kr = orc.rope(k[b], hd, L - 1, ts, freq_factors)
-        kref, vref = kc[b].copy(), vc[b].copy()
-        ref = orc.attention(qr, kr, v[b], kref, vref, max_ctx, n_kv, hd, L - 1, n_head, scale)
-        assert_f16_rows_close(kc_after[b], kref)  # rotated: cos/sin may differ from the C runtime by an ulp
+        kref, vref = kc[b], vc[b]  # the oracle appends into the host copies
+        ref = orc.attention(qr[b], kr[b], v[b], kref, vref, max_ctx, n_kv, hd, L - 1, n_head, scale)
+        if rope:
+            assert_f16_rows_close(kc_after[b], kref)  # rotated: cos/sin may differ from the C runtime by an ulp
+        else:
+            assert np.array_equal(kc_after[b], kref), "K row appended bit-exactly"
         assert np.array_equal(vc_after[b], vref), "V row appended bit-exactly"
         err = rel_l2(out[b], ref)
-        assert err < 1e-3, (b, err)
-        assert err < 1e-4, (b, err)  # scores exact; p.V re-associated across splits
+        assert err < 1e-3, (b, err)  # the north star's bound
+        if order == syn.ORDER_REFERENCE and not rope:
+            assert np.array_equal(out[b].view(np.uint32), ref.view(np.uint32)), (b, err)
+        else:
+            assert err < 1e-4, (b, err)
     return out
 
 
-@pytest.mark.parametrize("n_head,n_kv,hd", [(32, 8, 128), (6, 6, 48), (4, 2, 16), (64, 8, 128), (8, 2, 32)])
-@pytest.mark.parametrize("L", [1, 2, 33, 256, 257, 287, 1000])
-def test_attention_small(n_head, n_kv, hd, L):
-    attention_case(n_head, n_kv, hd, L, 1, seed=L * 13 + hd + n_head)
+SMALL_SHAPES = [(32, 8, 128), (6, 6, 48), (4, 2, 16), (64, 8, 128), (8, 2, 32)]
+SMALL_L = [1, 2, 33, 63, 64, 65, 256, 257, 287, 1000, 1025]
 
 
-@pytest.mark.parametrize("L,n_q", [(1024, 8), (4096, 1), (4096, 3), (16384, 1), (32768, 1)])
-def test_attention_microbench_shapes(L, n_q):
-    attention_case(32, 8, 128, L, n_q, seed=L + n_q, base=500000.0)
+@pytest.mark.parametrize("n_head,n_kv,hd", SMALL_SHAPES)
+@pytest.mark.parametrize("L", SMALL_L)
+def test_attention_reference_order_bit_exact(n_head, n_kv, hd, L):
+    # attention.hpp:185-244 in its own summation order at every length: the oracle's bits
+    attention_case(n_head, n_kv, hd, L, 1, seed=L * 13 + hd + n_head, rope=False, order=syn.ORDER_REFERENCE)
+
+
+@pytest.mark.parametrize("order", [0, 1])
+@pytest.mark.parametrize("n_head,n_kv,hd", SMALL_SHAPES)
+@pytest.mark.parametrize("L", SMALL_L)
+def test_attention_small(n_head, n_kv, hd, L, order):
+    attention_case(n_head, n_kv, hd, L, 1, seed=L * 13 + hd + n_head + 7, order=order)
+
+
+# BASELINE config 3: 32 query / 8 KV heads of 128, theta 500000, contexts 1k-32k, batch 1, 8 and 32
+CONFIG3 = [(1024, 1), (1024, 8), (1024, 32), (4096, 1), (4096, 3), (4096, 8), (4096, 32), (16384, 1), (16384, 8),
+           (32768, 1), (32768, 8)]
+
+
+@pytest.mark.parametrize("L,n_q", CONFIG3)
+def test_attention_config3_reference_order(L, n_q):
+    attention_case(32, 8, 128, L, n_q, seed=L + n_q, base=500000.0, rope=False, order=syn.ORDER_REFERENCE)
+
+
+@pytest.mark.parametrize("L,n_q", [(1024, 8), (4096, 1), (4096, 32), (16384, 1), (32768, 8)])
+def test_attention_config3_split_order(L, n_q):
+    attention_case(32, 8, 128, L, n_q, seed=L + n_q + 1, base=500000.0, order=syn.ORDER_SPLIT)
+
+
+def test_attention_rope_in_kernel_reference_order():
+    # the kernel's own rotation at 4k context (the session's path): within 1e-4 of the oracle
+    attention_case(32, 8, 128, 4096, 2, seed=77, base=500000.0, rope=True, order=syn.ORDER_REFERENCE)
 
 
 def test_attention_pos0_is_v():
