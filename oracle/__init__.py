@@ -56,6 +56,7 @@ def lib():
         L.orc_attention.argtypes = [vp, vp, vp, vp, vp, sz, sz, sz, ctypes.c_uint32, sz, ctypes.c_float, vp, vp]
         L.orc_attend_group.argtypes = [vp, vp, vp, sz, sz, sz, ctypes.c_uint32, sz, ctypes.c_float, vp, vp, sz]
         L.orc_softmax.argtypes = [vp, vp, sz]
+        L.orc_expf.argtypes = [vp, vp, sz]
         L.orc_rms_norm.argtypes = [vp, vp, ctypes.c_float, vp, sz]
         for name in ("orc_silu",):
             getattr(L, name).argtypes = [vp, vp, sz]
@@ -291,6 +292,14 @@ def silu(x):
     x = np.ascontiguousarray(x, dtype=np.float32)
     out = np.empty_like(x)
     lib().orc_silu(_p(x), _p(out), x.size)
+    return out
+
+
+def expf(x):
+    """The host C library's expf on each element (what the reference's std::exp on float gives)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty_like(x)
+    lib().orc_expf(_p(x), _p(out), x.size)
     return out
 
 

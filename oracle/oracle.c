@@ -521,6 +521,12 @@ size_t orc_attention_group_floats(size_t n_heads, size_t n_kv, size_t head_dim, 
     return n_heads / n_kv * (max_ctx + head_dim); /* attention.hpp:147-152 */
 }
 
+/* std::exp on float as the reference calls it (elementwise.hpp:79, :188): the
+ * host C library's expf, element by element. */
+void orc_expf(const float* x, float* y, size_t n) {
+    for (size_t i = 0; i < n; ++i) y[i] = expf(x[i]);
+}
+
 /* ---- kernels/elementwise.hpp:174-201: softmax (float exp, double sum) ---- */
 void orc_softmax(const float* x, float* out, size_t n) {
     float mx = x[0];

@@ -87,6 +87,7 @@ void orc_attention(const float* q, const float* k, const float* v, uint16_t* kc,
                    float* scratch);
 
 /* kernels/elementwise.hpp */
+void orc_expf(const float* x, float* y, size_t n);
 void orc_softmax(const float* x, float* out, size_t n);
 void orc_rms_norm(const float* x, const float* gamma, float eps, float* out, size_t n);
 void orc_silu(const float* x, float* out, size_t n);

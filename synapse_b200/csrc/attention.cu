@@ -49,6 +49,7 @@
 // Either way the split depends on the context only (fixed chunks), never on
 // the grid or the device, so any caller (a tensor-parallel rank included)
 // splits the same context the same way.
+#define SYN_DEVICE_EXPF  // softmax / silu: the device expf and its exception table
 #include "common.cuh"
 #include "internal.h"
 

@@ -10,6 +10,7 @@
 #include <stdint.h>
 
 #include "../../include/synapse_b200.h"
+#include "exp_table.h"
 #include "internal.h"
 
 namespace syn {
@@ -102,48 +103,40 @@ __device__ __forceinline__ Q8Lane quantize_q8_lane(float x) {
     return r;
 }
 
-// expf rounded once (elementwise.hpp:180 calls std::exp on float): a
-// table-driven evaluation in float-float arithmetic (Tang's method: x = (64 e
-// + j) ln2/64 + r, exp(x) = 2^e 2^(j/64) exp(r), |r| <= ln2/128) accurate to
-// about 2^-44 relative, then one rounding to float. It agrees with the
-// correctly rounded result except within 2^-20 ulp of a rounding midpoint,
-// i.e. as a correctly rounded C runtime expf does. Subnormal results, where
-// the final scaling would round a second time, come from double precision.
+// expf as the reference computes it (elementwise.hpp:79, :188 call std::exp
+// on float, i.e. the host C library's expf). The evaluation is table-driven
+// in float-float arithmetic (Tang's method: x = (64 e + j) ln2/64 + r, exp(x) =
+// 2^e 2^(j/64) exp(r), |r| <= ln2/128), accurate to about 2^-44 relative, then
+// rounded once to float: the correctly rounded result except within 2^-20 ulp
+// of a rounding midpoint. The host library is not correctly rounded everywhere
+// (glibc's expf: 0.502 ulp); on the inputs where it returns the other
+// neighbour, all within 0.002 ulp of a midpoint, the result follows it: a
+// result that lies within 0.004 ulp of a midpoint looks its input up in the
+// table of those inputs (g_expf_exc, made at build time by
+// libm_expf_scan.c from the host library over every float in [-40, 88.72]).
+// Subnormal results, where the final scaling would round a second time, come
+// from double precision.
 // Table: 2^(j/64) split into a float and the float nearest the remainder,
 // from the double 2^(j/64).
-__device__ const float2 kExp2J64[64] = {
-    {0x1.p+0f, 0.0f}, {0x1.02c9a4p+0f, -0x1.887fa0p-28f},
-    {0x1.059b0ep+0f, -0x1.9d4f52p-25f}, {0x1.087452p+0f, -0x1.e2990ep-26f},
-    {0x1.0b5586p+0f, 0x1.9f3122p-25f}, {0x1.0e3ec4p+0f, -0x1.a585ccp-25f},
-    {0x1.11301ep+0f, -0x1.fdb496p-25f}, {0x1.1429aap+0f, 0x1.d525bcp-25f},
-    {0x1.172b84p+0f, -0x1.c15742p-27f}, {0x1.1a35bep+0f, 0x1.6df96ep-25f},
-    {0x1.1d4874p+0f, -0x1.d2e8cap-25f}, {0x1.2063b8p+0f, 0x1.0c519ap-25f},
-    {0x1.2387a6p+0f, 0x1.ceac48p-25f}, {0x1.26b456p+0f, 0x1.789f38p-26f},
-    {0x1.29e9e0p+0f, -0x1.5c0424p-25f}, {0x1.2d285ap+0f, 0x1.b900c2p-26f},
-    {0x1.306fe0p+0f, 0x1.4636e2p-25f}, {0x1.33c08cp+0f, -0x1.b37d20p-25f},
-    {0x1.371a74p+0f, -0x1.18aac6p-25f}, {0x1.3a7db4p+0f, -0x1.634c02p-25f},
-    {0x1.3dea64p+0f, 0x1.824684p-25f}, {0x1.4160a2p+0f, 0x1.f72e2ap-28f},
-    {0x1.44e086p+0f, 0x1.8624b4p-30f}, {0x1.486a2cp+0f, -0x1.47d866p-25f},
-    {0x1.4bfdaep+0f, -0x1.593abcp-25f}, {0x1.4f9b28p+0f, -0x1.2c5a6cp-25f},
-    {0x1.5342b6p+0f, -0x1.2c5610p-25f}, {0x1.56f474p+0f, -0x1.295b04p-25f},
-    {0x1.5ab07ep+0f, -0x1.5bd5ecp-27f}, {0x1.5e76f2p+0f, -0x1.4a5bd8p-25f},
-    {0x1.6247ecp+0f, -0x1.f8b550p-25f}, {0x1.662388p+0f, 0x1.2a9112p-27f},
-    {0x1.6a09e6p+0f, 0x1.9fcef4p-26f}, {0x1.6dfb24p+0f, -0x1.cd72e8p-27f},
-    {0x1.71f75ep+0f, 0x1.1d8beep-25f}, {0x1.75feb6p+0f, -0x1.37b306p-25f},
-    {0x1.7a1148p+0f, -0x1.829fd0p-25f}, {0x1.7e2f34p+0f, -0x1.261634p-25f},
-    {0x1.82589ap+0f, -0x1.accc7cp-26f}, {0x1.868d9ap+0f, -0x1.2edb44p-26f},
-    {0x1.8ace54p+0f, 0x1.15506ep-27f}, {0x1.8f1aeap+0f, -0x1.baa232p-26f},
-    {0x1.93737cp+0f, -0x1.e64744p-25f}, {0x1.97d82ap+0f, -0x1.0d8d80p-31f},
-    {0x1.9c4918p+0f, 0x1.51f848p-27f}, {0x1.a0c668p+0f, -0x1.2886a6p-26f},
-    {0x1.a5503cp+0f, -0x1.b83b54p-25f}, {0x1.a9e6b6p+0f, -0x1.50c048p-25f},
-    {0x1.ae89fap+0f, -0x1.a94b14p-26f}, {0x1.b33a2cp+0f, -0x1.ec3a82p-26f},
-    {0x1.b7f770p+0f, -0x1.a09438p-25f}, {0x1.bcc1eap+0f, -0x1.f687c6p-25f},
-    {0x1.c199bep+0f, -0x1.3d56b2p-27f}, {0x1.c67f12p+0f, 0x1.cafa2ap-25f},
-    {0x1.cb720ep+0f, -0x1.8837ccp-27f}, {0x1.d072d4p+0f, 0x1.40f130p-25f},
-    {0x1.d5818ep+0f, -0x1.822dbcp-27f}, {0x1.da9e60p+0f, 0x1.ed9942p-27f},
-    {0x1.dfc974p+0f, -0x1.908c94p-25f}, {0x1.e502eep+0f, 0x1.e2cffep-26f},
-    {0x1.ea4afap+0f, 0x1.52486cp-27f}, {0x1.efa1bep+0f, 0x1.cc2b44p-25f},
-    {0x1.f50766p+0f, -0x1.246eb0p-26f}, {0x1.fa7c18p+0f, 0x1.9e90d8p-28f}};
+__device__ const float2 kExp2J64[64] = {SYN_EXP2_J64_TABLE};
+
+// Translation units that evaluate exp define SYN_DEVICE_EXPF before including
+// this header: the exception table is 2 MB of device data per unit.
+#ifdef SYN_DEVICE_EXPF
+#include "libm_expf_exc.inc"  // generated into the build directory (libm_expf_scan.c)
+
+// Whether x is one of the inputs where the host library's expf is the other
+// neighbour of the correctly rounded result (open addressing, bounded probes).
+static __device__ __noinline__ bool libm_expf_exception(uint32_t xb) {
+    const uint32_t mask = (1u << SYN_EXPF_EXC_BITS) - 1u;
+    const uint32_t h = (xb * SYN_EXPF_EXC_MUL) >> (32 - SYN_EXPF_EXC_BITS);
+    for (int i = 0; i < SYN_EXPF_EXC_PROBES; ++i) {
+        const uint32_t k = __ldg(&g_expf_exc[(h + uint32_t(i)) & mask]);
+        if (k == xb) return true;
+        if (k == 0u) return false;
+    }
+    return false;
+}
 
 __device__ __forceinline__ void two_sum(float a, float b, float& s, float& e) {
     s = __fadd_rn(a, b);
@@ -187,8 +180,16 @@ __device__ __forceinline__ float exp_rn_core(float x, const float2* tab) {
     const float y = __fadd_rn(a_hi, rest);
     // times 2^e, exact for a normal result (e in [-126, 128] here; 2^128 in two steps)
     const int e = k >> 6;
-    if (e > 127) return __fmul_rn(__fmul_rn(y, 0x1.p127f), 2.0f);
-    return __fmul_rn(y, __int_as_float((e + 127) << 23));
+    float out = e > 127 ? __fmul_rn(__fmul_rn(y, 0x1.p127f), 2.0f) : __fmul_rn(y, __int_as_float((e + 127) << 23));
+    // the unrounded value less y (exact - y to about 2^-44 relative), against the
+    // ulp on its side of y (half of it below a power of two)
+    const float res = __fadd_rn(__fsub_rn(a_hi, y), rest);
+    const uint32_t yb = __float_as_uint(y);
+    float ulp = __uint_as_float((yb & 0x7f800000u) - (23u << 23));
+    if (res < 0.0f && (yb & 0x007fffffu) == 0u) ulp = __fmul_rn(ulp, 0.5f);
+    if (fabsf(res) > __fmul_rn(0.496f, ulp) && libm_expf_exception(__float_as_uint(x)))
+        out = __uint_as_float(__float_as_uint(out) + (res > 0.0f ? 1u : 0xffffffffu));
+    return out;
 }
 
 __device__ __forceinline__ float exp_rn(float x) {
@@ -207,6 +208,7 @@ __device__ __forceinline__ float exp_rn_neg(float x, const float2* tab) {
     if (!(x > -87.0f)) return x != x ? x : 0.0f;
     return exp_rn_core<true>(x, tab);
 }
+#endif  // SYN_DEVICE_EXPF
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

@@ -1,6 +1,7 @@
 // The element-wise ops of a decode step (kernels/elementwise.hpp), with the
 // Q8_0 quantization of the next matmul's activations fused in where one
 // follows (rms_norm -> Q/K/V and gate/up, silu*mul -> down).
+#define SYN_DEVICE_EXPF  // softmax / silu: the device expf and its exception table
 #include "common.cuh"
 #include "internal.h"
 

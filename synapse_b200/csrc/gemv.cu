@@ -18,6 +18,7 @@
 //
 // Rows are split in contiguous ranges over a persistent grid (SMs x resident
 // CTAs), so every SM streams the same number of bytes.
+#define SYN_DEVICE_EXPF  // softmax / silu: the device expf and its exception table
 #include "gemv_core.cuh"
 
 #include <algorithm>

@@ -354,9 +354,11 @@ __device__ __forceinline__ float stage_row(const float* chsum, int nch, int rows
     return y;
 }
 
+#ifdef SYN_DEVICE_EXPF
 // silu(gate) * up (elementwise.hpp:76, :50)
 __device__ __forceinline__ float silu_mul1(float g, float u) {
     return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, exp_rn(-g))), u);
 }
+#endif
 
 }  // namespace syn

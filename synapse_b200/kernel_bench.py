@@ -119,6 +119,45 @@ def bench_gemv(type_name, rows, cols, batch, iters=50, mode="q8"):
             "GBps": round(alg / (ms * 1e-3) / 1e9, 1), "rotating_copies": copies}
 
 
+def bench_layers(type_name="q4_0", n_layer=32, iters=2):
+    """The four fused GEMVs of each of n_layer distinct Llama-3-8B-shaped layers, captured back to back as the
+    step graph runs them: qkv (rms_norm in), o (floats in, residual), gate/up pairs (rms_norm in, silu * up out),
+    down (floats in, residual). Attention is left out, so this is the GEMV part of a decode step."""
+    import torch
+    ty = TYPES[type_name]
+    d, ff, qkv_rows = 4096, 14336, 6144
+    shapes = [(qkv_rows, d, IN_RMSNORM, OUT_ROWS), (d, d, IN_F32, OUT_ROWS), (2 * ff, d, IN_RMSNORM, OUT_SILU_PAIRS),
+              (d, ff, IN_F32, OUT_ROWS)]
+    x = torch.randn(d, device="cuda")
+    qkv = torch.empty(qkv_rows, device="cuda")
+    act = torch.randn(ff, device="cuda") * 0.1
+    attn = torch.randn(d, device="cuda")
+    gamma = torch.ones(d, device="cuda")
+    keep, args = [], []
+    weight_bytes_total = 0
+    for l in range(n_layer):
+        for j, (r, c, im, om) in enumerate(shapes):
+            wb = weight_bytes(ty, r, c, LAYOUT_PLANAR)
+            w = empty_bytes(wb)
+            _fill_random(ty, r, c, w, 7000 + 10 * l + j)
+            keep.append(w)
+            weight_bytes_total += r * (c // 32) * (18 if ty == Q4_0 else 34)
+            inp = {0: x, 1: attn, 2: x, 3: act}[j]
+            out = {0: qkv, 1: x, 2: act, 3: x}[j]
+            res = x.data_ptr() if j in (1, 3) else None
+            args.append(GemvArgs(ty, LAYOUT_PLANAR, r, c, 1, w.data_ptr(), im, None, inp.data_ptr(),
+                                 gamma.data_ptr() if im == IN_RMSNORM else None, 1e-5, om, out.data_ptr(), res))
+
+    def launch(i):
+        for a in args:
+            check(lib().syn_gemv(ctypes.byref(a), _stream()), "syn_gemv")
+    launch(0)
+    ms = _graph_time(launch, iters) / 1.0
+    return {"kernel": "gemv_layers", "type": type_name, "layers": n_layer, "us_per_layer": round(ms * 1e3 / n_layer, 2),
+            "weight_bytes_per_layer": weight_bytes_total // n_layer,
+            "GBps": round(weight_bytes_total / (ms * 1e-3) / 1e9, 1)}
+
+
 K_TYPES = {"q4_k": Q4_K, "q6_k": Q6_K}
 
 
@@ -273,12 +312,15 @@ def main():
     p.add_argument("--no-pdl", action="store_true", help="capture without programmatic dependent launch")
     p.add_argument("--order", default="both", choices=["reference", "split", "both"],
                    help="attention: the summation order (syn_attention_args.order)")
-    p.add_argument("--mode", default="q8", choices=["q8", "f32", "rmsnorm", "silu", "step"],
-                   help="gemv input/output fusion; step: the four fused GEMVs of an 8B layer")
+    p.add_argument("--mode", default="q8", choices=["q8", "f32", "rmsnorm", "silu", "step", "layers"],
+                   help="gemv input/output fusion; step: the four fused GEMVs of an 8B layer, each timed alone; "
+                        "layers: those four GEMVs of 32 distinct layers back to back in one graph")
     a = p.parse_args()
     global PDL
     PDL = not a.no_pdl
-    if a.what in ("gemv", "all") and a.mode == "step":
+    if a.what == "gemv" and a.mode == "layers":
+        print(json.dumps(bench_layers(a.type or "q4_0", 32, a.iters or 2)), flush=True)
+    elif a.what in ("gemv", "all") and a.mode == "step":
         # the fused GEMVs of one Llama-3-8B layer: qkv (rms_norm in), o (f32 in), gate/up pairs, down (f32 in)
         for t in ([a.type] if a.type else ["q4_0"]):
             for mode, r, c in (("rmsnorm", 6144, 4096), ("f32", 4096, 4096), ("silu", 28672, 4096),
