@@ -276,12 +276,28 @@ typedef struct {
     int type_output;       /* output head; -1 = tied to token_embd */
 } syn_llama_config;
 
+/* What a session holds besides the model (graph/session.hpp:90-101 plans the
+ * arena for max_batch rows and states for max_ctx positions):
+ *   max_ctx   positions of each sequence's KV cache;
+ *   max_seqs  sequences with their own KV cache (syn_session_step_batch decodes
+ *             one token of each of the first n; the single-token calls use
+ *             sequence 0);
+ *   max_batch tokens one batched call may carry (a prefill chunk, or the
+ *             sequences of a batched decode step). */
+typedef struct {
+    int max_ctx, max_seqs, max_batch;
+} syn_session_options;
+
 /* Open a GGUF Llama file (models/llama.hpp:206-319 read_llama_config rules). */
 int syn_session_open_gguf(const char* path, int max_ctx, int device, syn_session** out);
 /* A model of random N(0, 0.02) weights quantized on the device (seeded),
  * norm weights 1; for benchmarks at shapes no file exists for. */
 int syn_session_open_synthetic(const syn_llama_config* c, int max_ctx, uint64_t seed, int device,
                                syn_session** out);
+/* The same with options (one GPU). */
+int syn_session_open_gguf_ex(const char* path, const syn_session_options* o, int device, syn_session** out);
+int syn_session_open_synthetic_ex(const syn_llama_config* c, const syn_session_options* o, uint64_t seed, int device,
+                                  syn_session** out);
 void syn_session_close(syn_session* s);
 int syn_session_config(const syn_session* s, syn_llama_config* out);
 /* Bytes of the device arena, of the weights and of the KV cache. */
@@ -290,16 +306,46 @@ int syn_session_memory(const syn_session* s, size_t* arena, size_t* weights, siz
 int syn_session_reset(syn_session* s);
 /* One token at pos (session.hpp:133 run(step)): host_logits (n_vocab floats)
  * and host_argmax may be NULL. Returns SYN_ERR_RANGE (running nothing) when
- * token >= n_vocab or pos >= max_ctx. Blocks until the outputs are on the host. */
+ * token >= n_vocab or pos >= max_ctx. Blocks until the outputs are on the host.
+ * Returns SYN_ERR_TIMEOUT when a bounded device wait of the step gave up (a
+ * tensor-parallel peer whose words never arrived, or a weight copy that never
+ * landed on this device); the session then stays failed: every later step and
+ * generate returns SYN_ERR_TIMEOUT until it is closed. */
 int syn_session_step(syn_session* s, uint32_t token, uint32_t pos, float* host_logits, int32_t* host_argmax);
 /* n_steps steps on the device from position pos, with no host round trip
  * between them: step i feeds prompt[i] while i < n_prompt, else the argmax of
  * step i - 1 (greedy decode, llama_decode.cpp:267-291); host_tokens (n_steps)
  * receives each step's argmax and the call returns when they are on the host;
  * with host_tokens NULL the call only enqueues the steps on the session's
- * stream (synchronise on syn_session_stream). 1 <= n_prompt <= n_steps. */
+ * stream (synchronise on syn_session_stream). 1 <= n_prompt <= n_steps. With
+ * host_tokens, a wait that gave up returns SYN_ERR_TIMEOUT as syn_session_step
+ * does. */
 int syn_session_generate(syn_session* s, const uint32_t* prompt, int n_prompt, uint32_t pos, int n_steps,
                          int32_t* host_tokens);
+/* run(batch) (session.hpp:143-156) for the tokens of one sequence: n <= max_batch
+ * tokens at positions pos .. pos + n - 1 of sequence seq, their K/V rows
+ * appended before any of them attends (session.hpp:349-356); host_logits
+ * (n_vocab floats) and host_argmax receive the last token's (op_last_row). Each
+ * token's arithmetic is a single-token step's, so a prompt in chunks gives the
+ * logits and cache rows a token-by-token decode gives (the reference's G1,
+ * tests/sdk/llama_prefill.cpp:20). Needs a session opened with max_batch > 1 or
+ * max_seqs > 1 (SYN_ERR_UNSUPPORTED otherwise, and for K-format or float layer
+ * matrices or tensor parallelism); SYN_ERR_RANGE for n, seq, pos or a token out
+ * of range. Blocks until the outputs are on the host. */
+int syn_session_prefill(syn_session* s, int seq, const uint32_t* tokens, int n, uint32_t pos, float* host_logits,
+                        int32_t* host_argmax);
+/* One decode token for each of sequences 0 .. n - 1 (n <= max_batch and
+ * max_seqs): tokens[i] at pos[i] of sequence i; host_logits receives n x n_vocab
+ * floats, host_argmax n tokens. The weights stream once for all n rows (the
+ * integer tensor-core GEMV from 3 rows); every row's bits are those of that
+ * sequence decoded alone. */
+int syn_session_step_batch(syn_session* s, int n, const uint32_t* tokens, const uint32_t* pos, float* host_logits,
+                           int32_t* host_argmax);
+/* Fill positions 0 .. n_pos - 1 of every sequence's KV cache with seeded
+ * N(0, 1) binary16 values: benchmark inputs at a long context without decoding
+ * up to it (no counterpart in the reference). */
+int syn_session_fill_kv_random(syn_session* s, int n_pos, uint64_t seed);
+
 /* Kernel launches one step makes (each graph replay launches exactly these). */
 int syn_session_launches_per_step(const syn_session* s);
 
@@ -365,7 +411,8 @@ int syn_session_tp_layout(const syn_session* s, syn_tp_layout* out);
  * stores its slice straight into every rank's memory (CUDA IPC over NVLink)
  * and the reading kernels wait on per-rank flags, 0 when NCCL all-gathers
  * run between the kernels (SYN_TP_P2P=0, or a peer could not be mapped);
- * *wait_errors counts flag waits that gave up after 2 s (0 in a healthy run). */
+ * *wait_errors counts peer word reads that gave up (0 in a healthy run); a read
+ * gives up after 2 s, or SYN_TP_WAIT_MS milliseconds when that is set at open. */
 int syn_session_tp_status(syn_session* s, int* peer_stores, int* wait_errors);
 
 /* Copy device memory to the host (synchronous), e.g. a KV cache for checking. */
@@ -375,7 +422,8 @@ int syn_copy_to_host(void* host_dst, const void* device_src, size_t bytes);
 float* syn_session_logits(syn_session* s);
 void* syn_session_stream(syn_session* s);
 /* Device pointer and geometry of a layer's KV cache (K then V, max_ctx rows of
- * n_head_kv * head_dim halves each). */
+ * n_head_kv * head_dim halves each) of sequence 0; with max_seqs > 1, sequence
+ * i's rows follow at i * max_ctx * n_head_kv * head_dim halves. */
 uint16_t* syn_session_kv(syn_session* s, int layer, int which /*0 K, 1 V*/);
 /* Copy a tensor of the model to the host in GGUF layout (for checking). */
 int syn_session_weight(syn_session* s, const char* name, void* host_out, size_t bytes, int* type, int* rows,

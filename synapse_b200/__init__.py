@@ -45,6 +45,11 @@ class LlamaConfig(ctypes.Structure):
         return {n: getattr(self, n) for n, _ in self._fields_}
 
 
+class SessionOptions(ctypes.Structure):
+    """syn_session_options: positions per sequence, sequences, tokens per batched call."""
+    _fields_ = [("max_ctx", ctypes.c_int), ("max_seqs", ctypes.c_int), ("max_batch", ctypes.c_int)]
+
+
 def build():
     from . import buildlib
     return buildlib.build()
@@ -122,6 +127,12 @@ def _declare(L):
                                                 ctypes.POINTER(vp)]),
         "syn_session_tp_layout": (i32, [vp, ctypes.POINTER(TPLayout)]),
         "syn_session_tp_status": (i32, [vp, ctypes.POINTER(i32), ctypes.POINTER(i32)]),
+        "syn_session_open_gguf_ex": (i32, [ctypes.c_char_p, ctypes.POINTER(SessionOptions), i32, ctypes.POINTER(vp)]),
+        "syn_session_open_synthetic_ex": (i32, [ctypes.POINTER(LlamaConfig), ctypes.POINTER(SessionOptions),
+                                                ctypes.c_uint64, i32, ctypes.POINTER(vp)]),
+        "syn_session_prefill": (i32, [vp, i32, vp, i32, ctypes.c_uint32, vp, vp]),
+        "syn_session_step_batch": (i32, [vp, i32, vp, vp, vp, vp]),
+        "syn_session_fill_kv_random": (i32, [vp, i32, ctypes.c_uint64]),
     })
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -492,8 +503,9 @@ class Session:
     tensor-parallel group): weights, activations and the F16 KV cache in one
     device arena; each step is a captured CUDA graph."""
 
-    def __init__(self, handle):
+    def __init__(self, handle, max_batch=1):
         self.h = handle
+        self.max_batch = max_batch
         c = LlamaConfig()
         check(lib().syn_session_config(self.h, ctypes.byref(c)), "syn_session_config")
         self.config = c.as_dict()
@@ -506,6 +518,49 @@ class Session:
         check(lib().syn_session_open_gguf_tp(str(path).encode(), int(max_ctx), int(device), tp.h if tp else None,
                                              ctypes.byref(h)), f"syn_session_open_gguf({path})")
         return cls(h)
+
+    @classmethod
+    def open_ex(cls, path, max_ctx, max_seqs=1, max_batch=1, device=0):
+        """A GGUF session holding max_seqs sequences' KV caches, taking up to max_batch tokens per batched call."""
+        h = ctypes.c_void_p()
+        o = SessionOptions(int(max_ctx), int(max_seqs), int(max_batch))
+        check(lib().syn_session_open_gguf_ex(str(path).encode(), ctypes.byref(o), int(device), ctypes.byref(h)),
+              f"syn_session_open_gguf_ex({path})")
+        return cls(h, max_batch)
+
+    @classmethod
+    def synthetic_ex(cls, cfg, max_ctx, max_seqs=1, max_batch=1, seed=0, device=0):
+        c = LlamaConfig(**{k: cfg[k] for k, _ in LlamaConfig._fields_ if k in cfg})
+        h = ctypes.c_void_p()
+        o = SessionOptions(int(max_ctx), int(max_seqs), int(max_batch))
+        check(lib().syn_session_open_synthetic_ex(ctypes.byref(c), ctypes.byref(o), int(seed), int(device),
+                                                  ctypes.byref(h)), "syn_session_open_synthetic_ex")
+        return cls(h, max_batch)
+
+    def prefill(self, tokens, pos, seq=0, logits=True):
+        """run(batch): the tokens of sequence seq at positions pos, pos + 1, ...; (last logits, last argmax)."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        out = np.empty(self.n_vocab, dtype=np.float32) if logits else None
+        nxt = ctypes.c_int32()
+        check(lib().syn_session_prefill(self.h, int(seq), t.ctypes.data_as(ctypes.c_void_p), t.size, int(pos),
+                                        out.ctypes.data_as(ctypes.c_void_p) if logits else None, ctypes.byref(nxt)),
+              "syn_session_prefill")
+        return out, int(nxt.value)
+
+    def step_batch(self, tokens, positions, logits=True):
+        """One token for each of sequences 0 .. n-1: (logits [n][vocab], argmax [n])."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        p = np.ascontiguousarray(positions, dtype=np.uint32)
+        out = np.empty((t.size, self.n_vocab), dtype=np.float32) if logits else None
+        nxt = np.empty(t.size, dtype=np.int32)
+        check(lib().syn_session_step_batch(self.h, t.size, t.ctypes.data_as(ctypes.c_void_p),
+                                           p.ctypes.data_as(ctypes.c_void_p),
+                                           out.ctypes.data_as(ctypes.c_void_p) if logits else None,
+                                           nxt.ctypes.data_as(ctypes.c_void_p)), "syn_session_step_batch")
+        return out, nxt
+
+    def fill_kv_random(self, n_pos, seed=0):
+        check(lib().syn_session_fill_kv_random(self.h, int(n_pos), int(seed)), "syn_session_fill_kv_random")
 
     @classmethod
     def synthetic(cls, cfg, max_ctx, seed=0, device=0, tp=None):

@@ -15,17 +15,17 @@
 //   scores: one CTA per (chunk of kChunk positions, KV head, query); the
 //           chunk's K rows land in shared memory by one bulk copy each; each
 //           thread scores one position for the G query heads, every dot a
-//           dimension-order chain of mixed-precision fmas (binary16 inputs,
-//           float accumulator: the reference's exact products and one
-//           rounding per add); the chunk's max per head;
+//           dimension-order chain of fmas on binary16 values (exact
+//           products, one rounding per add, as the reference's); the
+//           chunk's max per head;
 //   exp:    the context's max M per head from the chunk maxima, e_t =
 //           expf(s_t - M) in place of the scores, the chunk's double sum;
-//   p.V:    one CTA per (KV head, up to four of its query heads, 32 output
-//           columns); a producer warp streams the V tile of every 64
-//           positions (a tensor TMA copy) and the heads' e_t (bulk copies)
-//           through a ring of shared-memory slots; each consumer lane owns one
-//           output element and adds p_t V_t in position order, one fma per
-//           position (attention.hpp:231-243). The normaliser is the chunks'
+//   p.V:    one CTA per (query head, 32 output columns); a producer warp
+//           streams the V tile of every 64 positions (a tensor TMA copy) and
+//           the head's e_t (a bulk copy) through a ring of shared-memory
+//           slots; each consumer lane owns one output element and adds p_t
+//           V_t in position order, one fma per position
+//           (attention.hpp:231-243). The normaliser is the chunks'
 //           double sums added in chunk order (a re-association of double
 //           additions of float terms: exact whenever every term is a
 //           multiple of 2^-53 of the sum, and otherwise within a few double
@@ -72,7 +72,6 @@ static_assert(kChunk == kAttnThreads, "the p.V kernel gives each thread one posi
 constexpr int kPwStride = kChunk + 4;  // floats per head in the p buffer: heads 4 banks apart
 constexpr int kSlotPos = 64;           // positions per slot of the exact p.V kernel's ring
 constexpr int kSlots = 16;             // slots in the ring (1024 positions in flight)
-constexpr int kXvHeads = 4;            // query heads (consumer warps) per exact p.V CTA
 constexpr uint64_t kAttnWaitNs = 2000000000ull;  // bounded waits on bulk copies give up after 2 s
 
 __device__ unsigned g_attn_timeouts = 0;  // bounded waits that gave up (syn_device_errors)
@@ -716,45 +715,55 @@ __global__ void __launch_bounds__(kAttnThreads) attn_pv_kernel(AttnParams a) {
 
 // ---- the reference's order at any length (SYN_ORDER_REFERENCE) ------------------
 
-// c + a * b for binary16 a, b (exact product), rounded once to float: the
-// mixed-precision fma of sm_100. Pairs: the low halves first, then the high.
-__device__ __forceinline__ float fma_hh(uint16_t a, uint16_t b, float c) {
-    asm("fma.rn.f32.f16 %0, %1, %2, %0;" : "+f"(c) : "h"(a), "h"(b));
-    return c;
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, bool three,
+                                            uint64_t* bar) {
+    if (three)
+        asm volatile(
+            "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+            "%4}], [%5];" ::"r"(smem_addr(dst)),
+            "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
+            : "memory");
+    else
+        asm volatile(
+            "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+            "%3}], [%4];" ::"r"(smem_addr(dst)),
+            "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+            : "memory");
 }
-__device__ __forceinline__ float fma_h2(uint32_t a2, uint32_t b2, float c) {
-    asm("{\n .reg .b16 al, ah, bl, bh;\n mov.b32 {al, ah}, %1;\n mov.b32 {bl, bh}, %2;\n"
-        " fma.rn.f32.f16 %0, al, bl, %0;\n fma.rn.f32.f16 %0, ah, bh, %0;\n}"
-        : "+f"(c)
-        : "r"(a2), "r"(b2));
-    return c;
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
-// Shared memory of the exact scores kernel: cos/sin, the group's rotated q as
-// binary16, the appended K row, the chunk's K rows (pitch hd + 8 halves, so
-// consecutive threads' 16-byte reads of their rows spread over the banks).
+// Shared memory of the exact scores kernel: cos/sin, the group's rotated q
+// (binary16 values, held as floats), the appended K row, and the chunk's K rows: with SWZ (head_dim a
+// multiple of 64) as tensor-TMA tiles of 64 rows x 64 columns in the 128-byte
+// swizzle (16-byte piece c of row r at piece c ^ (r % 8), so consecutive
+// threads' 16-byte reads of their own rows hit distinct banks), [quarter of 64
+// rows][64-column box][row] x 128 bytes from a 1 KB boundary; otherwise rows
+// of hd + 8 halves filled by 16-byte copies (the padding spreads the banks).
 struct XsSmem {
     size_t cs, qh, krh, kt, total;
 };
-__host__ __device__ inline XsSmem xs_smem(int GT, int hd) {
+__host__ __device__ inline XsSmem xs_smem(int GT, int hd, bool swz) {
     XsSmem l;
     size_t off = 0;
-    auto take = [&](size_t bytes) {
+    auto take = [&](size_t bytes, size_t align) {
+        off = (off + align - 1) & ~(align - 1);
         const size_t o = off;
-        off = (off + bytes + 15) & ~size_t(15);
+        off += bytes;
         return o;
     };
-    l.cs = take(size_t(hd) * 4);
-    l.qh = take(size_t(GT) * hd * 2);
-    l.krh = take(size_t(hd) * 2);
-    l.kt = take(size_t(kChunk) * (hd + 8) * 2);
-    l.total = off;
+    l.cs = take(size_t(hd) * 4, 16);
+    l.qh = take(size_t(GT) * hd * 4, 16);
+    l.krh = take(size_t(hd) * 2, 16);
+    l.kt = swz ? take(size_t(kChunk) * hd * 2, 1024) : take(size_t(kChunk) * (hd + 8) * 2, 16);
+    l.total = ((off + 15) & ~size_t(15)) + (swz ? 1024 : 0);  // + the 1 KB alignment of the dynamic base
     return l;
 }
 
 // Exact scores of one chunk: CTA (j, g, b), thread r = position t0 + r.
-template <int GT>
-__global__ void __launch_bounds__(kAttnThreads) attn_xs_kernel(AttnParams a) {
+template <int GT, bool SWZ>
+__global__ void __launch_bounds__(kAttnThreads) attn_xs_kernel(AttnParams a, const __grid_constant__ CUtensorMap kmap) {
     const int j = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
     const int hd = a.hd, G = a.n_head / a.n_kv, H = a.n_head;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -765,42 +774,43 @@ __global__ void __launch_bounds__(kAttnThreads) attn_xs_kernel(AttnParams a) {
     const int t1 = min(L, t0 + kChunk), n = t1 - t0;
     const bool owns = a.append && P < t1;  // the chunk holds the appended row
 
-    extern __shared__ __align__(16) unsigned char smem[];
-    const XsSmem sl = xs_smem(GT, hd);
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    unsigned char* smem = SWZ ? smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u) : smem_raw;
+    const XsSmem sl = xs_smem(GT, hd, SWZ);
     float* cs = reinterpret_cast<float*>(smem + sl.cs);
-    uint16_t* qh = reinterpret_cast<uint16_t*>(smem + sl.qh);
+    float* qf = reinterpret_cast<float*>(smem + sl.qh);
     uint16_t* krh = reinterpret_cast<uint16_t*>(smem + sl.krh);
     uint16_t* kt = reinterpret_cast<uint16_t*>(smem + sl.kt);
-    __shared__ __align__(8) uint64_t bar[kAttnThreads / 64];  // one per 64 rows
+    __shared__ __align__(8) uint64_t bar[kAttnThreads / 64];  // SWZ: one per 64 rows
     __shared__ float red[GT][kAttnThreads / 32];
     __shared__ int bad;
-    const int rowh = hd + 8;
+    const int rowh = hd + 8, nbx = hd / 64;
     const size_t row = size_t(a.n_kv) * hd;
     uint16_t* kcb = a.kc + size_t(b) * a.cache_stride;
     uint16_t* vcb = a.vc + size_t(b) * a.cache_stride;
-    if (tid < kAttnThreads / 64) mbar_init(&bar[tid], 1);
+    if (SWZ && tid < kAttnThreads / 64) mbar_init(&bar[tid], 1);
     if (tid == 0) bad = 0;
     mbar_init_fence();
     __syncthreads();
 
     // With append, rows other than P were written by earlier calls: their
-    // copies start before the wait. Without it the caller's previous kernel
-    // may have written them (syn_rope_kv_append), so everything waits.
+    // copies start before the wait (row P's stale copy is overwritten below).
+    // Without it the caller's previous kernel may have written them
+    // (syn_rope_kv_append), so everything waits.
     if (!a.append) pdl_wait();
     float2 cs_v = make_float2(0.0f, 0.0f);
     if (a.rope && a.rope_tab && tid < hd / 2)
         cs_v = reinterpret_cast<const float2*>(a.rope_tab)[size_t(P) * (hd / 2) + tid];
-    {
-        const int r = tid, q = tid >> 6;
-        const bool copy = r < n && !(owns && t0 + r == P);
-        if ((tid & 63) == 0) {  // the quarter's bytes: its rows in the chunk, less the appended one
-            const int r0 = 64 * q, r1 = min(n, r0 + 64);
-            int rows = max(0, r1 - r0);
-            if (owns && P >= t0 + r0 && P < t0 + r1) --rows;
-            mbar_expect_tx(&bar[q], uint32_t(rows) * uint32_t(hd) * 2u);
-        }
-        if (copy)
-            bulk_copy_g2s(kt + r * rowh, kcb + size_t(t0 + r) * row + size_t(g) * hd, uint32_t(hd) * 2u, &bar[q]);
+    if (SWZ) {
+        if (tid == 0)
+            for (int q = 0; q * 64 < n; ++q) {
+                mbar_expect_tx(&bar[q], uint32_t(nbx) * 64u * 128u);
+                for (int bx = 0; bx < nbx; ++bx)
+                    tma_load_3d(smem + sl.kt + (size_t(q) * nbx + bx) * 64 * 128, &kmap, g * hd + 64 * bx,
+                                t0 + 64 * q, a.v3d ? b : 0, a.v3d != 0, &bar[q]);
+            }
+    } else {
+        copy_rows(kt, kcb, row, g, hd, t0, t1, owns ? P : -1);
     }
     if (a.rope) {
         if (a.rope_tab) {
@@ -826,11 +836,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_xs_kernel(AttnParams a) {
             pair_index(a.rope_mode, hd, pi, i0, i1);
             float o0, o1;
             rotate(qb[jh * hd + i0], qb[jh * hd + i1], cs[2 * pi], cs[2 * pi + 1], o0, o1);
-            qh[jh * hd + i0] = f16_bits(o0);
-            qh[jh * hd + i1] = f16_bits(o1);
+            qf[jh * hd + i0] = round_f16(o0);
+            qf[jh * hd + i1] = round_f16(o1);
         }
     } else {
-        for (int i = tid; i < G * hd; i += kAttnThreads) qh[i] = f16_bits(qb[i]);
+        for (int i = tid; i < G * hd; i += kAttnThreads) qf[i] = round_f16(qb[i]);
     }
     if (owns) {  // kv_append (attention.hpp:165-175): the rotated k and v as binary16 into row P
         const float* kb = a.k + size_t(b) * row + size_t(g) * hd;
@@ -854,36 +864,56 @@ __global__ void __launch_bounds__(kAttnThreads) attn_xs_kernel(AttnParams a) {
         }
         for (int d = tid; d < hd; d += kAttnThreads) vrow[d] = f16_bits(vb[d]);
     }
-    __syncthreads();
-    if (owns && tid < hd / 8)  // no copy was issued for this row
-        *reinterpret_cast<uint4*>(kt + (P - t0) * rowh + tid * 8) = *reinterpret_cast<const uint4*>(krh + tid * 8);
-    __syncthreads();
-    if (!mbar_wait_bounded(&bar[tid >> 6], 0, kAttnWaitNs)) {
-        atomicAdd(&g_attn_timeouts, 1u);
-        bad = 1;
+    if (SWZ) {
+        if (tid < n && !mbar_wait_bounded(&bar[tid >> 6], 0, kAttnWaitNs)) {
+            atomicAdd(&g_attn_timeouts, 1u);
+            bad = 1;
+        }
+    } else {
+        cp_async_wait_all();
     }
     __syncthreads();
     if (bad) return;
+    if (owns && tid < hd / 8) {  // the appended row over its stale copy
+        const int r = P - t0;
+        uint4* dst = SWZ ? reinterpret_cast<uint4*>(smem + sl.kt +
+                                                    (((size_t(r >> 6) * nbx + (tid >> 3)) * 64 + (r & 63)) * 128) +
+                                                    ((((tid & 7) ^ (r & 7))) << 4))
+                         : reinterpret_cast<uint4*>(kt + r * rowh + tid * 8);
+        *dst = *reinterpret_cast<const uint4*>(krh + tid * 8);
+    }
+    __syncthreads();
 
-    // s_t = (q . K_t) * scale, each head's dot in dimension order (attention.hpp:214-220)
+    // s_t = (q . K_t) * scale, each head's dot in dimension order (attention.hpp:214-220);
+    // each K value widened once for the group's heads, every product exact
     const size_t hb = size_t(b) * H + size_t(g) * G;
     float acc[GT];
 #pragma unroll
     for (int h = 0; h < GT; ++h) acc[h] = 0.0f;
     if (tid < n) {
         const uint4* kr = reinterpret_cast<const uint4*>(kt + tid * rowh);
+        const unsigned char* ks = smem + sl.kt + ((size_t(tid >> 6) * nbx) * 64 + (tid & 63)) * 128;
 #pragma unroll 2
         for (int d8 = 0; d8 < hd / 8; ++d8) {
-            const uint4 kv = kr[d8];
+            const uint4 kv = SWZ ? *reinterpret_cast<const uint4*>(ks + (d8 >> 3) * (64 * 128) +
+                                                                   (((d8 & 7) ^ (tid & 7)) << 4))
+                                 : kr[d8];
+            float kf[8];
+            unpack8(kv, kf);
 #pragma unroll
             for (int h = 0; h < GT; ++h) {
                 if (h < G) {
-                    const uint4 qv = reinterpret_cast<const uint4*>(qh + h * hd)[d8];
+                    const float4 q0 = reinterpret_cast<const float4*>(qf + h * hd)[2 * d8];
+                    const float4 q1 = reinterpret_cast<const float4*>(qf + h * hd)[2 * d8 + 1];
                     float c = acc[h];
-                    c = fma_h2(qv.x, kv.x, c);
-                    c = fma_h2(qv.y, kv.y, c);
-                    c = fma_h2(qv.z, kv.z, c);
-                    c = fma_h2(qv.w, kv.w, c);
+                    c = fmaf(q0.x, kf[0], c);
+                    c = fmaf(q0.y, kf[1], c);
+                    c = fmaf(q0.z, kf[2], c);
+                    c = fmaf(q0.w, kf[3], c);
+                    c = fmaf(q1.x, kf[4], c);
+                    c = fmaf(q1.y, kf[5], c);
+                    c = fmaf(q1.z, kf[6], c);
+                    c = fmaf(q1.w, kf[7], c);
                     acc[h] = c;
                 }
             }
@@ -957,51 +987,30 @@ __global__ void __launch_bounds__(kAttnThreads) attn_xe_kernel(AttnParams a) {
 }
 
 // Shared memory of the exact p.V kernel: the ring's V tiles (64 positions x 32
-// columns of binary16), the heads' e rows of each slot, the consumers' p
-// (binary16), and the barriers.
+// columns of binary16), the head's e row of each slot, the consumer's p of two
+// slots as floats, and the barriers.
 struct XvSmem {
-    size_t vt, es, ph, bars, total;
+    size_t vt, es, pf, bars, total;
 };
 __host__ __device__ inline XvSmem xv_smem() {
     XvSmem l;
-    l.vt = 0;                                                      // [kSlots][64][32] halves, 4 KB per slot
-    l.es = l.vt + size_t(kSlots) * kSlotPos * 32 * 2;              // [kSlots][4][64] floats
-    l.ph = l.es + size_t(kSlots) * kXvHeads * kSlotPos * 4;        // [4][64] halves
-    l.bars = l.ph + size_t(kXvHeads) * kSlotPos * 2;               // vfull, efull, empty: [kSlots] each
-    l.total = l.bars + size_t(3) * kSlots * 8 + 1024;  // + the alignment of the ring
+    l.vt = 0;                                           // [kSlots][64][32] halves, 4 KB per slot
+    l.es = l.vt + size_t(kSlots) * kSlotPos * 32 * 2;   // [kSlots][64] floats
+    l.pf = l.es + size_t(kSlots) * kSlotPos * 4;        // [2][64] floats
+    l.bars = l.pf + size_t(2) * kSlotPos * 4;           // vfull, efull, empty: [kSlots] each
+    l.total = l.bars + size_t(3) * kSlots * 8 + 1024;   // + the alignment of the ring
     return l;
 }
 
-__device__ __forceinline__ void tma_load_v(void* dst, const CUtensorMap* map, int x, int y, int z, bool three,
-                                           uint64_t* bar) {
-    if (three)
-        asm volatile(
-            "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
-            "%4}], [%5];" ::"r"(smem_addr(dst)),
-            "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
-            : "memory");
-    else
-        asm volatile(
-            "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
-            "%3}], [%4];" ::"r"(smem_addr(dst)),
-            "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
-            : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
-
-// p.V in position order: CTA (g, head quad hq, 32-column slice s) of query b;
-// warps 0..nw-1 consume (warp w = query head g*G + 4*hq + w, lane = column
-// 32*s + lane), warp nw produces.
-__global__ void __launch_bounds__(32 * (kXvHeads + 1)) attn_xv_kernel(AttnParams a,
-                                                                     const __grid_constant__ CUtensorMap vmap) {
+// p.V in position order: CTA (query head h, 32-column slice s) of query b; warp
+// 0 consumes (lane = output column 32 s + lane, one fma chain each), warp 1
+// produces. One consumer warp per CTA keeps the shared-memory loads per SM to
+// about one per position, under the fma latency the chains are bound by.
+__global__ void __launch_bounds__(64) attn_xv_kernel(AttnParams a, const __grid_constant__ CUtensorMap vmap) {
     const int G = a.n_head / a.n_kv, H = a.n_head, hd = a.hd;
-    const int ns = (hd + 31) / 32, nq = (G + kXvHeads - 1) / kXvHeads;
-    const int s = blockIdx.x % ns, hq = (blockIdx.x / ns) % nq, g = blockIdx.x / (ns * nq), b = blockIdx.y;
+    const int ns = (hd + 31) / 32;
+    const int s = blockIdx.x % ns, h = blockIdx.x / ns, g = h / G, b = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int nw = int(blockDim.x >> 5) - 1;          // consumer warps
-    const int nh = min(kXvHeads, G - kXvHeads * hq);  // of which hold a head
     const int P = a.pos[b], L = P + 1;
     if (P < 0 || L > a.max_len) return;
     const int nslot = (L + kSlotPos - 1) / kSlotPos, nchk = (L + kChunk - 1) / kChunk;
@@ -1012,7 +1021,7 @@ __global__ void __launch_bounds__(32 * (kXvHeads + 1)) attn_xv_kernel(AttnParams
     const XvSmem sl = xv_smem();
     uint16_t* vt = reinterpret_cast<uint16_t*>(smem + sl.vt);
     float* es = reinterpret_cast<float*>(smem + sl.es);
-    uint16_t* ph = reinterpret_cast<uint16_t*>(smem + sl.ph);
+    float* pf = reinterpret_cast<float*>(smem + sl.pf);
     uint64_t* vfull = reinterpret_cast<uint64_t*>(smem + sl.bars);
     uint64_t* efull = vfull + kSlots;
     uint64_t* empty = efull + kSlots;
@@ -1020,36 +1029,34 @@ __global__ void __launch_bounds__(32 * (kXvHeads + 1)) attn_xv_kernel(AttnParams
     if (tid < kSlots) {
         mbar_init(&vfull[tid], 1);
         mbar_init(&efull[tid], 1);
-        mbar_init(&empty[tid], uint32_t(nw));
+        mbar_init(&empty[tid], 1);
     }
     if (tid == 0) abort_flag = issued = 0;
     mbar_init_fence();
     __syncthreads();
 
-    const size_t hb = size_t(b) * H + size_t(g) * G + size_t(kXvHeads) * hq;  // this CTA's first query head
+    const size_t hb = size_t(b) * H + size_t(h);  // this CTA's query head
     const int vx = g * hd + 32 * s, vz = a.v3d ? b : 0;
-    const bool producer = warp == nw;
     auto issue_v = [&](int k) {
         uint64_t* bar = &vfull[k % kSlots];
         mbar_expect_tx(bar, uint32_t(kSlotPos) * 32u * 2u);
-        tma_load_v(vt + size_t(k % kSlots) * kSlotPos * 32, &vmap, vx, k * kSlotPos, vz, a.v3d != 0, bar);
+        tma_load_3d(vt + size_t(k % kSlots) * kSlotPos * 32, &vmap, vx, k * kSlotPos, vz, a.v3d != 0, bar);
     };
     auto issue_e = [&](int k) {
         uint64_t* bar = &efull[k % kSlots];
-        mbar_expect_tx(bar, uint32_t(nh) * kSlotPos * 4u);
-        for (int h = 0; h < nh; ++h)
-            bulk_copy_g2s(es + (size_t(k % kSlots) * kXvHeads + h) * kSlotPos,
-                          a.scores + (hb + h) * a.ld + size_t(k) * kSlotPos, kSlotPos * 4u, bar);
+        mbar_expect_tx(bar, kSlotPos * 4u);
+        bulk_copy_g2s(es + size_t(k % kSlots) * kSlotPos, a.scores + hb * a.ld + size_t(k) * kSlotPos,
+                      kSlotPos * 4u, bar);
     };
     // V rows below P were written by earlier calls: their tiles start before the wait
     const int first = min(kSlots, nslot);
-    if (producer && lane == 0)
+    if (warp == 1 && lane == 0)
         for (int k = 0; k < first; ++k)
             if ((k + 1) * kSlotPos <= P) issue_v(k);
     pdl_launch_dependents();
     pdl_wait();  // e, the chunk sums and the appended V row
 
-    if (producer) {
+    if (warp == 1) {
         if (lane == 0) {
             int k = 0;
             for (; k < first; ++k) {
@@ -1070,61 +1077,82 @@ __global__ void __launch_bounds__(32 * (kXvHeads + 1)) attn_xv_kernel(AttnParams
             issued = k;
         }
     } else {
-        const int w = warp;
-        const bool active = w < nh;
         // the normaliser: the chunks' double sums in chunk order; scale = float(1 / sum) (elementwise.hpp:192-193)
         float scale = 0.0f;
-        if (active && lane == 0) {
+        if (lane == 0) {
             double sum = 0.0;
-            for (int c = 0; c < nchk; ++c) sum += a.st_s[(hb + w) * a.nch + c];
+            for (int c = 0; c < nchk; ++c) sum += a.st_s[hb * a.nch + c];
             scale = float(1.0 / sum);
         }
         scale = __shfl_sync(0xffffffffu, scale, 0);
-        uint16_t* pw = ph + size_t(w) * kSlotPos;
+        // Two slots in flight: while slot k's fma chain runs, slot k + 1's data has
+        // been waited for, its p formed and its V values taken into registers (and its
+        // ring slot handed back to the producer), so the chain never waits on them.
+        // pf holds p of two slots, [k & 1][64].
         float acc = 0.0f;
-        for (int k = 0; k < nslot; ++k) {
+        bool ok = true;
+        // slot k's data: p_t = binary16(e_t * scale) as floats (attention.hpp:224-227) into pf[k & 1],
+        // its V values as binary16 pairs (positions 2i, 2i + 1) into v; the ring slot released
+        auto fetch = [&](int k, uint32_t (&v)[kSlotPos / 2]) {
             const int slot = k % kSlots;
             const uint32_t par = uint32_t((k / kSlots) & 1);
             const int n = min(kSlotPos, L - k * kSlotPos);
-            bool ok = mbar_wait_bounded(&efull[slot], par, kAttnWaitNs);
-            ok = ok && mbar_wait_bounded(&vfull[slot], par, kAttnWaitNs);
-            if (!__all_sync(0xffffffffu, ok) || *reinterpret_cast<volatile int*>(&abort_flag)) {
+            __syncwarp();  // the chain that last read pf[k & 1] is done in every lane
+            bool got = mbar_wait_bounded(&efull[slot], par, kAttnWaitNs);
+            got = got && mbar_wait_bounded(&vfull[slot], par, kAttnWaitNs);
+            if (!__all_sync(0xffffffffu, got) || *reinterpret_cast<volatile int*>(&abort_flag)) {
                 if (lane == 0 && !*reinterpret_cast<volatile int*>(&abort_flag)) {
                     atomicAdd(&g_attn_timeouts, 1u);
                     atomicExch(&abort_flag, 1);
                 }
-                break;
+                ok = false;
+                return;
             }
-            if (active) {
-                // p_t = binary16(e_t * scale) of positions 2 lane, 2 lane + 1 (attention.hpp:224-227)
-                const float2 e2 = reinterpret_cast<const float2*>(es + (size_t(slot) * kXvHeads + w) * kSlotPos)[lane];
-                const uint16_t p0 = 2 * lane < n ? f16_bits(__fmul_rn(e2.x, scale)) : uint16_t(0);
-                const uint16_t p1 = 2 * lane + 1 < n ? f16_bits(__fmul_rn(e2.y, scale)) : uint16_t(0);
-                reinterpret_cast<uint32_t*>(pw)[lane] = uint32_t(p0) | (uint32_t(p1) << 16);
-                __syncwarp();
-                // out_d += p_t * V_t,d for t in order (attention.hpp:231-243)
-                const uint16_t* vcol = vt + size_t(slot) * kSlotPos * 32 + lane;
-                if (n == kSlotPos) {
+            const float2 e2 = reinterpret_cast<const float2*>(es + size_t(slot) * kSlotPos)[lane];
+            reinterpret_cast<float2*>(pf + (k & 1) * kSlotPos)[lane] =
+                make_float2(2 * lane < n ? round_f16(__fmul_rn(e2.x, scale)) : 0.0f,
+                            2 * lane + 1 < n ? round_f16(__fmul_rn(e2.y, scale)) : 0.0f);
+            const uint16_t* vcol = vt + size_t(slot) * kSlotPos * 32 + lane;
 #pragma unroll
-                    for (int t8 = 0; t8 < kSlotPos / 8; ++t8) {
-                        const uint4 p8 = reinterpret_cast<const uint4*>(pw)[t8];
-                        const uint32_t pp[4] = {p8.x, p8.y, p8.z, p8.w};
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            acc = fma_hh(uint16_t(pp[u] & 0xffffu), vcol[(8 * t8 + 2 * u) * 32], acc);
-                            acc = fma_hh(uint16_t(pp[u] >> 16), vcol[(8 * t8 + 2 * u + 1) * 32], acc);
-                        }
-                    }
-                } else {
-                    for (int t = 0; t < n; ++t) acc = fma_hh(pw[t], vcol[t * 32], acc);
-                }
-                __syncwarp();
-            }
+            for (int i = 0; i < kSlotPos / 2; ++i)
+                v[i] = uint32_t(vcol[(2 * i) * 32]) | (uint32_t(vcol[(2 * i + 1) * 32]) << 16);
+            __syncwarp();  // every lane's V read and p written
             if (lane == 0) mbar_arrive(&empty[slot]);
+        };
+        // out_d += p_t * V_t,d for t in order (attention.hpp:231-243): one fma per position
+        auto chain = [&](int k, const uint32_t (&v)[kSlotPos / 2]) {
+            const int n = min(kSlotPos, L - k * kSlotPos);
+            const float* pk = pf + (k & 1) * kSlotPos;
+            if (n == kSlotPos) {
+#pragma unroll
+                for (int i = 0; i < kSlotPos / 4; ++i) {
+                    const float4 p4 = reinterpret_cast<const float4*>(pk)[i];
+                    const uint32_t w0 = v[2 * i], w1 = v[2 * i + 1];
+                    acc = fmaf(p4.x, f16_from_bits(uint16_t(w0 & 0xffffu)), acc);  // exact products: one
+                    acc = fmaf(p4.y, f16_from_bits(uint16_t(w0 >> 16)), acc);     // rounding per add
+                    acc = fmaf(p4.z, f16_from_bits(uint16_t(w1 & 0xffffu)), acc);
+                    acc = fmaf(p4.w, f16_from_bits(uint16_t(w1 >> 16)), acc);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < kSlotPos / 2; ++i) {
+                    if (2 * i < n) acc = fmaf(pk[2 * i], f16_from_bits(uint16_t(v[i] & 0xffffu)), acc);
+                    if (2 * i + 1 < n) acc = fmaf(pk[2 * i + 1], f16_from_bits(uint16_t(v[i] >> 16)), acc);
+                }
+            }
+        };
+        uint32_t va[kSlotPos / 2], vb[kSlotPos / 2];
+        fetch(0, va);
+        for (int k = 0; k < nslot && ok; k += 2) {
+            if (k + 1 < nslot) fetch(k + 1, vb);
+            chain(k, va);
+            if (!ok || k + 1 >= nslot) break;
+            if (k + 2 < nslot) fetch(k + 2, va);
+            chain(k + 1, vb);
         }
         const int d = 32 * s + lane;
-        if (active && d < hd && !*reinterpret_cast<volatile int*>(&abort_flag)) {
-            const size_t o = (hb + w) * hd + d;
+        if (d < hd && ok && !*reinterpret_cast<volatile int*>(&abort_flag)) {
+            const size_t o = hb * hd + d;
             if (a.tp.peers) tp_store(a.tp, o, acc, *reinterpret_cast<const volatile unsigned*>(a.tp.epoch));
             else a.out[o] = acc;
         }
@@ -1275,10 +1303,12 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-// The V cache as a tensor of binary16: x = column (n_kv * head_dim), y = position
-// (max_len rows), z = query (cache_stride apart; absent when the queries share
-// one cache); boxes of 32 columns x kSlotPos positions.
-int v_tensor_map(const AttnParams& a, CUtensorMap* m) {
+// A K or V cache as a tensor of binary16: x = column (n_kv * head_dim), y =
+// position (max_len rows), z = query (cache_stride apart; absent when the
+// queries share one cache); boxes of box_x columns x box_y positions, read
+// into shared memory as they are (V) or in the 128-byte swizzle (K).
+int cache_tensor_map(const AttnParams& a, const uint16_t* base, unsigned box_x, unsigned box_y, bool swizzle,
+                     CUtensorMap* m) {
     const auto encode = tensor_map_encoder();
     if (!encode) {
         syn_set_error("cuTensorMapEncodeTiled is not available from the driver");
@@ -1286,13 +1316,14 @@ int v_tensor_map(const AttnParams& a, CUtensorMap* m) {
     }
     const cuuint64_t dims[3] = {cuuint64_t(a.n_kv) * a.hd, cuuint64_t(a.max_len), cuuint64_t(a.n_q)};
     const cuuint64_t strides[2] = {cuuint64_t(a.n_kv) * a.hd * 2, cuuint64_t(a.cache_stride) * 2};
-    const cuuint32_t box[3] = {32, kSlotPos, 1};
+    const cuuint32_t box[3] = {box_x, box_y, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
-    const CUresult r = encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, a.v3d ? 3 : 2, a.vc, dims, strides, box, estr,
-                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+    const CUresult r = encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, a.v3d ? 3 : 2, const_cast<uint16_t*>(base), dims,
+                              strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
-        syn_set_error("cuTensorMapEncodeTiled rejected the V cache geometry");
+        syn_set_error("cuTensorMapEncodeTiled rejected the KV cache geometry");
         return SYN_ERR_INVALID;
     }
     return SYN_OK;
@@ -1321,23 +1352,35 @@ int launch_attention(AttnParams a, void* scratch, cudaStream_t s) {
         if (!st) st = syn_launch(attn_pv_kernel<GT>, grid, kAttnThreads, pv_smem(GT, a.hd).total, s, a);
         return st;
     }
-    st = opt_in(reinterpret_cast<const void*>(attn_xs_kernel<GT>), xs_smem(GT, 256).total);
+    const bool swz = a.hd % 64 == 0;
+    auto xs = swz ? attn_xs_kernel<GT, true> : attn_xs_kernel<GT, false>;
+    st = opt_in(reinterpret_cast<const void*>(xs), xs_smem(GT, 256, swz).total);
     if (!st) st = opt_in(reinterpret_cast<const void*>(attn_xv_kernel), xv_smem().total);
     if (st) return st;
     a.v3d = a.cache_stride != 0;
-    CUtensorMap vmap;
-    if ((st = v_tensor_map(a, &vmap))) return st;
-    const int G = a.n_head / a.n_kv, nw = std::min(kXvHeads, G);
-    const int ns = (a.hd + 31) / 32, nq = (G + kXvHeads - 1) / kXvHeads;
-    st = syn_launch(attn_xs_kernel<GT>, grid, kAttnThreads, xs_smem(GT, a.hd).total, s, a);
+    CUtensorMap vmap, kmap;
+    if ((st = cache_tensor_map(a, a.vc, 32, kSlotPos, false, &vmap))) return st;
+    if ((st = swz ? cache_tensor_map(a, a.kc, 64, 64, true, &kmap) : cache_tensor_map(a, a.kc, 32, kSlotPos, false, &kmap)))
+        return st;
+    const int ns = (a.hd + 31) / 32;
+    st = syn_launch(xs, grid, kAttnThreads, xs_smem(GT, a.hd, swz).total, s, a, kmap);
     if (!st) st = syn_launch(attn_xe_kernel<GT>, grid, kAttnThreads, 0, s, a);
     if (!st)
-        st = syn_launch(attn_xv_kernel, dim3(unsigned(a.n_kv * nq * ns), unsigned(a.n_q)), unsigned(32 * (nw + 1)),
-                        xv_smem().total, s, a, vmap);
+        st = syn_launch(attn_xv_kernel, dim3(unsigned(a.n_head * ns), unsigned(a.n_q)), 64u, xv_smem().total, s, a,
+                        vmap);
     return st;
 }
 
 }  // namespace
+
+unsigned* syn_attn_timeout_word() {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_attn_timeouts) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    return static_cast<unsigned*>(p);
+}
 
 // Bounded waits of the attention kernels that gave up on this device (syn_device_errors).
 int syn_attn_timeouts() {

@@ -127,7 +127,7 @@ __device__ const float2 kExp2J64[64] = {SYN_EXP2_J64_TABLE};
 
 // Whether x is one of the inputs where the host library's expf is the other
 // neighbour of the correctly rounded result (open addressing, bounded probes).
-static __device__ __noinline__ bool libm_expf_exception(uint32_t xb) {
+static __device__ __forceinline__ bool libm_expf_exception(uint32_t xb) {
     const uint32_t mask = (1u << SYN_EXPF_EXC_BITS) - 1u;
     const uint32_t h = (xb * SYN_EXPF_EXC_MUL) >> (32 - SYN_EXPF_EXC_BITS);
     for (int i = 0; i < SYN_EXPF_EXC_PROBES; ++i) {
@@ -296,7 +296,6 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 }
 
 // ---- tensor-parallel gathers by peer stores (TpSync, internal.h) ---------------
-constexpr uint64_t kTpWaitNs = 2000000000ull;  // a reader gives up after 2 s and counts an error
 
 __device__ __forceinline__ void st_word_sys(void* p, uint64_t v) {
     asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
@@ -332,15 +331,16 @@ template <int N>
 __device__ __forceinline__ void tp_load_n(const TpSync& t, const uint64_t* p, unsigned epoch, float (&v)[N]);
 
 // Consumer: the value of word p once it carries this step's epoch. A read
-// that waits 2 s is counted in *t.err and returns what is there; once one
-// has given up, later reads do not wait (the host reads the count and fails).
+// that waits t.wait_ns (2 s unless the session sets it) is counted in *t.err
+// and returns what is there; once one has given up, later reads do not wait
+// (the host reads the count and fails the step).
 __device__ inline float tp_load(const TpSync& t, const uint64_t* p, unsigned epoch) {
     uint64_t w = ld_word_sys(p);
     if (unsigned(w >> 32) == epoch) return word_value(w);
     const uint64_t t0 = global_ns();
     while (unsigned(w >> 32) != epoch) {
         if (*reinterpret_cast<const volatile unsigned*>(t.err) != 0) break;
-        if (global_ns() - t0 > kTpWaitNs) {
+        if (global_ns() - t0 > t.wait_ns) {
             atomicAdd(t.err, 1u);
             break;
         }

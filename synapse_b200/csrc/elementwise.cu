@@ -66,11 +66,18 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
     return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, exp_rn(-g))), u);
 }
 
+// PAIRS: g and u interleaved by element (g at 2i, u at 2i + 1 of each token's
+// 2 cols values: a GEMV over gate/up rows stored in pairs); else separate.
+template <bool PAIRS>
 __global__ void __launch_bounds__(256) silu_mul_kernel(const float* __restrict__ g, const float* __restrict__ u,
                                                        int n_tok, int cols, float* out, ActPlanes act) {
     pdl_launch_dependents();
     pdl_wait();
     const int lane = threadIdx.x & 31;
+    auto value = [&](size_t t, size_t c) {
+        return PAIRS ? silu_mul(g[t * 2 * cols + 2 * c], g[t * 2 * cols + 2 * c + 1])
+                     : silu_mul(g[t * cols + c], u[t * cols + c]);
+    };
     if (act.qs) {
         // one warp per 32-value block: compute, then quantize it
         const int nb = cols / QK;
@@ -78,7 +85,7 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const float* __restrict__
         if (blk >= long(n_tok) * nb) return;
         const long t = blk / nb, b = blk % nb;
         const size_t i = size_t(t) * cols + size_t(b) * QK + lane;
-        const float v = silu_mul(g[i], u[i]);
+        const float v = value(size_t(t), size_t(b) * QK + lane);
         if (out) out[i] = v;
         const Q8Lane r = quantize_q8_lane(v);
         act.qs[i] = r.q;
@@ -90,7 +97,7 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const float* __restrict__
     } else {
         const size_t n = size_t(n_tok) * cols;
         for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x)
-            out[i] = silu_mul(g[i], u[i]);
+            out[i] = value(i / size_t(cols), i % size_t(cols));
     }
 }
 
@@ -248,9 +255,10 @@ extern "C" int syn_rms_norm(const float* x, const float* gamma, int n_tok, int c
                       out_f32, a);
 }
 
-extern "C" int syn_silu_mul(const float* g, const float* u, int n_tok, int cols, float* out_f32, void* act,
-                            void* stream) {
-    if (!g || !u || n_tok <= 0 || cols <= 0 || (!out_f32 && !act)) return SYN_ERR_INVALID;
+namespace {
+int launch_silu_mul(bool pairs, const float* g, const float* u, int n_tok, int cols, float* out_f32, void* act,
+                    void* stream) {
+    if (!g || (!pairs && !u) || n_tok <= 0 || cols <= 0 || (!out_f32 && !act)) return SYN_ERR_INVALID;
     if (act && cols % QK) return SYN_ERR_INVALID;
     ActPlanes a{};
     long grid;
@@ -261,8 +269,20 @@ extern "C" int syn_silu_mul(const float* g, const float* u, int n_tok, int cols,
         grid = (long(n_tok) * cols + 255) / 256;
         if (grid > 4096) grid = 4096;
     }
-    return syn_launch(silu_mul_kernel, unsigned(grid), 256, 0, static_cast<cudaStream_t>(stream), g, u, n_tok, cols,
-                      out_f32, a);
+    return pairs ? syn_launch(silu_mul_kernel<true>, unsigned(grid), 256, 0, static_cast<cudaStream_t>(stream), g, u,
+                              n_tok, cols, out_f32, a)
+                 : syn_launch(silu_mul_kernel<false>, unsigned(grid), 256, 0, static_cast<cudaStream_t>(stream), g, u,
+                              n_tok, cols, out_f32, a);
+}
+}  // namespace
+
+extern "C" int syn_silu_mul(const float* g, const float* u, int n_tok, int cols, float* out_f32, void* act,
+                            void* stream) {
+    return launch_silu_mul(false, g, u, n_tok, cols, out_f32, act, stream);
+}
+
+int syn_silu_mul_pairs(const float* gu, int n_tok, int cols, float* out_f32, void* act, cudaStream_t stream) {
+    return launch_silu_mul(true, gu, nullptr, n_tok, cols, out_f32, act, stream);
 }
 
 extern "C" int syn_add(const float* a, const float* b, float* out, size_t n, void* stream) {

@@ -352,21 +352,22 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_lane_kernel(GemvArgs p) {
 // 32-byte reads spread over the banks) sit in shared memory once per CTA.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
-// W warps per CTA, batches of about BB bytes of rows.
-template <int TYPE, int W, int BB>
+// W warps per CTA, batches of about BB bytes of rows, NB batch buffers per warp
+// (NB - 1 batches in flight while the warp works on one).
+template <int TYPE, int W, int BB, int NB>
 __global__ void __launch_bounds__(W * 32) gemv_stage_kernel(GemvArgs p) {
     extern __shared__ __align__(128) unsigned char smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const StageShape sh = stage_shape(TYPE, p.cols, W, BB);
+    const StageShape sh = stage_shape(TYPE, p.cols, W, BB, NB);
     const int nb = sh.nb, nch = sh.nch, R = sh.R;
     const size_t row_b = sh.row_b, qbytes = planar_quant_bytes(TYPE, p.cols);
     uint8_t* aq = smem;
     float2* dsum = reinterpret_cast<float2*>(smem + a16(sact_off(nb)));
     unsigned char* wbase = smem + sh.act_bytes + size_t(warp) * sh.warp_bytes;
     uint64_t* bars = reinterpret_cast<uint64_t*>(wbase);
-    unsigned char* buf = wbase + 32;
-    float2* stage = reinterpret_cast<float2*>(buf + 2 * sh.batch_bytes);
-    float* chsum = reinterpret_cast<float*>(buf + 2 * sh.batch_bytes + a16(sh.stage_floats2 * 8));
+    unsigned char* buf = wbase + 64;
+    float2* stage = reinterpret_cast<float2*>(buf + NB * sh.batch_bytes);
+    float* chsum = reinterpret_cast<float*>(buf + NB * sh.batch_bytes + a16(sh.stage_floats2 * 8));
     const long n_batch = (p.rows + R - 1) / R;
     const long gw = long(blockIdx.x) * W + warp, nw = long(gridDim.x) * W;
     const long k0 = n_batch * gw / nw, k1 = n_batch * (gw + 1) / nw;
@@ -374,14 +375,14 @@ __global__ void __launch_bounds__(W * 32) gemv_stage_kernel(GemvArgs p) {
     auto batch_rows = [&](int k) { return int(min(long(R), long(p.rows) - (k0 + k) * R)); };
     auto issue = [&](int k) {
         const uint32_t bytes = uint32_t(size_t(batch_rows(k)) * row_b);
-        mbar_expect_tx(&bars[k & 1], bytes);
-        bulk_copy_g2s(buf + size_t(k & 1) * sh.batch_bytes, p.w + size_t((k0 + k) * R) * row_b, bytes, &bars[k & 1]);
+        mbar_expect_tx(&bars[k % NB], bytes);
+        bulk_copy_g2s(buf + size_t(k % NB) * sh.batch_bytes, p.w + size_t((k0 + k) * R) * row_b, bytes,
+                      &bars[k % NB]);
     };
     if (lane == 0) {
-        mbar_init(&bars[0], 1);
-        mbar_init(&bars[1], 1);
+        for (int i = 0; i < NB; ++i) mbar_init(&bars[i], 1);
         mbar_init_fence();
-        for (int k = 0; k < min(2, nbatch); ++k) issue(k);
+        for (int k = 0; k < min(NB, nbatch); ++k) issue(k);
     }
     __syncwarp();
     pdl_launch_dependents();
@@ -404,13 +405,13 @@ __global__ void __launch_bounds__(W * 32) gemv_stage_kernel(GemvArgs p) {
     int k = 0;
     bool ok = true;
     for (; k < nbatch; ++k) {
-        const bool got = mbar_wait_bounded(&bars[k & 1], uint32_t((k >> 1) & 1), kWaitLimitNs);
+        const bool got = mbar_wait_bounded(&bars[k % NB], uint32_t((k / NB) & 1), kWaitLimitNs);
         if (!__all_sync(0xffffffffu, got)) {
             ok = false;
             break;
         }
         const int rows_k = batch_rows(k);
-        stage_batch<TYPE>(buf + size_t(k & 1) * sh.batch_bytes, rows_k, sh, qbytes, aq, dsum, stage, chsum, lane);
+        stage_batch<TYPE>(buf + size_t(k % NB) * sh.batch_bytes, rows_k, sh, qbytes, aq, dsum, stage, chsum, lane);
         const float y = stage_row(chsum, nch, rows_k, lane);
         const long row = (k0 + k) * R + lane;
         if (p.out_mode == SYN_OUT_SILU_PAIRS) {
@@ -432,15 +433,15 @@ __global__ void __launch_bounds__(W * 32) gemv_stage_kernel(GemvArgs p) {
             else p.y[row] = v;
         }
         __syncwarp();
-        if (lane == 0 && k + 2 < nbatch) {
+        if (lane == 0 && k + NB < nbatch) {
             fence_async_shared();  // the warp's reads of this buffer come before the copy that refills it
-            issue(k + 2);
+            issue(k + NB);
         }
     }
     if (!ok && lane == 0) {
         // record it, then let the copies still in flight into this warp's buffers land (bounded)
         atomicAdd(&g_gemv_timeouts, 1u);
-        for (int q = k; q < min(nbatch, k + 2); ++q) mbar_wait_bounded(&bars[q & 1], uint32_t((q >> 1) & 1), kWaitLimitNs);
+        for (int q = k; q < min(nbatch, k + NB); ++q) mbar_wait_bounded(&bars[q % NB], uint32_t((q / NB) & 1), kWaitLimitNs);
     }
 }
 
@@ -591,44 +592,45 @@ int launch_lane(const GemvArgs& p, int S, cudaStream_t s) {
 struct StageCfg {
     int warps;
     int batch;
+    int nbuf;
 };
 // The configurations the staged kernel is built for: warps per CTA, batch bytes.
-constexpr StageCfg kStageCfgs[] = {{8, 9728}, {8, 16384}, {12, 4864}, {16, 4864}, {4, 16384}, {5, 16384}};
+constexpr StageCfg kStageCfgs[] = {{8, 9728, 2}, {8, 4864, 4}, {6, 9728, 3}, {8, 6400, 3}, {12, 4864, 3},
+                                   {16, 4864, 2}};
 
 StageCfg stage_cfg(int type, int rows, int cols) {
     (void)rows;
-    // SYN_GEMV_CFG="warps,batch" picks a built configuration (tuning sweeps); 8 warps
-    // of ~9.7 KB batches measured best on every Llama-3-8B shape
+    // SYN_GEMV_CFG="warps,batch,buffers" picks a built configuration (tuning sweeps)
     static const StageCfg forced = [] {
-        StageCfg c{0, 0};
+        StageCfg c{0, 0, 0};
         if (const char* e = std::getenv("SYN_GEMV_CFG")) {
-            int w = 0, b = 0;
-            if (std::sscanf(e, "%d,%d", &w, &b) == 2)
+            int w = 0, b = 0, n = 0;
+            if (std::sscanf(e, "%d,%d,%d", &w, &b, &n) == 3)
                 for (const StageCfg& k : kStageCfgs)
-                    if (k.warps == w && k.batch == b) c = k;
+                    if (k.warps == w && k.batch == b && k.nbuf == n) c = k;
         }
         return c;
     }();
     if (forced.warps) return forced;
     (void)type;
     (void)cols;
-    return {8, 9728};
+    return kStageCfgs[0];
 }
 
 // Whether the staged kernel takes this one-token shape (gate/up pairs need
 // even batches).
 bool stage_ok(int type, int rows, int cols, int out_mode) {
     const StageCfg cfg = stage_cfg(type, rows, cols);
-    const StageShape sh = stage_shape(type, cols, cfg.warps, size_t(cfg.batch));
+    const StageShape sh = stage_shape(type, cols, cfg.warps, size_t(cfg.batch), cfg.nbuf);
     if (sh.smem > 200 * 1024) return false;
     if (out_mode == SYN_OUT_SILU_PAIRS && (sh.R % 2 || rows % 2)) return false;
     return true;
 }
 
-template <int TYPE, int W, int BB>
+template <int TYPE, int W, int BB, int NB>
 int launch_stage_cfg(const GemvArgs& p, cudaStream_t s) {
-    auto k = gemv_stage_kernel<TYPE, W, BB>;
-    const StageShape sh = stage_shape(TYPE, p.cols, W, BB);
+    auto k = gemv_stage_kernel<TYPE, W, BB, NB>;
+    const StageShape sh = stage_shape(TYPE, p.cols, W, BB, NB);
     int st = configure(reinterpret_cast<const void*>(k), sh.smem);
     if (st) return st;
     // One CTA per SM (W warps streaming ~BB-byte batches of rows each).
@@ -640,12 +642,15 @@ int launch_stage_cfg(const GemvArgs& p, cudaStream_t s) {
 template <int TYPE>
 int launch_stage(const GemvArgs& p, cudaStream_t s) {
     const StageCfg c = stage_cfg(TYPE, p.rows, p.cols);
-    if (c.warps == 16 && c.batch == 4864) return launch_stage_cfg<TYPE, 16, 4864>(p, s);
-    if (c.warps == 12 && c.batch == 4864) return launch_stage_cfg<TYPE, 12, 4864>(p, s);
-    if (c.warps == 8 && c.batch == 16384) return launch_stage_cfg<TYPE, 8, 16384>(p, s);
-    if (c.warps == 4 && c.batch == 16384) return launch_stage_cfg<TYPE, 4, 16384>(p, s);
-    if (c.warps == 5 && c.batch == 16384) return launch_stage_cfg<TYPE, 5, 16384>(p, s);
-    return launch_stage_cfg<TYPE, 8, 9728>(p, s);
+#define SYN_STAGE_CFG(w, b, n) \
+    if (c.warps == w && c.batch == b && c.nbuf == n) return launch_stage_cfg<TYPE, w, b, n>(p, s);
+    SYN_STAGE_CFG(8, 4864, 4)
+    SYN_STAGE_CFG(6, 9728, 3)
+    SYN_STAGE_CFG(8, 6400, 3)
+    SYN_STAGE_CFG(12, 4864, 3)
+    SYN_STAGE_CFG(16, 4864, 2)
+#undef SYN_STAGE_CFG
+    return launch_stage_cfg<TYPE, 8, 9728, 2>(p, s);
 }
 
 // ---- batched tokens on integer tensor cores --------------------------------------
@@ -1026,6 +1031,56 @@ extern "C" int syn_gemv(const syn_gemv_args* a, void* stream) {
     if (a->type == SYN_Q4_0)
         return a->n_tok == 1 ? launch_lane<SYN_Q4_0, 1>(p, S, s) : launch_lane<SYN_Q4_0, 2>(p, S, s);
     return a->n_tok == 1 ? launch_lane<SYN_Q8_0, 1>(p, S, s) : launch_lane<SYN_Q8_0, 2>(p, S, s);
+}
+
+unsigned* syn_gemv_timeout_word() {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_gemv_timeouts) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    return static_cast<unsigned*>(p);
+}
+
+namespace {
+// 32 gathered words read as a GEMV input quantizer reads them (tp_load_n),
+// awaiting an epoch they never carry: every read must give up, not hang.
+__global__ void tp_wait_check_kernel(TpSync t, const uint64_t* words, float* out) {
+    const unsigned ep = *t.epoch;
+    float v[16];
+    tp_load_n(t, words + 16 * (threadIdx.x & 1), ep, v);
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) s += v[i];
+    out[threadIdx.x] = s;
+}
+}  // namespace
+
+extern "C" int syn_check_tp_wait(unsigned wait_us, int* errors) {
+    if (!errors) return SYN_ERR_INVALID;
+    char* buf = nullptr;
+    int st = syn_cuda_status(cudaMalloc(&buf, 4096));
+    if (st) return st;
+    st = syn_cuda_status(cudaMemset(buf, 0, 4096));  // words of epoch 0; the reads await epoch 1
+    unsigned one = 1;
+    if (!st) st = syn_cuda_status(cudaMemcpy(buf + 256, &one, 4, cudaMemcpyHostToDevice));
+    TpSync t;
+    t.peers = reinterpret_cast<char* const*>(buf + 512);
+    t.epoch = reinterpret_cast<const unsigned*>(buf + 256);
+    t.err = reinterpret_cast<unsigned*>(buf + 260);
+    t.world = 1;
+    t.in_ll = 1;
+    t.wait_ns = (unsigned long long)wait_us * 1000ull;
+    if (!st) {
+        tp_wait_check_kernel<<<1, 32>>>(t, reinterpret_cast<const uint64_t*>(buf + 1024), reinterpret_cast<float*>(buf + 2048));
+        st = syn_check_launch();
+    }
+    if (!st) st = syn_cuda_status(cudaDeviceSynchronize());
+    unsigned n = 0;
+    if (!st) st = syn_cuda_status(cudaMemcpy(&n, buf + 260, 4, cudaMemcpyDeviceToHost));
+    cudaFree(buf);
+    *errors = int(n);
+    return st;
 }
 
 extern "C" int syn_device_errors(void) {

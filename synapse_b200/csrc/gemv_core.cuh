@@ -248,7 +248,7 @@ struct StageShape {
 };
 
 __host__ __device__ inline StageShape stage_shape(int type, int cols, int warps = kStageWarps,
-                                                  size_t batch_target = kBatchBytes) {
+                                                  size_t batch_target = kBatchBytes, int nbuf = 2) {
     StageShape s;
     s.nb = cols / QK;
     s.nch = (s.nb + 31) / 32;
@@ -262,7 +262,7 @@ __host__ __device__ inline StageShape stage_shape(int type, int cols, int warps 
     s.batch_bytes = size_t(R) * s.row_b;
     s.act_bytes = a16(a16(sact_off(s.nb)) + size_t(s.nb) * 8);
     s.stage_floats2 = size_t(R) * (s.nb + s.nch);    // one float2 of padding per chunk
-    s.warp_bytes = 32 + 2 * s.batch_bytes + a16(s.stage_floats2 * 8) + a16(size_t(R) * s.nch * 4);
+    s.warp_bytes = 64 + size_t(nbuf) * s.batch_bytes + a16(s.stage_floats2 * 8) + a16(size_t(R) * s.nch * 4);
     s.smem = s.act_bytes + size_t(warps) * s.warp_bytes;
     return s;
 }

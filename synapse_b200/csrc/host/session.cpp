@@ -90,6 +90,11 @@ struct tensor {
 struct syn_session {
     syn_llama_config cfg{};
     int max_ctx = 0, device = 0;
+    // run(batch): sequences with their own KV cache, and tokens one batched call carries
+    int max_seqs = 1, max_batch = 1;
+    struct batch_buffers {
+        size_t tok, pos, arg, x, x2, q, k, v, attn, act, gu, g, u, logits, scratch, am_ws;
+    } bo{};
     syn_tp* tp = nullptr;   // tensor-parallel group (not owned); NULL = one GPU
     syn_tp_layout part{};   // this rank's share (the whole model when world = 1)
     // Gathers by peer stores (world > 1): the producers store into every
@@ -120,6 +125,15 @@ struct syn_session {
     int32_t* h_io = nullptr;   // pinned: token, pos
     float* h_logits = nullptr; // pinned
     int32_t* h_next = nullptr; // pinned
+    // Health of the last step, copied out by the step graph: the peer word reads
+    // that gave up (tensor parallelism) and the device's counters of bounded copy
+    // waits that gave up (GEMV, attention), against their values at open.
+    unsigned* h_status = nullptr;  // pinned: [0] peer wait errors, [1] GEMV, [2] attention
+    unsigned* gemv_to = nullptr;
+    unsigned* attn_to = nullptr;
+    unsigned status_base[2] = {0, 0};
+    unsigned long long tp_wait_ns = 2000000000ull;  // SYN_TP_WAIT_MS
+    bool failed = false;  // a step found a wait that gave up: every later step fails too
     cudaGraphExec_t step_exec = nullptr, gen_exec = nullptr, prof_exec = nullptr;
     std::vector<cudaEvent_t> prof_events;
     bool use_graph = true;
@@ -130,9 +144,10 @@ struct syn_session {
     float* logits() { return tf(p2p ? logits_plain_t : logits_t); }
     void* tb(int t) { return arena + act_off + tensors[t].off; }
     int32_t* io() { return at<int32_t>(io_off); }
-    uint16_t* kv(int layer, int which) {
-        const size_t per = size_t(max_ctx) * part.n_kv * cfg.head_dim;
-        return at<uint16_t>(kv_off) + (size_t(layer) * 2 + which) * per;
+    // halves of one sequence's cache of one layer (K or V); sequence i's rows follow sequence i - 1's
+    size_t seq_halves() const { return size_t(max_ctx) * part.n_kv * cfg.head_dim; }
+    uint16_t* kv(int layer, int which, int seq = 0) {
+        return at<uint16_t>(kv_off) + ((size_t(layer) * 2 + which) * max_seqs + seq) * seq_halves();
     }
 };
 
@@ -570,12 +585,36 @@ int enqueue_ops(syn_session& s, cudaStream_t st) {
     return SYN_OK;
 }
 
+// The step's health words into the pinned status block (see syn_session).
+int enqueue_status(syn_session& s, cudaStream_t st) {
+    int rc = SYN_OK;
+    if (s.p2p) rc = cuda(cudaMemcpyAsync(s.h_status, s.arena + s.tp_off + 68, 4, cudaMemcpyDeviceToHost, st));
+    if (!rc && s.gemv_to) rc = cuda(cudaMemcpyAsync(s.h_status + 1, s.gemv_to, 4, cudaMemcpyDeviceToHost, st));
+    if (!rc && s.attn_to) rc = cuda(cudaMemcpyAsync(s.h_status + 2, s.attn_to, 4, cudaMemcpyDeviceToHost, st));
+    return rc;
+}
+
+// SYN_ERR_TIMEOUT once a bounded wait has given up (the session stays failed:
+// a peer's words that never arrived leave later reads unwaited, and a copy
+// that never landed leaves its kernel's output incomplete).
+int check_status(syn_session& s) {
+    if (!s.failed && (s.h_status[0] != 0 || s.h_status[1] != s.status_base[0] || s.h_status[2] != s.status_base[1])) {
+        s.failed = true;
+        char msg[160];
+        std::snprintf(msg, sizeof msg, "a bounded wait gave up: %u peer word reads, %u GEMV and %u attention copies",
+                      s.h_status[0], s.h_status[1] - s.status_base[0], s.h_status[2] - s.status_base[1]);
+        syn_set_error(msg);
+    }
+    return s.failed ? SYN_ERR_TIMEOUT : SYN_OK;
+}
+
 int enqueue_step(syn_session& s, cudaStream_t st) {
     int rc = cuda(cudaMemcpyAsync(s.io(), s.h_io, 2 * sizeof(int32_t), cudaMemcpyHostToDevice, st));
     if (!rc) rc = enqueue_ops(s, st);
     if (!rc) rc = cuda(cudaMemcpyAsync(s.h_logits, s.logits(), size_t(s.cfg.n_vocab) * 4,
                                        cudaMemcpyDeviceToHost, st));
     if (!rc) rc = cuda(cudaMemcpyAsync(s.h_next, s.io() + 2, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+    if (!rc) rc = enqueue_status(s, st);
     return rc;
 }
 
@@ -621,7 +660,7 @@ int capture(syn_session& s, int (*fn)(syn_session&, cudaStream_t), cudaGraphExec
 int finish(syn_session& s, layout_builder& lb) {
     const syn_llama_config& c = s.cfg;
     s.weight_bytes = lb.off;
-    s.kv_bytes = size_t(c.n_layer) * 2 * s.max_ctx * s.part.n_kv * c.head_dim * 2;
+    s.kv_bytes = size_t(c.n_layer) * 2 * s.max_seqs * s.seq_halves() * 2;
     s.kv_off = lb.take(s.kv_bytes);
     build_step(s);
     plan_p2p(s);
@@ -634,6 +673,27 @@ int finish(syn_session& s, layout_builder& lb) {
     s.argmax_ws_off = lb.take(syn_argmax_ws_bytes(1));  // persistent: its counters must stay zero between steps
     s.rope_tab_off = lb.take(size_t(s.max_ctx) * c.head_dim * 4);
     if (s.n_gathers) s.tp_off = lb.take(128);  // peers[8], epoch at +64, wait errors at +68
+    if (s.max_batch > 1 || s.max_seqs > 1) {  // run(batch) buffers: max_batch rows each
+        const size_t B = size_t(s.max_batch), d = size_t(c.n_embd), hd = size_t(c.head_dim);
+        const size_t qall = size_t(c.n_head) * hd, kvall = size_t(c.n_head_kv) * hd, ff = size_t(c.n_ff);
+        const int widest = int(std::max({d, qall, ff}));
+        s.bo.tok = lb.take(B * 4);
+        s.bo.pos = lb.take(B * 4);
+        s.bo.arg = lb.take(B * 4);
+        s.bo.x = lb.take(B * d * 4);
+        s.bo.x2 = lb.take(B * d * 4);
+        s.bo.q = lb.take(B * qall * 4);
+        s.bo.k = lb.take(B * kvall * 4);
+        s.bo.v = lb.take(B * kvall * 4);
+        s.bo.attn = lb.take(B * qall * 4);
+        s.bo.act = lb.take(syn_q8_act_bytes(s.max_batch, widest));
+        s.bo.gu = lb.take(B * 2 * ff * 4);
+        s.bo.g = lb.take(B * ff * 4);
+        s.bo.u = lb.take(B * ff * 4);
+        s.bo.logits = lb.take(B * size_t(c.n_vocab) * 4);
+        s.bo.scratch = lb.take(syn_attention_scratch_bytes(s.max_batch, c.n_head, c.n_head_kv, c.head_dim, s.max_ctx));
+        s.bo.am_ws = lb.take(syn_argmax_ws_bytes(s.max_batch));
+    }
     s.arena_bytes = lb.off;
     if (const char* e = std::getenv("SYN_ATTN_ORDER")) s.attn_order = std::strcmp(e, "split") == 0 ? SYN_ORDER_SPLIT : SYN_ORDER_REFERENCE;
     s.theta_scale = std::pow(c.rope_base, -2.0f / float(c.head_dim));  // attention.hpp:47
@@ -643,8 +703,20 @@ int finish(syn_session& s, layout_builder& lb) {
     if ((rc = cuda(cudaMalloc(&s.arena, s.arena_bytes)))) return rc;
     if ((rc = cuda(cudaMemset(s.arena + s.kv_off, 0, s.arena_bytes - s.kv_off)))) return rc;
     if ((rc = cuda(cudaMallocHost(&s.h_io, 64)))) return rc;
-    if ((rc = cuda(cudaMallocHost(&s.h_logits, size_t(c.n_vocab) * 4)))) return rc;
+    if ((rc = cuda(cudaMallocHost(&s.h_logits, size_t(c.n_vocab) * 4 * std::max(1, s.max_batch))))) return rc;
     if ((rc = cuda(cudaMallocHost(&s.h_next, 64)))) return rc;
+    if ((rc = cuda(cudaMallocHost(&s.h_status, 64)))) return rc;
+    std::memset(s.h_status, 0, 64);
+    if (const char* e = std::getenv("SYN_TP_WAIT_MS")) {
+        const double ms = std::atof(e);
+        if (ms > 0) s.tp_wait_ns = (unsigned long long)(ms * 1e6);
+    }
+    s.gemv_to = syn_gemv_timeout_word();
+    s.attn_to = syn_attn_timeout_word();
+    if (s.gemv_to && (rc = cuda(cudaMemcpy(&s.status_base[0], s.gemv_to, 4, cudaMemcpyDeviceToHost)))) return rc;
+    if (s.attn_to && (rc = cuda(cudaMemcpy(&s.status_base[1], s.attn_to, 4, cudaMemcpyDeviceToHost)))) return rc;
+    s.h_status[1] = s.status_base[0];
+    s.h_status[2] = s.status_base[1];
     return SYN_OK;
 }
 
@@ -705,6 +777,7 @@ TpSync tp_sync(syn_session& s, const op& o) {
     t.in_ll = o.in_words;
     t.res_ll = o.res_words;
     t.out_ll = o.out_words;
+    t.wait_ns = s.tp_wait_ns;
     if (o.out_words) t.out_off = s.act_off + s.tensors[o.out].off + o.out_off * 8;
     return t;
 }
@@ -855,6 +928,7 @@ void destroy(syn_session* s) {
     if (s->h_io) cudaFreeHost(s->h_io);
     if (s->h_logits) cudaFreeHost(s->h_logits);
     if (s->h_next) cudaFreeHost(s->h_next);
+    if (s->h_status) cudaFreeHost(s->h_status);
     if (s->stream) cudaStreamDestroy(s->stream);
     delete s;
 }
@@ -963,8 +1037,30 @@ extern "C" int syn_session_open_gguf(const char* path, int max_ctx, int device, 
     return syn_session_open_gguf_tp(path, max_ctx, device, nullptr, out);
 }
 
+namespace {
+bool options_ok(const syn_session_options& o) {
+    return o.max_ctx > 0 && o.max_seqs >= 1 && o.max_batch >= 1 && o.max_seqs <= 4096 && o.max_batch <= 64;
+}
+int open_gguf(const char* path, const syn_session_options& o, int device, syn_tp* tp, syn_session** out);
+int open_synthetic(const syn_llama_config* cp, const syn_session_options& o, uint64_t seed, int device, syn_tp* tp,
+                   syn_session** out);
+}  // namespace
+
 extern "C" int syn_session_open_gguf_tp(const char* path, int max_ctx, int device, syn_tp* tp, syn_session** out) {
-    if (!path || !out || max_ctx <= 0) return SYN_ERR_INVALID;
+    const syn_session_options o{max_ctx, 1, 1};
+    return open_gguf(path, o, device, tp, out);
+}
+
+extern "C" int syn_session_open_gguf_ex(const char* path, const syn_session_options* o, int device,
+                                        syn_session** out) {
+    if (!o) return SYN_ERR_INVALID;
+    return open_gguf(path, *o, device, nullptr, out);
+}
+
+namespace {
+int open_gguf(const char* path, const syn_session_options& o, int device, syn_tp* tp, syn_session** out) {
+    const int max_ctx = o.max_ctx;
+    if (!path || !out || !options_ok(o)) return SYN_ERR_INVALID;
     *out = nullptr;
     std::unique_ptr<syn::gguf::file> f;
     std::string err;
@@ -1015,6 +1111,8 @@ extern "C" int syn_session_open_gguf_tp(const char* path, int max_ctx, int devic
     std::unique_ptr<syn_session, void (*)(syn_session*)> s(new syn_session(), destroy);
     s->device = device;
     s->max_ctx = max_ctx;
+    s->max_seqs = o.max_seqs;
+    s->max_batch = o.max_batch;
     syn_llama_config& c = s->cfg;
     c.n_layer = int(n_layer); c.n_embd = int(n_embd); c.n_ff = int(n_ff); c.n_head = int(n_head);
     c.n_head_kv = int(n_kv); c.head_dim = int(hd); c.n_vocab = int(te->ne[1]);
@@ -1080,6 +1178,7 @@ extern "C" int syn_session_open_gguf_tp(const char* path, int max_ctx, int devic
     *out = s.release();
     return SYN_OK;
 }
+}  // namespace
 
 extern "C" int syn_session_open_synthetic(const syn_llama_config* cp, int max_ctx, uint64_t seed, int device,
                                           syn_session** out) {
@@ -1088,7 +1187,21 @@ extern "C" int syn_session_open_synthetic(const syn_llama_config* cp, int max_ct
 
 extern "C" int syn_session_open_synthetic_tp(const syn_llama_config* cp, int max_ctx, uint64_t seed, int device,
                                              syn_tp* tp, syn_session** out) {
-    if (!cp || !out || max_ctx <= 0) return SYN_ERR_INVALID;
+    const syn_session_options o{max_ctx, 1, 1};
+    return open_synthetic(cp, o, seed, device, tp, out);
+}
+
+extern "C" int syn_session_open_synthetic_ex(const syn_llama_config* cp, const syn_session_options* o, uint64_t seed,
+                                             int device, syn_session** out) {
+    if (!o) return SYN_ERR_INVALID;
+    return open_synthetic(cp, *o, seed, device, nullptr, out);
+}
+
+namespace {
+int open_synthetic(const syn_llama_config* cp, const syn_session_options& o, uint64_t seed, int device, syn_tp* tp,
+                   syn_session** out) {
+    const int max_ctx = o.max_ctx;
+    if (!cp || !out || !options_ok(o)) return SYN_ERR_INVALID;
     *out = nullptr;
     const syn_llama_config& c0 = *cp;
     if (c0.n_layer <= 0 || c0.n_embd <= 0 || c0.n_ff <= 0 || c0.n_head <= 0 || c0.n_head_kv <= 0 ||
@@ -1102,6 +1215,8 @@ extern "C" int syn_session_open_synthetic_tp(const syn_llama_config* cp, int max
     std::unique_ptr<syn_session, void (*)(syn_session*)> s(new syn_session(), destroy);
     s->device = device;
     s->max_ctx = max_ctx;
+    s->max_seqs = o.max_seqs;
+    s->max_batch = o.max_batch;
     s->cfg = c0;
     s->cfg.rope_mode = 0;
     const syn_llama_config& c = s->cfg;
@@ -1134,6 +1249,7 @@ extern "C" int syn_session_open_synthetic_tp(const syn_llama_config* cp, int max
     *out = s.release();
     return SYN_OK;
 }
+}  // namespace
 
 extern "C" void syn_session_close(syn_session* s) { destroy(s); }
 
@@ -1189,12 +1305,14 @@ extern "C" int syn_session_step(syn_session* s, uint32_t token, uint32_t pos, fl
                                 int32_t* host_argmax) {
     if (!s) return SYN_ERR_INVALID;
     if (token >= uint32_t(s->cfg.n_vocab) || pos >= uint32_t(s->max_ctx)) return SYN_ERR_RANGE;
+    if (s->failed) return SYN_ERR_TIMEOUT;
     int rc = cuda(cudaSetDevice(s->device));
     if (rc) return rc;
     s->h_io[0] = int32_t(token);
     s->h_io[1] = int32_t(pos);
     rc = s->use_graph ? cuda(cudaGraphLaunch(s->step_exec, s->stream)) : enqueue_step(*s, s->stream);
     if (!rc) rc = cuda(cudaStreamSynchronize(s->stream));
+    if (!rc) rc = check_status(*s);
     if (rc) return rc;
     if (host_logits) std::memcpy(host_logits, s->h_logits, size_t(s->cfg.n_vocab) * 4);
     if (host_argmax) *host_argmax = s->h_next[0];
@@ -1205,6 +1323,7 @@ extern "C" int syn_session_generate(syn_session* s, const uint32_t* prompt, int 
                                     int32_t* host_tokens) {
     if (!s || !prompt || n_prompt <= 0 || n_steps <= 0 || n_prompt > n_steps) return SYN_ERR_INVALID;
     if (uint64_t(pos) + uint64_t(n_steps) > uint64_t(s->max_ctx)) return SYN_ERR_RANGE;
+    if (s->failed) return SYN_ERR_TIMEOUT;
     for (int i = 0; i < n_prompt; ++i)
         if (prompt[i] >= uint32_t(s->cfg.n_vocab)) return SYN_ERR_RANGE;
     int rc = cuda(cudaSetDevice(s->device));
@@ -1219,10 +1338,193 @@ extern "C" int syn_session_generate(syn_session* s, const uint32_t* prompt, int 
     if (!rc && host_tokens) {
         rc = cuda(cudaMemcpyAsync(host_tokens, s->at<int32_t>(s->hist_off), size_t(n_steps) * 4,
                                   cudaMemcpyDeviceToHost, s->stream));
+        if (!rc) rc = enqueue_status(*s, s->stream);
         if (!rc) rc = cuda(cudaStreamSynchronize(s->stream));
+        if (!rc) rc = check_status(*s);
     } else if (!rc) {
         rc = cuda(cudaGetLastError());
     }
+    return rc;
+}
+
+// ---- run(batch): prefill chunks and batched decode --------------------------------
+
+namespace {
+
+// Whether the batched path takes this session: one GPU, Q4_0 / Q8_0 layer
+// matrices (the integer tensor-core GEMV for 3+ rows), any head type but K.
+bool batch_supported(const syn_session& s) {
+    if (s.part.world != 1 || !(s.max_batch > 1 || s.max_seqs > 1)) return false;
+    for (const layer_w& L : s.layers)
+        for (const weight* w : {&L.q, &L.k, &L.v, &L.o, &L.gate, &L.up, &L.down})
+            if (w->type >= 0 && !w->quant()) return false;
+    return s.head.quant() || s.head.type == SYN_F32 || s.head.type == SYN_F16;
+}
+
+// Y[n][rows] = rows [row0, row0 + rows) of w times the Q8_0 activations (+ residual).
+int batch_matmul(syn_session& s, const weight& w, int row0, int rows, const void* act, int n, float* y,
+                 const float* residual) {
+    const char* base = s.arena + w.off + syn_weight_bytes(w.type, row0, w.cols, w.layout);
+    return syn_gemv_q(w.type, base, w.layout, rows, w.cols, act, n, y, residual, s.stream);
+}
+
+// run(batch) (session.hpp:143-156, the ops of session.hpp:287-374 over n rows),
+// launched op by op on the session's stream.
+//   prefill: rows are the tokens of sequence seq at positions pos[0], pos[0] + 1,
+//            ...; all their K/V rows are appended first (session.hpp:349-356),
+//            then every row attends over the shared cache up to its position;
+//            the logits are the last row's (op_last_row).
+//   decode:  row i is the next token of sequence i at pos[i]; logits of every row.
+// Every row's arithmetic is the one-token step's: the GEMV and attention give
+// each row the bits a single-token call gives it (the reference's G1).
+int run_batch(syn_session& s, int n, bool prefill, int seq) {
+    const syn_llama_config& c = s.cfg;
+    cudaStream_t st = s.stream;
+    const int d = c.n_embd, hd = c.head_dim, ff = c.n_ff;
+    const int qrows = c.n_head * hd, kvrows = c.n_head_kv * hd;
+    float *x = s.at<float>(s.bo.x), *x2 = s.at<float>(s.bo.x2), *q = s.at<float>(s.bo.q), *k = s.at<float>(s.bo.k),
+          *v = s.at<float>(s.bo.v), *attn = s.at<float>(s.bo.attn), *gu = s.at<float>(s.bo.gu),
+          *g = s.at<float>(s.bo.g), *u = s.at<float>(s.bo.u), *logits = s.at<float>(s.bo.logits);
+    void* act = s.arena + s.bo.act;
+    int32_t *tok = s.at<int32_t>(s.bo.tok), *pos = s.at<int32_t>(s.bo.pos), *arg = s.at<int32_t>(s.bo.arg);
+    int rc = syn_embed(s.embd.type, s.arena + s.embd.off, s.embd.layout, s.embd.rows, s.embd.cols, tok, n, x, st);
+    for (int l = 0; l < c.n_layer && !rc; ++l) {
+        const layer_w& L = s.layers[l];
+        rc = syn_rms_norm(x, s.at<float>(L.attn_norm.off), n, d, c.rms_eps, nullptr, act, st);
+        if (!rc && L.fused_qkv) {
+            rc = batch_matmul(s, L.q, 0, qrows, act, n, q, nullptr);
+            if (!rc) rc = batch_matmul(s, L.q, qrows, kvrows, act, n, k, nullptr);
+            if (!rc) rc = batch_matmul(s, L.q, qrows + kvrows, kvrows, act, n, v, nullptr);
+        } else if (!rc) {
+            rc = batch_matmul(s, L.q, 0, qrows, act, n, q, nullptr);
+            if (!rc) rc = batch_matmul(s, L.k, 0, kvrows, act, n, k, nullptr);
+            if (!rc) rc = batch_matmul(s, L.v, 0, kvrows, act, n, v, nullptr);
+        }
+        if (rc) break;
+        syn_attention_args a{};
+        a.q = q;
+        a.k = k;
+        a.v = v;
+        a.k_cache = s.kv(l, 0, prefill ? seq : 0);
+        a.v_cache = s.kv(l, 1, prefill ? seq : 0);
+        a.pos = pos;
+        a.out = attn;
+        a.scratch = s.arena + s.bo.scratch;
+        a.cache_stride = prefill ? 0 : s.seq_halves();
+        a.n_q = n;
+        a.n_head = c.n_head;
+        a.n_kv = c.n_head_kv;
+        a.head_dim = hd;
+        a.max_len = s.max_ctx;
+        a.append = prefill ? 0 : 1;
+        a.rope = 1;
+        a.rope_mode = c.rope_mode;
+        a.theta_scale = s.theta_scale;
+        a.scale = s.scale;
+        a.freq_factors = s.has_ff ? s.at<float>(s.ff_off) : nullptr;
+        a.rope_table = s.at<float>(s.rope_tab_off);
+        a.order = s.attn_order;
+        if (prefill) rc = syn_rope_kv_append(&a, st);  // every row's K/V before any row attends
+        if (!rc) rc = syn_attention(&a, st);
+        if (!rc) rc = syn_quantize_q8_0(attn, n, qrows, act, st);
+        if (!rc) rc = batch_matmul(s, L.o, 0, d, act, n, x2, x);
+        if (!rc) rc = syn_rms_norm(x2, s.at<float>(L.ffn_norm.off), n, d, c.rms_eps, nullptr, act, st);
+        if (rc) break;
+        if (L.gu_pairs) {  // gate i at row 2i, up i at 2i + 1
+            rc = batch_matmul(s, L.gate, 0, 2 * ff, act, n, gu, nullptr);
+            if (!rc) rc = syn_silu_mul_pairs(gu, n, ff, nullptr, act, st);
+        } else {
+            if (L.fused_gu) {
+                rc = batch_matmul(s, L.gate, 0, ff, act, n, g, nullptr);
+                if (!rc) rc = batch_matmul(s, L.gate, ff, ff, act, n, u, nullptr);
+            } else {
+                rc = batch_matmul(s, L.gate, 0, ff, act, n, g, nullptr);
+                if (!rc) rc = batch_matmul(s, L.up, 0, ff, act, n, u, nullptr);
+            }
+            if (!rc) rc = syn_silu_mul(g, u, n, ff, nullptr, act, st);
+        }
+        if (!rc) rc = batch_matmul(s, L.down, 0, d, act, n, x, x2);
+    }
+    if (rc) return rc;
+    // the output rows: the last one (prefill) or all of them
+    const int rows = prefill ? 1 : n;
+    const float* xo = prefill ? x + size_t(n - 1) * d : x;
+    const bool quant_head = s.head.quant();
+    rc = syn_rms_norm(xo, s.at<float>(s.out_norm.off), rows, d, c.rms_eps, quant_head ? nullptr : x2,
+                      quant_head ? act : nullptr, st);
+    if (!rc)
+        rc = quant_head ? syn_gemv_q(s.head.type, s.arena + s.head.off, s.head.layout, s.head.rows, s.head.cols, act,
+                                     rows, logits, nullptr, st)
+                        : syn_gemv_f(s.head.type, s.arena + s.head.off, s.head.rows, s.head.cols, x2, rows, logits,
+                                     nullptr, st);
+    if (!rc) rc = syn_argmax_ws(logits, rows, c.n_vocab, arg, s.arena + s.bo.am_ws, st);
+    return rc;
+}
+
+// Inputs to the device, run(batch), outputs back, the step's health.
+int batch_call(syn_session& s, int n, const int32_t* tokens, const int32_t* positions, bool prefill, int seq,
+               float* host_logits, int32_t* host_argmax) {
+    const int rows = prefill ? 1 : n;
+    int rc = cuda(cudaSetDevice(s.device));
+    if (!rc) rc = cuda(cudaMemcpyAsync(s.arena + s.bo.tok, tokens, size_t(n) * 4, cudaMemcpyHostToDevice, s.stream));
+    if (!rc) rc = cuda(cudaMemcpyAsync(s.arena + s.bo.pos, positions, size_t(n) * 4, cudaMemcpyHostToDevice, s.stream));
+    if (!rc) rc = run_batch(s, n, prefill, seq);
+    if (!rc && host_logits)
+        rc = cuda(cudaMemcpyAsync(s.h_logits, s.arena + s.bo.logits, size_t(rows) * s.cfg.n_vocab * 4,
+                                  cudaMemcpyDeviceToHost, s.stream));
+    if (!rc) rc = cuda(cudaMemcpyAsync(s.h_next, s.arena + s.bo.arg, size_t(rows) * 4, cudaMemcpyDeviceToHost, s.stream));
+    if (!rc) rc = enqueue_status(s, s.stream);
+    if (!rc) rc = cuda(cudaStreamSynchronize(s.stream));
+    if (!rc) rc = check_status(s);
+    if (rc) return rc;
+    if (host_logits) std::memcpy(host_logits, s.h_logits, size_t(rows) * s.cfg.n_vocab * 4);
+    if (host_argmax) std::memcpy(host_argmax, s.h_next, size_t(rows) * 4);
+    return SYN_OK;
+}
+
+}  // namespace
+
+extern "C" int syn_session_prefill(syn_session* s, int seq, const uint32_t* tokens, int n, uint32_t pos,
+                                   float* host_logits, int32_t* host_argmax) {
+    if (!s || !tokens || n <= 0) return SYN_ERR_INVALID;
+    if (!batch_supported(*s)) return SYN_ERR_UNSUPPORTED;
+    if (n > s->max_batch || seq < 0 || seq >= s->max_seqs) return SYN_ERR_RANGE;
+    if (uint64_t(pos) + uint64_t(n) > uint64_t(s->max_ctx)) return SYN_ERR_RANGE;
+    if (s->failed) return SYN_ERR_TIMEOUT;
+    std::vector<int32_t> t(n), p(n);
+    for (int i = 0; i < n; ++i) {
+        if (tokens[i] >= uint32_t(s->cfg.n_vocab)) return SYN_ERR_RANGE;
+        t[i] = int32_t(tokens[i]);
+        p[i] = int32_t(pos) + i;
+    }
+    return batch_call(*s, n, t.data(), p.data(), true, seq, host_logits, host_argmax);
+}
+
+extern "C" int syn_session_step_batch(syn_session* s, int n, const uint32_t* tokens, const uint32_t* pos,
+                                      float* host_logits, int32_t* host_argmax) {
+    if (!s || !tokens || !pos || n <= 0) return SYN_ERR_INVALID;
+    if (!batch_supported(*s)) return SYN_ERR_UNSUPPORTED;
+    if (n > s->max_batch || n > s->max_seqs) return SYN_ERR_RANGE;
+    if (s->failed) return SYN_ERR_TIMEOUT;
+    std::vector<int32_t> t(n), p(n);
+    for (int i = 0; i < n; ++i) {
+        if (tokens[i] >= uint32_t(s->cfg.n_vocab) || pos[i] >= uint32_t(s->max_ctx)) return SYN_ERR_RANGE;
+        t[i] = int32_t(tokens[i]);
+        p[i] = int32_t(pos[i]);
+    }
+    return batch_call(*s, n, t.data(), p.data(), false, 0, host_logits, host_argmax);
+}
+
+extern "C" int syn_session_fill_kv_random(syn_session* s, int n_pos, uint64_t seed) {
+    if (!s || n_pos <= 0 || n_pos > s->max_ctx) return SYN_ERR_INVALID;
+    int rc = cuda(cudaSetDevice(s->device));
+    const int row = s->part.n_kv * s->cfg.head_dim;
+    uint64_t id = 0;
+    for (int l = 0; l < s->cfg.n_layer && !rc; ++l)
+        for (int which = 0; which < 2 && !rc; ++which)
+            for (int q = 0; q < s->max_seqs && !rc; ++q)
+                rc = syn_fill_random(SYN_F16, n_pos, row, s->kv(l, which, q), n_pos, 0, seed, ++id, 1.0f, s->stream);
+    if (!rc) rc = cuda(cudaStreamSynchronize(s->stream));
     return rc;
 }
 

@@ -27,6 +27,11 @@ int syn_fill_f32(float* dst, size_t n, float v, cudaStream_t s);
 // argmax, advances the position and picks the next input token.
 int syn_advance(int32_t* io, const int32_t* forced, int32_t* history, cudaStream_t s);
 
+// silu(gate) * up of n_tok tokens whose gate and up values are interleaved
+// (gate i at 2i, up i at 2i + 1 of each token's 2 cols values), optionally
+// quantized to Q8_0 activations (as syn_silu_mul).
+int syn_silu_mul_pairs(const float* gu, int n_tok, int cols, float* out_f32, void* act, cudaStream_t stream);
+
 // Argmax with a caller-owned persistent workspace of syn_argmax_ws_bytes
 // (zeroed once; each launch leaves its counters zero again).
 size_t syn_argmax_ws_bytes(int n_tok);
@@ -79,6 +84,7 @@ struct TpSync {
     int out_ll = 0;                   // the output goes to every rank as words
     int in_ll = 0;                    // the input vector is words (wait for this step's)
     int res_ll = 0;                   // the residual is words (this rank's slice: complete)
+    unsigned long long wait_ns = 2000000000ull;  // a word read gives up after this long and counts an error
 };
 // syn_gemv / syn_attention / the session's argmax with a gather hook (the
 // staged GEMV path only: SYN_ERR_UNSUPPORTED when the shape does not take it).
@@ -91,6 +97,17 @@ int syn_tp_step_begin(unsigned* epoch, cudaStream_t s);
 
 // Bounded waits of the attention kernels that gave up on the current device (-1: unreadable).
 int syn_attn_timeouts();
+// Device addresses (current device) of the counters of bounded copy waits that
+// gave up in the GEMV and attention kernels, for a session to copy out after
+// every step; NULL if they cannot be looked up.
+unsigned* syn_gemv_timeout_word();
+unsigned* syn_attn_timeout_word();
+
+// Self-check of the bounded wait of a tensor-parallel word read: a kernel
+// reads 32 gathered words that never carry the awaited step's epoch, with a
+// limit of wait_us; *errors receives how many reads gave up (at least one when
+// the wait ends as it must). The call allocates its own small buffers.
+extern "C" int syn_check_tp_wait(unsigned wait_us, int* errors);
 
 // Self-check of the library's expf (exp_rn): y = exp_rn(x) and, for
 // comparison, y_ref = exp(double(x)) rounded to float, for n device floats.

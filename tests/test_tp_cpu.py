@@ -171,3 +171,64 @@ def test_sharded_logits_equal_one_process(world, cfg_name, type_layers):
     ref = orc.Llama(cfg, w, max_ctx=n_steps)
     want = np.stack([ref.step(t, pos) for pos, t in enumerate(_tokens(cfg, n_steps))])
     assert np.array_equal(got[0].view(np.uint32), want.view(np.uint32))
+
+
+def _leaving_rank_main(rank, world, port, n_steps, leave_after, q):
+    """Rank 1 decodes leave_after steps of the sharded model and leaves (between steps: nothing of its own is in
+    flight). Rank 0 carries on; its next gather must end with an error within the group's short timeout, not
+    wait forever, and rank 0 must then leave cleanly."""
+    import time
+
+    import torch
+    import torch.distributed as dist
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=3))
+
+    def gather(a):
+        t = torch.from_numpy(np.ascontiguousarray(a, np.float32))
+        parts = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(parts, t)
+        return torch.cat(parts).numpy()
+
+    cfg = TINY
+    w = _model(cfg, model.Q8_0)
+    toks = _tokens(cfg, n_steps)
+    result = {"rank": rank}
+    try:
+        if rank == 1:
+            sharded_decode(cfg, w, toks[:leave_after], n_steps, rank, world, gather)
+            result["left_after"] = leave_after
+            q.put((rank, result))
+            return  # leaves the group between steps
+        t0 = time.perf_counter()
+        try:
+            sharded_decode(cfg, w, toks, n_steps, rank, world, gather)
+            result["error"] = None
+        except Exception as e:  # the gather with the departed rank
+            result["error"] = type(e).__name__
+        result["seconds"] = time.perf_counter() - t0
+        q.put((rank, result))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def test_rank_leaving_between_steps_ends_the_others_next_gather_with_an_error():
+    # failure detection on the host, without a GPU: the group's short timeout turns the departed rank into an
+    # error on the next gather of every other rank
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaving_rank_main, args=(r, 2, port, 6, 2, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    assert got[1]["left_after"] == 2
+    assert got[0]["error"] is not None, got[0]
+    assert got[0]["seconds"] < 60, got[0]
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]

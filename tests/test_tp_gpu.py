@@ -42,7 +42,7 @@ def _tokens(cfg, n):
     return [int(t) for t in np.random.default_rng(11).integers(0, cfg["n_vocab"], n)]
 
 
-def _rank_main(rank, world, port, shape, max_ctx, positions, mode, q):
+def _rank_main(rank, world, port, shape, max_ctx, positions, mode, q, stop_after=None):
     import torch.distributed as dist
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     os.environ["SYN_TP_P2P"] = "1" if mode == "peer_stores" else "0"
@@ -56,6 +56,30 @@ def _rank_main(rank, world, port, shape, max_ctx, positions, mode, q):
         sess = syn.Session.synthetic(cfg, max_ctx=max_ctx, seed=5, device=rank, tp=tp)
         layout = sess.tp_layout()
         toks = _tokens(cfg, len(positions))
+        if stop_after is not None:
+            # every rank steps stop_after times; then rank 1 stops stepping (it stays up, runs nothing) and
+            # rank 0 runs the next step, whose peer word reads must give up after SYN_TP_WAIT_MS
+            import time
+            for t, pos in list(zip(toks, positions))[:stop_after]:
+                sess.step(t, pos)
+            result = {}
+            if rank == 0:
+                t0 = time.perf_counter()
+                try:
+                    sess.step(toks[stop_after], positions[stop_after])
+                    result["first"] = 0
+                except syn.SynapseError as e:
+                    result["first"] = e.status
+                result["seconds"] = time.perf_counter() - t0
+                try:
+                    sess.step(toks[stop_after], positions[stop_after])
+                    result["again"] = 0
+                except syn.SynapseError as e:
+                    result["again"] = e.status
+                result["status"] = sess.tp_status()
+            dist.barrier()  # rank 1 leaves the step loop only here, with nothing in flight
+            q.put((rank, result))
+            return
         logits, nxt = [], []
         for t, pos in zip(toks, positions):
             lg, n = sess.step(t, pos)
@@ -75,12 +99,12 @@ def _rank_main(rank, world, port, shape, max_ctx, positions, mode, q):
         dist.destroy_process_group()
 
 
-def _run_world(world, shape, max_ctx, positions, mode):
+def _run_world(world, shape, max_ctx, positions, mode, stop_after=None):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, shape, max_ctx, positions, mode, q))
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, shape, max_ctx, positions, mode, q, stop_after))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -126,3 +150,46 @@ def test_tp_equals_one_gpu(world, shape, mode):
         assert np.array_equal(g["logits"].view(np.uint32), want.view(np.uint32)), f"rank {r}"
         assert g["next"] == [int(np.argmax(x)) for x in want]
         assert np.array_equal(g["gen"], want_gen), f"rank {r} greedy tokens"
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_long_context_equals_one_gpu(world):
+    # positions past 4096 on the 8B-width model: every rank's logits and tokens are one GPU's bits
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    max_ctx = 4400
+    positions = [0, 1, 2, 3, 2047, 4095, 4096, 4300]
+    got = _run_world(world, "8b_2layer_q4_0", max_ctx, positions, "peer_stores")
+    want, want_gen = _one_gpu("8b_2layer_q4_0", max_ctx, positions)
+    for r in range(world):
+        assert got[r]["status"] == {"peer_stores": True, "wait_errors": 0}, got[r]["status"]
+        assert np.array_equal(got[r]["logits"].view(np.uint32), want.view(np.uint32)), f"rank {r}"
+        assert np.array_equal(got[r]["gen"], want_gen), f"rank {r} greedy tokens"
+
+
+def test_tp_rank_that_stops_stepping_fails_the_others_step(monkeypatch):
+    # failure detection without a GPU fault: rank 1 stops between steps (alive, nothing in flight); rank 0's
+    # next step gives up on rank 1's words after SYN_TP_WAIT_MS and returns SYN_ERR_TIMEOUT (5), and the
+    # session stays failed; both ranks then close normally
+    if _gpus() < 2:
+        pytest.skip("needs 2 GPUs")
+    monkeypatch.setenv("SYN_TP_WAIT_MS", "100")
+    got = _run_world(2, "8b_2layer_q4_0", 64, [0, 1, 2, 3, 4], "peer_stores", stop_after=3)
+    r0 = got[0]
+    assert r0["first"] == 5 and r0["again"] == 5, r0
+    assert r0["status"]["peer_stores"] and r0["status"]["wait_errors"] >= 1, r0
+    assert r0["seconds"] < 30, r0
+
+
+def test_tp_word_wait_gives_up_and_counts():
+    # one GPU: a kernel reads gathered words whose epoch never arrives; every read gives up after the limit
+    # and counts an error instead of waiting forever
+    import ctypes
+    import time
+    L = syn.lib()
+    L.syn_check_tp_wait.argtypes = [ctypes.c_uint, ctypes.POINTER(ctypes.c_int)]
+    errors = ctypes.c_int(-1)
+    t0 = time.perf_counter()
+    assert L.syn_check_tp_wait(5000, ctypes.byref(errors)) == 0
+    assert errors.value >= 1
+    assert time.perf_counter() - t0 < 10
