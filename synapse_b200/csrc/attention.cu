@@ -13,23 +13,23 @@
 // SYN_ORDER_REFERENCE (the default): every float sum in the reference's order
 // at any context length. Three stream-ordered kernels:
 //   scores: one CTA per (chunk of kChunk positions, KV head, query); the
-//           chunk's K rows land in shared memory by one bulk copy each; each
+//           chunk's K rows land in shared memory by tensor copies; each
 //           thread scores one position for the G query heads, every dot a
 //           dimension-order chain of fmas on binary16 values (exact
 //           products, one rounding per add, as the reference's); the
 //           chunk's max per head;
 //   exp:    the context's max M per head from the chunk maxima, e_t =
 //           expf(s_t - M) in place of the scores, the chunk's double sum;
-//   p.V:    one CTA per (query head, 32 output columns); a producer warp
-//           streams the V tile of every 64 positions (a tensor TMA copy) and
-//           the head's e_t (a bulk copy) through a ring of shared-memory
-//           slots; each consumer lane owns one output element and adds p_t
-//           V_t in position order, one fma per position
-//           (attention.hpp:231-243). The normaliser is the chunks'
-//           double sums added in chunk order (a re-association of double
-//           additions of float terms: exact whenever every term is a
-//           multiple of 2^-53 of the sum, and otherwise within a few double
-//           ulps, far inside one float ulp of 1 / sum).
+//   p.V:    one CTA per (query head, 32 output columns): a producer warp
+//           streams V tiles and e_t through a shared-memory ring, a second
+//           warp forms p_t, and a chain warp whose lanes each own one output
+//           element adds p_t V_t in position order, one fma per position
+//           (attention.hpp:231-243).
+//           The normaliser is the chunks' double sums added in chunk order
+//           (a re-association of double additions of float terms: exact
+//           whenever every term is a multiple of 2^-53 of the sum, and
+//           otherwise within a few double ulps, far inside one float ulp of
+//           1 / sum).
 //
 // SYN_ORDER_SPLIT: the p.V sums split over 256-position chunks on tensor
 // cores and re-associated (about 1e-6 relative from the reference past one
@@ -70,8 +70,7 @@ constexpr int kAttnThreads = 256;  // the decode kernel
 constexpr int kChunk = 256;        // positions per CTA: a context of up to kChunk is one chunk (exact order)
 static_assert(kChunk == kAttnThreads, "the p.V kernel gives each thread one position of its chunk");
 constexpr int kPwStride = kChunk + 4;  // floats per head in the p buffer: heads 4 banks apart
-constexpr int kSlotPos = 64;           // positions per slot of the exact p.V kernel's ring
-constexpr int kSlots = 16;             // slots in the ring (1024 positions in flight)
+constexpr int kSlotPos = 128;          // the score scratch's rows are padded to a multiple of this
 constexpr uint64_t kAttnWaitNs = 2000000000ull;  // bounded waits on bulk copies give up after 2 s
 
 __device__ unsigned g_attn_timeouts = 0;  // bounded waits that gave up (syn_device_errors)
@@ -986,49 +985,59 @@ __global__ void __launch_bounds__(kAttnThreads) attn_xe_kernel(AttnParams a) {
     }
 }
 
-// Shared memory of the exact p.V kernel: the ring's V tiles (64 positions x 32
-// columns of binary16), the head's e row of each slot, the consumer's p of two
-// slots as floats, and the barriers.
+// Shared memory of the exact p.V kernel: a ring of kNr slots, each the V tile
+// of kVSlot positions x 32 columns (binary16, as the tensor copy lands it),
+// e_t and p_t of those positions; then the barriers.
+constexpr int kVSlot = kSlotPos;  // positions per slot (128)
+constexpr int kNr = 6;            // slots (768 positions in flight)
+constexpr size_t kXvSmemMost = size_t(120) << 10;  // the p.V kernel's dynamic shared memory when it takes an SM alone
 struct XvSmem {
-    size_t vt, es, pf, bars, total;
+    static constexpr size_t v16 = 0;                                // [kNr][kVSlot][32] binary16
+    static constexpr size_t es = v16 + size_t(kNr) * kVSlot * 64;   // [kNr][kVSlot] e_t
+    static constexpr size_t p32 = es + size_t(kNr) * kVSlot * 4;    // [kNr][kVSlot] p_t as floats
+    static constexpr size_t bars = p32 + size_t(kNr) * kVSlot * 4;  // vfull, efull, pfull, empty: [kNr] each
+    static constexpr size_t total = bars + size_t(4 * kNr) * 8 + 1024;  // + the ring's alignment
 };
-__host__ __device__ inline XvSmem xv_smem() {
-    XvSmem l;
-    l.vt = 0;                                           // [kSlots][64][32] halves, 4 KB per slot
-    l.es = l.vt + size_t(kSlots) * kSlotPos * 32 * 2;   // [kSlots][64] floats
-    l.pf = l.es + size_t(kSlots) * kSlotPos * 4;        // [2][64] floats
-    l.bars = l.pf + size_t(2) * kSlotPos * 4;           // vfull, efull, empty: [kSlots] each
-    l.total = l.bars + size_t(3) * kSlots * 8 + 1024;   // + the alignment of the ring
-    return l;
-}
 
-// p.V in position order: CTA (query head h, 32-column slice s) of query b; warp
-// 0 consumes (lane = output column 32 s + lane, one fma chain each), warp 1
-// produces. One consumer warp per CTA keeps the shared-memory loads per SM to
-// about one per position, under the fma latency the chains are bound by.
-__global__ void __launch_bounds__(64) attn_xv_kernel(AttnParams a, const __grid_constant__ CUtensorMap vmap) {
-    const int G = a.n_head / a.n_kv, H = a.n_head, hd = a.hd;
-    const int ns = (hd + 31) / 32;
-    const int s = blockIdx.x % ns, h = blockIdx.x / ns, g = h / G, b = blockIdx.y;
+// p.V in position order over 32 output columns of one query head: CTA (h *
+// ns + c, b), ns = ceil(head_dim / 32). Three warps:
+//   warp 0, chain:    lane = output column 32 c + lane; acc = fma(p_t,
+//                     V_t,d, acc) for t in order (attention.hpp:231-243;
+//                     each product is exact, so the fma rounds exactly where
+//                     the reference's add does). V comes straight from the
+//                     ring as binary16, 16 positions loaded (and widened)
+//                     ahead of the fmas;
+//   warp 1, producer: one tensor copy of the V tile and one bulk copy of e_t
+//                     per kVSlot positions;
+//   warp 2, p:        p_t = binary16(e_t * scale) (elementwise.hpp:194-197,
+//                     attention.hpp:224-227), scale = float(1 / sum) with sum
+//                     the exp kernel's chunk sums added in chunk order
+//                     (elementwise.hpp:190-193); p_t = 0 and V rows zeroed past
+//                     the context, so that every slot runs whole (fma(0, 0,
+//                     acc) = acc).
+__global__ void __launch_bounds__(96) attn_xv_kernel(AttnParams a, const __grid_constant__ CUtensorMap vmap) {
+    const int G = a.n_head / a.n_kv, H = a.n_head, hd = a.hd, ns = (hd + 31) / 32;
+    const int h = blockIdx.x / ns, c = blockIdx.x % ns, g = h / G, b = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int P = a.pos[b], L = P + 1;
     if (P < 0 || L > a.max_len) return;
-    const int nslot = (L + kSlotPos - 1) / kSlotPos, nchk = (L + kChunk - 1) / kChunk;
+    const int nslot = (L + kVSlot - 1) / kVSlot, nchk = (L + kChunk - 1) / kChunk;
 
     extern __shared__ __align__(16) unsigned char smem_raw[];
     // tensor copies land 128-byte aligned: the ring starts at the next 1 KB boundary
     unsigned char* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
-    const XvSmem sl = xv_smem();
-    uint16_t* vt = reinterpret_cast<uint16_t*>(smem + sl.vt);
-    float* es = reinterpret_cast<float*>(smem + sl.es);
-    float* pf = reinterpret_cast<float*>(smem + sl.pf);
-    uint64_t* vfull = reinterpret_cast<uint64_t*>(smem + sl.bars);
-    uint64_t* efull = vfull + kSlots;
-    uint64_t* empty = efull + kSlots;
+    uint16_t* v16 = reinterpret_cast<uint16_t*>(smem + XvSmem::v16);
+    float* es = reinterpret_cast<float*>(smem + XvSmem::es);
+    float* p32 = reinterpret_cast<float*>(smem + XvSmem::p32);
+    uint64_t* vfull = reinterpret_cast<uint64_t*>(smem + XvSmem::bars);
+    uint64_t* efull = vfull + kNr;
+    uint64_t* pfull = efull + kNr;
+    uint64_t* empty = pfull + kNr;
     __shared__ int abort_flag, issued;
-    if (tid < kSlots) {
+    if (tid < kNr) {
         mbar_init(&vfull[tid], 1);
         mbar_init(&efull[tid], 1);
+        mbar_init(&pfull[tid], 1);
         mbar_init(&empty[tid], 1);
     }
     if (tid == 0) abort_flag = issued = 0;
@@ -1036,121 +1045,138 @@ __global__ void __launch_bounds__(64) attn_xv_kernel(AttnParams a, const __grid_
     __syncthreads();
 
     const size_t hb = size_t(b) * H + size_t(h);  // this CTA's query head
-    const int vx = g * hd + 32 * s, vz = a.v3d ? b : 0;
+    const int vx = g * hd + 32 * c, vz = a.v3d ? b : 0;
     auto issue_v = [&](int k) {
-        uint64_t* bar = &vfull[k % kSlots];
-        mbar_expect_tx(bar, uint32_t(kSlotPos) * 32u * 2u);
-        tma_load_3d(vt + size_t(k % kSlots) * kSlotPos * 32, &vmap, vx, k * kSlotPos, vz, a.v3d != 0, bar);
+        uint64_t* bar = &vfull[k % kNr];
+        mbar_expect_tx(bar, uint32_t(kVSlot) * 64u);
+        tma_load_3d(v16 + size_t(k % kNr) * kVSlot * 32, &vmap, vx, k * kVSlot, vz, a.v3d != 0, bar);
     };
-    auto issue_e = [&](int k) {
-        uint64_t* bar = &efull[k % kSlots];
-        mbar_expect_tx(bar, kSlotPos * 4u);
-        bulk_copy_g2s(es + size_t(k % kSlots) * kSlotPos, a.scores + hb * a.ld + size_t(k) * kSlotPos,
-                      kSlotPos * 4u, bar);
+    auto issue_e = [&](int k) {  // ld is a multiple of kVSlot: the slot's e_t lie inside the row
+        uint64_t* bar = &efull[k % kNr];
+        mbar_expect_tx(bar, kVSlot * 4u);
+        bulk_copy_g2s(es + size_t(k % kNr) * kVSlot, a.scores + hb * a.ld + size_t(k) * kVSlot, kVSlot * 4u, bar);
+    };
+    // A wait that gives up after kAttnWaitNs, or at once when another warp gave up.
+    auto wait = [&](uint64_t* bar, uint32_t par) -> bool {
+        if (mbar_try_wait(bar, par)) return true;
+        const uint64_t t0 = global_ns();
+        while (!mbar_try_wait(bar, par)) {
+            if (*reinterpret_cast<volatile int*>(&abort_flag)) return false;
+            if (global_ns() - t0 > kAttnWaitNs) {
+                if (atomicExch(&abort_flag, 1) == 0) atomicAdd(&g_attn_timeouts, 1u);
+                return false;
+            }
+        }
+        return true;
     };
     // V rows below P were written by earlier calls: their tiles start before the wait
-    const int first = min(kSlots, nslot);
+    const int first = min(kNr, nslot);
     if (warp == 1 && lane == 0)
         for (int k = 0; k < first; ++k)
-            if ((k + 1) * kSlotPos <= P) issue_v(k);
+            if ((k + 1) * kVSlot <= P) issue_v(k);
     pdl_launch_dependents();
-    pdl_wait();  // e, the chunk sums and the appended V row
+    pdl_wait();  // e_t, the chunk sums and the appended V row
 
     if (warp == 1) {
         if (lane == 0) {
             int k = 0;
             for (; k < first; ++k) {
-                if ((k + 1) * kSlotPos > P) issue_v(k);
+                if ((k + 1) * kVSlot > P) issue_v(k);
                 issue_e(k);
             }
             for (; k < nslot; ++k) {
-                const int slot = k % kSlots;
-                if (!mbar_wait_bounded(&empty[slot], uint32_t((k / kSlots - 1) & 1), kAttnWaitNs) ||
-                    *reinterpret_cast<volatile int*>(&abort_flag)) {
-                    if (!*reinterpret_cast<volatile int*>(&abort_flag)) atomicAdd(&g_attn_timeouts, 1u);
-                    atomicExch(&abort_flag, 1);
-                    break;
-                }
+                if (!wait(&empty[k % kNr], uint32_t((k / kNr - 1) & 1))) break;
                 issue_v(k);
                 issue_e(k);
             }
             issued = k;
         }
-    } else {
-        // the normaliser: the chunks' double sums in chunk order; scale = float(1 / sum) (elementwise.hpp:192-193)
+    } else if (warp == 2) {
         float scale = 0.0f;
         if (lane == 0) {
             double sum = 0.0;
-            for (int c = 0; c < nchk; ++c) sum += a.st_s[hb * a.nch + c];
+            for (int j = 0; j < nchk; ++j) sum += a.st_s[hb * a.nch + j];
             scale = float(1.0 / sum);
         }
         scale = __shfl_sync(0xffffffffu, scale, 0);
-        // Two slots in flight: while slot k's fma chain runs, slot k + 1's data has
-        // been waited for, its p formed and its V values taken into registers (and its
-        // ring slot handed back to the producer), so the chain never waits on them.
-        // pf holds p of two slots, [k & 1][64].
-        float acc = 0.0f;
-        bool ok = true;
-        // slot k's data: p_t = binary16(e_t * scale) as floats (attention.hpp:224-227) into pf[k & 1],
-        // its V values as binary16 pairs (positions 2i, 2i + 1) into v; the ring slot released
-        auto fetch = [&](int k, uint32_t (&v)[kSlotPos / 2]) {
-            const int slot = k % kSlots;
-            const uint32_t par = uint32_t((k / kSlots) & 1);
-            const int n = min(kSlotPos, L - k * kSlotPos);
-            __syncwarp();  // the chain that last read pf[k & 1] is done in every lane
-            bool got = mbar_wait_bounded(&efull[slot], par, kAttnWaitNs);
-            got = got && mbar_wait_bounded(&vfull[slot], par, kAttnWaitNs);
-            if (!__all_sync(0xffffffffu, got) || *reinterpret_cast<volatile int*>(&abort_flag)) {
-                if (lane == 0 && !*reinterpret_cast<volatile int*>(&abort_flag)) {
-                    atomicAdd(&g_attn_timeouts, 1u);
-                    atomicExch(&abort_flag, 1);
-                }
-                ok = false;
-                return;
+        for (int k = 0; k < nslot; ++k) {
+            const int slot = k % kNr;
+            const uint32_t par = uint32_t((k / kNr) & 1);
+            const int live = L - k * kVSlot;  // positions of this slot inside the context
+            bool got = wait(&efull[slot], par);
+            if (got && live < kVSlot) got = wait(&vfull[slot], par);  // its tile's rows past the context are zeroed
+            if (!__all_sync(0xffffffffu, got)) break;
+            static_assert(kVSlot == 128, "four positions per lane");
+            const float4 e4 = reinterpret_cast<const float4*>(es + size_t(slot) * kVSlot)[lane];
+            reinterpret_cast<float4*>(p32 + size_t(slot) * kVSlot)[lane] =
+                make_float4(4 * lane < live ? round_f16(__fmul_rn(e4.x, scale)) : 0.0f,
+                            4 * lane + 1 < live ? round_f16(__fmul_rn(e4.y, scale)) : 0.0f,
+                            4 * lane + 2 < live ? round_f16(__fmul_rn(e4.z, scale)) : 0.0f,
+                            4 * lane + 3 < live ? round_f16(__fmul_rn(e4.w, scale)) : 0.0f);
+            if (live < kVSlot) {
+                uint32_t* rows = reinterpret_cast<uint32_t*>(v16 + size_t(slot) * kVSlot * 32);  // 16 words per row
+                for (int i = live * 16 + lane; i < kVSlot * 16; i += 32) rows[i] = 0u;
             }
-            const float2 e2 = reinterpret_cast<const float2*>(es + size_t(slot) * kSlotPos)[lane];
-            reinterpret_cast<float2*>(pf + (k & 1) * kSlotPos)[lane] =
-                make_float2(2 * lane < n ? round_f16(__fmul_rn(e2.x, scale)) : 0.0f,
-                            2 * lane + 1 < n ? round_f16(__fmul_rn(e2.y, scale)) : 0.0f);
-            const uint16_t* vcol = vt + size_t(slot) * kSlotPos * 32 + lane;
-#pragma unroll
-            for (int i = 0; i < kSlotPos / 2; ++i)
-                v[i] = uint32_t(vcol[(2 * i) * 32]) | (uint32_t(vcol[(2 * i + 1) * 32]) << 16);
-            __syncwarp();  // every lane's V read and p written
-            if (lane == 0) mbar_arrive(&empty[slot]);
-        };
-        // out_d += p_t * V_t,d for t in order (attention.hpp:231-243): one fma per position
-        auto chain = [&](int k, const uint32_t (&v)[kSlotPos / 2]) {
-            const int n = min(kSlotPos, L - k * kSlotPos);
-            const float* pk = pf + (k & 1) * kSlotPos;
-            if (n == kSlotPos) {
-#pragma unroll
-                for (int i = 0; i < kSlotPos / 4; ++i) {
-                    const float4 p4 = reinterpret_cast<const float4*>(pk)[i];
-                    const uint32_t w0 = v[2 * i], w1 = v[2 * i + 1];
-                    acc = fmaf(p4.x, f16_from_bits(uint16_t(w0 & 0xffffu)), acc);  // exact products: one
-                    acc = fmaf(p4.y, f16_from_bits(uint16_t(w0 >> 16)), acc);     // rounding per add
-                    acc = fmaf(p4.z, f16_from_bits(uint16_t(w1 & 0xffffu)), acc);
-                    acc = fmaf(p4.w, f16_from_bits(uint16_t(w1 >> 16)), acc);
-                }
-            } else {
-#pragma unroll
-                for (int i = 0; i < kSlotPos / 2; ++i) {
-                    if (2 * i < n) acc = fmaf(pk[2 * i], f16_from_bits(uint16_t(v[i] & 0xffffu)), acc);
-                    if (2 * i + 1 < n) acc = fmaf(pk[2 * i + 1], f16_from_bits(uint16_t(v[i] >> 16)), acc);
-                }
-            }
-        };
-        uint32_t va[kSlotPos / 2], vb[kSlotPos / 2];
-        fetch(0, va);
-        for (int k = 0; k < nslot && ok; k += 2) {
-            if (k + 1 < nslot) fetch(k + 1, vb);
-            chain(k, va);
-            if (!ok || k + 1 >= nslot) break;
-            if (k + 2 < nslot) fetch(k + 2, va);
-            chain(k + 1, vb);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&pfull[slot]);
         }
-        const int d = 32 * s + lane;
+    } else {
+        // The chain: the slot's positions run as groups of 16 whose V (widened to
+        // float) and p sit in registers; each group's loads are issued before the
+        // previous group's fmas, so the chain does not wait on shared memory. The
+        // next slot's barriers are tested early in each slot and waited on only
+        // if they were not complete then.
+        float acc = 0.0f;
+        float va[16], vb[16];
+        float4 pa[4], pb[4];
+        auto load = [&](int slot, int i0, float (&v)[16], float4 (&p)[4]) {
+            const uint16_t* vr = v16 + size_t(slot) * kVSlot * 32 + size_t(i0) * 32 + lane;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = f16_from_bits(vr[j * 32]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) p[j] = reinterpret_cast<const float4*>(p32 + size_t(slot) * kVSlot + i0)[j];
+        };
+        auto run = [&](const float (&v)[16], const float4 (&p)[4]) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                acc = fmaf(p[j].x, v[4 * j + 0], acc);  // exact products: one rounding per add
+                acc = fmaf(p[j].y, v[4 * j + 1], acc);
+                acc = fmaf(p[j].z, v[4 * j + 2], acc);
+                acc = fmaf(p[j].w, v[4 * j + 3], acc);
+            }
+        };
+        // slot k is ready when its V tile has landed and its p is formed
+        auto ready = [&](int k) {
+            const uint32_t par = uint32_t((k / kNr) & 1);
+            return __all_sync(0xffffffffu, wait(&vfull[k % kNr], par) && wait(&pfull[k % kNr], par));
+        };
+        constexpr int kGroups = kVSlot / 16;
+        static_assert(kGroups % 2 == 0, "groups alternate between two register sets");
+        bool ok = ready(0);
+        if (ok) load(0, 0, va, pa);
+        for (int k = 0; k < nslot && ok; ++k) {
+            const int slot = k % kNr;
+            const bool more = k + 1 < nslot;
+            const uint32_t npar = uint32_t(((k + 1) / kNr) & 1);
+            bool early = false;
+#pragma unroll
+            for (int gi = 0; gi < kGroups; gi += 2) {
+                load(slot, 16 * (gi + 1), vb, pb);
+                if (gi == 0 && more)
+                    early = mbar_test_wait(&vfull[(k + 1) % kNr], npar) && mbar_test_wait(&pfull[(k + 1) % kNr], npar);
+                run(va, pa);
+                if (gi + 2 < kGroups) {
+                    load(slot, 16 * (gi + 2), va, pa);
+                } else if (more) {
+                    ok = __all_sync(0xffffffffu, early) || ready(k + 1);
+                    if (ok) load((k + 1) % kNr, 0, va, pa);
+                }
+                run(vb, pb);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+        const int d = 32 * c + lane;
         if (d < hd && ok && !*reinterpret_cast<volatile int*>(&abort_flag)) {
             const size_t o = hb * hd + d;
             if (a.tp.peers) tp_store(a.tp, o, acc, *reinterpret_cast<const volatile unsigned*>(a.tp.epoch));
@@ -1160,9 +1186,9 @@ __global__ void __launch_bounds__(64) attn_xv_kernel(AttnParams a, const __grid_
     // A CTA that gave up lets its copies still in flight land before it leaves (bounded).
     __syncthreads();
     if (abort_flag && tid == 0) {
-        for (int k = max(0, issued - kSlots); k < issued; ++k) {
-            mbar_wait_bounded(&vfull[k % kSlots], uint32_t((k / kSlots) & 1), kAttnWaitNs);
-            mbar_wait_bounded(&efull[k % kSlots], uint32_t((k / kSlots) & 1), kAttnWaitNs);
+        for (int k = max(0, issued - kNr); k < issued; ++k) {
+            mbar_wait_bounded(&vfull[k % kNr], uint32_t((k / kNr) & 1), kAttnWaitNs);
+            mbar_wait_bounded(&efull[k % kNr], uint32_t((k / kNr) & 1), kAttnWaitNs);
         }
     }
 }
@@ -1355,19 +1381,30 @@ int launch_attention(AttnParams a, void* scratch, cudaStream_t s) {
     const bool swz = a.hd % 64 == 0;
     auto xs = swz ? attn_xs_kernel<GT, true> : attn_xs_kernel<GT, false>;
     st = opt_in(reinterpret_cast<const void*>(xs), xs_smem(GT, 256, swz).total);
-    if (!st) st = opt_in(reinterpret_cast<const void*>(attn_xv_kernel), xv_smem().total);
+    if (!st) st = opt_in(reinterpret_cast<const void*>(attn_xv_kernel), kXvSmemMost);
     if (st) return st;
     a.v3d = a.cache_stride != 0;
     CUtensorMap vmap, kmap;
-    if ((st = cache_tensor_map(a, a.vc, 32, kSlotPos, false, &vmap))) return st;
+    if ((st = cache_tensor_map(a, a.vc, 32, kVSlot, false, &vmap))) return st;
     if ((st = swz ? cache_tensor_map(a, a.kc, 64, 64, true, &kmap) : cache_tensor_map(a, a.kc, 32, kSlotPos, false, &kmap)))
         return st;
     const int ns = (a.hd + 31) / 32;
     st = syn_launch(xs, grid, kAttnThreads, xs_smem(GT, a.hd, swz).total, s, a, kmap);
     if (!st) st = syn_launch(attn_xe_kernel<GT>, grid, kAttnThreads, 0, s, a);
-    if (!st)
-        st = syn_launch(attn_xv_kernel, dim3(unsigned(a.n_head * ns), unsigned(a.n_q)), 64u, xv_smem().total, s, a,
-                        vmap);
+    if (!st) {
+        // One p.V CTA per SM while the grid fits the device: each chain warp then has its
+        // scheduler to itself (the kernel starts early, beside the previous kernels' CTAs,
+        // and would otherwise stack several CTAs on the SMs that are free first).
+        const unsigned ctas = unsigned(a.n_head * ns) * unsigned(a.n_q);
+        size_t smem = XvSmem::total;
+        int dev = 0, sms = 0, per_sm = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess &&
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess &&
+            cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) == cudaSuccess &&
+            ctas <= unsigned(sms))
+            smem = std::min(std::max(smem, size_t(per_sm) / 2 + 1024), kXvSmemMost);
+        st = syn_launch(attn_xv_kernel, dim3(unsigned(a.n_head * ns), unsigned(a.n_q)), 96u, smem, s, a, vmap);
+    }
     return st;
 }
 

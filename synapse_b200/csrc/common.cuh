@@ -280,6 +280,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// Whether phase `parity` of `bar` has completed, without waiting.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
 __device__ __forceinline__ uint64_t global_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -290,8 +300,10 @@ __device__ __forceinline__ uint64_t global_ns() {
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
-    while (!mbar_try_wait(bar, parity))
+    while (!mbar_try_wait(bar, parity)) {
         if (global_ns() - t0 > limit_ns) return false;
+        __nanosleep(32);  // back off: a waiting warp leaves the shared-memory pipe to the others
+    }
     return true;
 }
 

@@ -4,6 +4,7 @@
   python -m synapse_b200.kernel_bench attention [--ctx L] [--batch B] [--iters I]
   python -m synapse_b200.kernel_bench gemv_k [--type q4_k|q6_k] [--rows R --cols C] [--batch N]
   python -m synapse_b200.kernel_bench load [--path DIR]
+  python -m synapse_b200.kernel_bench llama70b [--batch B] [--ctx L] [--iters STEPS]
 
 gemv: the quantized GEMV (syn_gemv_q, planar weights) at the sweep shapes
 (4096x4096, 14336x4096, 4096x14336, 128256x4096) and batches 1/4/16, weights
@@ -158,6 +159,55 @@ def bench_layers(type_name="q4_0", n_layer=32, iters=2):
             "GBps": round(weight_bytes_total / (ms * 1e-3) / 1e9, 1)}
 
 
+LLAMA70B = dict(n_layer=80, n_embd=8192, n_ff=28672, n_head=64, n_head_kv=8, head_dim=128, n_vocab=128256,
+                rms_eps=1e-5, rope_base=500000.0)
+
+
+def bench_llama70b(batch, ctx=8192, steps=8, n_layer=80):
+    """the Llama-3-70B-shaped decode (Q4_0 everywhere, F16 KV) at context ctx, batch 1
+    (the captured step graph) or batch sequences per step (syn_session_step_batch: the weights stream once for
+    all of them). The KV caches hold seeded N(0,1) values for positions 0 .. ctx - steps - 1, so the timed
+    steps attend over ctx - steps .. ctx - 1 positions; weights random N(0, 0.02), quantized on the device."""
+    import time
+    import torch
+    from . import Q4_0 as _Q4, Session
+    cfg = dict(LLAMA70B, n_layer=n_layer, type_embd=_Q4, type_layers=_Q4, type_output=_Q4)
+    t0 = time.perf_counter()
+    if batch == 1:
+        sess = Session.synthetic(cfg, max_ctx=ctx, seed=70)
+    else:
+        sess = Session.synthetic_ex(cfg, max_ctx=ctx, max_seqs=batch, max_batch=batch, seed=70)
+    sess.fill_kv_random(ctx - steps, seed=71)
+    open_s = time.perf_counter() - t0
+    stream = torch.cuda.ExternalStream(sess.stream_handle())
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    pos0 = ctx - steps
+    if batch == 1:
+        sess.generate([1], pos0 - 2, 2)  # warm-up
+        ev[0].record(stream)
+        sess.generate([7], pos0, steps, wait=False)
+        ev[1].record(stream)
+        ev[1].synchronize()
+    else:
+        toks = [int(t) for t in np.random.default_rng(1).integers(0, LLAMA70B["n_vocab"], batch)]
+        sess.step_batch(toks, [pos0 - 1] * batch, logits=False)  # warm-up
+        ev[0].record(stream)
+        for i in range(steps):
+            _, nxt = sess.step_batch(toks, [pos0 + i] * batch, logits=False)
+            toks = [int(t) for t in nxt]
+        ev[1].record(stream)
+        ev[1].synchronize()
+    ms = ev[0].elapsed_time(ev[1]) / steps
+    row = LLAMA70B["n_head_kv"] * LLAMA70B["head_dim"]
+    weights = n_layer * ((8192 + 2 * 1024) * 8192 + 8192 * 8192 + 3 * 28672 * 8192) // 32 * 18 + 128256 * 8192 // 32 * 18
+    kv = batch * n_layer * 2 * (pos0 + steps // 2) * row * 2
+    sess.close()
+    return {"kernel": "llama70b_decode", "batch": batch, "ctx": ctx, "layers": n_layer, "ms_per_step": round(ms, 3),
+            "tok_s": round(batch / (ms * 1e-3), 2), "GBps": round((weights + kv) / (ms * 1e-3) / 1e9, 1),
+            "bytes_per_step": weights + kv, "open_s": round(open_s, 1),
+            "path": "step graph" if batch == 1 else "syn_session_step_batch (op by op)"}
+
+
 K_TYPES = {"q4_k": Q4_K, "q6_k": Q6_K}
 
 
@@ -301,7 +351,7 @@ def bench_attention(ctx, batch, iters=20, n_head=32, n_kv=8, hd=128, order=0):
 
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("what", choices=["gemv", "gemv_k", "attention", "load", "all"])
+    p.add_argument("what", choices=["gemv", "gemv_k", "attention", "load", "llama70b", "all"])
     p.add_argument("--path", default=None, help="load: directory for the synthetic GGUF file")
     p.add_argument("--type", default=None)
     p.add_argument("--rows", type=int, default=None)
@@ -340,6 +390,9 @@ def main():
                     print(json.dumps(bench_gemv_k(t, r, c, n, a.iters or 50)), flush=True)
     if a.what == "load":
         print(json.dumps(bench_load(a.path)), flush=True)
+    if a.what == "llama70b":
+        for b in ([a.batch] if a.batch else [1, 16]):
+            print(json.dumps(bench_llama70b(b, a.ctx or 8192, a.iters or 8)), flush=True)
     if a.what in ("attention", "all"):
         for L in ([a.ctx] if a.ctx else [1024, 4096, 16384, 32768]):
             for b in ([a.batch] if a.batch else [1, 8, 32]):
