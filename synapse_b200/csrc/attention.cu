@@ -1056,11 +1056,12 @@ __global__ void __launch_bounds__(96) attn_xv_kernel(AttnParams a, const __grid_
         mbar_expect_tx(bar, kVSlot * 4u);
         bulk_copy_g2s(es + size_t(k % kNr) * kVSlot, a.scores + hb * a.ld + size_t(k) * kVSlot, kVSlot * 4u, bar);
     };
-    // A wait that gives up after kAttnWaitNs, or at once when another warp gave up.
+    // A wait that gives up after kAttnWaitNs, or at once when another warp gave up;
+    // a waiting warp sleeps in the barrier (up to 1 us per try) instead of polling.
     auto wait = [&](uint64_t* bar, uint32_t par) -> bool {
         if (mbar_try_wait(bar, par)) return true;
         const uint64_t t0 = global_ns();
-        while (!mbar_try_wait(bar, par)) {
+        while (!mbar_try_wait_sleep(bar, par, 1000u)) {
             if (*reinterpret_cast<volatile int*>(&abort_flag)) return false;
             if (global_ns() - t0 > kAttnWaitNs) {
                 if (atomicExch(&abort_flag, 1) == 0) atomicAdd(&g_attn_timeouts, 1u);

@@ -125,12 +125,23 @@ __device__ const float2 kExp2J64[64] = {SYN_EXP2_J64_TABLE};
 #ifdef SYN_DEVICE_EXPF
 #include "libm_expf_exc.inc"  // generated into the build directory (libm_expf_scan.c)
 
+// The exception table's home slot of x and its first key, read at once (the
+// load is issued where the exp starts, so that its latency hides behind the
+// polynomial instead of following it).
+static __device__ __forceinline__ uint32_t libm_expf_slot(uint32_t xb, uint32_t& h) {
+    h = (xb * SYN_EXPF_EXC_MUL) >> (32 - SYN_EXPF_EXC_BITS);
+    uint32_t k;
+    asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(k) : "l"(&g_expf_exc[h]));
+    return k;
+}
 // Whether x is one of the inputs where the host library's expf is the other
-// neighbour of the correctly rounded result (open addressing, bounded probes).
-static __device__ __forceinline__ bool libm_expf_exception(uint32_t xb) {
+// neighbour of the correctly rounded result (open addressing, bounded probes);
+// k0 is the key in x's home slot h.
+static __device__ __forceinline__ bool libm_expf_exception(uint32_t xb, uint32_t h, uint32_t k0) {
+    if (k0 == xb) return true;
+    if (k0 == 0u) return false;
     const uint32_t mask = (1u << SYN_EXPF_EXC_BITS) - 1u;
-    const uint32_t h = (xb * SYN_EXPF_EXC_MUL) >> (32 - SYN_EXPF_EXC_BITS);
-    for (int i = 0; i < SYN_EXPF_EXC_PROBES; ++i) {
+    for (int i = 1; i < SYN_EXPF_EXC_PROBES; ++i) {
         const uint32_t k = __ldg(&g_expf_exc[(h + uint32_t(i)) & mask]);
         if (k == xb) return true;
         if (k == 0u) return false;
@@ -149,6 +160,8 @@ __device__ __forceinline__ void two_sum(float a, float b, float& s, float& e) {
 // through the read-only cache) or a shared-memory copy of it.
 template <bool kSharedTab>
 __device__ __forceinline__ float exp_rn_core(float x, const float2* tab) {
+    uint32_t slot;
+    const uint32_t key0 = libm_expf_slot(__float_as_uint(x), slot);
     const float kf = rintf(__fmul_rn(x, 0x1.715476p+6f));  // 64 / ln2
     const int k = int(kf);
     // r = x - k ln2/64 as r_hi + r_lo: k * C_hi exactly (product and its
@@ -187,7 +200,7 @@ __device__ __forceinline__ float exp_rn_core(float x, const float2* tab) {
     const uint32_t yb = __float_as_uint(y);
     float ulp = __uint_as_float((yb & 0x7f800000u) - (23u << 23));
     if (res < 0.0f && (yb & 0x007fffffu) == 0u) ulp = __fmul_rn(ulp, 0.5f);
-    if (fabsf(res) > __fmul_rn(0.496f, ulp) && libm_expf_exception(__float_as_uint(x)))
+    if (fabsf(res) > __fmul_rn(0.496f, ulp) && libm_expf_exception(__float_as_uint(x), slot, key0))
         out = __uint_as_float(__float_as_uint(out) + (res > 0.0f ? 1u : 0xffffffffu));
     return out;
 }
@@ -277,6 +290,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
         : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// As mbar_try_wait, but a thread whose phase is not complete sleeps in the
+// barrier until it completes or about `hint_ns` pass (no polling of the
+// shared-memory pipe meanwhile).
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
         : "memory");
     return ok != 0;
 }

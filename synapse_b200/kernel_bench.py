@@ -5,6 +5,7 @@
   python -m synapse_b200.kernel_bench gemv_k [--type q4_k|q6_k] [--rows R --cols C] [--batch N]
   python -m synapse_b200.kernel_bench load [--path DIR]
   python -m synapse_b200.kernel_bench llama70b [--batch B] [--ctx L] [--iters STEPS]
+  python -m synapse_b200.kernel_bench excursions [--ctx L]
 
 gemv: the quantized GEMV (syn_gemv_q, planar weights) at the sweep shapes
 (4096x4096, 14336x4096, 4096x14336, 128256x4096) and batches 1/4/16, weights
@@ -27,6 +28,7 @@ import argparse
 import ctypes
 import json
 import math
+import os
 
 import numpy as np
 
@@ -208,6 +210,44 @@ def bench_llama70b(batch, ctx=8192, steps=8, n_layer=80):
             "path": "step graph" if batch == 1 else "syn_session_step_batch (op by op)"}
 
 
+def bench_excursions(ctx=4096, seed=1234):
+    """How often the split attention order moves the logits past the north-star tolerance: two sessions of the
+    8B-shaped Q4_0 model with the same seeded weights, one with the attention sums in the reference's order
+    (bit-identical to the oracle) and one with SYN_ATTN_ORDER=split, fed the same seeded random tokens at
+    positions 0 .. ctx - 1 (teacher-forced). Per step: d = max |logit_split - logit_exact| / std(logit_exact)."""
+    from . import Q4_0 as _Q4, Q8_0 as _Q8, Session
+    cfg = dict(n_layer=32, n_embd=4096, n_ff=14336, n_head=32, n_head_kv=8, head_dim=128, n_vocab=128256,
+               rms_eps=1e-5, rope_base=500000.0, type_embd=_Q4, type_layers=_Q4, type_output=_Q8)
+    prev = os.environ.pop("SYN_ATTN_ORDER", None)
+    exact = Session.synthetic(cfg, max_ctx=ctx, seed=seed)
+    os.environ["SYN_ATTN_ORDER"] = "split"
+    split = Session.synthetic(cfg, max_ctx=ctx, seed=seed)
+    if prev is None:
+        os.environ.pop("SYN_ATTN_ORDER")
+    else:
+        os.environ["SYN_ATTN_ORDER"] = prev
+    toks = np.random.default_rng(seed).integers(0, cfg["n_vocab"], ctx)
+    d = np.zeros(ctx)
+    argmax_diff = 0
+    for pos in range(ctx):
+        le, ae = exact.step(int(toks[pos]), pos)
+        ls, as_ = split.step(int(toks[pos]), pos)
+        d[pos] = float(np.max(np.abs(ls - le)) / np.std(le))
+        argmax_diff += int(ae != as_)
+    exact.close()
+    split.close()
+    past = d[256:]
+    over = np.nonzero(d > 1e-2)[0]
+    return {"kernel": "excursions", "ctx": ctx, "steps": ctx, "steps_past_256": int(past.size),
+            "first_over_1e-2_std": int(over[0]) if over.size else None,
+            "d_at_257_264": [float(x) for x in d[257:265]],
+            "steps_differing": int(np.count_nonzero(d)), "steps_over_1e-2_std": int(np.count_nonzero(d > 1e-2)),
+            "max_d": float(d.max()), "p99_d": float(np.percentile(past, 99)), "median_d": float(np.median(past)),
+            "argmax_differs": argmax_diff,
+            "note": "d = max|logit_split - logit_exact| / std(logit_exact) per step; positions <= 256 are one chunk "
+                    "(both orders exact)"}
+
+
 K_TYPES = {"q4_k": Q4_K, "q6_k": Q6_K}
 
 
@@ -351,7 +391,7 @@ def bench_attention(ctx, batch, iters=20, n_head=32, n_kv=8, hd=128, order=0):
 
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("what", choices=["gemv", "gemv_k", "attention", "load", "llama70b", "all"])
+    p.add_argument("what", choices=["gemv", "gemv_k", "attention", "load", "llama70b", "excursions", "all"])
     p.add_argument("--path", default=None, help="load: directory for the synthetic GGUF file")
     p.add_argument("--type", default=None)
     p.add_argument("--rows", type=int, default=None)
@@ -390,6 +430,8 @@ def main():
                     print(json.dumps(bench_gemv_k(t, r, c, n, a.iters or 50)), flush=True)
     if a.what == "load":
         print(json.dumps(bench_load(a.path)), flush=True)
+    if a.what == "excursions":
+        print(json.dumps(bench_excursions(a.ctx or 4096)), flush=True)
     if a.what == "llama70b":
         for b in ([a.batch] if a.batch else [1, 16]):
             print(json.dumps(bench_llama70b(b, a.ctx or 8192, a.iters or 8)), flush=True)
