@@ -1,7 +1,8 @@
 """Kernel microbenchmarks of the decode path (BASELINE configs 2 and 3).
 
   python -m synapse_b200.kernel_bench gemv [--type q4_0|q8_0] [--rows R --cols C] [--batch N] [--iters I]
-  python -m synapse_b200.kernel_bench attention [--ctx L] [--batch B] [--iters I]
+  python -m synapse_b200.kernel_bench attention [--ctx L] [--batch B] [--iters I] [--order reference|split|both]
+  torchrun --nproc-per-node N -m synapse_b200.kernel_bench attention ...   (KV-head-sharded over N GPUs)
   python -m synapse_b200.kernel_bench gemv_k [--type q4_k|q6_k] [--rows R --cols C] [--batch N]
   python -m synapse_b200.kernel_bench load [--path DIR]
   python -m synapse_b200.kernel_bench llama70b [--batch B] [--ctx L] [--iters STEPS]
@@ -389,6 +390,37 @@ def bench_attention(ctx, batch, iters=20, n_head=32, n_kv=8, hd=128, order=0):
             "rotating_copies": copies}
 
 
+def bench_attention_sharded(a, world):
+    """BASELINE config 3 KV-head-sharded (run under torchrun, one rank per GPU): rank r holds KV heads
+    [r * 8 / world, (r + 1) * 8 / world) and their query heads, as the tensor-parallel session shards them, and
+    times its own attention call; the line reports the slowest rank (the ranks meet in a gloo reduction of
+    their times only: the attention itself exchanges nothing)."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    rank = int(os.environ.get("RANK", "0"))
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", str(rank))))
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+    try:
+        n_head, n_kv = 32 // world, 8 // world
+        for L in ([a.ctx] if a.ctx else [1024, 4096, 16384, 32768]):
+            for b in ([a.batch] if a.batch else [1, 8, 32]):
+                for o in ({"reference": [0], "split": [1], "both": [0, 1]}[a.order]):
+                    r = bench_attention(L, b, a.iters or 20, n_head=n_head, n_kv=n_kv, order=o)
+                    t = torch.tensor([r["us_per_launch"]], dtype=torch.float64)
+                    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                    if rank == 0:
+                        alg = r["bytes_per_launch"] * world
+                        print(json.dumps({"kernel": "attention_sharded", "order": r["order"], "ctx": L, "batch": b,
+                                          "gpus": world, "heads_per_gpu": r["heads"],
+                                          "us_per_launch_max_over_ranks": round(float(t.item()), 3),
+                                          "bytes_all_gpus": alg,
+                                          "GBps_all_gpus": round(alg / (float(t.item()) * 1e-6) / 1e9, 1)}),
+                              flush=True)
+    finally:
+        dist.destroy_process_group()
+
+
 def main():
     p = argparse.ArgumentParser()
     p.add_argument("what", choices=["gemv", "gemv_k", "attention", "load", "llama70b", "excursions", "all"])
@@ -436,6 +468,10 @@ def main():
         for b in ([a.batch] if a.batch else [1, 16]):
             print(json.dumps(bench_llama70b(b, a.ctx or 8192, a.iters or 8)), flush=True)
     if a.what in ("attention", "all"):
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        if world > 1:
+            bench_attention_sharded(a, world)
+            return
         for L in ([a.ctx] if a.ctx else [1024, 4096, 16384, 32768]):
             for b in ([a.batch] if a.batch else [1, 8, 32]):
                 for o in ({"reference": [0], "split": [1], "both": [0, 1]}[a.order]):
