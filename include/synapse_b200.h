@@ -167,8 +167,8 @@ int syn_gemv_fusable(int type, int layout, int rows, int cols, int n_tok, int ou
  *   max_ctx * n_kv * head_dim for independent sequences (batched decode), or 0
  *   for tokens of one sequence (then append must be 0: use syn_rope_kv_append
  *   first, as session.hpp:349-356 appends every token before attending).
- * max_len bounds pos[b] + 1 for every b (it sizes the CTA cluster per KV head
- * and the score scratch).
+ * max_len bounds pos[b] + 1 for every b (it sizes the grid and the score
+ * scratch).
  * rope_mode: 0 normal (Llama), 1 neox. freq_factors: NULL or head_dim/2 floats
  * (device). yarn: NULL or 5 floats {freq_scale, ext_factor, attn_factor,
  * corr_low, corr_high} (host), attention.hpp:60-66.

@@ -385,6 +385,12 @@ __global__ void __launch_bounds__(W * 32) gemv_stage_kernel(GemvArgs p) {
         for (int k = 0; k < min(NB, nbatch); ++k) issue(k);
     }
     __syncwarp();
+    // this thread's first half-block of gamma (a weight: read before the wait)
+    float4 gpre[4];
+    const bool pre = p.in_mode == SYN_IN_RMSNORM && int(threadIdx.x) < p.cols / 16;
+    if (pre)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) gpre[k] = __ldg(reinterpret_cast<const float4*>(p.gamma + size_t(threadIdx.x) * 16) + k);
     pdl_launch_dependents();
     pdl_wait();  // the activations (and the residual) come from the previous kernel
     const bool push = p.tp.peers && p.tp.out_ll;
@@ -396,9 +402,10 @@ __global__ void __launch_bounds__(W * 32) gemv_stage_kernel(GemvArgs p) {
         for (int i = threadIdx.x; i < nb; i += blockDim.x)
             dsum[i] = make_float2(__ldg(p.act.d + i), __int_as_float(__ldg(p.act.sum + i)));
     } else if (p.tp.peers && p.tp.in_ll) {  // a gathered vector: every rank's words of this step
-        quantize_act1<true>(p.x, p.gamma, p.eps, p.in_mode == SYN_IN_RMSNORM, p.cols, aq, dsum, &p.tp, ep);
+        quantize_act1<true>(p.x, p.gamma, p.eps, p.in_mode == SYN_IN_RMSNORM, p.cols, aq, dsum, &p.tp, ep,
+                            pre ? gpre : nullptr);
     } else {
-        quantize_act1(p.x, p.gamma, p.eps, p.in_mode == SYN_IN_RMSNORM, p.cols, aq, dsum);
+        quantize_act1(p.x, p.gamma, p.eps, p.in_mode == SYN_IN_RMSNORM, p.cols, aq, dsum, nullptr, 0u, pre ? gpre : nullptr);
     }
     __syncthreads();
 

@@ -149,7 +149,8 @@ __device__ void quantize_act(const float* x, const float* gamma, float eps, bool
 
 // One token's input quantized into the staged layout by the whole block: each
 // thread takes 16-value halves of blocks (lanes 2k, 2k+1 form one block, so the
-// block's amax and sum meet by one shuffle), all its loads in flight at once.
+// block's amax and sum meet by one shuffle), the loads of up to two halves in
+// flight at once.
 // The same arithmetic as quantize_act: rms_norm (double sum of float squares,
 // mean, 1 / sqrt(mean + eps), (x * scale) * gamma), then quant/q8.hpp:54-69.
 // Every thread of the block calls it (it synchronizes the block).
@@ -157,9 +158,11 @@ __device__ void quantize_act(const float* x, const float* gamma, float eps, bool
 // TpSync); each value is read once its word carries this step's epoch.
 template <bool WORDS = false>
 __device__ inline void quantize_act1(const float* x, const float* gamma, float eps, bool norm, int cols, uint8_t* aq,
-                              float2* dsum, const TpSync* tp = nullptr, unsigned epoch = 0) {
+                              float2* dsum, const TpSync* tp = nullptr, unsigned epoch = 0,
+                              const float4* gamma_first = nullptr) {
     __shared__ double red[32];
-    const int nh = cols / 16, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int kIt = 2;  // half-blocks per thread whose loads are in flight together
+    const int nh = cols / 16, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nt = int(blockDim.x);
     // the 16 values of half-block h
     auto load16 = [&](int h, float (&v)[16]) {
         if constexpr (WORDS) {
@@ -175,20 +178,19 @@ __device__ inline void quantize_act1(const float* x, const float* gamma, float e
     };
     float scale = 1.0f;
     if (norm) {
+        // thread t sums its half-blocks t, t + nt, ... in that order
         double sum = 0.0;
-        for (int h = threadIdx.x; h < nh; h += blockDim.x) {
-            float fv[16];
-            load16(h, fv);
-            float4 f[4];
+        for (int h0 = 0; h0 < nh; h0 += kIt * nt) {
+            float v[kIt][16];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) f[k] = make_float4(fv[4 * k], fv[4 * k + 1], fv[4 * k + 2], fv[4 * k + 3]);
+            for (int i = 0; i < kIt; ++i)
+                if (h0 + i * nt + int(threadIdx.x) < nh) load16(h0 + i * nt + int(threadIdx.x), v[i]);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                sum += double(__fmul_rn(f[k].x, f[k].x));
-                sum += double(__fmul_rn(f[k].y, f[k].y));
-                sum += double(__fmul_rn(f[k].z, f[k].z));
-                sum += double(__fmul_rn(f[k].w, f[k].w));
-            }
+            for (int i = 0; i < kIt; ++i)
+                if (h0 + i * nt + int(threadIdx.x) < nh) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) sum += double(__fmul_rn(v[i][j], v[i][j]));
+                }
         }
         sum = warp_sum_d(sum);
         if (lane == 0) red[warp] = sum;
@@ -198,47 +200,55 @@ __device__ inline void quantize_act1(const float* x, const float* gamma, float e
         const float mean = float(tot / double(cols));
         scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
     }
-    for (int h0 = 0; h0 < nh; h0 += blockDim.x) {
-        const int h = h0 + int(threadIdx.x);
-        // lanes of this pass (a prefix of the warp; block pairs never straddle it)
-        const int live = min(32, max(0, nh - (h0 + warp * 32)));
-        if (h >= nh) continue;
-        const unsigned mask = live == 32 ? 0xffffffffu : ((1u << live) - 1u);
-        float v[16];
-        load16(h, v);
-        if (norm) {
-            const float4* g4 = reinterpret_cast<const float4*>(gamma + size_t(h) * 16);
+    for (int h0 = 0; h0 < nh; h0 += kIt * nt) {
+        float vv[kIt][16];
+#pragma unroll
+        for (int i = 0; i < kIt; ++i)
+            if (h0 + i * nt + int(threadIdx.x) < nh) load16(h0 + i * nt + int(threadIdx.x), vv[i]);
+#pragma unroll
+        for (int i = 0; i < kIt; ++i) {
+            const int hp = h0 + i * nt, h = hp + int(threadIdx.x);
+            // lanes of this pass (a prefix of the warp; block pairs never straddle it)
+            const int live = min(32, max(0, nh - (hp + warp * 32)));
+            if (h >= nh) continue;
+            const unsigned mask = live == 32 ? 0xffffffffu : ((1u << live) - 1u);
+            float* v = vv[i];
+            if (norm) {
+                const float4* g4 = reinterpret_cast<const float4*>(gamma + size_t(h) * 16);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    // the first half-block's gamma may have been read before the kernel's wait
+                    const float4 g = gamma_first && h == int(threadIdx.x) ? gamma_first[k] : __ldg(g4 + k);
+                    v[4 * k] = __fmul_rn(__fmul_rn(v[4 * k], scale), g.x);
+                    v[4 * k + 1] = __fmul_rn(__fmul_rn(v[4 * k + 1], scale), g.y);
+                    v[4 * k + 2] = __fmul_rn(__fmul_rn(v[4 * k + 2], scale), g.z);
+                    v[4 * k + 3] = __fmul_rn(__fmul_rn(v[4 * k + 3], scale), g.w);
+                }
+            }
+            float amax = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(v[j]));
+            amax = fmaxf(amax, __shfl_xor_sync(mask, amax, 1));
+            const float d = __fdiv_rn(amax, 127.0f);
+            const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+            int qsum = 0;
+            uint32_t packed[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                const float4 g = __ldg(g4 + k);
-                v[4 * k] = __fmul_rn(__fmul_rn(v[4 * k], scale), g.x);
-                v[4 * k + 1] = __fmul_rn(__fmul_rn(v[4 * k + 1], scale), g.y);
-                v[4 * k + 2] = __fmul_rn(__fmul_rn(v[4 * k + 2], scale), g.z);
-                v[4 * k + 3] = __fmul_rn(__fmul_rn(v[4 * k + 3], scale), g.w);
+                const int q0 = int(roundf(__fmul_rn(v[4 * k], id)));
+                const int q1 = int(roundf(__fmul_rn(v[4 * k + 1], id)));
+                const int q2 = int(roundf(__fmul_rn(v[4 * k + 2], id)));
+                const int q3 = int(roundf(__fmul_rn(v[4 * k + 3], id)));
+                qsum += q0 + q1 + q2 + q3;
+                packed[k] = (uint32_t(q0) & 0xffu) | ((uint32_t(q1) & 0xffu) << 8) | ((uint32_t(q2) & 0xffu) << 16) |
+                            ((uint32_t(q3) & 0xffu) << 24);
             }
+            qsum += __shfl_xor_sync(mask, qsum, 1);
+            const int b = h >> 1;
+            *reinterpret_cast<uint4*>(aq + sact_off(b) + 16 * (h & 1)) =
+                make_uint4(packed[0], packed[1], packed[2], packed[3]);
+            if ((h & 1) == 0) dsum[b] = make_float2(f16_from_bits(f16_bits(d)), __int_as_float(qsum));
         }
-        float amax = 0.0f;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(v[j]));
-        amax = fmaxf(amax, __shfl_xor_sync(mask, amax, 1));
-        const float d = __fdiv_rn(amax, 127.0f);
-        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-        int qsum = 0;
-        uint32_t packed[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int q0 = int(roundf(__fmul_rn(v[4 * k], id)));
-            const int q1 = int(roundf(__fmul_rn(v[4 * k + 1], id)));
-            const int q2 = int(roundf(__fmul_rn(v[4 * k + 2], id)));
-            const int q3 = int(roundf(__fmul_rn(v[4 * k + 3], id)));
-            qsum += q0 + q1 + q2 + q3;
-            packed[k] = (uint32_t(q0) & 0xffu) | ((uint32_t(q1) & 0xffu) << 8) | ((uint32_t(q2) & 0xffu) << 16) |
-                        ((uint32_t(q3) & 0xffu) << 24);
-        }
-        qsum += __shfl_xor_sync(mask, qsum, 1);
-        const int b = h >> 1;
-        *reinterpret_cast<uint4*>(aq + sact_off(b) + 16 * (h & 1)) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-        if ((h & 1) == 0) dsum[b] = make_float2(f16_from_bits(f16_bits(d)), __int_as_float(qsum));
     }
 }
 
