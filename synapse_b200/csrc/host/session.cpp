@@ -1531,7 +1531,9 @@ extern "C" int syn_session_fill_kv_random(syn_session* s, int n_pos, uint64_t se
 extern "C" int syn_session_launches_per_step(const syn_session* s) {
     if (!s) return 0;
     int n = 1 + (s->p2p ? 1 : 0);  // advance (and the epoch under peer gathers)
-    for (const op& o : s->ops) n += o.kind == opk::attention ? 2 : o.kind == opk::allgather ? 0 : 1;  // NCCL's own kernels aside
+    // attention: scores, exp and p.V kernels in the reference order, two kernels split; NCCL's own kernels aside
+    const int attn = s->attn_order == SYN_ORDER_SPLIT ? 2 : 3;
+    for (const op& o : s->ops) n += o.kind == opk::attention ? attn : o.kind == opk::allgather ? 0 : 1;
     return n;
 }
 

@@ -7,6 +7,7 @@
   python -m synapse_b200.kernel_bench load [--path DIR]
   python -m synapse_b200.kernel_bench llama70b [--batch B] [--ctx L] [--iters STEPS]
   python -m synapse_b200.kernel_bench excursions [--ctx L]
+  python -m synapse_b200.kernel_bench decode [--ctx L] [--iters STEPS]
 
 gemv: the quantized GEMV (syn_gemv_q, planar weights) at the sweep shapes
 (4096x4096, 14336x4096, 4096x14336, 128256x4096) and batches 1/4/16, weights
@@ -209,6 +210,36 @@ def bench_llama70b(batch, ctx=8192, steps=8, n_layer=80):
             "tok_s": round(batch / (ms * 1e-3), 2), "GBps": round((weights + kv) / (ms * 1e-3) / 1e9, 1),
             "bytes_per_step": weights + kv, "open_s": round(open_s, 1),
             "path": "step graph" if batch == 1 else "syn_session_step_batch (op by op)"}
+
+
+def bench_decode(ctx=4096, steps=20):
+    """One Llama-3-8B-shaped Q4_0 decode step (the captured step graph) at context ctx: the KV
+    caches hold seeded values for positions 0 .. ctx - steps - 2, one untimed step warms up, then steps - 1
+    timed device steps; the step at position ctx - 1 alone runs between cudaProfilerStart and cudaProfilerStop,
+    so `ncu --profile-from-start off` lists exactly one step's launches."""
+    import torch
+    from . import Q4_0 as _Q4, Q8_0 as _Q8, Session
+    cfg = dict(n_layer=32, n_embd=4096, n_ff=14336, n_head=32, n_head_kv=8, head_dim=128, n_vocab=128256,
+               rms_eps=1e-5, rope_base=500000.0, type_embd=_Q4, type_layers=_Q4, type_output=_Q8)
+    sess = Session.synthetic(cfg, max_ctx=ctx, seed=1234)
+    pos0 = ctx - steps - 1
+    sess.fill_kv_random(pos0, seed=5)
+    stream = torch.cuda.ExternalStream(sess.stream_handle())
+    sess.generate([1], pos0, 1)  # warm-up
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    ev[0].record(stream)
+    sess.generate([7], pos0 + 1, steps - 1, wait=False)
+    ev[1].record(stream)
+    ev[1].synchronize()
+    torch.cuda.profiler.start()
+    sess.generate([9], ctx - 1, 1)
+    torch.cuda.profiler.stop()
+    ms = ev[0].elapsed_time(ev[1]) / max(1, steps - 1)
+    n = sess.launches_per_step()
+    sess.close()
+    return {"kernel": "decode_step", "ctx": ctx, "timed_steps": steps - 1, "ms_per_step": round(ms, 4),
+            "tok_s": round(1e3 / ms, 2), "launches_per_step": n,
+            "positions": f"{pos0 + 1}..{ctx - 2} timed, {ctx - 1} between the profiler marks"}
 
 
 def bench_excursions(ctx=4096, seed=1234):
@@ -423,7 +454,7 @@ def bench_attention_sharded(a, world):
 
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("what", choices=["gemv", "gemv_k", "attention", "load", "llama70b", "excursions", "all"])
+    p.add_argument("what", choices=["gemv", "gemv_k", "attention", "load", "llama70b", "excursions", "decode", "all"])
     p.add_argument("--path", default=None, help="load: directory for the synthetic GGUF file")
     p.add_argument("--type", default=None)
     p.add_argument("--rows", type=int, default=None)
@@ -462,6 +493,8 @@ def main():
                     print(json.dumps(bench_gemv_k(t, r, c, n, a.iters or 50)), flush=True)
     if a.what == "load":
         print(json.dumps(bench_load(a.path)), flush=True)
+    if a.what == "decode":
+        print(json.dumps(bench_decode(a.ctx or 4096, a.iters or 20)), flush=True)
     if a.what == "excursions":
         print(json.dumps(bench_excursions(a.ctx or 4096)), flush=True)
     if a.what == "llama70b":
