@@ -170,6 +170,25 @@ def test_synthetic_8b_shape_against_oracle():
     sess.close()
 
 
+def test_synthetic_70b_shape_one_layer_against_oracle():
+    # BASELINE config 5's shapes (one of the 80 layers): d 8192, 64 query / 8 KV heads, ff 28672, Q4_0 throughout
+    # (embedding, layers and head), weights made on the device; the oracle runs on the same weights copied back
+    cfg70 = dict(n_layer=1, n_embd=8192, n_ff=28672, n_head=64, n_head_kv=8, head_dim=128, n_vocab=128256,
+                 rms_eps=1e-5, rope_base=500000.0)
+    cfg = dict(cfg70, type_embd=syn.Q4_0, type_layers=syn.Q4_0, type_output=syn.Q4_0)
+    sess = syn.Session.synthetic(cfg, max_ctx=64, seed=70)
+    ref = orc.Llama(cfg70, session_weights(sess, 1), max_ctx=64)
+    tok = 4242
+    for pos in range(3):
+        got, nxt = sess.step(tok, pos)
+        want = ref.step(tok, pos)
+        assert np.max(np.abs(got - want)) <= logit_tol(want), pos
+        if nxt != int(np.argmax(want)):
+            assert top2_gap(want) < logit_tol(want), pos
+        tok = int(np.argmax(want))
+    sess.close()
+
+
 def test_long_context_8b_shape_teacher_forced_against_oracle():
     # BASELINE config 4 past one attention chunk: a 2-layer 8B-shaped model (Q4_0 layers, Q8_0 head) decodes
     # greedily on the GPU to position 4095. At sampled positions the oracle runs the same step on the GPU's own
